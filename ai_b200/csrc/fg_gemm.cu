@@ -1,0 +1,505 @@
+// tcgen05 TF32 / split-TF32 GEMM for sm_100a with fused epilogues.
+//
+// C[M, Nout] = epilogue(A · Bᵀ), A [M, K] and B [Nb, K] row-major (both
+// K-major operands, the layout the encoder keeps its [out, in] weights in).
+// This replaces the reference's blocked SGEMM (internal/blas/gemm.go:562-702)
+// and its epilogue (gemm.go:316-347) on the encoder's hot path.
+//
+// Structure: a persistent kernel, one CTA per SM, 6 warps.
+//   warp 0      TMA producer: 128-byte-swizzled [rows × 32 fp32] tiles of A
+//               (and A_lo), B (and B_lo) into a multi-stage smem ring.
+//   warp 1      TMEM allocator and MMA issuer: one thread issues
+//               tcgen05.mma.kind::tf32 (M=128, N=BN, K=8) per pass, into one
+//               of two TMEM accumulators (double buffered, 2·BN columns).
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator (one row per
+//               thread), fused row scale / bias / activation / gate / mul /
+//               residual, optional split of the result into TF32 hi/lo, and
+//               the global store; overlaps the next tile's main loop.
+// Split-TF32 accumulates A·B + A·B_lo + A_lo·B into the same accumulator;
+// an operand whose low part is identically zero (bf16-exact weights) has
+// no low pass, which changes nothing in the result.
+#include <algorithm>
+#include <cudaTypedefs.h>
+
+#include "fg_internal.h"
+#include "fg_ptx.cuh"
+
+namespace fg {
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 32;  // fp32 per 128-byte swizzle row
+constexpr int kUmmaK = 8;
+constexpr int kThreads = 192;
+constexpr int kSmemLimit = 232448;  // 227 KB opt-in dynamic shared memory
+
+struct KParams {
+  int M, Nout, K;
+  int ntm, ntn, nk;
+  GemmEpilogue e;
+  int* err;
+};
+
+template <int BN, bool SA, bool SB>
+struct Cfg {
+  static constexpr uint32_t kABytes = kBM * kBK * 4;
+  static constexpr uint32_t kBBytes = BN * kBK * 4;
+  static constexpr uint32_t kStageBytes = kABytes * (SA ? 2 : 1) + kBBytes * (SB ? 2 : 1);
+  static constexpr int kStagesRaw = (kSmemLimit - 2048) / kStageBytes;
+  static constexpr int kStages = kStagesRaw > 6 ? 6 : kStagesRaw;
+  static constexpr uint32_t kTmemCols = 2 * BN;
+  static constexpr size_t kSmemBytes = 1024 + size_t(kStages) * kStageBytes + 256;
+  static_assert(kStages >= 2, "tile too large for shared memory");
+};
+
+// Eigen's rational tanh for float (the method the reference's kernels use,
+// internal/kernel/generic.go:309-360): odd degree-13 over even degree-6
+// polynomial after clamping to the point where it reaches ±1.
+__device__ __forceinline__ float tanh_rational(float x) {
+  if (x > -0.0004f && x < 0.0004f) return x;
+  if (x >= 9.f) return 1.f;
+  if (x <= -9.f) return -1.f;
+  const float c = 7.99881172180175781f;
+  x = fminf(fmaxf(x, -c), c);
+  const float x2 = x * x;
+  float p = -2.76076847742355e-16f;
+  p = p * x2 + 2.00018790482477e-13f;
+  p = p * x2 + -8.60467152213735e-11f;
+  p = p * x2 + 5.12229709037114e-08f;
+  p = p * x2 + 1.48572235717979e-05f;
+  p = p * x2 + 6.37261928875436e-04f;
+  p = p * x2 + 4.89352455891786e-03f;
+  p = p * x;
+  float q = 1.19825839466702e-06f;
+  q = q * x2 + 1.18534705686654e-04f;
+  q = q * x2 + 2.26843463243900e-03f;
+  q = q * x2 + 4.89352518554385e-03f;
+  return p / q;
+}
+
+// tanh-GELU in the reference's operation order (internal/kernel/math.go:122-143):
+// u = c·(x + 0.044715·x³); 0.5·x·(1 + tanh(u)).
+__device__ __forceinline__ float gelu_tanh(float x) {
+  float z = x * x;
+  z = z * x;
+  z = z * 0.044715f;
+  z = x + z;
+  z = z * 0.7978845608028654f;
+  float t = tanh_rational(z);
+  t = t + 1.f;
+  t = t * x;
+  return t * 0.5f;
+}
+
+__device__ __forceinline__ float apply_act(float v, int act) {
+  if (act == FG_ACT_RELU) return fmaxf(v, 0.f);
+  if (act == FG_ACT_GELU) return gelu_tanh(v);
+  if (act == kActTanh) return tanh_rational(v);
+  return v;
+}
+
+__device__ __forceinline__ void store_row32(float* dst, const float (&v)[32], int ncols,
+                                            bool vec_ok) {
+  if (vec_ok && ncols == 32) {
+    float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < ncols) dst[j] = v[j];
+  }
+}
+
+template <int BN, bool SA, bool SB>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tf32_kernel(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mAlo,
+                     const __grid_constant__ CUtensorMap mB, const __grid_constant__ CUtensorMap mBlo,
+                     const KParams p) {
+  using C = Cfg<BN, SA, SB>;
+  constexpr int S = C::kStages;
+  constexpr uint32_t kIdesc = idesc_tf32(kBM, BN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + size_t(S) * C::kStageBytes);
+  // bars[0..S) full, [S..2S) empty, [2S..2S+2) acc_full, [2S+2..2S+4) acc_empty, [2S+4] drain
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int ntiles = p.ntm * p.ntn;
+
+  auto full_bar = [&](int s) { return smem_u32(&bars[s]); };
+  auto empty_bar = [&](int s) { return smem_u32(&bars[S + s]); };
+  auto accf_bar = [&](int a) { return smem_u32(&bars[2 * S + a]); };
+  auto acce_bar = [&](int a) { return smem_u32(&bars[2 * S + 2 + a]); };
+  const uint32_t drain_bar = smem_u32(&bars[2 * S + 4]);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(accf_bar(a), 1);
+      mbar_init(acce_bar(a), 128);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&mA);
+    tma_prefetch_desc(&mB);
+    if (SA) tma_prefetch_desc(&mAlo);
+    if (SB) tma_prefetch_desc(&mBlo);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_holder), C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------ TMA producer
+      int armed[S];
+#pragma unroll
+      for (int s = 0; s < S; ++s) armed[s] = 0;
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = blockIdx.x; tile < ntiles && !*abort_flag; tile += gridDim.x) {
+        const int tm = tile / p.ntn, tn = tile % p.ntn;
+        for (int kb = 0; kb < p.nk; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag, p.err, kDevTimeoutEmpty)) break;
+          const uint32_t fb = full_bar(stage);
+          mbar_arrive_expect_tx(fb, C::kStageBytes);
+          armed[stage]++;
+          uint32_t dst = smem_u32(smem + size_t(stage) * C::kStageBytes);
+          tma_load_2d(dst, &mA, fb, kb * kBK, tm * kBM);
+          dst += C::kABytes;
+          if (SA) {
+            tma_load_2d(dst, &mAlo, fb, kb * kBK, tm * kBM);
+            dst += C::kABytes;
+          }
+          tma_load_2d(dst, &mB, fb, kb * kBK, tn * BN);
+          dst += C::kBBytes;
+          if (SB) tma_load_2d(dst, &mBlo, fb, kb * kBK, tn * BN);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (*abort_flag) {
+        // Let every load this thread issued land before the CTA retires.
+        for (int s = 0; s < S; ++s) {
+          if (armed[s] == 0) continue;
+          const uint32_t par = uint32_t(armed[s] - 1) & 1u;
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(full_bar(s), par)) {
+            if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+              atomicCAS(p.err, 0, kDevTimeoutDrain);
+              break;
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------ MMA issuer
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool issued = false;
+      for (int tile = blockIdx.x; tile < ntiles && !*abort_flag; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_par = uint32_t(local >> 1) & 1u;
+        if (!mbar_wait(acce_bar(acc), acc_par ^ 1, abort_flag, p.err, kDevTimeoutAccEmpty)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
+        bool ok = true;
+        for (int kb = 0; kb < p.nk; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, abort_flag, p.err, kDevTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + size_t(stage) * C::kStageBytes);
+          const uint32_t alo_addr = a_addr + C::kABytes;
+          const uint32_t b_addr = a_addr + C::kABytes * (SA ? 2 : 1);
+          const uint32_t blo_addr = b_addr + C::kBBytes;
+#pragma unroll
+          for (int k = 0; k < kBK / kUmmaK; ++k) {
+            const uint32_t koff = uint32_t(k * kUmmaK * 4);
+            const uint64_t da = sw128_kmajor_desc(a_addr + koff);
+            const uint64_t db = sw128_kmajor_desc(b_addr + koff);
+            mma_tf32(d_tmem, da, db, kIdesc, (kb | k) != 0 ? 1u : 0u);
+            if (SB) mma_tf32(d_tmem, da, sw128_kmajor_desc(blo_addr + koff), kIdesc, 1u);
+            if (SA) mma_tf32(d_tmem, sw128_kmajor_desc(alo_addr + koff), db, kIdesc, 1u);
+          }
+          issued = true;
+          mma_commit(empty_bar(stage));
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit(accf_bar(acc));
+      }
+      if (issued) {
+        // Every MMA issued above must finish before TMEM is released.
+        mma_commit(drain_bar);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(drain_bar, 0)) {
+          if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+            atomicCAS(p.err, 0, kDevTimeoutDrain);
+            break;
+          }
+        }
+      }
+    }
+  } else {
+    // -------------------------------------------------- epilogue (warps 2..5)
+    const int quad = warp & 3;
+    const int rloc = quad * 32 + lane;
+    const GemmEpilogue& e = p.e;
+    const bool vec_out = (e.ldo % 4 == 0) && ((reinterpret_cast<uintptr_t>(e.out) & 15) == 0);
+    const bool vec_lo = e.out_lo && (e.ldo_lo % 4 == 0) && ((reinterpret_cast<uintptr_t>(e.out_lo) & 15) == 0);
+    int local = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_par = uint32_t(local >> 1) & 1u;
+      if (!mbar_wait(accf_bar(acc), acc_par, abort_flag, p.err, kDevTimeoutAccFull)) break;
+      tc_fence_after();
+      const int tm = tile / p.ntn, tn = tile % p.ntn;
+      const int row = tm * kBM + rloc;
+      const bool row_ok = row < p.M;
+      const float rs = (e.rowscale && row_ok) ? e.rowscale[row] : 1.f;
+      const uint32_t taddr = tmem_base + (uint32_t(quad * 32) << 16) + uint32_t(acc * BN);
+      if (e.geglu) {
+        // Tile columns [0, BN/2) are gate, [BN/2, BN) the matching up columns.
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN / 2; c0 += 32) {
+          uint32_t rg[32], ru[32];
+          tmem_ld_32x32b_x32(taddr + uint32_t(c0), rg);
+          tmem_ld_32x32b_x32(taddr + uint32_t(BN / 2 + c0), ru);
+          tmem_ld_wait();
+          const int col0 = tn * (BN / 2) + c0;
+          const int ncols = min(32, p.Nout - col0);
+          if (row_ok && ncols > 0) {
+            float v[32], vl[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float g = __uint_as_float(rg[j]) * rs;
+              const float u = __uint_as_float(ru[j]) * rs;
+              const float o = gelu_tanh(g) * u;
+              v[j] = o;
+              vl[j] = tf32_lo(o);
+            }
+            store_row32(e.out + int64_t(row) * e.ldo + col0, v, ncols, vec_out);
+            if (e.out_lo) store_row32(e.out_lo + int64_t(row) * e.ldo_lo + col0, vl, ncols, vec_lo);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(taddr + uint32_t(c0), r);
+          tmem_ld_wait();
+          const int col0 = tn * BN + c0;
+          const int ncols = min(32, p.Nout - col0);
+          if (row_ok && ncols > 0) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              float x = __uint_as_float(r[j]);
+              const int col = col0 + j;
+              if (e.bias && j < ncols) x = x + e.bias[col];
+              x = x * rs;
+              x = apply_act(x, e.act);
+              if (e.mul && j < ncols) x = x * e.mul[int64_t(row) * e.ldm + col];
+              if (e.residual && j < ncols) x = x + e.residual[int64_t(row) * e.ldr + col];
+              v[j] = x;
+            }
+            store_row32(e.out + int64_t(row) * e.ldo + col0, v, ncols, vec_out);
+            if (e.out_lo) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = tf32_lo(v[j]);
+              store_row32(e.out_lo + int64_t(row) * e.ldo_lo + col0, v, ncols, vec_lo);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(acce_bar(acc));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int get_encode() {
+  if (g_encode) return FG_OK;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr)
+    return set_error(FG_ECUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  return FG_OK;
+}
+
+// Row-major [rows, cols] fp32 matrix, tiles of [box_rows × 32] with 128B swizzle.
+int make_map(CUtensorMap* m, const float* ptr, int64_t rows, int64_t cols, int64_t ld,
+             int box_rows) {
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) != 0)
+    return set_error(FG_EINVAL, "GEMM operand %p is not 16-byte aligned", (const void*)ptr);
+  if (ld % 4 != 0) return set_error(FG_EINVAL, "GEMM row stride %lld is not a multiple of 4 floats", (long long)ld);
+  cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(ld) * 4};
+  cuuint32_t box[2] = {32u, cuuint32_t(box_rows)};
+  cuuint32_t es[2] = {1u, 1u};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims, strides, box,
+                        es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(FG_ECUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
+  return FG_OK;
+}
+
+template <int BN, bool SA, bool SB>
+int launch_variant(const GemmArgs& g, const KParams& kp, int* dev_err, cudaStream_t stream) {
+  using C = Cfg<BN, SA, SB>;
+  CUtensorMap mA, mAlo, mB, mBlo;
+  FG_TRY(make_map(&mA, g.A, g.M, g.K, g.lda, kBM));
+  FG_TRY(make_map(&mB, g.B, g.Nb, g.K, g.ldb, BN));
+  if (SA) FG_TRY(make_map(&mAlo, g.A_lo, g.M, g.K, g.lda, kBM)); else mAlo = mA;
+  if (SB) FG_TRY(make_map(&mBlo, g.B_lo, g.Nb, g.K, g.ldb, BN)); else mBlo = mB;
+  auto kern = gemm_tf32_kernel<BN, SA, SB>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    FG_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(C::kSmemBytes)));
+    attr_set[dev & 63] = true;
+  }
+  const int ntiles = kp.ntm * kp.ntn;
+  const int grid = std::max(1, std::min(ntiles, sm_count()));
+  kern<<<grid, kThreads, C::kSmemBytes, stream>>>(mA, mAlo, mB, mBlo, kp);
+  FG_CUDA_TRY(cudaGetLastError());
+  (void)dev_err;
+  return FG_OK;
+}
+
+}  // namespace
+
+int gemm_tn(const GemmArgs& g, int* dev_err, cudaStream_t stream) {
+  if (g.M <= 0 || g.Nb <= 0 || g.K <= 0) {
+    if (g.M == 0 || g.Nb == 0) return FG_OK;
+    return set_error(FG_EINVAL, "gemm: bad shape M=%d Nb=%d K=%d", g.M, g.Nb, g.K);
+  }
+  if (g.epi.out == nullptr) return set_error(FG_EINVAL, "gemm: no output");
+  if (g.epi.geglu && (g.Nb % 256) != 0)
+    return set_error(FG_EINVAL, "gemm: gated product needs B rows in multiples of 256, got %d", g.Nb);
+  FG_TRY(get_encode());
+  KParams kp;
+  kp.M = g.M;
+  kp.K = g.K;
+  kp.e = g.epi;
+  kp.err = dev_err;
+  kp.nk = (g.K + kBK - 1) / kBK;
+  kp.ntm = (g.M + kBM - 1) / kBM;
+  const bool sa = g.A_lo != nullptr, sb = g.B_lo != nullptr;
+  if (g.epi.geglu) {
+    kp.Nout = g.Nb / 2;
+    kp.ntn = g.Nb / 256;
+    if (sa && sb) return launch_variant<256, true, true>(g, kp, dev_err, stream);
+    if (sa) return launch_variant<256, true, false>(g, kp, dev_err, stream);
+    if (sb) return launch_variant<256, false, true>(g, kp, dev_err, stream);
+    return launch_variant<256, false, false>(g, kp, dev_err, stream);
+  }
+  kp.Nout = g.Nb;
+  if (g.Nb <= 128) {
+    kp.ntn = 1;
+    if (sa && sb) return launch_variant<128, true, true>(g, kp, dev_err, stream);
+    if (sa) return launch_variant<128, true, false>(g, kp, dev_err, stream);
+    if (sb) return launch_variant<128, false, true>(g, kp, dev_err, stream);
+    return launch_variant<128, false, false>(g, kp, dev_err, stream);
+  }
+  kp.ntn = (g.Nb + 255) / 256;
+  if (sa && sb) return launch_variant<256, true, true>(g, kp, dev_err, stream);
+  if (sa) return launch_variant<256, true, false>(g, kp, dev_err, stream);
+  if (sb) return launch_variant<256, false, true>(g, kp, dev_err, stream);
+  return launch_variant<256, false, false>(g, kp, dev_err, stream);
+}
+
+// ---------------------------------------------------------------- helpers
+namespace {
+__global__ void split_tf32_kernel(const float* __restrict__ x, float* __restrict__ hi,
+                                  float* __restrict__ lo, int64_t n, int* any) {
+  int found = 0;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const float v = x[i];
+    const float h = tf32_hi(v);
+    const float l = v - h;
+    if (hi) hi[i] = h;
+    if (lo) lo[i] = l;
+    found |= (l != 0.f);
+  }
+  if (any && __any_sync(0xffffffffu, found) && (threadIdx.x & 31) == 0) atomicOr(any, 1);
+}
+
+__global__ void transpose_kernel(const float* __restrict__ src, int64_t lds, int64_t rows,
+                                 int64_t cols, float* __restrict__ dst, int64_t ldd) {
+  __shared__ float tile[32][33];
+  const int64_t r0 = int64_t(blockIdx.y) * 32, c0 = int64_t(blockIdx.x) * 32;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int64_t r = r0 + i, c = c0 + threadIdx.x;
+    if (r < rows && c < cols) tile[i][threadIdx.x] = src[r * lds + c];
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int64_t c = c0 + i, r = r0 + threadIdx.x;
+    if (r < rows && c < cols) dst[c * ldd + r] = tile[threadIdx.x][i];
+  }
+}
+}  // namespace
+
+int split_tf32(const float* x, float* hi, float* lo, int64_t n, int* any, cudaStream_t stream) {
+  if (n <= 0) return FG_OK;
+  const int threads = 256;
+  const int64_t want = (n + threads - 1) / threads;
+  const int grid = int(std::min<int64_t>(want, int64_t(sm_count()) * 16));
+  split_tf32_kernel<<<grid, threads, 0, stream>>>(x, hi, lo, n, any);
+  FG_CUDA_TRY(cudaGetLastError());
+  return FG_OK;
+}
+
+int transpose_f32(const float* src, int64_t lds, int64_t rows, int64_t cols, float* dst,
+                  int64_t ldd, cudaStream_t stream) {
+  if (rows <= 0 || cols <= 0) return FG_OK;
+  dim3 grid(unsigned((cols + 31) / 32), unsigned((rows + 31) / 32));
+  transpose_kernel<<<grid, dim3(32, 8), 0, stream>>>(src, lds, rows, cols, dst, ldd);
+  FG_CUDA_TRY(cudaGetLastError());
+  return FG_OK;
+}
+
+}  // namespace fg

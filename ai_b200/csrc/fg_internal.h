@@ -1,0 +1,92 @@
+// Host-side internals shared by the library's translation units: status
+// codes, the thread-local last-error message, CUDA error checks, and the
+// launch entry points of each kernel family.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include "../../include/fgemma.h"
+
+namespace fg {
+
+// Records a formatted message as this thread's last error and returns code.
+int set_error(int code, const char* fmt, ...);
+void clear_error();
+const char* last_error();
+
+#define FG_CUDA_TRY(expr)                                                              \
+  do {                                                                                 \
+    cudaError_t e_ = (expr);                                                           \
+    if (e_ != cudaSuccess)                                                             \
+      return ::fg::set_error(FG_ECUDA, "%s failed: %s (%s:%d)", #expr,                 \
+                             cudaGetErrorString(e_), __FILE__, __LINE__);              \
+  } while (0)
+
+#define FG_TRY(expr)          \
+  do {                        \
+    int rc_ = (expr);         \
+    if (rc_ != FG_OK) return rc_; \
+  } while (0)
+
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+// Device error word of the current device; kernels record bounded-wait
+// timeouts there. check_device_error_word() synchronises the device and
+// turns a recorded timeout into FG_ETIMEOUT, resetting the word.
+int device_error_word(int** out);
+int check_device_error_word();
+
+// Internal activation code beyond the public FG_ACT_*: tanh (Dense head
+// layers with a Tanh activation, models/gemma/model.go:297-303).
+constexpr int kActTanh = 3;
+
+// ------------------------------------------------------------------ GEMM
+// C[M, Nout] = epilogue(A · Bᵀ) with A [M, K] and B [Nb, K], both row-major
+// (K contiguous), on the tcgen05 tensor cores in TF32 with FP32 accumulation.
+// Split-TF32: when A_lo / B_lo are given, the passes A·B, A·B_lo and A_lo·B
+// are accumulated into the same TMEM tile (the A_lo·B_lo term, ~2^-22 of the
+// product, is dropped). A plain-TF32 product passes neither.
+struct GemmEpilogue {
+  float* out = nullptr;          // [M, Nout]
+  int64_t ldo = 0;
+  float* out_lo = nullptr;       // optional split-TF32 low part of out
+  int64_t ldo_lo = 0;
+  const float* rowscale = nullptr;  // [M]
+  const float* bias = nullptr;      // [Nout]
+  const float* mul = nullptr;       // [M, Nout]
+  int64_t ldm = 0;
+  const float* residual = nullptr;  // [M, Nout]
+  int64_t ldr = 0;
+  int act = 0;                      // FG_ACT_*
+  int geglu = 0;  // B rows interleaved per 128: gate rows then up rows; out = GELU(rs·g)·(rs·u)
+};
+
+struct GemmArgs {
+  int M = 0, Nb = 0, K = 0;      // Nb = rows of B (= 2·Nout for geglu)
+  const float* A = nullptr;
+  const float* A_lo = nullptr;
+  int64_t lda = 0;
+  const float* B = nullptr;
+  const float* B_lo = nullptr;
+  int64_t ldb = 0;
+  GemmEpilogue epi;
+};
+
+int gemm_tn(const GemmArgs& g, int* dev_err, cudaStream_t stream);
+
+// Elementwise split of n floats into TF32 high and exact low parts.
+// *any_lo_nonzero (device int, optional) is set to 1 when some low part is non-zero.
+int split_tf32(const float* x, float* hi, float* lo, int64_t n, int* any_lo_nonzero,
+               cudaStream_t stream);
+// dst[c, r] = src[r, c] for a rows×cols row-major src with leading dimension lds.
+int transpose_f32(const float* src, int64_t lds, int64_t rows, int64_t cols, float* dst,
+                  int64_t ldd, cudaStream_t stream);
+
+}  // namespace fg

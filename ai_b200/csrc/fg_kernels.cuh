@@ -1,0 +1,84 @@
+// Launch wrappers of the memory-bound encoder kernels and the attention
+// kernel (definitions in fg_elementwise.cu and fg_attention.cu).
+#pragma once
+
+#include "fg_internal.h"
+
+namespace fg {
+
+// Embedding gather with √hidden scaling (embed.go:175-176) and the first
+// layer's folded pre-norm factor rowscale = 1/√(Σx²/n + eps)
+// (matmul_fused.go:125-143, embed.go:432-438). ids/lengths are [B·T]/[B];
+// positions at or past max(len, 1) are written as zeros; a length-0
+// sequence embeds the pad id 0 at position 0.
+int embed_gather(const float* table, int64_t vocab, const int32_t* ids, const int32_t* lengths,
+                 int B, int T, int hidden, float emb_scale, float eps, float* x, float* x_lo,
+                 float* rowscale, int* dev_err, cudaStream_t s);
+
+// Per-head RMSNorm of q and k with their gains (attention.go:292-337), then
+// rotate-half RoPE with the layer's cos/sin tables [T, D/2] (rope.go:66-87),
+// in place on the token-major qkv buffer [B·T, (Hq+2·Hkv)·D]; v untouched.
+// Optional lo buffer (same layout) receives split-TF32 low parts of q, k, v.
+int qk_norm_rope(float* qkv, float* qkv_lo, int64_t rows, int Hq, int Hkv, int D,
+                 const float* qgain, const float* kgain, float eps, const float* cos_t,
+                 const float* sin_t, int T, cudaStream_t s);
+
+// x ← x + RMSNorm(o, gain) (embed.go:216-220, 231-235), then the next
+// pre-norm factor rowscale = 1/√(Σx²/n + eps). x_lo (optional) receives the
+// split-TF32 low part of the new x. When final_gain is given, x is replaced
+// by RMSNorm(x_new, final_gain) instead (embed.go:237) and rowscale/x_lo are
+// not written.
+int residual_postnorm(float* x, float* x_lo, const float* o, const float* gain, float eps,
+                      float* rowscale, const float* final_gain, int64_t rows, int n,
+                      cudaStream_t s);
+
+// pooled[b] = mean over t < max(len_b, 1) of h[b, t] (embed.go:381-404);
+// pooled_lo (optional) gets its split-TF32 low part.
+int mean_pool(const float* h, const int32_t* lengths, int B, int T, int n, float* pooled,
+              float* pooled_lo, cudaStream_t s);
+
+// out[b, :dim] = x[b, :dim] / √(Σ x² + 1e-12) (embed.go:472-475), or a copy
+// of the first dim columns when l2 == 0.
+int l2_normalize(const float* x, int64_t ldx, int B, int dim, int l2, float* out,
+                 cudaStream_t s);
+
+// Row sums of squares and RMSNorm for the op-level API.
+int row_sum_squares(const float* x, int64_t rows, int64_t n, int64_t ldx, float* out,
+                    cudaStream_t s);
+int rmsnorm(const float* x, int64_t rows, int64_t n, const float* g, float eps, float* out,
+            cudaStream_t s);
+int rope(const float* x, int64_t rows, int T, int D, const float* cos_t, const float* sin_t,
+         float* out, cudaStream_t s);
+
+// Split a strided [rows, cols] matrix into TF32 high (truncated) and exact
+// low parts with leading dimension ldd; hi may be a plain copy when
+// truncate_hi == 0; lo may be null.
+int split_copy_2d(const float* src, int64_t lds, int64_t rows, int64_t cols, float* hi,
+                  float* lo, int64_t ldd, int truncate_hi, cudaStream_t s);
+
+// Attention over strided q/k/v/out (element offsets b·sb + h·sh + t·st, d
+// contiguous): softmax(scale·q·kᵀ, masked)·v where key j is visible to query
+// i of batch b when j < klen[b] (klen null: S) and, if window > 0,
+// |i − j| < window. Query rows i ≥ qlen[b] (qlen null: T) are written as 0.
+struct AttnArgs {
+  const float* q;
+  const float* k;
+  const float* v;
+  float* out;
+  float* out_lo;  // optional split-TF32 low part of out (same strides)
+  int64_t qsb, qsh, qst;
+  int64_t ksb, ksh, kst;
+  int64_t vsb, vsh, vst;
+  int64_t osb, osh, ost;
+  int B, Hq, Hkv, T, S, D;
+  const int32_t* klen;
+  const int32_t* qlen;
+  int window;
+  float scale;
+};
+int attention_simt(const AttnArgs& a, cudaStream_t s);
+// Rewrites the rows that have no visible key with the reference's result for
+// them: the mean of the values of the keys hidden by the fewest −1e9 masks.
+int attention_masked_rows(const AttnArgs& a, cudaStream_t s);
+
+}  // namespace fg

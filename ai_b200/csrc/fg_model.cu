@@ -1,0 +1,658 @@
+// EmbeddingGemma encoder model: weight intake and load-time folds
+// (gemma.Load, models/gemma/model.go:76-232), device-resident weights, and
+// the batch forward (embedBatch → encode → pool → applyHead → l2normalize,
+// models/gemma/embed.go:118-240, 381-475) as a sequence of sm_100a kernels
+// on one stream.
+//
+// Device layout (all fp32, row-major, [out, in] = K-major for every
+// projection, the layout the tensor cores read without packing):
+//   embed      [vocab, hidden]
+//   per layer  Wqkv [(Hq+2·Hkv)·D, hidden]  rows q | k | v, pre-norm folded
+//              Wo   [hidden, Hq·D]
+//              Wgu  [2·ffn, hidden]  gate and up rows interleaved in blocks
+//                   of 128 (gate 128j.., up 128j..) so one 256-row tile of B
+//                   yields 128 finished GeGLU columns; pre-norm folded
+//              Wd   [hidden, ffn]
+//              each with its TF32 low part when it is non-zero
+//   activations, token-major [B·T, ·]: x (residual stream) + x_lo, qkv,
+//   att + att_lo, gu + gu_lo, tmp; rowscale [B·T].
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "fg_internal.h"
+#include "fg_kernels.cuh"
+
+namespace fg {
+
+namespace {
+
+float bf16_to_f32(uint16_t h) {
+  uint32_t u = uint32_t(h) << 16;
+  float f;
+  std::memcpy(&f, &u, 4);
+  return f;
+}
+
+float f16_to_f32(uint16_t h) {
+  const uint32_t sign = uint32_t(h & 0x8000u) << 16;
+  uint32_t exp = (h >> 10) & 0x1f;
+  uint32_t mant = h & 0x3ffu;
+  uint32_t u;
+  if (exp == 0) {
+    if (mant == 0) {
+      u = sign;
+    } else {
+      uint32_t e = 127 - 15 + 1;
+      while ((mant & 0x400u) == 0) {
+        mant <<= 1;
+        --e;
+      }
+      mant &= 0x3ffu;
+      u = sign | (e << 23) | (mant << 13);
+    }
+  } else if (exp == 0x1f) {
+    u = sign | 0x7f800000u | (mant << 13);
+  } else {
+    u = sign | ((exp + 127 - 15) << 23) | (mant << 13);
+  }
+  float f;
+  std::memcpy(&f, &u, 4);
+  return f;
+}
+
+struct HostTensor {
+  std::vector<int64_t> shape;
+  std::vector<float> data;
+};
+
+struct DevBuf {
+  float* p = nullptr;
+  size_t n = 0;
+};
+
+// A K-major operand resident on the device with its optional low part.
+struct DevMat {
+  float* hi = nullptr;
+  float* lo = nullptr;  // null when every low part is zero
+  int rows = 0, cols = 0;
+};
+
+struct Layer {
+  DevMat wqkv, wo, wgu, wd;
+  float* qgain = nullptr;
+  float* kgain = nullptr;
+  float* post_attn = nullptr;
+  float* post_ffn = nullptr;
+  int rope = 0;  // index into the model's rope tables
+};
+
+struct Dense {
+  DevMat w;
+  int in = 0, out = 0;
+  bool tanh = false;
+};
+
+}  // namespace
+
+}  // namespace fg
+
+struct fg_model {
+  int device = 0;
+  fg_config cfg{};
+  std::vector<int> sliding;
+  std::vector<double> rope_base;
+  std::map<std::string, fg::HostTensor> host;
+  bool finalized = false;
+
+  // device weights
+  float* embed = nullptr;
+  std::vector<fg::Layer> layers;
+  float* final_gain = nullptr;
+  std::vector<fg::Dense> dense;
+  std::vector<float*> rope_cos, rope_sin;
+  std::vector<double> rope_bases;  // distinct bases, index = Layer::rope
+  std::vector<void*> allocations;
+
+  // workspace
+  int64_t cap_tokens = 0;
+  int cap_batch = 0;
+  float *x = nullptr, *x_lo = nullptr, *rowscale = nullptr, *qkv = nullptr, *att = nullptr,
+        *att_lo = nullptr, *gu = nullptr, *gu_lo = nullptr, *tmp = nullptr;
+  float *pooled = nullptr, *pooled_lo = nullptr, *head_a = nullptr, *head_a_lo = nullptr,
+        *head_b = nullptr, *head_b_lo = nullptr;
+  int32_t* eff_len = nullptr;
+  int* err = nullptr;
+  // host-API staging
+  int32_t* d_ids = nullptr;
+  int64_t d_ids_cap = 0;
+  int32_t* d_len = nullptr;
+  float* d_out = nullptr;
+  int64_t d_out_cap = 0;
+  int d_len_cap = 0;
+  cudaStream_t stream = nullptr;
+};
+
+namespace fg {
+namespace {
+
+int dev_alloc(fg_model* m, void** p, size_t bytes) {
+  if (bytes == 0) bytes = 16;
+  if (cudaMalloc(p, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    *p = nullptr;
+    return set_error(FG_ENOMEM, "device allocation of %zu bytes failed", bytes);
+  }
+  m->allocations.push_back(*p);
+  return FG_OK;
+}
+
+template <class T>
+int dev_alloc_t(fg_model* m, T** p, size_t count) {
+  void* v = nullptr;
+  FG_TRY(dev_alloc(m, &v, count * sizeof(T)));
+  *p = static_cast<T*>(v);
+  return FG_OK;
+}
+
+int upload(fg_model* m, const std::vector<float>& h, float** out) {
+  FG_TRY(dev_alloc_t(m, out, h.size()));
+  FG_CUDA_TRY(cudaMemcpy(*out, h.data(), h.size() * sizeof(float), cudaMemcpyHostToDevice));
+  return FG_OK;
+}
+
+// Uploads a K-major [rows, cols] fp32 matrix and its split-TF32 parts.
+int upload_mat(fg_model* m, const std::vector<float>& h, int rows, int cols, DevMat* out) {
+  float* raw = nullptr;
+  FG_TRY(upload(m, h, &raw));
+  float* lo = nullptr;
+  FG_TRY(dev_alloc_t(m, &lo, h.size()));
+  int* flag = nullptr;
+  FG_TRY(dev_alloc_t(m, &flag, 1));
+  FG_CUDA_TRY(cudaMemset(flag, 0, sizeof(int)));
+  // hi in place: the truncated TF32 value; lo: the exact remainder
+  FG_TRY(split_tf32(raw, raw, lo, int64_t(h.size()), flag, nullptr));
+  int any = 0;
+  FG_CUDA_TRY(cudaMemcpy(&any, flag, sizeof(int), cudaMemcpyDeviceToHost));
+  out->hi = raw;
+  out->lo = any ? lo : nullptr;
+  out->rows = rows;
+  out->cols = cols;
+  return FG_OK;
+}
+
+const HostTensor* find(fg_model* m, const std::string& name) {
+  auto it = m->host.find(name);
+  return it == m->host.end() ? nullptr : &it->second;
+}
+
+int need(fg_model* m, const std::string& name, std::vector<int64_t> shape, const HostTensor** out) {
+  const HostTensor* t = find(m, name);
+  if (!t) return set_error(FG_EINVAL, "gemma: weight %s not found", name.c_str());
+  if (t->shape != shape) {
+    std::string want, got;
+    for (auto s : shape) want += std::to_string(s) + ",";
+    for (auto s : t->shape) got += std::to_string(s) + ",";
+    return set_error(FG_EINVAL, "gemma: weight %s has shape [%s], want [%s]", name.c_str(), got.c_str(), want.c_str());
+  }
+  *out = t;
+  return FG_OK;
+}
+
+// Gemma's (1 + w) norm gain (model.go:131-140).
+std::vector<float> plus_one(const HostTensor& t) {
+  std::vector<float> g(t.data.size());
+  for (size_t i = 0; i < g.size(); ++i) g[i] = t.data[i] + 1.0f;
+  return g;
+}
+
+// Folds a pre-norm gain into a [out, in] projection: W'[n][k] = W[n][k]·g[k]
+// (the reference's diag(g)·Wᵀ on the transposed weight, model.go:206-222).
+void fold_into(const HostTensor& w, const std::vector<float>& g, float* dst) {
+  const int64_t rows = w.shape[0], cols = w.shape[1];
+  for (int64_t r = 0; r < rows; ++r)
+    for (int64_t c = 0; c < cols; ++c) dst[r * cols + c] = w.data[r * cols + c] * g[c];
+}
+
+void rope_table(double base, int T, int D, std::vector<float>& c, std::vector<float>& s) {
+  const int half = D / 2;
+  std::vector<double> inv(half);
+  for (int i = 0; i < half; ++i) inv[i] = std::pow(base, -double(2 * i) / double(D));
+  c.resize(size_t(T) * half);
+  s.resize(size_t(T) * half);
+  for (int t = 0; t < T; ++t)
+    for (int i = 0; i < half; ++i) {
+      const double a = double(t) * inv[i];
+      c[size_t(t) * half + i] = float(std::cos(a));
+      s[size_t(t) * half + i] = float(std::sin(a));
+    }
+}
+
+__global__ void eff_len_kernel(const int32_t* len, int B, int T, int32_t* eff) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b < B) eff[b] = max(min(len[b], T), 1);
+}
+
+int ensure_workspace(fg_model* m, int64_t tokens, int batch) {
+  const fg_config& c = m->cfg;
+  if (tokens > m->cap_tokens) {
+    if (m->x) return set_error(FG_EINVAL, "batch of %lld tokens exceeds the workspace (%lld)", (long long)tokens, (long long)m->cap_tokens);
+    const int64_t H = c.hidden_size, D = c.head_dim;
+    const int64_t qkvw = int64_t(c.num_heads + 2 * c.num_kv_heads) * D;
+    const int64_t attw = int64_t(c.num_heads) * D;
+    const int64_t F = c.intermediate_size;
+    FG_TRY(dev_alloc_t(m, &m->x, tokens * H));
+    FG_TRY(dev_alloc_t(m, &m->x_lo, tokens * H));
+    FG_TRY(dev_alloc_t(m, &m->rowscale, tokens));
+    FG_TRY(dev_alloc_t(m, &m->qkv, tokens * qkvw));
+    FG_TRY(dev_alloc_t(m, &m->att, tokens * attw));
+    FG_TRY(dev_alloc_t(m, &m->att_lo, tokens * attw));
+    FG_TRY(dev_alloc_t(m, &m->gu, tokens * F));
+    FG_TRY(dev_alloc_t(m, &m->gu_lo, tokens * F));
+    FG_TRY(dev_alloc_t(m, &m->tmp, tokens * std::max(H, attw)));
+    m->cap_tokens = tokens;
+  }
+  if (batch > m->cap_batch) {
+    int widest = c.hidden_size;
+    for (auto& d : m->dense) widest = std::max(widest, std::max(d.in, d.out));
+    const int64_t nb = std::max(batch, 1);
+    FG_TRY(dev_alloc_t(m, &m->pooled, nb * c.hidden_size));
+    FG_TRY(dev_alloc_t(m, &m->pooled_lo, nb * c.hidden_size));
+    FG_TRY(dev_alloc_t(m, &m->head_a, nb * widest));
+    FG_TRY(dev_alloc_t(m, &m->head_a_lo, nb * widest));
+    FG_TRY(dev_alloc_t(m, &m->head_b, nb * widest));
+    FG_TRY(dev_alloc_t(m, &m->head_b_lo, nb * widest));
+    FG_TRY(dev_alloc_t(m, &m->eff_len, nb));
+    m->cap_batch = int(nb);
+  }
+  return FG_OK;
+}
+
+int finalize(fg_model* m, int64_t max_tokens) {
+  const fg_config& c = m->cfg;
+  const int64_t H = c.hidden_size, D = c.head_dim, Hq = c.num_heads, Hkv = c.num_kv_heads;
+  const int64_t F = c.intermediate_size;
+  if (F % 128 != 0) return set_error(FG_EINVAL, "intermediate_size %lld must be a multiple of 128", (long long)F);
+  if (H % 128 != 0 || H > 1024) return set_error(FG_EINVAL, "hidden_size %lld must be a multiple of 128 up to 1024", (long long)H);
+  if (D % 4 != 0 || D > 256) return set_error(FG_EINVAL, "head_dim %lld unsupported (multiple of 4, at most 256)", (long long)D);
+  FG_CUDA_TRY(cudaSetDevice(m->device));
+  FG_TRY(device_error_word(&m->err));
+
+  const HostTensor* t = nullptr;
+  FG_TRY(need(m, "embed_tokens.weight", {c.vocab_size, H}, &t));
+  FG_TRY(upload(m, t->data, &m->embed));
+
+  // distinct rope bases
+  for (int l = 0; l < c.num_layers; ++l) {
+    int idx = -1;
+    for (size_t i = 0; i < m->rope_bases.size(); ++i)
+      if (m->rope_bases[i] == m->rope_base[l]) idx = int(i);
+    if (idx < 0) {
+      idx = int(m->rope_bases.size());
+      m->rope_bases.push_back(m->rope_base[l]);
+      std::vector<float> cs, sn;
+      rope_table(m->rope_base[l], c.max_tokens, int(D), cs, sn);
+      float *dc = nullptr, *ds = nullptr;
+      FG_TRY(upload(m, cs, &dc));
+      FG_TRY(upload(m, sn, &ds));
+      m->rope_cos.push_back(dc);
+      m->rope_sin.push_back(ds);
+    }
+  }
+
+  m->layers.resize(c.num_layers);
+  for (int l = 0; l < c.num_layers; ++l) {
+    const std::string p = "layers." + std::to_string(l) + ".";
+    Layer& L = m->layers[l];
+    L.rope = 0;
+    for (size_t i = 0; i < m->rope_bases.size(); ++i)
+      if (m->rope_bases[i] == m->rope_base[l]) L.rope = int(i);
+    const HostTensor *in_norm, *pa_norm, *pf_norm, *pff_norm, *qn, *kn, *wq, *wk, *wv, *wo, *wg, *wu, *wd;
+    FG_TRY(need(m, p + "input_layernorm.weight", {H}, &in_norm));
+    FG_TRY(need(m, p + "post_attention_layernorm.weight", {H}, &pa_norm));
+    FG_TRY(need(m, p + "pre_feedforward_layernorm.weight", {H}, &pf_norm));
+    FG_TRY(need(m, p + "post_feedforward_layernorm.weight", {H}, &pff_norm));
+    FG_TRY(need(m, p + "self_attn.q_norm.weight", {D}, &qn));
+    FG_TRY(need(m, p + "self_attn.k_norm.weight", {D}, &kn));
+    FG_TRY(need(m, p + "self_attn.q_proj.weight", {Hq * D, H}, &wq));
+    FG_TRY(need(m, p + "self_attn.k_proj.weight", {Hkv * D, H}, &wk));
+    FG_TRY(need(m, p + "self_attn.v_proj.weight", {Hkv * D, H}, &wv));
+    FG_TRY(need(m, p + "self_attn.o_proj.weight", {H, Hq * D}, &wo));
+    FG_TRY(need(m, p + "mlp.gate_proj.weight", {F, H}, &wg));
+    FG_TRY(need(m, p + "mlp.up_proj.weight", {F, H}, &wu));
+    FG_TRY(need(m, p + "mlp.down_proj.weight", {H, F}, &wd));
+
+    const std::vector<float> g_in = plus_one(*in_norm), g_pf = plus_one(*pf_norm);
+    const int64_t qkv_rows = (Hq + 2 * Hkv) * D;
+    std::vector<float> wqkv(size_t(qkv_rows * H));
+    fold_into(*wq, g_in, wqkv.data());
+    fold_into(*wk, g_in, wqkv.data() + Hq * D * H);
+    fold_into(*wv, g_in, wqkv.data() + (Hq + Hkv) * D * H);
+    FG_TRY(upload_mat(m, wqkv, int(qkv_rows), int(H), &L.wqkv));
+    FG_TRY(upload_mat(m, wo->data, int(H), int(Hq * D), &L.wo));
+
+    std::vector<float> gate(size_t(F * H)), up(size_t(F * H)), gu(size_t(2 * F * H));
+    fold_into(*wg, g_pf, gate.data());
+    fold_into(*wu, g_pf, up.data());
+    for (int64_t j = 0; j < F / 128; ++j) {
+      std::memcpy(gu.data() + (2 * j) * 128 * H, gate.data() + j * 128 * H, size_t(128 * H) * 4);
+      std::memcpy(gu.data() + (2 * j + 1) * 128 * H, up.data() + j * 128 * H, size_t(128 * H) * 4);
+    }
+    FG_TRY(upload_mat(m, gu, int(2 * F), int(H), &L.wgu));
+    FG_TRY(upload_mat(m, wd->data, int(H), int(F), &L.wd));
+
+    FG_TRY(upload(m, plus_one(*qn), &L.qgain));
+    FG_TRY(upload(m, plus_one(*kn), &L.kgain));
+    FG_TRY(upload(m, plus_one(*pa_norm), &L.post_attn));
+    FG_TRY(upload(m, plus_one(*pff_norm), &L.post_ffn));
+  }
+  const HostTensor* fn = nullptr;
+  FG_TRY(need(m, "norm.weight", {H}, &fn));
+  FG_TRY(upload(m, plus_one(*fn), &m->final_gain));
+
+  int prev = int(H);
+  for (int j = 0; j < c.num_dense; ++j) {
+    const HostTensor* w = nullptr;
+    FG_TRY(need(m, "dense." + std::to_string(j) + ".linear.weight", {c.dense_out[j], c.dense_in[j]}, &w));
+    if (c.dense_in[j] != prev) return set_error(FG_EINVAL, "dense layer %d takes %d features, previous gives %d", j, c.dense_in[j], prev);
+    if (c.dense_in[j] % 4 != 0) return set_error(FG_EINVAL, "dense layer %d input width must be a multiple of 4", j);
+    Dense d;
+    d.in = c.dense_in[j];
+    d.out = c.dense_out[j];
+    d.tanh = c.dense_tanh[j] != 0;
+    FG_TRY(upload_mat(m, w->data, d.out, d.in, &d.w));
+    m->dense.push_back(d);
+    prev = d.out;
+  }
+  m->host.clear();
+  FG_TRY(ensure_workspace(m, std::max<int64_t>(max_tokens, 1), 1));
+  FG_CUDA_TRY(cudaDeviceSynchronize());
+  m->finalized = true;
+  return FG_OK;
+}
+
+GemmArgs make_gemm(int M, const float* A, const float* A_lo, int64_t lda, const DevMat& B,
+                   bool split) {
+  GemmArgs g;
+  g.M = M;
+  g.Nb = B.rows;
+  g.K = B.cols;
+  g.A = A;
+  g.A_lo = split ? A_lo : nullptr;
+  g.lda = lda;
+  g.B = B.hi;
+  g.B_lo = split ? B.lo : nullptr;
+  g.ldb = B.cols;
+  return g;
+}
+
+int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int T, int dim,
+            int precision, float* out, cudaStream_t s) {
+  const fg_config& c = m->cfg;
+  const bool split = precision == FG_PREC_SPLIT_TF32;
+  const int H = c.hidden_size, D = c.head_dim, Hq = c.num_heads, Hkv = c.num_kv_heads;
+  const int F = c.intermediate_size;
+  const int64_t M = int64_t(B) * T;
+  if (M > INT32_MAX) return set_error(FG_EINVAL, "batch too large");
+  FG_TRY(ensure_workspace(m, M, B));
+  const int qkvw = (Hq + 2 * Hkv) * D, attw = Hq * D;
+  float* x_lo = split ? m->x_lo : nullptr;
+
+  eff_len_kernel<<<(B + 127) / 128, 128, 0, s>>>(lengths, B, T, m->eff_len);
+  FG_CUDA_TRY(cudaGetLastError());
+  const float emb_scale = float(std::sqrt(double(H)));
+  FG_TRY(embed_gather(m->embed, c.vocab_size, ids, lengths, B, T, H, emb_scale, c.rms_norm_eps,
+                      m->x, x_lo, m->rowscale, m->err, s));
+
+  for (int l = 0; l < c.num_layers; ++l) {
+    const Layer& L = m->layers[l];
+    const bool last = l == c.num_layers - 1;
+    // q|k|v = rowscale ⊙ (x · Wqkv'ᵀ)   (embed.go:193-197)
+    GemmArgs g = make_gemm(int(M), m->x, x_lo, H, L.wqkv, split);
+    g.epi.out = m->qkv;
+    g.epi.ldo = qkvw;
+    g.epi.rowscale = m->rowscale;
+    FG_TRY(gemm_tn(g, m->err, s));
+    // QK-norm + RoPE (embed.go:198-207)
+    FG_TRY(qk_norm_rope(m->qkv, nullptr, M, Hq, Hkv, D, L.qgain, L.kgain, c.rms_norm_eps,
+                        m->rope_cos[L.rope], m->rope_sin[L.rope], T, s));
+    // attention (embed.go:209, attention.go:130)
+    AttnArgs a{};
+    a.q = m->qkv;
+    a.k = m->qkv + int64_t(Hq) * D;
+    a.v = m->qkv + int64_t(Hq + Hkv) * D;
+    a.out = m->att;
+    a.out_lo = split ? m->att_lo : nullptr;
+    a.qsb = int64_t(T) * qkvw; a.qsh = D; a.qst = qkvw;
+    a.ksb = a.qsb; a.ksh = D; a.kst = qkvw;
+    a.vsb = a.qsb; a.vsh = D; a.vst = qkvw;
+    a.osb = int64_t(T) * attw; a.osh = D; a.ost = attw;
+    a.B = B; a.Hq = Hq; a.Hkv = Hkv; a.T = T; a.S = T; a.D = D;
+    a.klen = m->eff_len;
+    a.qlen = m->eff_len;
+    a.window = (c.window > 0 && m->sliding[l]) ? c.window : 0;
+    a.scale = c.attn_scale;
+    FG_TRY(attention_simt(a, s));
+    // o0 = att · Wo   (embed.go:212-214)
+    g = make_gemm(int(M), m->att, m->att_lo, attw, L.wo, split);
+    g.epi.out = m->tmp;
+    g.epi.ldo = H;
+    FG_TRY(gemm_tn(g, m->err, s));
+    // x += RMSNorm(o0)   (embed.go:216-220), and the FFN pre-norm factor
+    FG_TRY(residual_postnorm(m->x, x_lo, m->tmp, L.post_attn, c.rms_norm_eps, m->rowscale,
+                             nullptr, M, H, s));
+    // gu = GELU(rs·x·Wg') ⊙ (rs·x·Wu')   (embed.go:224-227)
+    g = make_gemm(int(M), m->x, x_lo, H, L.wgu, split);
+    g.epi.out = m->gu;
+    g.epi.ldo = F;
+    g.epi.out_lo = split ? m->gu_lo : nullptr;
+    g.epi.ldo_lo = F;
+    g.epi.rowscale = m->rowscale;
+    g.epi.geglu = 1;
+    FG_TRY(gemm_tn(g, m->err, s));
+    // mlp0 = gu · Wd   (embed.go:229)
+    g = make_gemm(int(M), m->gu, m->gu_lo, F, L.wd, split);
+    g.epi.out = m->tmp;
+    g.epi.ldo = H;
+    FG_TRY(gemm_tn(g, m->err, s));
+    // x += RMSNorm(mlp0)   (embed.go:231-235); final norm on the last layer (embed.go:237)
+    FG_TRY(residual_postnorm(m->x, x_lo, m->tmp, L.post_ffn, c.rms_norm_eps, m->rowscale,
+                             last ? m->final_gain : nullptr, M, H, s));
+  }
+  if (c.num_layers == 0) return set_error(FG_EINVAL, "model has no layers");
+
+  // pool (embed.go:381-404), head (embed.go:408-429), L2 (embed.go:472-475)
+  FG_TRY(mean_pool(m->x, m->eff_len, B, T, H, m->pooled, split ? m->pooled_lo : nullptr, s));
+  const float* cur = m->pooled;
+  const float* cur_lo = m->pooled_lo;
+  int width = H;
+  float* bufs[2] = {m->head_a, m->head_b};
+  float* bufs_lo[2] = {m->head_a_lo, m->head_b_lo};
+  for (size_t j = 0; j < m->dense.size(); ++j) {
+    const Dense& d = m->dense[j];
+    GemmArgs g = make_gemm(B, cur, cur_lo, width, d.w, split);
+    g.epi.out = bufs[j & 1];
+    g.epi.ldo = d.out;
+    g.epi.out_lo = split ? bufs_lo[j & 1] : nullptr;
+    g.epi.ldo_lo = d.out;
+    g.epi.act = d.tanh ? kActTanh : FG_ACT_NONE;
+    FG_TRY(gemm_tn(g, m->err, s));
+    cur = bufs[j & 1];
+    cur_lo = bufs_lo[j & 1];
+    width = d.out;
+  }
+  if (dim > width) return set_error(FG_EINVAL, "gemma: Dim(%d) outside 1..%d", dim, width);
+  FG_TRY(l2_normalize(cur, width, B, dim, c.l2_normalize, out, s));
+  return FG_OK;
+}
+
+int model_dim(const fg_model* m) {
+  return m->cfg.num_dense > 0 ? m->cfg.dense_out[m->cfg.num_dense - 1] : m->cfg.hidden_size;
+}
+
+}  // namespace
+}  // namespace fg
+
+using namespace fg;
+
+extern "C" {
+
+int fg_model_create(const fg_config* cfg, int device, fg_model** out) {
+  clear_error();
+  if (!cfg || !out) return set_error(FG_EINVAL, "fg_model_create: null argument");
+  *out = nullptr;
+  const fg_config& c = *cfg;
+  if (c.hidden_size <= 0 || c.num_layers <= 0 || c.num_heads <= 0 || c.num_kv_heads <= 0 ||
+      c.head_dim <= 0 || c.vocab_size <= 0 || c.intermediate_size <= 0 || c.max_tokens <= 0)
+    return set_error(FG_EINVAL, "gemma: config is missing sizes");
+  if (c.head_dim % 2 != 0) return set_error(FG_EINVAL, "gemma: head_dim %d must be even for RoPE", c.head_dim);
+  if (c.num_heads % c.num_kv_heads != 0)
+    return set_error(FG_EINVAL, "gemma: %d query heads not a multiple of %d key/value heads", c.num_heads, c.num_kv_heads);
+  if (c.num_dense < 0 || c.num_dense > FG_MAX_DENSE) return set_error(FG_EINVAL, "gemma: %d dense layers", c.num_dense);
+  if (!c.sliding || !c.rope_base) return set_error(FG_EINVAL, "gemma: per-layer sliding / rope_base arrays missing");
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) {
+    cudaGetLastError();
+    return set_error(FG_ENODEV, "no CUDA device %d", device);
+  }
+  int major = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device);
+  if (major != 10) return set_error(FG_ENODEV, "device %d is not an sm_100 part (cc %d.x)", device, major);
+  auto* m = new fg_model();
+  m->device = device;
+  m->cfg = c;
+  m->sliding.assign(c.sliding, c.sliding + c.num_layers);
+  m->rope_base.assign(c.rope_base, c.rope_base + c.num_layers);
+  m->cfg.sliding = m->sliding.data();
+  m->cfg.rope_base = m->rope_base.data();
+  *out = m;
+  return FG_OK;
+}
+
+int fg_model_set_weight(fg_model* m, const char* name, int dtype, const int64_t* shape, int ndim,
+                        const void* data) {
+  clear_error();
+  if (!m || !name || (!shape && ndim > 0) || ndim < 0 || ndim > 4)
+    return set_error(FG_EINVAL, "fg_model_set_weight: bad arguments");
+  if (m->finalized) return set_error(FG_ESTATE, "fg_model_set_weight after finalize");
+  int64_t n = 1;
+  HostTensor t;
+  for (int i = 0; i < ndim; ++i) {
+    if (shape[i] < 0) return set_error(FG_EINVAL, "negative dimension");
+    n *= shape[i];
+    t.shape.push_back(shape[i]);
+  }
+  if (n > 0 && !data) return set_error(FG_EINVAL, "fg_model_set_weight: null data for %s", name);
+  t.data.resize(size_t(n));
+  switch (dtype) {
+    case FG_DT_F32:
+      std::memcpy(t.data.data(), data, size_t(n) * 4);
+      break;
+    case FG_DT_BF16: {
+      const uint16_t* s = static_cast<const uint16_t*>(data);
+      for (int64_t i = 0; i < n; ++i) t.data[i] = bf16_to_f32(s[i]);
+      break;
+    }
+    case FG_DT_F16: {
+      const uint16_t* s = static_cast<const uint16_t*>(data);
+      for (int64_t i = 0; i < n; ++i) t.data[i] = f16_to_f32(s[i]);
+      break;
+    }
+    default:
+      return set_error(FG_EINVAL, "fg_model_set_weight: unknown dtype %d", dtype);
+  }
+  m->host[name] = std::move(t);
+  return FG_OK;
+}
+
+int fg_model_finalize(fg_model* m, int64_t max_batch_tokens) {
+  clear_error();
+  if (!m) return set_error(FG_EINVAL, "null model");
+  if (m->finalized) return set_error(FG_ESTATE, "model already finalized");
+  if (max_batch_tokens < 0) return set_error(FG_EINVAL, "negative token capacity");
+  return finalize(m, max_batch_tokens);
+}
+
+int fg_embed_ids_device(fg_model* m, const int32_t* d_ids, const int32_t* d_lengths, int B, int T,
+                        int dim, int precision, float* d_out, void* stream) {
+  clear_error();
+  if (!m) return set_error(FG_EINVAL, "null model");
+  if (!m->finalized) return set_error(FG_ESTATE, "embed before fg_model_finalize");
+  if (B < 0 || T < 0) return set_error(FG_EINVAL, "negative batch shape");
+  if (B == 0) return FG_OK;
+  if (T == 0) return set_error(FG_EINVAL, "T must be at least 1");
+  if (T > m->cfg.max_tokens) return set_error(FG_EINVAL, "T=%d exceeds max_tokens %d", T, m->cfg.max_tokens);
+  if (precision != FG_PREC_SPLIT_TF32 && precision != FG_PREC_TF32)
+    return set_error(FG_EINVAL, "unknown precision %d", precision);
+  const int full = model_dim(m);
+  if (dim < 1 || dim > full) return set_error(FG_EINVAL, "gemma: Dim(%d) outside 1..%d", dim, full);
+  FG_CUDA_TRY(cudaSetDevice(m->device));
+  return forward(m, d_ids, d_lengths, B, T, dim, precision, d_out, static_cast<cudaStream_t>(stream));
+}
+
+int fg_embed_ids(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int T, int dim,
+                 int precision, float* out) {
+  clear_error();
+  if (!m) return set_error(FG_EINVAL, "null model");
+  if (!m->finalized) return set_error(FG_ESTATE, "embed before fg_model_finalize");
+  if (B < 0 || T < 0) return set_error(FG_EINVAL, "negative batch shape");
+  if (B == 0) return FG_OK;
+  if (!ids || !lengths || !out) return set_error(FG_EINVAL, "null buffer");
+  for (int b = 0; b < B; ++b) {
+    if (lengths[b] < 0 || lengths[b] > T)
+      return set_error(FG_EINVAL, "length %d of sequence %d outside 0..%d", lengths[b], b, T);
+    for (int t = 0; t < lengths[b]; ++t) {
+      const int32_t id = ids[int64_t(b) * T + t];
+      if (id < 0 || id >= m->cfg.vocab_size)
+        return set_error(FG_EINVAL, "token id %d at [%d, %d] outside the vocabulary", id, b, t);
+    }
+  }
+  FG_CUDA_TRY(cudaSetDevice(m->device));
+  if (!m->stream) FG_CUDA_TRY(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
+  const int64_t nid = int64_t(B) * T;
+  if (nid > m->d_ids_cap) {
+    if (m->d_ids) cudaFree(m->d_ids);
+    FG_CUDA_TRY(cudaMalloc(&m->d_ids, size_t(nid) * 4));
+    m->d_ids_cap = nid;
+  }
+  if (B > m->d_len_cap) {
+    if (m->d_len) cudaFree(m->d_len);
+    FG_CUDA_TRY(cudaMalloc(&m->d_len, size_t(B) * 4));
+    m->d_len_cap = B;
+  }
+  const int64_t nout = int64_t(B) * dim;
+  if (nout > m->d_out_cap) {
+    if (m->d_out) cudaFree(m->d_out);
+    FG_CUDA_TRY(cudaMalloc(&m->d_out, size_t(nout) * 4));
+    m->d_out_cap = nout;
+  }
+  FG_CUDA_TRY(cudaMemcpyAsync(m->d_ids, ids, size_t(nid) * 4, cudaMemcpyHostToDevice, m->stream));
+  FG_CUDA_TRY(cudaMemcpyAsync(m->d_len, lengths, size_t(B) * 4, cudaMemcpyHostToDevice, m->stream));
+  FG_TRY(fg_embed_ids_device(m, m->d_ids, m->d_len, B, T, dim, precision, m->d_out, m->stream));
+  FG_CUDA_TRY(cudaMemcpyAsync(out, m->d_out, size_t(nout) * 4, cudaMemcpyDeviceToHost, m->stream));
+  FG_CUDA_TRY(cudaStreamSynchronize(m->stream));
+  return fg_model_check(m);
+}
+
+int fg_model_check(fg_model* m) {
+  if (!m) return set_error(FG_EINVAL, "null model");
+  FG_CUDA_TRY(cudaSetDevice(m->device));
+  return check_device_error_word();
+}
+
+void fg_model_destroy(fg_model* m) {
+  if (!m) return;
+  cudaSetDevice(m->device);
+  cudaDeviceSynchronize();
+  for (void* p : m->allocations) cudaFree(p);
+  if (m->d_ids) cudaFree(m->d_ids);
+  if (m->d_len) cudaFree(m->d_len);
+  if (m->d_out) cudaFree(m->d_out);
+  if (m->stream) cudaStreamDestroy(m->stream);
+  delete m;
+}
+
+}  // extern "C"

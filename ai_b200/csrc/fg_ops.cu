@@ -1,0 +1,217 @@
+// Op-level C ABI: the tensor operations the encoder calls, on device
+// pointers. Scratch space for operand splitting and packing is
+// stream-ordered (cudaMallocAsync / cudaFreeAsync on the caller's stream).
+#include <cmath>
+#include <vector>
+
+#include "fg_internal.h"
+#include "fg_kernels.cuh"
+
+namespace fg {
+namespace {
+
+int64_t round4(int64_t v) { return (v + 3) / 4 * 4; }
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+struct StreamScratch {
+  cudaStream_t s;
+  void* p = nullptr;
+  explicit StreamScratch(cudaStream_t st) : s(st) {}
+  int alloc(size_t bytes) {
+    if (bytes == 0) return FG_OK;
+    if (cudaMallocAsync(&p, bytes, s) != cudaSuccess) {
+      cudaGetLastError();
+      p = nullptr;
+      return set_error(FG_ENOMEM, "scratch allocation of %zu bytes failed", bytes);
+    }
+    return FG_OK;
+  }
+  ~StreamScratch() {
+    if (p) cudaFreeAsync(p, s);
+  }
+};
+
+// cos/sin tables [T, D/2] in float64, stored as float32 (tensor/rope.go:36-50).
+void rope_tables(double base, const int32_t* positions, int T, int D, std::vector<float>& cos_t,
+                 std::vector<float>& sin_t) {
+  const int half = D / 2;
+  std::vector<double> inv(half);
+  for (int i = 0; i < half; ++i) inv[i] = std::pow(base, -double(2 * i) / double(D));
+  cos_t.resize(size_t(T) * half);
+  sin_t.resize(size_t(T) * half);
+  for (int t = 0; t < T; ++t) {
+    const double p = double(positions ? positions[t] : t);
+    for (int i = 0; i < half; ++i) {
+      const double a = p * inv[i];
+      cos_t[size_t(t) * half + i] = float(std::cos(a));
+      sin_t[size_t(t) * half + i] = float(std::sin(a));
+    }
+  }
+}
+
+}  // namespace
+}  // namespace fg
+
+using namespace fg;
+
+extern "C" {
+
+int fg_matmul(int64_t m, int64_t n, int64_t k, const float* x, int64_t ldx, const float* w,
+              int64_t ldw, int w_transposed, float* out, int64_t ldo, const fg_epilogue* epi,
+              int precision, void* stream) {
+  clear_error();
+  if (m < 0 || n < 0 || k < 0 || m > INT32_MAX || n > INT32_MAX || k > INT32_MAX)
+    return set_error(FG_EINVAL, "fg_matmul: bad shape m=%lld n=%lld k=%lld", (long long)m, (long long)n, (long long)k);
+  if (precision != FG_PREC_SPLIT_TF32 && precision != FG_PREC_TF32)
+    return set_error(FG_EINVAL, "fg_matmul: unknown precision %d", precision);
+  if (m == 0 || n == 0) return FG_OK;
+  if (!x || !w || !out) return set_error(FG_EINVAL, "fg_matmul: null operand");
+  if (ldx < k || ldo < n || (w_transposed ? ldw < k : ldw < n))
+    return set_error(FG_EINVAL, "fg_matmul: leading dimension smaller than the row");
+  if (epi && epi->act != FG_ACT_NONE && epi->act != FG_ACT_RELU && epi->act != FG_ACT_GELU)
+    return set_error(FG_EINVAL, "fg_matmul: unknown activation %d", epi->act);
+  if (epi && ((epi->mul && epi->ldm < n) || (epi->residual && epi->ldr < n)))
+    return set_error(FG_EINVAL, "fg_matmul: Mul/Residual leading dimension smaller than n");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int* err = nullptr;
+  FG_TRY(device_error_word(&err));
+
+  GemmEpilogue e;
+  e.out = out;
+  e.ldo = ldo;
+  if (epi) {
+    e.bias = epi->bias;
+    e.rowscale = epi->row_scale;
+    e.act = epi->act;
+    e.mul = epi->mul;
+    e.ldm = epi->ldm;
+    e.residual = epi->residual;
+    e.ldr = epi->ldr;
+  }
+  if (k == 0) {
+    // Empty inner dimension: the product is zero; the epilogue still applies.
+    return set_error(FG_EINVAL, "fg_matmul: k = 0 is not supported");
+  }
+
+  const bool split = precision == FG_PREC_SPLIT_TF32;
+  const int64_t kp = round4(k);
+  const bool a_direct = !split && aligned16(x) && ldx % 4 == 0;
+  const bool b_direct = !split && w_transposed && aligned16(w) && ldw % 4 == 0;
+  // scratch: A hi/lo [m, kp], B (packed [n, kp]) hi/lo
+  size_t need = 0;
+  const size_t a_elems = size_t(m) * kp, b_elems = size_t(n) * kp;
+  if (!a_direct) need += a_elems * (split ? 2 : 1);
+  if (!w_transposed) need += b_elems;  // transposed copy of w
+  if (!b_direct) need += b_elems * (split ? 2 : 1);
+  StreamScratch scratch(s);
+  FG_TRY(scratch.alloc(need * sizeof(float)));
+  float* cur = static_cast<float*>(scratch.p);
+  auto take = [&](size_t elems) {
+    float* r = cur;
+    cur += elems;
+    return r;
+  };
+
+  GemmArgs g;
+  g.M = int(m);
+  g.Nb = int(n);
+  g.K = int(k);
+  if (a_direct) {
+    g.A = x;
+    g.lda = ldx;
+  } else {
+    float* ahi = take(a_elems);
+    float* alo = split ? take(a_elems) : nullptr;
+    FG_TRY(split_copy_2d(x, ldx, m, k, ahi, alo, kp, split ? 1 : 0, s));
+    g.A = ahi;
+    g.A_lo = alo;
+    g.lda = kp;
+  }
+  const float* bsrc = w;
+  int64_t ldb_src = ldw;
+  if (!w_transposed) {
+    float* bt = take(b_elems);
+    FG_TRY(transpose_f32(w, ldw, k, n, bt, kp, s));
+    bsrc = bt;
+    ldb_src = kp;
+  }
+  if (b_direct) {
+    g.B = w;
+    g.ldb = ldw;
+  } else {
+    float* bhi = take(b_elems);
+    float* blo = split ? take(b_elems) : nullptr;
+    FG_TRY(split_copy_2d(bsrc, ldb_src, n, k, bhi, blo, kp, split ? 1 : 0, s));
+    g.B = bhi;
+    g.B_lo = blo;
+    g.ldb = kp;
+  }
+  g.epi = e;
+  return gemm_tn(g, err, s);
+}
+
+int fg_row_sum_squares(const float* x, int64_t rows, int64_t n, int64_t ldx, float* out,
+                       void* stream) {
+  clear_error();
+  if (rows < 0 || n < 0 || ldx < n) return set_error(FG_EINVAL, "fg_row_sum_squares: bad shape");
+  return row_sum_squares(x, rows, n, ldx, out, static_cast<cudaStream_t>(stream));
+}
+
+int fg_rmsnorm(const float* x, int64_t rows, int64_t n, const float* g, float eps, float* out,
+               void* stream) {
+  clear_error();
+  if (rows < 0 || n <= 0) return set_error(FG_EINVAL, "fg_rmsnorm: bad shape");
+  return rmsnorm(x, rows, n, g, eps, out, static_cast<cudaStream_t>(stream));
+}
+
+int fg_rope(const float* x, int64_t rows, int T, int D, double base, const int32_t* positions,
+            float* out, void* stream) {
+  clear_error();
+  if (D % 2 != 0) return set_error(FG_EINVAL, "fg_rope: head dimension %d must be even", D);
+  if (T <= 0 || rows < 0 || rows % T != 0) return set_error(FG_EINVAL, "fg_rope: rows %lld not a multiple of T=%d", (long long)rows, T);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  std::vector<float> ct, st;
+  rope_tables(base, positions, T, D, ct, st);
+  const size_t tb = ct.size() * sizeof(float);
+  StreamScratch scratch(s);
+  FG_TRY(scratch.alloc(2 * tb));
+  float* dc = static_cast<float*>(scratch.p);
+  float* ds = dc + ct.size();
+  if (tb) {
+    FG_CUDA_TRY(cudaMemcpyAsync(dc, ct.data(), tb, cudaMemcpyHostToDevice, s));
+    FG_CUDA_TRY(cudaMemcpyAsync(ds, st.data(), tb, cudaMemcpyHostToDevice, s));
+  }
+  FG_TRY(rope(x, rows, T, D, dc, ds, out, s));
+  // the host tables must outlive the copies
+  FG_CUDA_TRY(cudaStreamSynchronize(s));
+  return FG_OK;
+}
+
+int fg_attention(const float* q, const float* k, const float* v, int B, int Hq, int Hkv, int T,
+                 int S, int D, const int32_t* key_lengths, int window, float scale, float* out,
+                 int precision, void* stream) {
+  clear_error();
+  if (B < 0 || Hq <= 0 || Hkv <= 0 || T < 0 || S < 0 || D <= 0)
+    return set_error(FG_EINVAL, "fg_attention: bad shape");
+  if (precision != FG_PREC_SPLIT_TF32 && precision != FG_PREC_TF32)
+    return set_error(FG_EINVAL, "fg_attention: unknown precision %d", precision);
+  AttnArgs a{};
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.out = out;
+  a.out_lo = nullptr;
+  a.qsb = int64_t(Hq) * T * D; a.qsh = int64_t(T) * D; a.qst = D;
+  a.ksb = int64_t(Hkv) * S * D; a.ksh = int64_t(S) * D; a.kst = D;
+  a.vsb = a.ksb; a.vsh = a.ksh; a.vst = D;
+  a.osb = a.qsb; a.osh = a.qsh; a.ost = D;
+  a.B = B; a.Hq = Hq; a.Hkv = Hkv; a.T = T; a.S = S; a.D = D;
+  a.klen = key_lengths;
+  a.qlen = nullptr;
+  a.window = window;
+  a.scale = scale;
+  FG_TRY(attention_simt(a, static_cast<cudaStream_t>(stream)));
+  return attention_masked_rows(a, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,131 @@
+// Library runtime: thread-local error messages, device queries, the
+// per-device error word kernels report bounded-wait timeouts into, and the
+// device-memory helpers of the C ABI.
+#include <mutex>
+#include <vector>
+
+#include "fg_internal.h"
+
+namespace fg {
+
+namespace {
+thread_local std::string t_last_error;
+std::mutex g_mu;
+std::vector<int*> g_dev_err;  // per device, lazily allocated
+std::vector<int> g_sms;
+}  // namespace
+
+int set_error(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return code;
+}
+
+void clear_error() { t_last_error.clear(); }
+const char* last_error() { return t_last_error.c_str(); }
+
+int sm_count() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (int(g_sms.size()) <= dev) g_sms.resize(dev + 1, 0);
+  if (g_sms[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    g_sms[dev] = n > 0 ? n : 148;
+  }
+  return g_sms[dev];
+}
+
+// Device error word of the current device (zeroed at allocation).
+int device_error_word(int** out) {
+  int dev = 0;
+  FG_CUDA_TRY(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (int(g_dev_err.size()) <= dev) g_dev_err.resize(dev + 1, nullptr);
+  if (g_dev_err[dev] == nullptr) {
+    int* p = nullptr;
+    FG_CUDA_TRY(cudaMalloc(&p, sizeof(int)));
+    FG_CUDA_TRY(cudaMemset(p, 0, sizeof(int)));
+    g_dev_err[dev] = p;
+  }
+  *out = g_dev_err[dev];
+  return FG_OK;
+}
+
+// Synchronises the current device and converts a recorded kernel timeout
+// into FG_ETIMEOUT (resetting the word).
+int check_device_error_word() {
+  FG_CUDA_TRY(cudaDeviceSynchronize());
+  int* w = nullptr;
+  FG_TRY(device_error_word(&w));
+  int v = 0;
+  FG_CUDA_TRY(cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost));
+  if (v != 0) {
+    FG_CUDA_TRY(cudaMemset(w, 0, sizeof(int)));
+    return set_error(FG_ETIMEOUT, "a device wait gave up (kernel status %d)", v);
+  }
+  return FG_OK;
+}
+
+}  // namespace fg
+
+extern "C" {
+
+const char* fg_last_error(void) { return fg::last_error(); }
+
+int fg_device_count(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  int good = 0;
+  for (int d = 0; d < n; ++d) {
+    int major = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, d);
+    if (major == 10) ++good;
+  }
+  return good;
+}
+
+int fg_malloc(int device, int64_t bytes, void** out) {
+  if (!out || bytes < 0) return fg::set_error(FG_EINVAL, "fg_malloc: bad arguments");
+  FG_CUDA_TRY(cudaSetDevice(device));
+  *out = nullptr;
+  if (bytes == 0) return FG_OK;
+  if (cudaMalloc(out, size_t(bytes)) != cudaSuccess) {
+    cudaGetLastError();
+    return fg::set_error(FG_ENOMEM, "fg_malloc: %lld bytes", (long long)bytes);
+  }
+  return FG_OK;
+}
+
+int fg_free(int device, void* ptr) {
+  FG_CUDA_TRY(cudaSetDevice(device));
+  if (ptr) FG_CUDA_TRY(cudaFree(ptr));
+  return FG_OK;
+}
+
+int fg_memcpy_h2d(int device, void* dst, const void* src, int64_t bytes) {
+  FG_CUDA_TRY(cudaSetDevice(device));
+  if (bytes > 0) FG_CUDA_TRY(cudaMemcpy(dst, src, size_t(bytes), cudaMemcpyHostToDevice));
+  return FG_OK;
+}
+
+int fg_memcpy_d2h(int device, void* dst, const void* src, int64_t bytes) {
+  FG_CUDA_TRY(cudaSetDevice(device));
+  if (bytes > 0) FG_CUDA_TRY(cudaMemcpy(dst, src, size_t(bytes), cudaMemcpyDeviceToHost));
+  return FG_OK;
+}
+
+int fg_synchronize(int device) {
+  FG_CUDA_TRY(cudaSetDevice(device));
+  return fg::check_device_error_word();
+}
+
+}  // extern "C"

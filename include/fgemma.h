@@ -1,0 +1,200 @@
+/*
+ * fgemma.h — C ABI of the B200 (sm_100a) EmbeddingGemma encoder library.
+ *
+ * This is the drop-in boundary for the fiber/ai `models/gemma` encoder hot
+ * path and the `tensor` operations it calls. Every entry point is plain C:
+ * pointers, sizes and status codes, no C++ or torch types. Each function
+ * returns FG_OK (0) or a negative FG_E* code and never aborts the process;
+ * fg_last_error() returns the calling thread's last message.
+ *
+ * Reference interfaces replaced (paths inside the fiber/ai repository):
+ *   models/gemma/model.go:76-232   gemma.Load (weights → fg_model_* below)
+ *   models/gemma/embed.go:118-157  (*Model).embedBatch → fg_embed_ids
+ *   models/gemma/embed.go:160-240  (*Model).encode     (inside fg_embed_ids)
+ *   models/gemma/embed.go:381-475  pool / applyHead / l2normalize (inside fg_embed_ids)
+ *   tensor/matmul.go:19            tensor.MatMul         → fg_matmul
+ *   tensor/matmul_fused.go:40      tensor.MatMulFused    → fg_matmul with fg_epilogue
+ *   tensor/matmul_fused.go:125     (*Tensor).RowSumSquares → fg_row_sum_squares
+ *   tensor/attention.go:67         tensor.AttentionScaled (padding / window masks) → fg_attention
+ *   tensor/attention.go:292        tensor.RMSNorm        → fg_rmsnorm
+ *   tensor/rope.go:20              tensor.RoPE           → fg_rope
+ *
+ * Threading: a model is driven by one host thread at a time. Op-level calls
+ * take device pointers and a CUDA stream (NULL = legacy default stream) and
+ * are asynchronous on that stream unless stated otherwise.
+ */
+#ifndef FGEMMA_H
+#define FGEMMA_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define FG_OK 0
+#define FG_EINVAL (-1)   /* bad argument: shape, stride, alignment, name */
+#define FG_ENOMEM (-2)   /* device or host allocation failed */
+#define FG_ECUDA (-3)    /* a CUDA runtime/driver call failed */
+#define FG_ETIMEOUT (-4) /* a bounded device wait gave up (kernel reported it) */
+#define FG_ESTATE (-5)   /* call out of order (e.g. embed before finalize) */
+#define FG_ENODEV (-6)   /* no usable sm_100 device */
+
+/* ---- arithmetic modes -------------------------------------------------- */
+#define FG_PREC_SPLIT_TF32 0 /* 3-pass split TF32: fp32-level products (default) */
+#define FG_PREC_TF32 1       /* one TF32 pass per product */
+
+/* ---- activations: blas.Activation, internal/blas/gemm.go:270-274 -------- */
+#define FG_ACT_NONE 0
+#define FG_ACT_RELU 1
+#define FG_ACT_GELU 2 /* tanh approximation, internal/kernel/math.go:117-143 */
+
+/* ---- host weight dtypes: safetensors/convert.go:16-21 -------------------- */
+#define FG_DT_F32 0
+#define FG_DT_BF16 1
+#define FG_DT_F16 2
+
+/* tensor.Fused (tensor/matmul_fused.go:17-23): applied in the order
+ * bias → row_scale → act → mul → residual (internal/blas/gemm.go:276-288).
+ * NULL pointers are skipped. mul / residual are [m, n] with row strides. */
+typedef struct fg_epilogue {
+  const float* bias;      /* [n] */
+  const float* row_scale; /* [m] */
+  int act;                /* FG_ACT_* */
+  const float* mul;       /* [m, n] */
+  int64_t ldm;
+  const float* residual;  /* [m, n] */
+  int64_t ldr;
+} fg_epilogue;
+
+/* The Config fields encode() reads (models/gemma/config.go:19-37), with the
+ * per-layer derivations already resolved by the caller:
+ *   window       = Config.window()      (config.go:331-339); 0 = no sliding layers
+ *   sliding[l]   = Config.isSliding(l)  (config.go:342)
+ *   rope_base[l] = Config.ropeBase(l)   (config.go:346-362)
+ *   attn_scale   = 1/sqrt(query_pre_attn_scalar)  (model.go:100)
+ * Dense head layers follow modules.json (model.go:277-304). */
+#define FG_MAX_DENSE 4
+typedef struct fg_config {
+  int hidden_size;
+  int intermediate_size;
+  int num_layers;
+  int num_heads;
+  int num_kv_heads;
+  int head_dim;
+  int vocab_size;
+  int window;
+  float rms_norm_eps;
+  float attn_scale;
+  int max_tokens;          /* sequence cap (model.go:98-104), ≤ 2048 */
+  const int* sliding;      /* [num_layers] */
+  const double* rope_base; /* [num_layers] */
+  int num_dense;
+  int dense_in[FG_MAX_DENSE];
+  int dense_out[FG_MAX_DENSE];
+  int dense_tanh[FG_MAX_DENSE];
+  int l2_normalize;        /* Normalize module present (model.go:262-263, 305-306) */
+} fg_config;
+
+typedef struct fg_model fg_model;
+
+/* ---- library ----------------------------------------------------------- */
+/* Number of CUDA devices of compute capability 10.x. */
+int fg_device_count(void);
+/* Last error message of the calling thread ("" when none). */
+const char* fg_last_error(void);
+
+/* Device memory helpers, so a caller without the CUDA runtime (a cgo
+ * binding) can stage tensors. Synchronous. */
+int fg_malloc(int device, int64_t bytes, void** out);
+int fg_free(int device, void* ptr);
+int fg_memcpy_h2d(int device, void* dst, const void* src, int64_t bytes);
+int fg_memcpy_d2h(int device, void* dst, const void* src, int64_t bytes);
+/* Waits for all work on `device`; returns FG_ETIMEOUT (and clears the
+ * record) when a kernel's bounded wait gave up since the last check. */
+int fg_synchronize(int device);
+
+/* ---- model: gemma.Load + (*Model).embedBatch ---------------------------- */
+/* Creates an empty model on `device` for the given configuration.
+ * Replaces the allocation half of gemma.Load (models/gemma/model.go:76-104). */
+int fg_model_create(const fg_config* cfg, int device, fg_model** out);
+
+/* Hands one weight to the model, by its safetensors name without the
+ * "model." / "language_model." prefixes (model.go:112-119), e.g.
+ * "embed_tokens.weight", "layers.3.self_attn.q_proj.weight", "norm.weight";
+ * the Dense head layers are "dense.<i>.linear.weight" ([out, in]).
+ * data is host memory of the given dtype and shape ([out, in] for
+ * projections, as stored); it is copied, the caller keeps ownership.
+ * Replaces model.go:142-205 (get / transpose / norm). */
+int fg_model_set_weight(fg_model* m, const char* name, int dtype, const int64_t* shape, int ndim,
+                        const void* data);
+
+/* Checks every weight is present, applies the (1+w) norm offset and folds
+ * the pre-norms into the projections (model.go:131-140, 206-222), splits
+ * the projections into TF32 high/low parts and uploads them.
+ * max_batch_tokens sizes the device workspace (B·T of the largest call). */
+int fg_model_finalize(fg_model* m, int64_t max_batch_tokens);
+
+/* Embeds B sequences of ids, right-padded to T, and writes [B, dim] float
+ * embeddings (mean-pooled, Dense head, Matryoshka-narrowed, L2-normalised)
+ * in input order. Host buffers; synchronous. Same semantics as
+ * (*Model).embedBatch (models/gemma/embed.go:118-157) after the ids are
+ * padded: ids[b*T + t] for t < lengths[b] are read, padding is ignored.
+ * lengths[b] may be 0 (pooled as one row, embed.go:386-389). */
+int fg_embed_ids(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int T, int dim,
+                 int precision, float* out);
+
+/* As fg_embed_ids with device buffers on the model's device, asynchronous
+ * on `stream` (a cudaStream_t, NULL = default stream). */
+int fg_embed_ids_device(fg_model* m, const int32_t* d_ids, const int32_t* d_lengths, int B, int T,
+                        int dim, int precision, float* d_out, void* stream);
+
+/* Reads back the device error word of the last device call and resets it
+ * (FG_ETIMEOUT when a bounded wait gave up). Synchronises the model's device. */
+int fg_model_check(fg_model* m);
+
+void fg_model_destroy(fg_model* m);
+
+/* ---- tensor operations (device pointers) ------------------------------- */
+/* out[m, n] = epilogue(x[m, k] · w) — tensor.MatMul (tensor/matmul.go:19)
+ * and tensor.MatMulFused (tensor/matmul_fused.go:40). w is [k, n] row-major
+ * with leading dimension ldw, or, when w_transposed != 0, the transposed
+ * view of an [n, k] row-major matrix (x · Wᵀ, the `w.T()` case). epi may be
+ * NULL. Row strides must be multiples of 4 floats and pointers 16-byte
+ * aligned. */
+int fg_matmul(int64_t m, int64_t n, int64_t k, const float* x, int64_t ldx, const float* w,
+              int64_t ldw, int w_transposed, float* out, int64_t ldo, const fg_epilogue* epi,
+              int precision, void* stream);
+
+/* out[r] = Σ_c x[r, c]² — (*Tensor).RowSumSquares (tensor/matmul_fused.go:125-143). */
+int fg_row_sum_squares(const float* x, int64_t rows, int64_t n, int64_t ldx, float* out,
+                       void* stream);
+
+/* out = x / sqrt(mean(x²) + eps) · g over the last dimension n —
+ * tensor.RMSNorm (tensor/attention.go:292-337). g holds the final gains
+ * (the caller adds Gemma's 1 as the reference's Load does). */
+int fg_rmsnorm(const float* x, int64_t rows, int64_t n, const float* g, float eps, float* out,
+               void* stream);
+
+/* Rotate-half RoPE over contiguous [rows, D] vectors whose slot is
+ * (row % T), at positions[slot] — tensor.RoPE (tensor/rope.go:20-87). */
+int fg_rope(const float* x, int64_t rows, int T, int D, double base, const int32_t* positions,
+            float* out, void* stream);
+
+/* softmax(scale·q·kᵀ + mask)·v for q [B, Hq, T, D], k and v [B, Hkv, S, D]
+ * (contiguous), with Hq a multiple of Hkv (grouped-query heads share a KV
+ * head, the Expand view of tensor/attention.go:62-66). The mask is the
+ * additive −1e9 mask the encoder builds: key j of batch b is hidden when
+ * j >= key_lengths[b] (PaddingMask, attention.go:33-42; NULL = none) or,
+ * when window > 0, when |i − j| >= window (WindowMask, attention.go:97-107).
+ * — tensor.AttentionScaled (tensor/attention.go:67). */
+int fg_attention(const float* q, const float* k, const float* v, int B, int Hq, int Hkv, int T,
+                 int S, int D, const int32_t* key_lengths, int window, float scale, float* out,
+                 int precision, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FGEMMA_H */
