@@ -1,0 +1,208 @@
+"""GPU parity of the whole encoder path (fg_embed_ids) against the CPU
+oracle and the committed Hugging Face goldens.
+
+Bar (split-TF32, the default): per-sentence cosine ≥ 0.99999 and max-abs
+elementwise error ≤ 1e-4 against the float64 oracle and the goldens.
+Plain TF32 is measured and reported, with a looser sanity bound.
+"""
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+GOLD = Path(__file__).resolve().parent / "golden"
+COS_MIN = 0.99999
+MAXABS = 1e-4
+
+
+def _cmp(got, want):
+    got = got.astype(np.float64)
+    want = want.astype(np.float64)
+    cos = (got * want).sum(1) / np.linalg.norm(got, axis=1) / np.linalg.norm(want, axis=1)
+    return float(cos.min()), float(np.abs(got - want).max())
+
+
+def _case(name):
+    from ai_b200 import synthetic as S
+
+    m = json.loads((GOLD / "manifest.json").read_text())[name]
+    cfg = dict(S.EMBEDDINGGEMMA_300M)
+    cfg.update(m["config"])
+    w = S.make_weights(cfg, seed=m["seed"], norm_std=m["norm_std"])
+    z = np.load(GOLD / f"{name}.npz")
+    return cfg, w, z
+
+
+@pytest.fixture(scope="module")
+def c1():
+    from ai_b200 import gemma
+    from oracle import oracle as O
+
+    cfg, w, z = _case("c1")
+    model = gemma.from_synthetic(cfg, w, device=0, max_batch_tokens=4096)
+    orc = O.from_bf16(cfg, w)
+    yield cfg, w, z, model, orc
+    model.close()
+
+
+def test_c1_split_tf32_matches_goldens_and_oracle(c1):
+    from oracle import oracle as O
+
+    cfg, w, z, model, orc = c1
+    got = model.embed_padded(z["ids"], z["lengths"])
+    ref64 = orc.embed_padded(z["ids"], z["lengths"], mode=O.F64)
+    ref32 = orc.embed_padded(z["ids"], z["lengths"], mode=O.F32)
+    c_hf, m_hf = _cmp(got, z["hf"])
+    c_or, m_or = _cmp(got, ref64)
+    c_rr, m_rr = _cmp(ref32, ref64)
+    print(f"\nC1 split-TF32 vs HF: cos {c_hf:.9f} maxabs {m_hf:.3e}; vs oracle f64: cos {c_or:.9f} "
+          f"maxabs {m_or:.3e}; reference-f32 arithmetic vs f64: cos {c_rr:.9f} maxabs {m_rr:.3e}")
+    assert c_hf >= COS_MIN and m_hf <= MAXABS
+    assert c_or >= COS_MIN and m_or <= MAXABS
+
+
+def test_c1_plain_tf32_deviation(c1):
+    from ai_b200 import gemma
+
+    cfg, w, z, model, orc = c1
+    got = model.embed_padded(z["ids"], z["lengths"], precision=gemma.PREC_TF32)
+    c, m = _cmp(got, z["hf"])
+    print(f"\nC1 plain TF32 vs HF: cos {c:.9f} maxabs {m:.3e}")
+    assert c >= 0.999
+
+
+def test_c1_deterministic(c1):
+    cfg, w, z, model, orc = c1
+    a = model.embed_padded(z["ids"], z["lengths"])
+    b = model.embed_padded(z["ids"], z["lengths"])
+    assert np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("name", ["window", "ragged"])
+def test_padded_window_and_ragged_goldens(name):
+    from ai_b200 import gemma
+    from oracle import oracle as O
+
+    cfg, w, z = _case(name)
+    model = gemma.from_synthetic(cfg, w, device=0, max_batch_tokens=4096)
+    try:
+        got = model.embed_padded(z["ids"], z["lengths"])
+        ref = O.from_bf16(cfg, w).embed_padded(z["ids"], z["lengths"], mode=O.F64)
+    finally:
+        model.close()
+    c_hf, m_hf = _cmp(got, z["hf"])
+    c_or, m_or = _cmp(got, ref)
+    print(f"\n{name}: vs HF cos {c_hf:.9f} maxabs {m_hf:.3e}; vs oracle cos {c_or:.9f} maxabs {m_or:.3e}")
+    assert c_hf >= COS_MIN and m_hf <= MAXABS
+    assert c_or >= COS_MIN and m_or <= MAXABS
+
+
+@pytest.fixture(scope="module")
+def small():
+    from ai_b200 import gemma
+    from ai_b200 import synthetic as S
+    from oracle import oracle as O
+
+    cfg = S.small_config(layers=6, vocab=4096)
+    w = S.make_weights(cfg, seed=21, norm_std=0.1)
+    model = gemma.from_synthetic(cfg, w, device=0, max_batch_tokens=8192)
+    yield cfg, w, model, O.from_bf16(cfg, w)
+    model.close()
+
+
+def test_length_zero_and_one(small):
+    """A length-0 sequence embeds as the reference's all-padding row 0
+    (embed.go:131-137, 386-389); checked against the oracle, which runs the
+    reference's literal masks."""
+    from ai_b200 import synthetic as S
+    from oracle import oracle as O
+
+    cfg, w, model, orc = small
+    ids = S.make_ids(4, 40, 3, cfg["vocab_size"])
+    lengths = np.array([0, 1, 40, 0], np.int32)
+    got = model.embed_padded(ids, lengths)
+    ref = orc.embed_padded(ids, lengths, mode=O.F64)
+    c, m = _cmp(got, ref)
+    assert c >= COS_MIN and m <= MAXABS, (c, m)
+
+
+def test_batch_invariance(small):
+    """A sequence embeds the same alone and inside a padded batch
+    (models/gemma/gemma_test.go:117-135 asks ≥ 0.9999)."""
+    from ai_b200 import synthetic as S
+
+    cfg, w, model, orc = small
+    seqs, _ = S.make_ragged(6, 5, 400, 9, cfg["vocab_size"])
+    together = model.embed_batch(seqs)
+    for i, s in enumerate(seqs):
+        alone = model.embed_batch([s])
+        c, m = _cmp(alone, together[i:i + 1])
+        assert c >= COS_MIN and m <= MAXABS, (i, c, m)
+
+
+def test_matryoshka_dim(small):
+    """Dim(d) narrows the head output and renormalises (embed.go:421-427)."""
+    from ai_b200 import synthetic as S
+
+    cfg, w, model, orc = small
+    ids = S.make_ids(3, 50, 4, cfg["vocab_size"])
+    lengths = np.array([50, 30, 10], np.int32)
+    full = model.embed_padded(ids, lengths)
+    part = model.embed_padded(ids, lengths, dim=256)
+    want = full[:, :256] / np.linalg.norm(full[:, :256].astype(np.float64), axis=1, keepdims=True)
+    assert np.abs(part - want).max() <= 1e-6
+
+
+def test_embed_ids_batches_and_restores_order(small):
+    from ai_b200 import gemma
+    from ai_b200 import synthetic as S
+
+    cfg, w, model, orc = small
+    seqs, _ = S.make_ragged(10, 1, 300, 13, cfg["vocab_size"])
+    model.batch_tokens = 600  # forces several greedy batches (embed.go:61-74)
+    try:
+        got = np.stack(model.embed_ids(seqs))
+    finally:
+        model.batch_tokens = 8192
+    want = np.stack([model.embed_batch([s])[0] for s in seqs])
+    c, m = _cmp(got, want)
+    assert c >= COS_MIN and m <= MAXABS
+
+
+def test_errors_are_reported_not_fatal(small):
+    from ai_b200 import _lib, gemma
+
+    cfg, w, model, orc = small
+    with pytest.raises(_lib.FGError) as e:
+        model.embed_padded(np.full((1, 4), cfg["vocab_size"], np.int32), np.array([4], np.int32))
+    assert e.value.code == _lib.FG_EINVAL
+    with pytest.raises(gemma.GemmaError):
+        model.embed_ids([[2, 5, 6]], Dim=769)
+    with pytest.raises(_lib.FGError):
+        model.embed_padded(np.zeros((1, 3000), np.int32), np.array([3000], np.int32))
+    # the model still works afterwards
+    out = model.embed_padded(np.array([[2, 7, 9]], np.int32), np.array([3], np.int32))
+    assert np.isfinite(out).all()
+    model.check()
+
+
+def test_device_api(small):
+    import torch
+
+    from ai_b200 import synthetic as S
+
+    cfg, w, model, orc = small
+    ids = S.make_ids(4, 64, 17, cfg["vocab_size"])
+    lengths = np.array([64, 10, 33, 1], np.int32)
+    d_ids = torch.from_numpy(ids).cuda()
+    d_len = torch.from_numpy(lengths).cuda()
+    out = torch.empty((4, 768), dtype=torch.float32, device="cuda")
+    s = torch.cuda.current_stream()
+    model.embed_device(d_ids, d_len, 4, 64, 768, out, s)
+    s.synchronize()
+    model.check()
+    want = model.embed_padded(ids, lengths)
+    assert np.array_equal(out.cpu().numpy(), want)
