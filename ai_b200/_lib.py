@@ -32,6 +32,10 @@ DT_F16 = 2
 
 MAX_DENSE = 4
 
+# Phases of fg_model_read_profile (include/fgemma.h FG_PHASE_*).
+PHASES = ["embed", "gemm_qkv", "qk_norm_rope", "attention", "gemm_o", "residual",
+          "gemm_gate_up", "gemm_down", "pool_head"]
+
 # Every symbol include/fgemma.h declares, with (restype, argtypes).
 _i64 = C.c_int64
 _fp = C.POINTER(C.c_float)
@@ -92,6 +96,9 @@ SIGNATURES = {
     "fg_embed_ids_device": (C.c_int, [_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp]),
     "fg_model_check": (C.c_int, [_vp]),
     "fg_model_destroy": (None, [_vp]),
+    "fg_model_set_profiling": (C.c_int, [_vp, C.c_int]),
+    "fg_model_read_profile": (C.c_int, [_vp, C.POINTER(C.c_double), C.POINTER(C.c_int64),
+                                        C.POINTER(C.c_double), C.c_int]),
     "fg_matmul": (C.c_int, [_i64, _i64, _i64, _vp, _i64, _vp, _i64, C.c_int, _vp, _i64,
                             C.POINTER(Epilogue), C.c_int, _vp]),
     "fg_row_sum_squares": (C.c_int, [_vp, _i64, _i64, _i64, _vp, _vp]),

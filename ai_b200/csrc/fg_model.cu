@@ -16,6 +16,7 @@
 //              each with its TF32 low part when it is non-zero
 //   activations, token-major [B·T, ·]: x (residual stream) + x_lo, qkv,
 //   att + att_lo, gu + gu_lo, tmp; rowscale [B·T].
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <map>
@@ -134,6 +135,18 @@ struct fg_model {
   int64_t d_out_cap = 0;
   int d_len_cap = 0;
   cudaStream_t stream = nullptr;
+
+  // measurement: launch counts and algorithmic work per phase (always),
+  // CUDA-event pairs around each launch while profiling is enabled
+  bool prof = false;
+  struct Mark {
+    int phase;
+    cudaEvent_t a, b;
+  };
+  std::vector<Mark> marks;
+  std::vector<cudaEvent_t> event_pool;
+  int64_t launches[FG_NUM_PHASES] = {};
+  double work[FG_NUM_PHASES] = {};
 };
 
 namespace fg {
@@ -177,8 +190,13 @@ int upload_mat(fg_model* m, const std::vector<float>& h, int rows, int cols, Dev
   FG_TRY(split_tf32(raw, raw, lo, int64_t(h.size()), flag, nullptr));
   int any = 0;
   FG_CUDA_TRY(cudaMemcpy(&any, flag, sizeof(int), cudaMemcpyDeviceToHost));
+  if (!any) {  // bf16-exact weights: no low pass, release the buffer
+    FG_CUDA_TRY(cudaFree(lo));
+    m->allocations.erase(std::find(m->allocations.begin(), m->allocations.end(), static_cast<void*>(lo)));
+    lo = nullptr;
+  }
   out->hi = raw;
-  out->lo = any ? lo : nullptr;
+  out->lo = lo;
   out->rows = rows;
   out->cols = cols;
   return FG_OK;
@@ -374,6 +392,53 @@ int finalize(fg_model* m, int64_t max_tokens) {
   return FG_OK;
 }
 
+cudaEvent_t take_event(fg_model* m) {
+  if (!m->event_pool.empty()) {
+    cudaEvent_t e = m->event_pool.back();
+    m->event_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  if (cudaEventCreate(&e) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  return e;
+}
+
+// Brackets the launches of one phase: counts them, adds their algorithmic
+// work, and, while profiling, records an event pair on the stream.
+struct PhaseScope {
+  fg_model* m;
+  int phase;
+  cudaStream_t s;
+  cudaEvent_t a = nullptr;
+  PhaseScope(fg_model* m_, int p, cudaStream_t s_, double work, int nlaunch = 1)
+      : m(m_), phase(p), s(s_) {
+    m->launches[p] += nlaunch;
+    m->work[p] += work;
+    if (m->prof) {
+      a = take_event(m);
+      if (a) cudaEventRecord(a, s);
+    }
+  }
+  ~PhaseScope() {
+    if (!a) return;
+    cudaEvent_t b = take_event(m);
+    if (!b) {
+      m->event_pool.push_back(a);
+      return;
+    }
+    cudaEventRecord(b, s);
+    m->marks.push_back({phase, a, b});
+  }
+};
+
+double gemm_flops(const GemmArgs& g) {
+  const double nout = g.epi.geglu ? g.Nb : g.Nb;
+  return 2.0 * double(g.M) * nout * double(g.K);
+}
+
 GemmArgs make_gemm(int M, const float* A, const float* A_lo, int64_t lda, const DevMat& B,
                    bool split) {
   GemmArgs g;
@@ -401,11 +466,15 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
   const int qkvw = (Hq + 2 * Hkv) * D, attw = Hq * D;
   float* x_lo = split ? m->x_lo : nullptr;
 
-  eff_len_kernel<<<(B + 127) / 128, 128, 0, s>>>(lengths, B, T, m->eff_len);
-  FG_CUDA_TRY(cudaGetLastError());
-  const float emb_scale = float(std::sqrt(double(H)));
-  FG_TRY(embed_gather(m->embed, c.vocab_size, ids, lengths, B, T, H, emb_scale, c.rms_norm_eps,
-                      m->x, x_lo, m->rowscale, m->err, s));
+  const double act_bytes = double(M) * H * 4.0;
+  {
+    PhaseScope ps(m, FG_PHASE_EMBED, s, act_bytes * (split ? 3 : 2) + double(M) * 8, 2);
+    eff_len_kernel<<<(B + 127) / 128, 128, 0, s>>>(lengths, B, T, m->eff_len);
+    FG_CUDA_TRY(cudaGetLastError());
+    const float emb_scale = float(std::sqrt(double(H)));
+    FG_TRY(embed_gather(m->embed, c.vocab_size, ids, lengths, B, T, H, emb_scale, c.rms_norm_eps,
+                        m->x, x_lo, m->rowscale, m->err, s));
+  }
 
   for (int l = 0; l < c.num_layers; ++l) {
     const Layer& L = m->layers[l];
@@ -415,10 +484,16 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
     g.epi.out = m->qkv;
     g.epi.ldo = qkvw;
     g.epi.rowscale = m->rowscale;
-    FG_TRY(gemm_tn(g, m->err, s));
+    {
+      PhaseScope ps(m, FG_PHASE_GEMM_QKV, s, gemm_flops(g));
+      FG_TRY(gemm_tn(g, m->err, s));
+    }
     // QK-norm + RoPE (embed.go:198-207)
-    FG_TRY(qk_norm_rope(m->qkv, nullptr, M, Hq, Hkv, D, L.qgain, L.kgain, c.rms_norm_eps,
-                        m->rope_cos[L.rope], m->rope_sin[L.rope], T, s));
+    {
+      PhaseScope ps(m, FG_PHASE_QK_NORM_ROPE, s, double(M) * (Hq + Hkv) * D * 8.0);
+      FG_TRY(qk_norm_rope(m->qkv, nullptr, M, Hq, Hkv, D, L.qgain, L.kgain, c.rms_norm_eps,
+                          m->rope_cos[L.rope], m->rope_sin[L.rope], T, s));
+    }
     // attention (embed.go:209, attention.go:130)
     AttnArgs a{};
     a.q = m->qkv;
@@ -435,15 +510,24 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
     a.qlen = m->eff_len;
     a.window = (c.window > 0 && m->sliding[l]) ? c.window : 0;
     a.scale = c.attn_scale;
-    FG_TRY(attention_simt(a, s));
+    {
+      PhaseScope ps(m, FG_PHASE_ATTENTION, s, 0.0);
+      FG_TRY(attention_simt(a, s));
+    }
     // o0 = att · Wo   (embed.go:212-214)
     g = make_gemm(int(M), m->att, m->att_lo, attw, L.wo, split);
     g.epi.out = m->tmp;
     g.epi.ldo = H;
-    FG_TRY(gemm_tn(g, m->err, s));
+    {
+      PhaseScope ps(m, FG_PHASE_GEMM_O, s, gemm_flops(g));
+      FG_TRY(gemm_tn(g, m->err, s));
+    }
     // x += RMSNorm(o0)   (embed.go:216-220), and the FFN pre-norm factor
-    FG_TRY(residual_postnorm(m->x, x_lo, m->tmp, L.post_attn, c.rms_norm_eps, m->rowscale,
-                             nullptr, M, H, s));
+    {
+      PhaseScope ps(m, FG_PHASE_RESIDUAL, s, act_bytes * (split ? 4 : 3) + double(M) * 4);
+      FG_TRY(residual_postnorm(m->x, x_lo, m->tmp, L.post_attn, c.rms_norm_eps, m->rowscale,
+                               nullptr, M, H, s));
+    }
     // gu = GELU(rs·x·Wg') ⊙ (rs·x·Wu')   (embed.go:224-227)
     g = make_gemm(int(M), m->x, x_lo, H, L.wgu, split);
     g.epi.out = m->gu;
@@ -452,19 +536,29 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
     g.epi.ldo_lo = F;
     g.epi.rowscale = m->rowscale;
     g.epi.geglu = 1;
-    FG_TRY(gemm_tn(g, m->err, s));
+    {
+      PhaseScope ps(m, FG_PHASE_GEMM_GATE_UP, s, gemm_flops(g));
+      FG_TRY(gemm_tn(g, m->err, s));
+    }
     // mlp0 = gu · Wd   (embed.go:229)
     g = make_gemm(int(M), m->gu, m->gu_lo, F, L.wd, split);
     g.epi.out = m->tmp;
     g.epi.ldo = H;
-    FG_TRY(gemm_tn(g, m->err, s));
+    {
+      PhaseScope ps(m, FG_PHASE_GEMM_DOWN, s, gemm_flops(g));
+      FG_TRY(gemm_tn(g, m->err, s));
+    }
     // x += RMSNorm(mlp0)   (embed.go:231-235); final norm on the last layer (embed.go:237)
-    FG_TRY(residual_postnorm(m->x, x_lo, m->tmp, L.post_ffn, c.rms_norm_eps, m->rowscale,
-                             last ? m->final_gain : nullptr, M, H, s));
+    {
+      PhaseScope ps(m, FG_PHASE_RESIDUAL, s, act_bytes * ((split && !last) ? 4 : 3) + double(M) * 4);
+      FG_TRY(residual_postnorm(m->x, x_lo, m->tmp, L.post_ffn, c.rms_norm_eps, m->rowscale,
+                               last ? m->final_gain : nullptr, M, H, s));
+    }
   }
   if (c.num_layers == 0) return set_error(FG_EINVAL, "model has no layers");
 
   // pool (embed.go:381-404), head (embed.go:408-429), L2 (embed.go:472-475)
+  PhaseScope ps(m, FG_PHASE_POOL_HEAD, s, act_bytes, 2 + int(m->dense.size()));
   FG_TRY(mean_pool(m->x, m->eff_len, B, T, H, m->pooled, split ? m->pooled_lo : nullptr, s));
   const float* cur = m->pooled;
   const float* cur_lo = m->pooled_lo;
@@ -643,10 +737,48 @@ int fg_model_check(fg_model* m) {
   return check_device_error_word();
 }
 
+int fg_model_set_profiling(fg_model* m, int enable) {
+  clear_error();
+  if (!m) return set_error(FG_EINVAL, "null model");
+  m->prof = enable != 0;
+  return FG_OK;
+}
+
+int fg_model_read_profile(fg_model* m, double* ms, int64_t* launches, double* work, int n) {
+  clear_error();
+  if (!m || n < 0) return set_error(FG_EINVAL, "fg_model_read_profile: bad arguments");
+  FG_CUDA_TRY(cudaSetDevice(m->device));
+  double acc[FG_NUM_PHASES] = {};
+  for (auto& mk : m->marks) {
+    float t = 0.f;
+    FG_CUDA_TRY(cudaEventSynchronize(mk.b));
+    FG_CUDA_TRY(cudaEventElapsedTime(&t, mk.a, mk.b));
+    acc[mk.phase] += t;
+    m->event_pool.push_back(mk.a);
+    m->event_pool.push_back(mk.b);
+  }
+  m->marks.clear();
+  for (int p = 0; p < n && p < FG_NUM_PHASES; ++p) {
+    if (ms) ms[p] = acc[p];
+    if (launches) launches[p] = m->launches[p];
+    if (work) work[p] = m->work[p];
+  }
+  for (int p = 0; p < FG_NUM_PHASES; ++p) {
+    m->launches[p] = 0;
+    m->work[p] = 0;
+  }
+  return FG_OK;
+}
+
 void fg_model_destroy(fg_model* m) {
   if (!m) return;
   cudaSetDevice(m->device);
   cudaDeviceSynchronize();
+  for (auto& mk : m->marks) {
+    cudaEventDestroy(mk.a);
+    cudaEventDestroy(mk.b);
+  }
+  for (auto e : m->event_pool) cudaEventDestroy(e);
   for (void* p : m->allocations) cudaFree(p);
   if (m->d_ids) cudaFree(m->d_ids);
   if (m->d_len) cudaFree(m->d_len);

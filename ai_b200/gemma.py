@@ -279,15 +279,19 @@ class Model:
 
     # -- embedBatch / Embed
     def embed_padded(self, ids: np.ndarray, lengths: np.ndarray, dim: Optional[int] = None,
-                     precision: int = PREC_SPLIT_TF32) -> np.ndarray:
-        """One forward over an already padded [B, T] batch (host buffers)."""
+                     precision: int = PREC_SPLIT_TF32, out: Optional[np.ndarray] = None) -> np.ndarray:
+        """One forward over an already padded [B, T] batch (host buffers;
+        pinned ones are copied without staging)."""
         ids = np.ascontiguousarray(ids, dtype=np.int32)
         lengths = np.ascontiguousarray(lengths, dtype=np.int32)
         B, T = ids.shape
         dim = self.Dim() if dim is None else dim
         if dim < 1 or dim > self.Dim():
             raise GemmaError(f"gemma: Dim({dim}) outside 1..{self.Dim()}")
-        out = np.empty((B, dim), dtype=np.float32)
+        if out is None:
+            out = np.empty((B, dim), dtype=np.float32)
+        elif out.shape != (B, dim) or out.dtype != np.float32 or not out.flags.c_contiguous:
+            raise GemmaError("gemma: out must be a contiguous float32 [B, dim] array")
         _lib.check(_lib.lib().fg_embed_ids(self._h, ids.ctypes.data_as(C.c_void_p),
                                            lengths.ctypes.data_as(C.c_void_p), B, T, dim,
                                            precision, out.ctypes.data_as(C.c_void_p)))
@@ -317,6 +321,21 @@ class Model:
     def check(self) -> None:
         """Raises if a kernel's bounded wait gave up since the last check."""
         _lib.check(_lib.lib().fg_model_check(self._h))
+
+    def set_profiling(self, on: bool) -> None:
+        """Brackets every kernel launch with CUDA events on its stream."""
+        _lib.check(_lib.lib().fg_model_set_profiling(self._h, int(on)))
+
+    def read_profile(self) -> Dict[str, dict]:
+        """Per phase: device ms, launches and algorithmic work since the
+        last read (FLOPs for GEMM phases, bytes for memory-bound ones)."""
+        n = len(_lib.PHASES)
+        ms = (C.c_double * n)()
+        launches = (C.c_int64 * n)()
+        work = (C.c_double * n)()
+        _lib.check(_lib.lib().fg_model_read_profile(self._h, ms, launches, work, n))
+        return {p: {"ms": ms[i], "launches": launches[i], "work": work[i]}
+                for i, p in enumerate(_lib.PHASES)}
 
     def embed_ids(self, seqs: Sequence[Sequence[int]], Dim: Optional[int] = None,
                   precision: int = PREC_SPLIT_TF32) -> List[np.ndarray]:

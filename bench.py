@@ -1,0 +1,364 @@
+#!/usr/bin/env python
+"""Benchmark of the EmbeddingGemma encoder path on N B200s.
+
+Metric: EmbeddingGemma embeddings/s at 256×512 tokens.
+Workload: benchmark config 2 — the EmbeddingGemma-300m-shaped encoder with
+random-init weights (seed 0, bf16 widened to fp32) on a batch of 256
+sequences × 512 tokens, all full length, ids from seed 1. A step is one
+forward of that batch (ids → L2-normalised 768-d embeddings) on every GPU,
+plus the NCCL gather of the embeddings onto rank 0 when N > 1. Each GPU is
+an independent replica with its own 256×512 batch (weak scaling, no
+collective on the data path besides that gather).
+
+Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+(N > 1 under torchrun). Rank 0 prints one JSON line.
+
+--impl reference times the reference's CPU path on this host: the Go
+reference cannot be built here (no Go toolchain), so the CPU restatement
+in oracle/ (float32 arithmetic of the reference, all host threads) stands
+in for it on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "EmbeddingGemma embeddings/s at 256×512 tok, 1/2/4/8 B200; % TC/HBM roofline"
+UNIT = "embeddings/s"
+BATCH, SEQ = 256, 512
+CPU_SAMPLE_SEQS = 4  # sequences of 512 tokens per CPU-baseline step
+
+
+def model_work(cfg: dict, T: int):
+    """Algorithmic FLOPs of one sequence of T tokens (all valid)."""
+    H, F, D = cfg["hidden_size"], cfg["intermediate_size"], cfg["head_dim"]
+    Hq, Hkv, L = cfg["num_attention_heads"], cfg["num_key_value_heads"], cfg["num_hidden_layers"]
+    linear = 2 * (H * Hq * D + 2 * H * Hkv * D + Hq * D * H + 3 * H * F) * L * T
+    w = cfg["sliding_window"] // 2 + 1
+    i = np.arange(T)
+    local_pairs = int(np.sum(np.minimum(T - 1, i + w - 1) - np.maximum(0, i - w + 1) + 1)) if T > w else T * T
+    glob = sum(1 for l in range(L) if (l + 1) % 6 == 0)
+    attn = 4 * Hq * D * (glob * T * T + (L - glob) * local_pairs)
+    head = 2 * (768 * 3072 + 3072 * 768)
+    return linear, attn, head
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16": d["bf16_tflops"],
+                "bf16_sustained": d["bf16_tflops_sustained"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus):
+        self.gpus = gpus
+        self.lines = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", ",".join(str(g) for g in self.gpus)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, smax, power, reasons = [], [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+                power.append(float(f[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "power_w_max": max(power) if power else None,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def cpu_time_sample(cfg, w32, ids, lengths, threads):
+    from oracle import oracle as O
+
+    om = O.OracleModel(cfg, w32)
+    t0 = time.perf_counter()
+    om.embed_padded(ids, lengths, mode=O.F32, threads=threads)
+    return time.perf_counter() - t0
+
+
+def f32_weights(w):
+    from ai_b200.synthetic import bf16_to_f32
+
+    return {k: bf16_to_f32(v) for k, v in w.items()}
+
+
+def run_reference(args, rank, world, cfg):
+    """Reference arm: the CPU path on this host's cores (rank 0 only)."""
+    if rank != 0:
+        return
+    from ai_b200 import synthetic as S
+
+    threads = os.cpu_count() or 1
+    w = f32_weights(S.make_weights(cfg, seed=0))
+    ids = S.make_ids(CPU_SAMPLE_SEQS, SEQ, 1)
+    lengths = np.full(CPU_SAMPLE_SEQS, SEQ, np.int32)
+    for _ in range(args.warmup):
+        cpu_time_sample(cfg, w, ids, lengths, threads)
+    times = [cpu_time_sample(cfg, w, ids, lengths, threads) for _ in range(args.steps)]
+    per_step = sum(times) / len(times)
+    value = CPU_SAMPLE_SEQS / per_step
+    sample = (f"{CPU_SAMPLE_SEQS} sequences x {SEQ} tokens of config 2 per step "
+              f"(same weights and ids seed), oracle float32 mode = the reference's arithmetic")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: random-init weights seed 0 (bf16), ids seed 1",
+        "config": {"workload": "config 2: 256 x 512 tokens, all full length (CPU: bounded sample)",
+                   "seq_len": SEQ, "parallelism": "host threads"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "Go reference unbuildable here (no Go toolchain on this box or the GPU box); "
+                "timed CPU restatement of its float32 path",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank, local_rank, world, cfg):
+    import torch
+    import torch.distributed as dist
+
+    from ai_b200 import gemma
+    from ai_b200 import synthetic as S
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    prec = gemma.PREC_TF32 if args.precision == "tf32" else gemma.PREC_SPLIT_TF32
+    w = S.make_weights(cfg, seed=0)
+    model = gemma.from_synthetic(cfg, w, device=local_rank, max_batch_tokens=BATCH * SEQ)
+    dim = model.Dim()
+    ids_np = S.make_ids(BATCH, SEQ, 1 if rank == 0 else 1000 + rank)
+    len_np = np.full(BATCH, SEQ, np.int32)
+    d_ids = torch.from_numpy(ids_np).to(dev)
+    d_len = torch.from_numpy(len_np).to(dev)
+    out = torch.empty((BATCH, dim), dtype=torch.float32, device=dev)
+    gathered = [torch.empty_like(out) for _ in range(world)] if world > 1 else None
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        model.embed_device(d_ids, d_len, BATCH, SEQ, dim, out, stream, prec)
+        if world > 1:
+            dist.all_gather(gathered, out)
+
+    def sync_all():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+            torch.cuda.synchronize(dev)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    model.check()
+    model.read_profile()  # discard warm-up counts
+
+    # ---- device-timed value (inputs resident in HBM)
+    sampler = ClockSampler(list(range(world)) if rank == 0 else [])
+    sync_all()
+    if rank == 0:
+        sampler.start()
+        time.sleep(0.5)
+    model.set_profiling(True)
+    sync_all()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    sync_all()
+    ms = e0.elapsed_time(e1)
+    model.set_profiling(False)
+    prof = model.read_profile()
+    clocks = sampler.stop() if rank == 0 else None
+    model.check()
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    per_step_s = ms_max / 1e3 / args.steps
+    value = world * BATCH / per_step_s
+
+    # ---- end to end through the public host API (pinned host buffers)
+    ids_pin = torch.from_numpy(ids_np).pin_memory().numpy()
+    len_pin = torch.from_numpy(len_np).pin_memory().numpy()
+    out_pin = torch.empty((BATCH, dim), dtype=torch.float32).pin_memory().numpy()
+    host_res = torch.empty((BATCH, dim), dtype=torch.float32, device=dev)
+    g2 = [torch.empty_like(host_res) for _ in range(world)] if world > 1 else None
+
+    def e2e_step():
+        model.embed_padded(ids_pin, len_pin, dim, prec, out=out_pin)
+        if world > 1:
+            host_res.copy_(torch.from_numpy(out_pin), non_blocking=False)
+            dist.all_gather(g2, host_res)
+            if rank == 0:
+                torch.cat(g2).cpu()
+
+    e2e_step()
+    sync_all()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step()
+    sync_all()
+    e2e_s = time.perf_counter() - t0
+    te = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = world * BATCH * args.steps / float(te.item())
+
+    # ---- roofline of the dominant kernel family (the tcgen05 GEMM)
+    pk = peaks()
+    linear, attn, head = model_work(cfg, SEQ)
+    gemm_phases = ["gemm_qkv", "gemm_o", "gemm_gate_up", "gemm_down"]
+    gemm_ms = sum(prof[p]["ms"] for p in gemm_phases)
+    gemm_launches = sum(prof[p]["launches"] for p in gemm_phases)
+    gemm_flops = linear * BATCH * args.steps
+    tf32_peak = pk["bf16_sustained"] / 2.0
+    achieved = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else None
+    passes = 1 if prec == gemma.PREC_TF32 else 2
+    traffic = None
+    tp = ROOT / "profiles" / "gemm_traffic.json"
+    if tp.exists():
+        traffic = json.loads(tp.read_text()).get("bytes_per_launch")
+    roofline = {
+        "bound": "tensor", "kernel": "gemm_tf32_kernel (all encoder projections)",
+        "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s",
+        "frac": achieved / tf32_peak if achieved else None, "traffic": traffic,
+        "peak_source": f"{pk['source']} bf16 sustained {pk['bf16_sustained']} TFLOP/s / 2 "
+                       "(dense TF32 runs at half the bf16 rate)",
+        "issued_mma_passes": passes,
+        "issued_frac": (achieved * passes / tf32_peak) if achieved else None,
+        "launches": gemm_launches,
+    }
+    phases = {p: round(v["ms"] / args.steps, 3) for p, v in prof.items()}
+    attn_ms = prof["attention"]["ms"]
+    launches_total = sum(v["launches"] for v in prof.values())
+
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            threads = os.cpu_count() or 1
+            w32 = f32_weights(w)
+            ids_s = ids_np[:CPU_SAMPLE_SEQS]
+            secs = cpu_time_sample(cfg, w32, ids_s, len_np[:CPU_SAMPLE_SEQS], threads)
+            cpu = {"value": CPU_SAMPLE_SEQS / secs, "unit": UNIT, "cores": threads, "kind": "port",
+                   "sample": f"{CPU_SAMPLE_SEQS} sequences x {SEQ} tokens of config 2, oracle "
+                             "float32 mode (the reference's arithmetic), one pass"}
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic: random-init EmbeddingGemma-300m-shaped weights (seed 0, bf16 "
+                    "widened to fp32), ids uniform in [3, 262144) seed 1, BOS first",
+            "config": {"workload": "config 2: 256 sequences x 512 tokens per GPU, all full length",
+                       "global_batch": BATCH * world, "seq_len": SEQ,
+                       "parallelism": f"replicas x{world} + NCCL all-gather of embeddings" if world > 1 else "single GPU",
+                       "precision": args.precision,
+                       "l2_flush": "none: inputs larger than L2 (weights 1.2 GB, activations > 4 GB per step)"},
+            "tokens_per_s": value * SEQ,
+            "attention_tflops": (attn * BATCH * args.steps / (attn_ms / 1e3) / 1e12) if attn_ms else None,
+            "clocks": clocks,
+            "e2e": {"value": e2e_value, "unit": UNIT,
+                    "h2d_bytes_per_step": int(ids_np.nbytes + len_np.nbytes),
+                    "d2h_bytes_per_step": int(BATCH * dim * 4)},
+            "gpu_launches": int(launches_total),
+            "roofline": roofline,
+            "phases_ms_per_step": phases,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    model.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--precision", choices=["split_tf32", "tf32"], default="split_tf32")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=BATCH,
+                    help="sequences per GPU (default 256; smaller only for profiling runs)")
+    ap.add_argument("--seq", type=int, default=SEQ, help="tokens per sequence (default 512)")
+    args = ap.parse_args()
+    global BATCH, SEQ
+    BATCH, SEQ = args.batch, args.seq
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    if "WORLD_SIZE" not in os.environ and args.gpus != 1:
+        world = 1  # launched without torchrun: one process, one GPU
+    from ai_b200 import synthetic as S
+
+    cfg = dict(S.EMBEDDINGGEMMA_300M)
+    if args.impl == "reference":
+        run_reference(args, rank, world, cfg)
+    else:
+        run_ours(args, rank, local_rank, world, cfg)
+
+
+if __name__ == "__main__":
+    main()

@@ -156,6 +156,26 @@ int fg_model_check(fg_model* m);
 
 void fg_model_destroy(fg_model* m);
 
+/* Per-phase device timing of forwards, for measurement (no reference
+ * counterpart; the reference's bench prints wall times, cmd/bench).
+ * While enabled, every kernel launch of fg_embed_ids(_device) is bracketed
+ * by CUDA events on its stream. fg_model_read_profile synchronises, writes
+ * for each phase p < n the summed milliseconds, launches and algorithmic
+ * work (FLOPs for GEMM/attention phases, bytes for memory-bound phases),
+ * then clears the record. Launch counts are kept even when disabled. */
+#define FG_PHASE_EMBED 0
+#define FG_PHASE_GEMM_QKV 1
+#define FG_PHASE_QK_NORM_ROPE 2
+#define FG_PHASE_ATTENTION 3
+#define FG_PHASE_GEMM_O 4
+#define FG_PHASE_RESIDUAL 5
+#define FG_PHASE_GEMM_GATE_UP 6
+#define FG_PHASE_GEMM_DOWN 7
+#define FG_PHASE_POOL_HEAD 8
+#define FG_NUM_PHASES 9
+int fg_model_set_profiling(fg_model* m, int enable);
+int fg_model_read_profile(fg_model* m, double* ms, int64_t* launches, double* work, int n);
+
 /* ---- tensor operations (device pointers) ------------------------------- */
 /* out[m, n] = epilogue(x[m, k] · w) — tensor.MatMul (tensor/matmul.go:19)
  * and tensor.MatMulFused (tensor/matmul_fused.go:40). w is [k, n] row-major
