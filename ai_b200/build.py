@@ -24,6 +24,7 @@ SOURCES = [
     "fg_gemm.cu",
     "fg_elementwise.cu",
     "fg_attention.cu",
+    "fg_attn_tc.cu",
     "fg_ops.cu",
     "fg_model.cu",
 ]

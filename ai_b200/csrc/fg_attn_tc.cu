@@ -1,0 +1,596 @@
+// Flash attention on the tcgen05 tensor cores for head_dim 256, fp32 inputs
+// carried as split-bf16 operands.
+//
+// Replaces attentionFused / AttentionBlock (tensor/attention.go:130-287,
+// internal/blas/attention.go:61-136) on the encoder path. Every fp32
+// operand x is held as hi = bf16(x) and lo = bf16(x − hi) (x − hi − lo is
+// below 2^-17·|x|); each product accumulates hi·hi + hi·lo + lo·hi in FP32
+// TMEM, three kind::f16 MMAs — the cost of 1.5 TF32 passes, with products
+// good to ~2^-16 relative. (An fp32 Q tile of 128 rows × 256 is 128 KB per
+// part: a TF32 hi/lo pair does not fit shared memory beside the K/V ring,
+// the bf16 pair does.)
+//
+// One CTA per (query tile of 128 rows, query head, sequence), 6 warps:
+//   warp 0      TMA producer: Q (hi/lo, resident), then per key tile the K
+//               d-chunks and the Vᵀ (d-half × key-half) chunks through a
+//               3-stage ring of 32 KB, in the order the MMA warp uses them.
+//   warp 1      TMEM allocation (512 columns) and the MMA issuer:
+//               S_j = Q·K_jᵀ into one of two 128-column S buffers while the
+//               softmax warps work on S_{j−1}; then O += P_{j−1}·V_{j−1}
+//               with P read from TMEM (A operand), O in columns 256..511.
+//   warps 2..5  softmax, one query row per thread: visibility by index
+//               arithmetic (padding: j < len; sliding layers: |i−j| < window),
+//               running max with lazy rescaling (O is rescaled in TMEM only
+//               when the max grows by more than 2^8), P = exp2 written back
+//               over S as packed bf16 hi/lo; the final 1/Σ and the store.
+// Key tiles outside a query tile's window or past the sequence length are
+// never loaded. Masked keys get weight exactly 0, as the reference's
+// flushing exp gives them (internal/kernel/generic.go:283-291).
+#include <algorithm>
+#include <cfloat>
+#include <cudaTypedefs.h>
+
+#include "fg_internal.h"
+#include "fg_kernels.cuh"
+#include "fg_ptx.cuh"
+
+namespace fg {
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode_bf16 = nullptr;
+
+constexpr int kQ = 128;    // query rows per CTA
+constexpr int kKT = 128;   // keys per tile
+constexpr int kD = 256;    // head dimension
+constexpr int kStages = 3;
+constexpr uint32_t kChunk = 128 * 64 * 2;           // [128 rows × 64 bf16] = 16 KB
+constexpr uint32_t kQBytes = 2 * 4 * kChunk;        // Q hi/lo × 4 d-chunks = 128 KB
+constexpr uint32_t kStageBytes = 2 * kChunk;        // hi + lo chunk = 32 KB
+constexpr size_t kSmem = 1024 + kQBytes + kStages * kStageBytes + 256;
+constexpr int kThreads = 192;
+constexpr uint32_t kIdesc = idesc_bf16(128, 128);
+constexpr float kRescaleLog2 = 8.f;  // rescale O when the max grows by more than 2^8
+
+struct Params {
+  int B, T, S, Hq, Hkv;
+  int window;
+  float scale_log2;  // attention scale · log2(e)
+  const int32_t* qlen;  // rows computed per sequence (null: T); later rows are written as 0
+  const int32_t* klen;  // visible keys per sequence (null: S)
+  float* out;
+  float* out_lo;
+  int64_t osb, osh, ost;
+  int* err;
+};
+
+__device__ __forceinline__ bool waitb(uint32_t bar, uint32_t par, volatile int* ab, int* err, int code) {
+  return mbar_wait(bar, par, ab, err, code);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap mQ0, const __grid_constant__ CUtensorMap mQ1,
+                   const __grid_constant__ CUtensorMap mK0, const __grid_constant__ CUtensorMap mK1,
+                   const __grid_constant__ CUtensorMap mV0, const __grid_constant__ CUtensorMap mV1,
+                   const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                       // [part][chunk] 16 KB each
+  uint8_t* sRing = smem + kQBytes;          // [stage][part] 16 KB each
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sRing + kStages * kStageBytes);
+  // bars: 0 q_full | 1..3 kv_full | 4..6 kv_empty | 7,8 s_full | 9,10 p_full |
+  //       11,12 s_free | 13 o_prog | 14 o_final | 15 drain
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 16);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int hk = h / (p.Hq / p.Hkv);
+  const int i0 = qt * kQ;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qlen = p.qlen ? min(p.qlen[b], p.T) : p.T;
+  const int klen = p.klen ? max(0, min(p.klen[b], p.S)) : p.S;
+  float* obase = p.out + b * p.osb + h * p.osh;
+  float* olbase = p.out_lo ? p.out_lo + b * p.osb + h * p.osh : nullptr;
+  int kbeg = 0, kend = klen;
+  if (p.window > 0) {
+    kbeg = max(0, i0 - p.window + 1);
+    kend = min(klen, i0 + kQ - 1 + p.window);
+  }
+
+  if (i0 >= qlen || kend <= kbeg) {  // no row to compute or no visible key: zeros
+    for (int r = warp; r < kQ; r += kThreads / 32) {
+      const int i = i0 + r;
+      if (i >= p.T) break;
+      float* o = obase + i * p.ost;
+      float* ol = olbase ? olbase + i * p.ost : nullptr;
+      for (int c = lane; c < kD; c += 32) {
+        o[c] = 0.f;
+        if (ol) ol[c] = 0.f;
+      }
+    }
+    return;
+  }
+  const int kt0 = kbeg / kKT;
+  const int ntiles = (kend + kKT - 1) / kKT - kt0;
+
+  auto bar = [&](int k) { return smem_u32(&bars[k]); };
+  const uint32_t q_full = bar(0), s_full0 = bar(7), p_full0 = bar(9), s_free0 = bar(11);
+  const uint32_t o_prog = bar(13), o_final = bar(14), drain = bar(15);
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(bar(1 + s), 1);
+      mbar_init(bar(4 + s), 1);
+    }
+    for (int k = 0; k < 2; ++k) {
+      mbar_init(bar(7 + k), 1);
+      mbar_init(bar(9 + k), 128);
+      mbar_init(bar(11 + k), 1);
+    }
+    mbar_init(o_prog, 1);
+    mbar_init(o_final, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_holder), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const uint32_t tO = tmem + 256;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer
+      tma_prefetch_desc(&mQ0);
+      tma_prefetch_desc(&mK0);
+      tma_prefetch_desc(&mV0);
+      const int qrow = b * p.T + i0;
+      mbar_arrive_expect_tx(q_full, kQBytes);
+      for (int c = 0; c < 4; ++c) {
+        tma_load_2d(smem_u32(sQ + (0 * 4 + c) * kChunk), &mQ0, q_full, h * kD + c * 64, qrow);
+        tma_load_2d(smem_u32(sQ + (1 * 4 + c) * kChunk), &mQ1, q_full, h * kD + c * 64, qrow);
+      }
+      int armed[kStages] = {0, 0, 0};
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      auto next = [&](const CUtensorMap* m0, const CUtensorMap* m1, int x, int y) {
+        if (!waitb(bar(4 + stage), phase ^ 1, abort_flag, p.err, kDevTimeoutEmpty)) return false;
+        const uint32_t fb = bar(1 + stage);
+        mbar_arrive_expect_tx(fb, kStageBytes);
+        armed[stage]++;
+        uint8_t* dst = sRing + stage * kStageBytes;
+        tma_load_2d(smem_u32(dst), m0, fb, x, y);
+        tma_load_2d(smem_u32(dst + kChunk), m1, fb, x, y);
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1;
+        }
+        return true;
+      };
+      auto load_k = [&](int j) {
+        const int key0 = (kt0 + j) * kKT;
+        for (int c = 0; c < 4 && ok; ++c) ok = next(&mK0, &mK1, hk * kD + c * 64, b * p.S + key0);
+      };
+      auto load_v = [&](int j) {
+        const int key0 = (kt0 + j) * kKT;
+        const int vrow = (b * p.Hkv + hk) * kD;
+        for (int dh = 0; dh < 2 && ok; ++dh)
+          for (int kh = 0; kh < 2 && ok; ++kh) ok = next(&mV0, &mV1, key0 + kh * 64, vrow + dh * 128);
+      };
+      for (int j = 0; j < ntiles && ok; ++j) {
+        load_k(j);
+        if (j >= 1) load_v(j - 1);
+      }
+      if (ok) load_v(ntiles - 1);
+      if (*abort_flag) {
+        for (int s = 0; s < kStages; ++s) {
+          if (!armed[s]) continue;
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(bar(1 + s), uint32_t(armed[s] - 1) & 1u))
+            if (globaltimer_ns() - t0 > kWaitTimeoutNs) break;
+        }
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(q_full, 0))
+          if (globaltimer_ns() - t0 > kWaitTimeoutNs) break;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ MMA issuer
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = waitb(q_full, 0, abort_flag, p.err, kDevTimeoutFull);
+      bool issued = false;
+      tc_fence_after();
+      auto pv = [&](int jj) {
+        const int sb = jj & 1;
+        if (!waitb(bar(9 + sb), uint32_t(jj >> 1) & 1u, abort_flag, p.err, kDevTimeoutAccFull)) return false;
+        tc_fence_after();
+        const uint32_t tP = tmem + uint32_t(sb * 128);
+        for (int dh = 0; dh < 2; ++dh) {
+          for (int kh = 0; kh < 2; ++kh) {
+            if (!waitb(bar(1 + stage), phase, abort_flag, p.err, kDevTimeoutFull)) return false;
+            tc_fence_after();
+            const uint32_t v0 = smem_u32(sRing + stage * kStageBytes);
+            const uint32_t v1 = v0 + kChunk;
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint32_t col = uint32_t(kh * 32 + kk * 8);
+              const uint64_t b0 = sw128_kmajor_desc(v0 + kk * 32);
+              const uint64_t b1 = sw128_kmajor_desc(v1 + kk * 32);
+              const uint32_t d = tO + uint32_t(dh * 128);
+              const uint32_t first = (jj == 0 && kh == 0 && kk == 0) ? 0u : 1u;
+              mma_bf16_ts(d, tP + col, b0, kIdesc, first);        // p_hi · v_hi
+              mma_bf16_ts(d, tP + col, b1, kIdesc, 1u);           // p_hi · v_lo
+              mma_bf16_ts(d, tP + 64 + col, b0, kIdesc, 1u);      // p_lo · v_hi
+            }
+            mma_commit(bar(4 + stage));
+            if (++stage == kStages) {
+              stage = 0;
+              phase ^= 1;
+            }
+          }
+        }
+        mma_commit(bar(11 + sb));  // S/P buffer free
+        mma_commit(o_prog);
+        return true;
+      };
+      for (int j = 0; j < ntiles && ok; ++j) {
+        const int sb = j & 1;
+        if (j >= 2) {
+          if (!waitb(bar(11 + sb), uint32_t((j - 2) >> 1) & 1u, abort_flag, p.err, kDevTimeoutAccEmpty)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
+        const uint32_t tS = tmem + uint32_t(sb * 128);
+        for (int c = 0; c < 4 && ok; ++c) {
+          if (!waitb(bar(1 + stage), phase, abort_flag, p.err, kDevTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t k0 = smem_u32(sRing + stage * kStageBytes);
+          const uint32_t k1 = k0 + kChunk;
+          const uint32_t q0 = smem_u32(sQ + c * kChunk);
+          const uint32_t q1 = smem_u32(sQ + (4 + c) * kChunk);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t a0 = sw128_kmajor_desc(q0 + kk * 32);
+            const uint64_t a1 = sw128_kmajor_desc(q1 + kk * 32);
+            const uint64_t b0 = sw128_kmajor_desc(k0 + kk * 32);
+            const uint64_t b1 = sw128_kmajor_desc(k1 + kk * 32);
+            mma_bf16_ss(tS, a0, b0, kIdesc, (c | kk) != 0 ? 1u : 0u);  // q_hi · k_hi
+            mma_bf16_ss(tS, a0, b1, kIdesc, 1u);                       // q_hi · k_lo
+            mma_bf16_ss(tS, a1, b0, kIdesc, 1u);                       // q_lo · k_hi
+          }
+          issued = true;
+          mma_commit(bar(4 + stage));
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit(bar(7 + sb));
+        if (j >= 1 && !pv(j - 1)) {
+          ok = false;
+          break;
+        }
+      }
+      if (ok && pv(ntiles - 1)) mma_commit(o_final);
+      if (issued) {
+        mma_commit(drain);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(drain, 0))
+          if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+            atomicCAS(p.err, 0, kDevTimeoutDrain);
+            break;
+          }
+      }
+    }
+  } else {
+    // -------------------------------------------------------------- softmax
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const int i = i0 + r;
+    const uint32_t lane_off = uint32_t(quad * 32) << 16;
+    // visible keys of row i: [vlo, vhi)
+    int vlo = 0, vhi = klen;
+    if (p.window > 0) {
+      vlo = max(0, i - p.window + 1);
+      vhi = min(klen, i + p.window);
+    }
+    const float c = p.scale_log2;
+    float m = -FLT_MAX;
+    bool have = false;
+    float l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      const int sb = j & 1;
+      const int key0 = (kt0 + j) * kKT;
+      const bool got = waitb(bar(7 + sb), uint32_t(j >> 1) & 1u, abort_flag, p.err, kDevTimeoutAccFull);
+      if (!__all_sync(0xffffffffu, got)) {  // warp-uniform before the collective tcgen05.ld
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t tS = tmem + lane_off + uint32_t(sb * 128);
+      uint32_t sr[4][32];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) tmem_ld_32x32b_x32(tS + uint32_t(q * 32), sr[q]);
+      tmem_ld_wait();
+      const int lo_c = vlo - key0, hi_c = vhi - key0;  // visible columns [lo_c, hi_c)
+      float mt = -FLT_MAX;
+      bool any = false;
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int col = q * 32 + e;
+          if (col >= lo_c && col < hi_c) {
+            mt = fmaxf(mt, __uint_as_float(sr[q][e]));
+            any = true;
+          }
+        }
+      float factor = 1.f;
+      if (any) {
+        if (!have) {
+          m = mt;
+          have = true;
+        } else if ((mt - m) * c > kRescaleLog2) {
+          factor = ex2_approx((m - mt) * c);
+          m = mt;
+        }
+      }
+      // O rows rescale: the whole warp takes part if any lane needs it
+      const bool need = factor != 1.f;
+      if (__any_sync(0xffffffffu, need) && j > 0) {
+        const bool done = waitb(o_prog, uint32_t(j - 1) & 1u, abort_flag, p.err, kDevTimeoutAccFull);
+        if (!__all_sync(0xffffffffu, done)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll 1
+        for (int ch = 0; ch < 8; ++ch) {
+          uint32_t ov[32];
+          const uint32_t ta = tO + lane_off + uint32_t(ch * 32);
+          tmem_ld_32x32b_x32(ta, ov);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * factor);
+          tmem_st_32x32b_x32(ta, ov);
+        }
+        tmem_st_wait();
+      }
+      l *= factor;
+      const float mc = m * c;
+      // probabilities, split into packed bf16 hi / lo, written over S
+      float psum = 0.f;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint32_t hw[16], lw[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int col = q * 32 + 2 * e;
+          float a = 0.f, bb = 0.f;
+          if (have && col >= lo_c && col < hi_c) a = ex2_approx(fmaf(__uint_as_float(sr[q][2 * e]), c, -mc));
+          if (have && col + 1 >= lo_c && col + 1 < hi_c)
+            bb = ex2_approx(fmaf(__uint_as_float(sr[q][2 * e + 1]), c, -mc));
+          psum += a + bb;
+          const float ah = bf16_round_f32(a), bh = bf16_round_f32(bb);
+          hw[e] = pack_bf16x2(ah, bh);
+          lw[e] = pack_bf16x2(a - ah, bb - bh);
+        }
+        tmem_st_32x32b_x16(tS + uint32_t(q * 16), hw);
+        tmem_st_32x32b_x16(tS + uint32_t(64 + q * 16), lw);
+      }
+      l += psum;
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(bar(9 + sb));
+    }
+    // ---------------------------------------------------------- epilogue
+    const bool fin = ok && waitb(o_final, 0, abort_flag, p.err, kDevTimeoutAccFull);
+    if (__all_sync(0xffffffffu, fin)) {
+      tc_fence_after();
+      const bool row_ok = i < p.T;
+      const float inv = (i < qlen && l > 0.f) ? 1.f / l : 0.f;
+      float* o = obase + int64_t(i) * p.ost;
+      float* ol = olbase ? olbase + int64_t(i) * p.ost : nullptr;
+#pragma unroll 1
+      for (int ch = 0; ch < 8; ++ch) {
+        uint32_t ov[32];
+        tmem_ld_32x32b_x32(tO + lane_off + uint32_t(ch * 32), ov);
+        tmem_ld_wait();
+        if (row_ok) {
+          float4* o4 = reinterpret_cast<float4*>(o + ch * 32);
+          float4* l4 = ol ? reinterpret_cast<float4*>(ol + ch * 32) : nullptr;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            float4 v;
+            v.x = __uint_as_float(ov[4 * e]) * inv;
+            v.y = __uint_as_float(ov[4 * e + 1]) * inv;
+            v.z = __uint_as_float(ov[4 * e + 2]) * inv;
+            v.w = __uint_as_float(ov[4 * e + 3]) * inv;
+            o4[e] = v;
+            if (l4) l4[e] = make_float4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// Split of q or k (strided [B, H, T, D] element offsets b·sb + h·sh + t·st)
+// into token-major bf16 hi/lo [B·T, H·D]: one thread per 2 elements.
+__global__ void split_bf16_rows_kernel(const float* __restrict__ src, int64_t sb, int64_t sh,
+                                       int64_t st, int B, int T, int H,
+                                       __nv_bfloat16* __restrict__ hi,
+                                       __nv_bfloat16* __restrict__ lo) {
+  const int cols = H * kD;
+  const int64_t rows = int64_t(B) * T;
+  const int64_t total = rows * (cols / 2);
+  for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < total;
+       e += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = e / (cols / 2);
+    const int cc = int(e % (cols / 2)) * 2;
+    const int b = int(r / T), t = int(r % T), hd = cc / kD, d = cc % kD;
+    const float2 v = *reinterpret_cast<const float2*>(src + b * sb + hd * sh + t * st + d);
+    const __nv_bfloat16 h0 = __float2bfloat16_rn(v.x), h1 = __float2bfloat16_rn(v.y);
+    __nv_bfloat162 hh;
+    hh.x = h0;
+    hh.y = h1;
+    __nv_bfloat162 ll;
+    ll.x = __float2bfloat16_rn(v.x - __bfloat162float(h0));
+    ll.y = __float2bfloat16_rn(v.y - __bfloat162float(h1));
+    *reinterpret_cast<__nv_bfloat162*>(hi + r * cols + cc) = hh;
+    *reinterpret_cast<__nv_bfloat162*>(lo + r * cols + cc) = ll;
+  }
+}
+
+// V (strided, fp32) → Vᵀ bf16 hi/lo [B·Hkv·D rows, ldt keys], 32 keys ×
+// 32 dims per block through shared memory.
+__global__ void transpose_v_kernel(const float* __restrict__ v, int64_t sb, int64_t sh, int64_t st,
+                                   int B, int T, int Hkv, int D, __nv_bfloat16* __restrict__ hi,
+                                   __nv_bfloat16* __restrict__ lo, int64_t ldt) {
+  __shared__ float tile[32][33];
+  const int t0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
+  const int bh = blockIdx.z;  // b * Hkv + hk
+  const int b = bh / Hkv, hk = bh % Hkv;
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int t = t0 + r;
+    tile[r][threadIdx.x] = t < T ? v[b * sb + hk * sh + int64_t(t) * st + d0 + threadIdx.x] : 0.f;
+  }
+  __syncthreads();
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int d = d0 + r, t = t0 + threadIdx.x;
+    if (t < T) {
+      const float x = tile[threadIdx.x][r];
+      const __nv_bfloat16 h = __float2bfloat16_rn(x);
+      const int64_t off = (int64_t(bh) * D + d) * ldt + t;
+      hi[off] = h;
+      lo[off] = __float2bfloat16_rn(x - __bfloat162float(h));
+    }
+  }
+}
+
+int make_map_bf16(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int64_t ld_elems,
+                  int box_rows) {
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) != 0 || (ld_elems * 2) % 16 != 0)
+    return set_error(FG_EINVAL, "attention operand alignment");
+  cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(ld_elems) * 2};
+  cuuint32_t box[2] = {64u, cuuint32_t(box_rows)};
+  cuuint32_t es[2] = {1u, 1u};
+  CUresult r = g_encode_bf16(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides,
+                             box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(FG_ECUDA, "cuTensorMapEncodeTiled (bf16) failed (%d)", int(r));
+  return FG_OK;
+}
+
+}  // namespace
+
+size_t attn_tc_workspace_bytes(int B, int T, int S, int Hq, int Hkv) {
+  const int64_t ldt = (S + 7) / 8 * 8;
+  return size_t(B) * T * Hq * kD * 2 * 2 + size_t(B) * S * Hkv * kD * 2 * 2 +
+         size_t(B) * Hkv * kD * ldt * 2 * 2 + 8 * 256;
+}
+
+bool attn_tc_supported(const AttnArgs& a) {
+  const bool al = ((reinterpret_cast<uintptr_t>(a.q) | reinterpret_cast<uintptr_t>(a.k) |
+                    reinterpret_cast<uintptr_t>(a.v)) & 7) == 0 &&
+                  ((a.qsb | a.qsh | a.qst | a.ksb | a.ksh | a.kst) % 2) == 0;
+  const bool out_al = (reinterpret_cast<uintptr_t>(a.out) & 15) == 0 &&
+                      ((a.osb | a.osh | a.ost) % 4) == 0 &&
+                      (!a.out_lo || (reinterpret_cast<uintptr_t>(a.out_lo) & 15) == 0);
+  return a.D == kD && a.Hkv > 0 && a.Hq % a.Hkv == 0 && al && out_al && a.T > 0 && a.S > 0 &&
+         int64_t(a.B) * a.T < (int64_t(1) << 31) && int64_t(a.B) * a.S < (int64_t(1) << 31);
+}
+
+int attention_tc(const AttnArgs& a, void* ws, size_t ws_bytes, int* err, cudaStream_t s) {
+  if (!attn_tc_supported(a)) return set_error(FG_EINVAL, "tensor-core attention: unsupported shape or alignment");
+  const int B = a.B, T = a.T, S = a.S, Hq = a.Hq, Hkv = a.Hkv;
+  if (B == 0) return FG_OK;
+  if (ws_bytes < attn_tc_workspace_bytes(B, T, S, Hq, Hkv))
+    return set_error(FG_EINVAL, "attention workspace too small");
+  FG_TRY(tensor_map_encoder(&g_encode_bf16));
+  const int64_t ldt = (S + 7) / 8 * 8;
+  const int64_t MQ = int64_t(B) * T, MK = int64_t(B) * S;
+  auto align = [](uint8_t* q) { return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(q) + 255) & ~uintptr_t(255)); };
+  uint8_t* w = align(static_cast<uint8_t*>(ws));
+  __nv_bfloat16* q0 = reinterpret_cast<__nv_bfloat16*>(w);
+  w = align(w + size_t(MQ) * Hq * kD * 2);
+  __nv_bfloat16* q1 = reinterpret_cast<__nv_bfloat16*>(w);
+  w = align(w + size_t(MQ) * Hq * kD * 2);
+  __nv_bfloat16* k0 = reinterpret_cast<__nv_bfloat16*>(w);
+  w = align(w + size_t(MK) * Hkv * kD * 2);
+  __nv_bfloat16* k1 = reinterpret_cast<__nv_bfloat16*>(w);
+  w = align(w + size_t(MK) * Hkv * kD * 2);
+  __nv_bfloat16* v0 = reinterpret_cast<__nv_bfloat16*>(w);
+  w = align(w + size_t(B) * Hkv * kD * ldt * 2);
+  __nv_bfloat16* v1 = reinterpret_cast<__nv_bfloat16*>(w);
+  {
+    auto grid_of = [](int64_t n) { return int(std::min<int64_t>((n + 255) / 256, int64_t(sm_count()) * 16)); };
+    split_bf16_rows_kernel<<<grid_of(MQ * Hq * kD / 2), 256, 0, s>>>(a.q, a.qsb, a.qsh, a.qst, B, T, Hq, q0, q1);
+    split_bf16_rows_kernel<<<grid_of(MK * Hkv * kD / 2), 256, 0, s>>>(a.k, a.ksb, a.ksh, a.kst, B, S, Hkv, k0, k1);
+    dim3 tg(unsigned((S + 31) / 32), unsigned(kD / 32), unsigned(B * Hkv));
+    transpose_v_kernel<<<tg, dim3(32, 8), 0, s>>>(a.v, a.vsb, a.vsh, a.vst, B, S, Hkv, kD, v0, v1, ldt);
+    FG_CUDA_TRY(cudaGetLastError());
+  }
+  CUtensorMap mq0, mq1, mk0, mk1, mv0, mv1;
+  FG_TRY(make_map_bf16(&mq0, q0, MQ, Hq * kD, Hq * kD, 128));
+  FG_TRY(make_map_bf16(&mq1, q1, MQ, Hq * kD, Hq * kD, 128));
+  FG_TRY(make_map_bf16(&mk0, k0, MK, Hkv * kD, Hkv * kD, 128));
+  FG_TRY(make_map_bf16(&mk1, k1, MK, Hkv * kD, Hkv * kD, 128));
+  FG_TRY(make_map_bf16(&mv0, v0, int64_t(B) * Hkv * kD, S, ldt, 128));
+  FG_TRY(make_map_bf16(&mv1, v1, int64_t(B) * Hkv * kD, S, ldt, 128));
+  Params prm;
+  prm.B = B;
+  prm.T = T;
+  prm.S = S;
+  prm.Hq = Hq;
+  prm.Hkv = Hkv;
+  prm.window = a.window;
+  prm.scale_log2 = a.scale * 1.4426950408889634f;
+  prm.qlen = a.qlen;
+  prm.klen = a.klen;
+  prm.out = a.out;
+  prm.out_lo = a.out_lo;
+  prm.osb = a.osb;
+  prm.osh = a.osh;
+  prm.ost = a.ost;
+  prm.err = err;
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr[dev & 63]) {
+    FG_CUDA_TRY(cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmem)));
+    attr[dev & 63] = true;
+  }
+  if ((T + kQ - 1) / kQ > 65535 || B > 65535) return set_error(FG_EINVAL, "attention grid too large");
+  dim3 grid(unsigned((T + kQ - 1) / kQ), unsigned(Hq), unsigned(B));
+  attn_tc_kernel<<<grid, kThreads, kSmem, s>>>(mq0, mq1, mk0, mk1, mv0, mv1, prm);
+  FG_CUDA_TRY(cudaGetLastError());
+  return FG_OK;
+}
+
+}  // namespace fg

@@ -278,7 +278,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++local) {
       const int acc = local & 1;
       const uint32_t acc_par = uint32_t(local >> 1) & 1u;
-      if (!mbar_wait(accf_bar(acc), acc_par, abort_flag, p.err, kDevTimeoutAccFull)) break;
+      const bool got = mbar_wait(accf_bar(acc), acc_par, abort_flag, p.err, kDevTimeoutAccFull);
+      if (!__all_sync(0xffffffffu, got)) break;  // warp-uniform before the collective tcgen05.ld
       tc_fence_after();
       const int tm = tile / p.ntn, tn = tile % p.ntn;
       const int row = tm * kBM + rloc;
@@ -356,16 +357,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------- host side
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
-int get_encode() {
-  if (g_encode) return FG_OK;
-  void* fn = nullptr;
-  cudaDriverEntryPointQueryResult q;
-  cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
-  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr)
-    return set_error(FG_ECUDA, "cuTensorMapEncodeTiled entry point unavailable");
-  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-  return FG_OK;
-}
+int get_encode() { return tensor_map_encoder(&g_encode); }
 
 // Row-major [rows, cols] fp32 matrix, tiles of [box_rows × 32] with 128B swizzle.
 int make_map(CUtensorMap* m, const float* ptr, int64_t rows, int64_t cols, int64_t ld,

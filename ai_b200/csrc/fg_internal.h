@@ -4,6 +4,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <cstdarg>
@@ -42,6 +43,10 @@ int sm_count();
 // turns a recorded timeout into FG_ETIMEOUT, resetting the word.
 int device_error_word(int** out);
 int check_device_error_word();
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no
+// libcuda link dependency); resolved once.
+int tensor_map_encoder(PFN_cuTensorMapEncodeTiled_v12000* fn);
 
 // Internal activation code beyond the public FG_ACT_*: tanh (Dense head
 // layers with a Tanh activation, models/gemma/model.go:297-303).

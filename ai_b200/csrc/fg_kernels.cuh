@@ -77,6 +77,12 @@ struct AttnArgs {
   float scale;
 };
 int attention_simt(const AttnArgs& a, cudaStream_t s);
+
+// The same attention on the tcgen05 tensor cores (head_dim 256, split-bf16
+// operands); ws must hold attn_tc_workspace_bytes() for the shapes.
+size_t attn_tc_workspace_bytes(int B, int T, int S, int Hq, int Hkv);
+bool attn_tc_supported(const AttnArgs& a);
+int attention_tc(const AttnArgs& a, void* ws, size_t ws_bytes, int* err, cudaStream_t s);
 // Rewrites the rows that have no visible key with the reference's result for
 // them: the mean of the values of the keys hidden by the fewest −1e9 masks.
 int attention_masked_rows(const AttnArgs& a, cudaStream_t s);

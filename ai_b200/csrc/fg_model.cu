@@ -18,6 +18,7 @@
 //   att + att_lo, gu + gu_lo, tmp; rowscale [B·T].
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -127,6 +128,9 @@ struct fg_model {
         *head_b = nullptr, *head_b_lo = nullptr;
   int32_t* eff_len = nullptr;
   int* err = nullptr;
+  void* attn_ws = nullptr;  // split-bf16 operands of the tensor-core attention
+  size_t attn_ws_bytes = 0;
+  bool attn_simt = false;   // FG_ATTENTION=simt selects the SIMT kernel
   // host-API staging
   int32_t* d_ids = nullptr;
   int64_t d_ids_cap = 0;
@@ -511,8 +515,24 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
     a.window = (c.window > 0 && m->sliding[l]) ? c.window : 0;
     a.scale = c.attn_scale;
     {
-      PhaseScope ps(m, FG_PHASE_ATTENTION, s, 0.0);
-      FG_TRY(attention_simt(a, s));
+      const bool tc = !m->attn_simt && attn_tc_supported(a);
+      PhaseScope ps(m, FG_PHASE_ATTENTION, s, 0.0, tc ? 4 : 1);
+      if (tc) {
+        const size_t need = attn_tc_workspace_bytes(B, T, T, Hq, Hkv);
+        if (need > m->attn_ws_bytes) {
+          if (m->attn_ws) {
+            FG_CUDA_TRY(cudaStreamSynchronize(s));
+            FG_CUDA_TRY(cudaFree(m->attn_ws));
+            m->attn_ws = nullptr;
+            m->attn_ws_bytes = 0;
+          }
+          FG_CUDA_TRY(cudaMalloc(&m->attn_ws, need));
+          m->attn_ws_bytes = need;
+        }
+        FG_TRY(attention_tc(a, m->attn_ws, m->attn_ws_bytes, m->err, s));
+      } else {
+        FG_TRY(attention_simt(a, s));
+      }
     }
     // o0 = att · Wo   (embed.go:212-214)
     g = make_gemm(int(M), m->att, m->att_lo, attw, L.wo, split);
@@ -622,6 +642,8 @@ int fg_model_create(const fg_config* cfg, int device, fg_model** out) {
   m->rope_base.assign(c.rope_base, c.rope_base + c.num_layers);
   m->cfg.sliding = m->sliding.data();
   m->cfg.rope_base = m->rope_base.data();
+  const char* att = std::getenv("FG_ATTENTION");
+  m->attn_simt = att && std::string(att) == "simt";
   *out = m;
   return FG_OK;
 }
@@ -779,6 +801,7 @@ void fg_model_destroy(fg_model* m) {
     cudaEventDestroy(mk.b);
   }
   for (auto e : m->event_pool) cudaEventDestroy(e);
+  if (m->attn_ws) cudaFree(m->attn_ws);
   for (void* p : m->allocations) cudaFree(p);
   if (m->d_ids) cudaFree(m->d_ids);
   if (m->d_len) cudaFree(m->d_len);

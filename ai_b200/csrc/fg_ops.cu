@@ -2,6 +2,8 @@
 // pointers. Scratch space for operand splitting and packing is
 // stream-ordered (cudaMallocAsync / cudaFreeAsync on the caller's stream).
 #include <cmath>
+#include <cstdlib>
+#include <string>
 #include <vector>
 
 #include "fg_internal.h"
@@ -210,8 +212,19 @@ int fg_attention(const float* q, const float* k, const float* v, int B, int Hq, 
   a.qlen = nullptr;
   a.window = window;
   a.scale = scale;
-  FG_TRY(attention_simt(a, static_cast<cudaStream_t>(stream)));
-  return attention_masked_rows(a, static_cast<cudaStream_t>(stream));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const char* att = std::getenv("FG_ATTENTION");
+  if (!(att && std::string(att) == "simt") && attn_tc_supported(a)) {
+    int* err = nullptr;
+    FG_TRY(device_error_word(&err));
+    const size_t need = attn_tc_workspace_bytes(B, T, S, Hq, Hkv);
+    StreamScratch scratch(s);
+    FG_TRY(scratch.alloc(need));
+    FG_TRY(attention_tc(a, scratch.p, need, err, s));
+  } else {
+    FG_TRY(attention_simt(a, s));
+  }
+  return attention_masked_rows(a, s);
 }
 
 }  // extern "C"

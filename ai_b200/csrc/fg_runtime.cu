@@ -72,6 +72,22 @@ int check_device_error_word() {
   return FG_OK;
 }
 
+int tensor_map_encoder(PFN_cuTensorMapEncodeTiled_v12000* fn) {
+  static PFN_cuTensorMapEncodeTiled_v12000 cached = nullptr;
+  if (!cached) {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || f == nullptr) {
+      cudaGetLastError();
+      return set_error(FG_ECUDA, "cuTensorMapEncodeTiled entry point unavailable");
+    }
+    cached = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }
+  *fn = cached;
+  return FG_OK;
+}
+
 }  // namespace fg
 
 extern "C" {

@@ -344,8 +344,7 @@ def main():
                     help="sequences per GPU (default 256; smaller only for profiling runs)")
     ap.add_argument("--seq", type=int, default=SEQ, help="tokens per sequence (default 512)")
     args = ap.parse_args()
-    global BATCH, SEQ
-    BATCH, SEQ = args.batch, args.seq
+    globals().update(BATCH=args.batch, SEQ=args.seq)
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))

@@ -208,3 +208,55 @@ def test_rope_known_answers(cuda):
     r = T.RoPE(_t(y, cuda), 1e6, [0, 5, 9, 100, 500, 1000, 3, 7]).cpu().numpy()
     xn, yn = (y.astype(np.float64) ** 2).sum(-1), (r.astype(np.float64) ** 2).sum(-1)
     assert np.all(np.abs(xn - yn) <= 1e-3 * (xn + 1))
+
+
+@pytest.mark.parametrize("T,window,lens", [(2048, 0, [2048]), (2048, 257, [2048]),
+                                           (1000, 257, [1000, 700]), (129, 0, [129, 1])])
+def test_attention_tensor_core_long(cuda, T, window, lens):
+    """head_dim 256 runs on the tcgen05 kernel: long global and windowed rows."""
+    from ai_b200 import tensor as TT
+    import torch
+
+    rng = np.random.default_rng(T + window)
+    B = len(lens)
+    q = rng.standard_normal((B, 3, T, 256), dtype=np.float32)
+    k = rng.standard_normal((B, 1, T, 256), dtype=np.float32)
+    v = rng.standard_normal((B, 1, T, 256), dtype=np.float32)
+    lens = np.array(lens, np.int32)
+    want = _naive_attention(q, k, v, lens, window, 1 / 16)
+    got = TT.AttentionScaled(_t(q, cuda), _t(k, cuda), _t(v, cuda), torch.from_numpy(lens),
+                             window, 1 / 16).cpu().numpy()
+    err = np.abs(got - want).max()
+    print(f"\ntc attention T={T} window={window}: max err {err:.3e}")
+    assert err <= 1e-4
+
+
+def test_attention_running_max_rescale(cuda):
+    """Scores that grow by far more than 2^8 from one key tile to the next
+    exercise the O rescaling in tensor memory."""
+    from ai_b200 import tensor as TT
+
+    T = 640
+    rng = np.random.default_rng(2)
+    q = (np.ones((1, 1, T, 256)) * 0.5 + 0.01 * rng.standard_normal((1, 1, T, 256))).astype(np.float32)
+    ramp = np.linspace(0.0, 3.0, T)[None, None, :, None]
+    k = (ramp * (1 + 0.01 * rng.standard_normal((1, 1, T, 256)))).astype(np.float32)
+    v = rng.standard_normal((1, 1, T, 256), dtype=np.float32)
+    want = _naive_attention(q, k, v, None, 0, 1 / 16)
+    got = TT.AttentionScaled(_t(q, cuda), _t(k, cuda), _t(v, cuda), None, 0, 1 / 16).cpu().numpy()
+    assert np.abs(got - want).max() <= 1e-4, np.abs(got - want).max()
+
+
+def test_attention_tensor_core_matches_simt(cuda, monkeypatch):
+    from ai_b200 import tensor as TT
+    import torch
+
+    rng = np.random.default_rng(9)
+    q = rng.standard_normal((2, 3, 300, 256), dtype=np.float32)
+    k = rng.standard_normal((2, 1, 300, 256), dtype=np.float32)
+    v = rng.standard_normal((2, 1, 300, 256), dtype=np.float32)
+    lens = torch.tensor([300, 123], dtype=torch.int32)
+    tc = TT.AttentionScaled(_t(q, cuda), _t(k, cuda), _t(v, cuda), lens, 257, 1 / 16).cpu().numpy()
+    monkeypatch.setenv("FG_ATTENTION", "simt")
+    simt = TT.AttentionScaled(_t(q, cuda), _t(k, cuda), _t(v, cuda), lens, 257, 1 / 16).cpu().numpy()
+    assert np.abs(tc - simt).max() <= 1e-4
