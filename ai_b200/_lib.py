@@ -101,6 +101,8 @@ SIGNATURES = {
                                         C.POINTER(C.c_double), C.c_int]),
     "fg_matmul": (C.c_int, [_i64, _i64, _i64, _vp, _i64, _vp, _i64, C.c_int, _vp, _i64,
                             C.POINTER(Epilogue), C.c_int, _vp]),
+    "fg_matmul_noalloc": (C.c_int, [_i64, _i64, _i64, _vp, _i64, _vp, _i64, C.c_int, _vp, _i64,
+                                    C.POINTER(Epilogue), C.c_int, _vp]),
     "fg_row_sum_squares": (C.c_int, [_vp, _i64, _i64, _i64, _vp, _vp]),
     "fg_rmsnorm": (C.c_int, [_vp, _i64, _i64, _vp, C.c_float, _vp, _vp]),
     "fg_rope": (C.c_int, [_vp, _i64, C.c_int, C.c_int, C.c_double, _vp, _vp, _vp]),

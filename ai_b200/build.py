@@ -27,6 +27,7 @@ SOURCES = [
     "fg_attn_tc.cu",
     "fg_ops.cu",
     "fg_model.cu",
+    "fg_noalloc.cu",
 ]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -187,6 +187,25 @@ int fg_matmul(int64_t m, int64_t n, int64_t k, const float* x, int64_t ldx, cons
               int64_t ldw, int w_transposed, float* out, int64_t ldo, const fg_epilogue* epi,
               int precision, void* stream);
 
+/* fg_matmul for callers that cannot allocate device memory during a call:
+ * a host whose own allocator has reserved the GPU's memory up front (a
+ * cudaMalloc from inside the library would fail or fragment that pool), or
+ * a latency-critical path that cannot take the implicit synchronisation of
+ * cudaMalloc/cudaFree. No counterpart in the reference (its Go code
+ * allocates host memory freely). Same arguments and results as fg_matmul;
+ * the splitting/packing scratch lives in a fixed 32 MiB device array owned
+ * by the library (held by every GPU that loads it, until exit), so calls
+ * whose scratch would exceed 32 MiB — 4·(2·m·k' + 3·n·k') bytes in the worst
+ * case, k' = k rounded up to 4 — are refused with FG_EINVAL. The first call
+ * on a device looks up the array's device address (cudaGetSymbolAddress)
+ * and should come before any stream capture. All calls share the array:
+ * calls that overlap on the GPU race on it and must be serialised by the
+ * caller. Allocates nothing: no cudaMalloc, cudaFree or allocating library
+ * routine. */
+int fg_matmul_noalloc(int64_t m, int64_t n, int64_t k, const float* x, int64_t ldx,
+                      const float* w, int64_t ldw, int w_transposed, float* out, int64_t ldo,
+                      const fg_epilogue* epi, int precision, void* stream);
+
 /* out[r] = Σ_c x[r, c]² — (*Tensor).RowSumSquares (tensor/matmul_fused.go:125-143). */
 int fg_row_sum_squares(const float* x, int64_t rows, int64_t n, int64_t ldx, float* out,
                        void* stream);
