@@ -526,43 +526,40 @@ bool attn_tc_supported(const AttnArgs& a) {
          int64_t(a.B) * a.T < (int64_t(1) << 31) && int64_t(a.B) * a.S < (int64_t(1) << 31);
 }
 
-int attention_tc(const AttnArgs& a, void* ws, size_t ws_bytes, int* err, cudaStream_t s) {
-  if (!attn_tc_supported(a)) return set_error(FG_EINVAL, "tensor-core attention: unsupported shape or alignment");
-  const int B = a.B, T = a.T, S = a.S, Hq = a.Hq, Hkv = a.Hkv;
-  if (B == 0) return FG_OK;
-  if (ws_bytes < attn_tc_workspace_bytes(B, T, S, Hq, Hkv))
-    return set_error(FG_EINVAL, "attention workspace too small");
-  FG_TRY(tensor_map_encoder(&g_encode_bf16));
+int attn_tc_carve(void* ws, int B, int T, int S, int Hq, int Hkv, AttnOperands* o) {
   const int64_t ldt = (S + 7) / 8 * 8;
   const int64_t MQ = int64_t(B) * T, MK = int64_t(B) * S;
   auto align = [](uint8_t* q) { return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(q) + 255) & ~uintptr_t(255)); };
   uint8_t* w = align(static_cast<uint8_t*>(ws));
-  __nv_bfloat16* q0 = reinterpret_cast<__nv_bfloat16*>(w);
+  o->q_hi = w;
   w = align(w + size_t(MQ) * Hq * kD * 2);
-  __nv_bfloat16* q1 = reinterpret_cast<__nv_bfloat16*>(w);
+  o->q_lo = w;
   w = align(w + size_t(MQ) * Hq * kD * 2);
-  __nv_bfloat16* k0 = reinterpret_cast<__nv_bfloat16*>(w);
+  o->k_hi = w;
   w = align(w + size_t(MK) * Hkv * kD * 2);
-  __nv_bfloat16* k1 = reinterpret_cast<__nv_bfloat16*>(w);
+  o->k_lo = w;
   w = align(w + size_t(MK) * Hkv * kD * 2);
-  __nv_bfloat16* v0 = reinterpret_cast<__nv_bfloat16*>(w);
+  o->vt_hi = w;
   w = align(w + size_t(B) * Hkv * kD * ldt * 2);
-  __nv_bfloat16* v1 = reinterpret_cast<__nv_bfloat16*>(w);
-  {
-    auto grid_of = [](int64_t n) { return int(std::min<int64_t>((n + 255) / 256, int64_t(sm_count()) * 16)); };
-    split_bf16_rows_kernel<<<grid_of(MQ * Hq * kD / 2), 256, 0, s>>>(a.q, a.qsb, a.qsh, a.qst, B, T, Hq, q0, q1);
-    split_bf16_rows_kernel<<<grid_of(MK * Hkv * kD / 2), 256, 0, s>>>(a.k, a.ksb, a.ksh, a.kst, B, S, Hkv, k0, k1);
-    dim3 tg(unsigned((S + 31) / 32), unsigned(kD / 32), unsigned(B * Hkv));
-    transpose_v_kernel<<<tg, dim3(32, 8), 0, s>>>(a.v, a.vsb, a.vsh, a.vst, B, S, Hkv, kD, v0, v1, ldt);
-    FG_CUDA_TRY(cudaGetLastError());
-  }
+  o->vt_lo = w;
+  o->ldt = ldt;
+  return FG_OK;
+}
+
+int attention_tc_operands(const AttnArgs& a, const AttnOperands& o, int* err, cudaStream_t s) {
+  const int B = a.B, T = a.T, S = a.S, Hq = a.Hq, Hkv = a.Hkv;
+  if (B == 0) return FG_OK;
+  if (a.D != kD || Hkv <= 0 || Hq % Hkv != 0 || T <= 0 || S <= 0)
+    return set_error(FG_EINVAL, "tensor-core attention: unsupported shape");
+  FG_TRY(tensor_map_encoder(&g_encode_bf16));
+  const int64_t MQ = int64_t(B) * T, MK = int64_t(B) * S;
   CUtensorMap mq0, mq1, mk0, mk1, mv0, mv1;
-  FG_TRY(make_map_bf16(&mq0, q0, MQ, Hq * kD, Hq * kD, 128));
-  FG_TRY(make_map_bf16(&mq1, q1, MQ, Hq * kD, Hq * kD, 128));
-  FG_TRY(make_map_bf16(&mk0, k0, MK, Hkv * kD, Hkv * kD, 128));
-  FG_TRY(make_map_bf16(&mk1, k1, MK, Hkv * kD, Hkv * kD, 128));
-  FG_TRY(make_map_bf16(&mv0, v0, int64_t(B) * Hkv * kD, S, ldt, 128));
-  FG_TRY(make_map_bf16(&mv1, v1, int64_t(B) * Hkv * kD, S, ldt, 128));
+  FG_TRY(make_map_bf16(&mq0, o.q_hi, MQ, Hq * kD, Hq * kD, 128));
+  FG_TRY(make_map_bf16(&mq1, o.q_lo, MQ, Hq * kD, Hq * kD, 128));
+  FG_TRY(make_map_bf16(&mk0, o.k_hi, MK, Hkv * kD, Hkv * kD, 128));
+  FG_TRY(make_map_bf16(&mk1, o.k_lo, MK, Hkv * kD, Hkv * kD, 128));
+  FG_TRY(make_map_bf16(&mv0, o.vt_hi, int64_t(B) * Hkv * kD, S, o.ldt, 128));
+  FG_TRY(make_map_bf16(&mv1, o.vt_lo, int64_t(B) * Hkv * kD, S, o.ldt, 128));
   Params prm;
   prm.B = B;
   prm.T = T;
@@ -591,6 +588,25 @@ int attention_tc(const AttnArgs& a, void* ws, size_t ws_bytes, int* err, cudaStr
   attn_tc_kernel<<<grid, kThreads, kSmem, s>>>(mq0, mq1, mk0, mk1, mv0, mv1, prm);
   FG_CUDA_TRY(cudaGetLastError());
   return FG_OK;
+}
+
+int attention_tc(const AttnArgs& a, void* ws, size_t ws_bytes, int* err, cudaStream_t s) {
+  if (!attn_tc_supported(a)) return set_error(FG_EINVAL, "tensor-core attention: unsupported shape or alignment");
+  const int B = a.B, T = a.T, S = a.S, Hq = a.Hq, Hkv = a.Hkv;
+  if (B == 0) return FG_OK;
+  if (ws_bytes < attn_tc_workspace_bytes(B, T, S, Hq, Hkv))
+    return set_error(FG_EINVAL, "attention workspace too small");
+  AttnOperands o;
+  FG_TRY(attn_tc_carve(ws, B, T, S, Hq, Hkv, &o));
+  const int64_t MQ = int64_t(B) * T, MK = int64_t(B) * S;
+  auto bf = [](void* p) { return static_cast<__nv_bfloat16*>(p); };
+  auto grid_of = [](int64_t n) { return int(std::min<int64_t>((n + 255) / 256, int64_t(sm_count()) * 16)); };
+  split_bf16_rows_kernel<<<grid_of(MQ * Hq * kD / 2), 256, 0, s>>>(a.q, a.qsb, a.qsh, a.qst, B, T, Hq, bf(o.q_hi), bf(o.q_lo));
+  split_bf16_rows_kernel<<<grid_of(MK * Hkv * kD / 2), 256, 0, s>>>(a.k, a.ksb, a.ksh, a.kst, B, S, Hkv, bf(o.k_hi), bf(o.k_lo));
+  dim3 tg(unsigned((S + 31) / 32), unsigned(kD / 32), unsigned(B * Hkv));
+  transpose_v_kernel<<<tg, dim3(32, 8), 0, s>>>(a.v, a.vsb, a.vsh, a.vst, B, S, Hkv, kD, bf(o.vt_hi), bf(o.vt_lo), o.ldt);
+  FG_CUDA_TRY(cudaGetLastError());
+  return attention_tc_operands(a, o, err, s);
 }
 
 }  // namespace fg

@@ -19,6 +19,7 @@
 // an operand whose low part is identically zero (bf16-exact weights) has
 // no low pass, which changes nothing in the result.
 #include <algorithm>
+#include <cstdlib>
 #include <cudaTypedefs.h>
 
 #include "fg_internal.h"
@@ -29,7 +30,6 @@ namespace fg {
 namespace {
 
 constexpr int kBM = 128;
-constexpr int kBK = 32;  // fp32 per 128-byte swizzle row
 constexpr int kUmmaK = 8;
 constexpr int kThreads = 192;
 constexpr int kSmemLimit = 232448;  // 227 KB opt-in dynamic shared memory
@@ -41,16 +41,21 @@ struct KParams {
   int* err;
 };
 
-template <int BN, bool SA, bool SB>
+// BK fp32 of K per pipeline stage: 32 (128-byte swizzled rows) or 16
+// (64-byte rows: half the bytes per stage, so more stages in flight).
+template <int BN, bool SA, bool SB, int BK>
 struct Cfg {
-  static constexpr uint32_t kABytes = kBM * kBK * 4;
-  static constexpr uint32_t kBBytes = BN * kBK * 4;
+  static constexpr int kSwizzle = BK * 4;
+  static constexpr uint32_t kABytes = kBM * BK * 4;
+  static constexpr uint32_t kBBytes = BN * BK * 4;
   static constexpr uint32_t kStageBytes = kABytes * (SA ? 2 : 1) + kBBytes * (SB ? 2 : 1);
   static constexpr int kStagesRaw = (kSmemLimit - 2048) / kStageBytes;
-  static constexpr int kStages = kStagesRaw > 6 ? 6 : kStagesRaw;
+  static constexpr int kMaxStages = BK == 16 ? 8 : 6;
+  static constexpr int kStages = kStagesRaw > kMaxStages ? kMaxStages : kStagesRaw;
   static constexpr uint32_t kTmemCols = 2 * BN;
   static constexpr size_t kSmemBytes = 1024 + size_t(kStages) * kStageBytes + 256;
   static_assert(kStages >= 2, "tile too large for shared memory");
+  static_assert(BK == 16 || BK == 32, "stage depth");
 };
 
 // Eigen's rational tanh for float (the method the reference's kernels use,
@@ -112,13 +117,116 @@ __device__ __forceinline__ void store_row32(float* dst, const float (&v)[32], in
   }
 }
 
-template <int BN, bool SA, bool SB>
+__device__ __forceinline__ void store_bf16_split(__nv_bfloat16* hi, __nv_bfloat16* lo, int64_t off,
+                                                 float y) {
+  const __nv_bfloat16 h = __float2bfloat16_rn(y);
+  hi[off] = h;
+  lo[off] = __float2bfloat16_rn(y - __bfloat162float(h));
+}
+
+// Epilogue of the QKV projection when it feeds the tensor-core attention:
+// the accumulator tile is one head (256 columns). q/k heads: y = rs·acc,
+// per-head RMSNorm with gain (attention.go:312-337: v·inv·g, inv from the
+// float32 mean and a float64 root), rotate-half RoPE at slot t = row % T
+// (rope.go:66-87), then bf16 hi/lo parts, token-major. v heads: rs·acc as
+// bf16 hi/lo written transposed per sequence (vt[(b·Hkv+hk)·256 + d][t]).
+// tcgen05.ld is warp-collective, so every lane loads even for rows ≥ M.
+__device__ __forceinline__ void qkv_attn_epilogue(const GemmEpilogue& e, uint32_t taddr, int tn,
+                                                  int row, bool row_ok, float rs) {
+  constexpr int D = 256, H2 = 128;
+  if (tn < e.Hq + e.Hkv) {
+    const bool is_q = tn < e.Hq;
+    const float* g = is_q ? e.qgain : e.kgain;
+    // pass 1: Σ y² over the head
+    float ss = 0.f;
+#pragma unroll 1
+    for (int c0 = 0; c0 < D; c0 += 32) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(taddr + uint32_t(c0), r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float y = __fmul_rn(__uint_as_float(r[j]), rs);
+        ss = __fadd_rn(ss, __fmul_rn(y, y));
+      }
+    }
+    const float m = __fadd_rn(__fdiv_rn(ss, float(D)), e.eps);
+    const float inv = float(1.0 / sqrt(double(m)));
+    const int t = row % e.T;
+    const float* cs = e.rope_cos + int64_t(t) * H2;
+    const float* sn = e.rope_sin + int64_t(t) * H2;
+    __nv_bfloat16* hi = static_cast<__nv_bfloat16*>(is_q ? e.q_hi : e.k_hi);
+    __nv_bfloat16* lo = static_cast<__nv_bfloat16*>(is_q ? e.q_lo : e.k_lo);
+    const int width = (is_q ? e.Hq : e.Hkv) * D;
+    const int head = is_q ? tn : tn - e.Hq;
+    const int64_t base = int64_t(row) * width + int64_t(head) * D;
+    // pass 2: normalise, rotate the pairs (i, i + 128), split, store
+#pragma unroll 1
+    for (int c0 = 0; c0 < H2; c0 += 32) {
+      uint32_t ra[32], rb[32];
+      tmem_ld_32x32b_x32(taddr + uint32_t(c0), ra);
+      tmem_ld_32x32b_x32(taddr + uint32_t(H2 + c0), rb);
+      tmem_ld_wait();
+      if (row_ok) {
+#pragma unroll
+        for (int j0 = 0; j0 < 32; j0 += 8) {
+          uint32_t h1[4], l1[4], h2[4], l2[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            float y1[2], y2[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int j = j0 + 2 * q + u, i = c0 + j;
+              const float x1 = __fmul_rn(__fmul_rn(__fmul_rn(__uint_as_float(ra[j]), rs), inv), g[i]);
+              const float x2 = __fmul_rn(__fmul_rn(__fmul_rn(__uint_as_float(rb[j]), rs), inv), g[i + H2]);
+              const float c = cs[i], s = sn[i];
+              y1[u] = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+              y2[u] = __fadd_rn(__fmul_rn(x1, s), __fmul_rn(x2, c));
+            }
+            const float a0 = bf16_round_f32(y1[0]), a1 = bf16_round_f32(y1[1]);
+            const float b0 = bf16_round_f32(y2[0]), b1 = bf16_round_f32(y2[1]);
+            h1[q] = pack_bf16x2(a0, a1);
+            l1[q] = pack_bf16x2(y1[0] - a0, y1[1] - a1);
+            h2[q] = pack_bf16x2(b0, b1);
+            l2[q] = pack_bf16x2(y2[0] - b0, y2[1] - b1);
+          }
+          const int64_t o1 = base + c0 + j0, o2 = o1 + H2;
+          *reinterpret_cast<uint4*>(hi + o1) = make_uint4(h1[0], h1[1], h1[2], h1[3]);
+          *reinterpret_cast<uint4*>(lo + o1) = make_uint4(l1[0], l1[1], l1[2], l1[3]);
+          *reinterpret_cast<uint4*>(hi + o2) = make_uint4(h2[0], h2[1], h2[2], h2[3]);
+          *reinterpret_cast<uint4*>(lo + o2) = make_uint4(l2[0], l2[1], l2[2], l2[3]);
+        }
+      }
+    }
+  } else {
+    const int hk = tn - e.Hq - e.Hkv;
+    const int b = row / e.T, t = row % e.T;
+    __nv_bfloat16* hi = static_cast<__nv_bfloat16*>(e.vt_hi);
+    __nv_bfloat16* lo = static_cast<__nv_bfloat16*>(e.vt_lo);
+    const int64_t base = (int64_t(b) * e.Hkv + hk) * D * e.ldt + t;
+#pragma unroll 1
+    for (int c0 = 0; c0 < D; c0 += 32) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(taddr + uint32_t(c0), r);
+      tmem_ld_wait();
+      if (row_ok) {
+#pragma unroll 8
+        for (int j = 0; j < 32; ++j)
+          store_bf16_split(hi, lo, base + int64_t(c0 + j) * e.ldt,
+                           __fmul_rn(__uint_as_float(r[j]), rs));
+      }
+    }
+  }
+}
+
+template <int BN, bool SA, bool SB, int BK>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mAlo,
                      const __grid_constant__ CUtensorMap mB, const __grid_constant__ CUtensorMap mBlo,
                      const KParams p) {
-  using C = Cfg<BN, SA, SB>;
+  using C = Cfg<BN, SA, SB, BK>;
   constexpr int S = C::kStages;
+  constexpr int kSw = C::kSwizzle;
   constexpr uint32_t kIdesc = idesc_tf32(kBM, BN);
 
   extern __shared__ uint8_t smem_raw[];
@@ -182,15 +290,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_expect_tx(fb, C::kStageBytes);
           armed[stage]++;
           uint32_t dst = smem_u32(smem + size_t(stage) * C::kStageBytes);
-          tma_load_2d(dst, &mA, fb, kb * kBK, tm * kBM);
+          tma_load_2d(dst, &mA, fb, kb * BK, tm * kBM);
           dst += C::kABytes;
           if (SA) {
-            tma_load_2d(dst, &mAlo, fb, kb * kBK, tm * kBM);
+            tma_load_2d(dst, &mAlo, fb, kb * BK, tm * kBM);
             dst += C::kABytes;
           }
-          tma_load_2d(dst, &mB, fb, kb * kBK, tn * BN);
+          tma_load_2d(dst, &mB, fb, kb * BK, tn * BN);
           dst += C::kBBytes;
-          if (SB) tma_load_2d(dst, &mBlo, fb, kb * kBK, tn * BN);
+          if (SB) tma_load_2d(dst, &mBlo, fb, kb * BK, tn * BN);
           if (++stage == S) {
             stage = 0;
             phase ^= 1;
@@ -237,13 +345,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t b_addr = a_addr + C::kABytes * (SA ? 2 : 1);
           const uint32_t blo_addr = b_addr + C::kBBytes;
 #pragma unroll
-          for (int k = 0; k < kBK / kUmmaK; ++k) {
+          for (int k = 0; k < BK / kUmmaK; ++k) {
             const uint32_t koff = uint32_t(k * kUmmaK * 4);
-            const uint64_t da = sw128_kmajor_desc(a_addr + koff);
-            const uint64_t db = sw128_kmajor_desc(b_addr + koff);
+            const uint64_t da = kmajor_desc<kSw>(a_addr + koff);
+            const uint64_t db = kmajor_desc<kSw>(b_addr + koff);
             mma_tf32(d_tmem, da, db, kIdesc, (kb | k) != 0 ? 1u : 0u);
-            if (SB) mma_tf32(d_tmem, da, sw128_kmajor_desc(blo_addr + koff), kIdesc, 1u);
-            if (SA) mma_tf32(d_tmem, sw128_kmajor_desc(alo_addr + koff), db, kIdesc, 1u);
+            if (SB) mma_tf32(d_tmem, da, kmajor_desc<kSw>(blo_addr + koff), kIdesc, 1u);
+            if (SA) mma_tf32(d_tmem, kmajor_desc<kSw>(alo_addr + koff), db, kIdesc, 1u);
           }
           issued = true;
           mma_commit(empty_bar(stage));
@@ -286,7 +394,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool row_ok = row < p.M;
       const float rs = (e.rowscale && row_ok) ? e.rowscale[row] : 1.f;
       const uint32_t taddr = tmem_base + (uint32_t(quad * 32) << 16) + uint32_t(acc * BN);
-      if (e.geglu) {
+      if (BN == 256 && e.qkv_attn) {
+        qkv_attn_epilogue(e, taddr, tn, row, row_ok, rs);
+      } else if (e.geglu) {
         // Tile columns [0, BN/2) are gate, [BN/2, BN) the matching up columns.
 #pragma unroll 1
         for (int c0 = 0; c0 < BN / 2; c0 += 32) {
@@ -359,32 +469,34 @@ PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
 int get_encode() { return tensor_map_encoder(&g_encode); }
 
-// Row-major [rows, cols] fp32 matrix, tiles of [box_rows × 32] with 128B swizzle.
+// Row-major [rows, cols] fp32 matrix, tiles of [box_rows × bk] whose rows of
+// bk·4 bytes are swizzled to match the MMA descriptors (128 or 64 bytes).
 int make_map(CUtensorMap* m, const float* ptr, int64_t rows, int64_t cols, int64_t ld,
-             int box_rows) {
+             int box_rows, int bk) {
   if ((reinterpret_cast<uintptr_t>(ptr) & 15) != 0)
     return set_error(FG_EINVAL, "GEMM operand %p is not 16-byte aligned", (const void*)ptr);
   if (ld % 4 != 0) return set_error(FG_EINVAL, "GEMM row stride %lld is not a multiple of 4 floats", (long long)ld);
   cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
   cuuint64_t strides[1] = {cuuint64_t(ld) * 4};
-  cuuint32_t box[2] = {32u, cuuint32_t(box_rows)};
+  cuuint32_t box[2] = {cuuint32_t(bk), cuuint32_t(box_rows)};
   cuuint32_t es[2] = {1u, 1u};
+  const CUtensorMapSwizzle sw = bk == 32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims, strides, box,
-                        es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                        es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(FG_ECUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
   return FG_OK;
 }
 
-template <int BN, bool SA, bool SB>
+template <int BN, bool SA, bool SB, int BK>
 int launch_variant(const GemmArgs& g, const KParams& kp, int* dev_err, cudaStream_t stream) {
-  using C = Cfg<BN, SA, SB>;
+  using C = Cfg<BN, SA, SB, BK>;
   CUtensorMap mA, mAlo, mB, mBlo;
-  FG_TRY(make_map(&mA, g.A, g.M, g.K, g.lda, kBM));
-  FG_TRY(make_map(&mB, g.B, g.Nb, g.K, g.ldb, BN));
-  if (SA) FG_TRY(make_map(&mAlo, g.A_lo, g.M, g.K, g.lda, kBM)); else mAlo = mA;
-  if (SB) FG_TRY(make_map(&mBlo, g.B_lo, g.Nb, g.K, g.ldb, BN)); else mBlo = mB;
-  auto kern = gemm_tf32_kernel<BN, SA, SB>;
+  FG_TRY(make_map(&mA, g.A, g.M, g.K, g.lda, kBM, BK));
+  FG_TRY(make_map(&mB, g.B, g.Nb, g.K, g.ldb, BN, BK));
+  if (SA) FG_TRY(make_map(&mAlo, g.A_lo, g.M, g.K, g.lda, kBM, BK)); else mAlo = mA;
+  if (SB) FG_TRY(make_map(&mBlo, g.B_lo, g.Nb, g.K, g.ldb, BN, BK)); else mBlo = mB;
+  auto kern = gemm_tf32_kernel<BN, SA, SB, BK>;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -400,6 +512,42 @@ int launch_variant(const GemmArgs& g, const KParams& kp, int* dev_err, cudaStrea
   return FG_OK;
 }
 
+template <int BK>
+int dispatch(const GemmArgs& g, KParams& kp, int* dev_err, cudaStream_t stream) {
+  const bool sa = g.A_lo != nullptr, sb = g.B_lo != nullptr;
+  kp.nk = (g.K + BK - 1) / BK;
+  if (g.epi.geglu) {
+    kp.Nout = g.Nb / 2;
+    kp.ntn = g.Nb / 256;
+    if (sa && sb) return launch_variant<256, true, true, BK>(g, kp, dev_err, stream);
+    if (sa) return launch_variant<256, true, false, BK>(g, kp, dev_err, stream);
+    if (sb) return launch_variant<256, false, true, BK>(g, kp, dev_err, stream);
+    return launch_variant<256, false, false, BK>(g, kp, dev_err, stream);
+  }
+  kp.Nout = g.Nb;
+  if (g.Nb <= 128) {
+    kp.ntn = 1;
+    if (sa && sb) return launch_variant<128, true, true, BK>(g, kp, dev_err, stream);
+    if (sa) return launch_variant<128, true, false, BK>(g, kp, dev_err, stream);
+    if (sb) return launch_variant<128, false, true, BK>(g, kp, dev_err, stream);
+    return launch_variant<128, false, false, BK>(g, kp, dev_err, stream);
+  }
+  kp.ntn = (g.Nb + 255) / 256;
+  if (sa && sb) return launch_variant<256, true, true, BK>(g, kp, dev_err, stream);
+  if (sa) return launch_variant<256, true, false, BK>(g, kp, dev_err, stream);
+  if (sb) return launch_variant<256, false, true, BK>(g, kp, dev_err, stream);
+  return launch_variant<256, false, false, BK>(g, kp, dev_err, stream);
+}
+
+// Stage depth: FG_GEMM_BK=16 selects 64-byte stages (more in flight).
+int stage_bk() {
+  static int bk = [] {
+    const char* v = std::getenv("FG_GEMM_BK");
+    return (v && std::atoi(v) == 16) ? 16 : 32;
+  }();
+  return bk;
+}
+
 }  // namespace
 
 int gemm_tn(const GemmArgs& g, int* dev_err, cudaStream_t stream) {
@@ -407,7 +555,9 @@ int gemm_tn(const GemmArgs& g, int* dev_err, cudaStream_t stream) {
     if (g.M == 0 || g.Nb == 0) return FG_OK;
     return set_error(FG_EINVAL, "gemm: bad shape M=%d Nb=%d K=%d", g.M, g.Nb, g.K);
   }
-  if (g.epi.out == nullptr) return set_error(FG_EINVAL, "gemm: no output");
+  if (g.epi.out == nullptr && !g.epi.qkv_attn) return set_error(FG_EINVAL, "gemm: no output");
+  if (g.epi.qkv_attn && (g.Nb != (g.epi.Hq + 2 * g.epi.Hkv) * 256 || g.epi.T <= 0))
+    return set_error(FG_EINVAL, "gemm: attention-operand epilogue needs 256-wide heads");
   if (g.epi.geglu && (g.Nb % 256) != 0)
     return set_error(FG_EINVAL, "gemm: gated product needs B rows in multiples of 256, got %d", g.Nb);
   FG_TRY(get_encode());
@@ -416,30 +566,8 @@ int gemm_tn(const GemmArgs& g, int* dev_err, cudaStream_t stream) {
   kp.K = g.K;
   kp.e = g.epi;
   kp.err = dev_err;
-  kp.nk = (g.K + kBK - 1) / kBK;
   kp.ntm = (g.M + kBM - 1) / kBM;
-  const bool sa = g.A_lo != nullptr, sb = g.B_lo != nullptr;
-  if (g.epi.geglu) {
-    kp.Nout = g.Nb / 2;
-    kp.ntn = g.Nb / 256;
-    if (sa && sb) return launch_variant<256, true, true>(g, kp, dev_err, stream);
-    if (sa) return launch_variant<256, true, false>(g, kp, dev_err, stream);
-    if (sb) return launch_variant<256, false, true>(g, kp, dev_err, stream);
-    return launch_variant<256, false, false>(g, kp, dev_err, stream);
-  }
-  kp.Nout = g.Nb;
-  if (g.Nb <= 128) {
-    kp.ntn = 1;
-    if (sa && sb) return launch_variant<128, true, true>(g, kp, dev_err, stream);
-    if (sa) return launch_variant<128, true, false>(g, kp, dev_err, stream);
-    if (sb) return launch_variant<128, false, true>(g, kp, dev_err, stream);
-    return launch_variant<128, false, false>(g, kp, dev_err, stream);
-  }
-  kp.ntn = (g.Nb + 255) / 256;
-  if (sa && sb) return launch_variant<256, true, true>(g, kp, dev_err, stream);
-  if (sa) return launch_variant<256, true, false>(g, kp, dev_err, stream);
-  if (sb) return launch_variant<256, false, true>(g, kp, dev_err, stream);
-  return launch_variant<256, false, false>(g, kp, dev_err, stream);
+  return stage_bk() == 16 ? dispatch<16>(g, kp, dev_err, stream) : dispatch<32>(g, kp, dev_err, stream);
 }
 
 // ---------------------------------------------------------------- helpers

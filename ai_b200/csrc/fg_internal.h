@@ -71,6 +71,26 @@ struct GemmEpilogue {
   int64_t ldr = 0;
   int act = 0;                      // FG_ACT_*
   int geglu = 0;  // B rows interleaved per 128: gate rows then up rows; out = GELU(rs·g)·(rs·u)
+
+  // QKV projection → attention operands (BN = 256 = head_dim, so N-tile tn
+  // is head tn of q | k | v). For q and k heads: rs·acc, per-head RMSNorm
+  // with gains (1+w), rotate-half RoPE at position row % T, written as bf16
+  // hi/lo; for v heads: rs·acc written transposed as bf16 hi/lo
+  // vt[(b·Hkv + hk)·256 + d][t]. `out` is unused in this mode.
+  int qkv_attn = 0;
+  int Hq = 0, Hkv = 0, T = 0;
+  const float* qgain = nullptr;
+  const float* kgain = nullptr;
+  float eps = 0.f;
+  const float* rope_cos = nullptr;  // [>= T, 128]
+  const float* rope_sin = nullptr;
+  void* q_hi = nullptr;  // bf16 [M, Hq·256]
+  void* q_lo = nullptr;
+  void* k_hi = nullptr;  // bf16 [M, Hkv·256]
+  void* k_lo = nullptr;
+  void* vt_hi = nullptr;  // bf16 [B·Hkv·256, ldt]
+  void* vt_lo = nullptr;
+  int64_t ldt = 0;
 };
 
 struct GemmArgs {

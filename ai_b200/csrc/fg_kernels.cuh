@@ -83,6 +83,22 @@ int attention_simt(const AttnArgs& a, cudaStream_t s);
 size_t attn_tc_workspace_bytes(int B, int T, int S, int Hq, int Hkv);
 bool attn_tc_supported(const AttnArgs& a);
 int attention_tc(const AttnArgs& a, void* ws, size_t ws_bytes, int* err, cudaStream_t s);
+// The split-bf16 operands as the tensor-core kernel reads them: q, k
+// token-major [B·T, H·256], Vᵀ per sequence [B·Hkv·256, ldt keys].
+struct AttnOperands {
+  void* q_hi;
+  void* q_lo;
+  void* k_hi;
+  void* k_lo;
+  void* vt_hi;
+  void* vt_lo;
+  int64_t ldt;
+};
+// Carves ws (attn_tc_workspace_bytes) into the operand buffers.
+int attn_tc_carve(void* ws, int B, int T, int S, int Hq, int Hkv, AttnOperands* o);
+// Attention on operands already split (e.g. by the QKV GEMM's epilogue);
+// a's q/k/v pointers are not read.
+int attention_tc_operands(const AttnArgs& a, const AttnOperands& o, int* err, cudaStream_t s);
 // Rewrites the rows that have no visible key with the reference's result for
 // them: the mean of the values of the keys hidden by the fewest −1e9 masks.
 int attention_masked_rows(const AttnArgs& a, cudaStream_t s);

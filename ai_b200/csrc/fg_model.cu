@@ -483,22 +483,7 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
   for (int l = 0; l < c.num_layers; ++l) {
     const Layer& L = m->layers[l];
     const bool last = l == c.num_layers - 1;
-    // q|k|v = rowscale ⊙ (x · Wqkv'ᵀ)   (embed.go:193-197)
-    GemmArgs g = make_gemm(int(M), m->x, x_lo, H, L.wqkv, split);
-    g.epi.out = m->qkv;
-    g.epi.ldo = qkvw;
-    g.epi.rowscale = m->rowscale;
-    {
-      PhaseScope ps(m, FG_PHASE_GEMM_QKV, s, gemm_flops(g));
-      FG_TRY(gemm_tn(g, m->err, s));
-    }
-    // QK-norm + RoPE (embed.go:198-207)
-    {
-      PhaseScope ps(m, FG_PHASE_QK_NORM_ROPE, s, double(M) * (Hq + Hkv) * D * 8.0);
-      FG_TRY(qk_norm_rope(m->qkv, nullptr, M, Hq, Hkv, D, L.qgain, L.kgain, c.rms_norm_eps,
-                          m->rope_cos[L.rope], m->rope_sin[L.rope], T, s));
-    }
-    // attention (embed.go:209, attention.go:130)
+    // attention arguments (embed.go:209, attention.go:130)
     AttnArgs a{};
     a.q = m->qkv;
     a.k = m->qkv + int64_t(Hq) * D;
@@ -514,22 +499,63 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
     a.qlen = m->eff_len;
     a.window = (c.window > 0 && m->sliding[l]) ? c.window : 0;
     a.scale = c.attn_scale;
-    {
-      const bool tc = !m->attn_simt && attn_tc_supported(a);
-      PhaseScope ps(m, FG_PHASE_ATTENTION, s, 0.0, tc ? 4 : 1);
-      if (tc) {
-        const size_t need = attn_tc_workspace_bytes(B, T, T, Hq, Hkv);
-        if (need > m->attn_ws_bytes) {
-          if (m->attn_ws) {
-            FG_CUDA_TRY(cudaStreamSynchronize(s));
-            FG_CUDA_TRY(cudaFree(m->attn_ws));
-            m->attn_ws = nullptr;
-            m->attn_ws_bytes = 0;
-          }
-          FG_CUDA_TRY(cudaMalloc(&m->attn_ws, need));
-          m->attn_ws_bytes = need;
+    // Tensor-core attention: the QKV GEMM's epilogue applies QK-norm and
+    // RoPE and writes the split-bf16 operands straight into its workspace.
+    const bool tc = !m->attn_simt && attn_tc_supported(a);
+    AttnOperands ops{};
+    if (tc) {
+      const size_t need = attn_tc_workspace_bytes(B, T, T, Hq, Hkv);
+      if (need > m->attn_ws_bytes) {
+        if (m->attn_ws) {
+          FG_CUDA_TRY(cudaStreamSynchronize(s));
+          FG_CUDA_TRY(cudaFree(m->attn_ws));
+          m->attn_ws = nullptr;
+          m->attn_ws_bytes = 0;
         }
-        FG_TRY(attention_tc(a, m->attn_ws, m->attn_ws_bytes, m->err, s));
+        FG_CUDA_TRY(cudaMalloc(&m->attn_ws, need));
+        m->attn_ws_bytes = need;
+      }
+      FG_TRY(attn_tc_carve(m->attn_ws, B, T, T, Hq, Hkv, &ops));
+    }
+    // q|k|v = rowscale ⊙ (x · Wqkv'ᵀ)   (embed.go:193-197)
+    GemmArgs g = make_gemm(int(M), m->x, x_lo, H, L.wqkv, split);
+    g.epi.rowscale = m->rowscale;
+    if (tc) {
+      // + QK-norm and RoPE (embed.go:198-207) in the epilogue
+      g.epi.qkv_attn = 1;
+      g.epi.Hq = Hq;
+      g.epi.Hkv = Hkv;
+      g.epi.T = T;
+      g.epi.qgain = L.qgain;
+      g.epi.kgain = L.kgain;
+      g.epi.eps = c.rms_norm_eps;
+      g.epi.rope_cos = m->rope_cos[L.rope];
+      g.epi.rope_sin = m->rope_sin[L.rope];
+      g.epi.q_hi = ops.q_hi;
+      g.epi.q_lo = ops.q_lo;
+      g.epi.k_hi = ops.k_hi;
+      g.epi.k_lo = ops.k_lo;
+      g.epi.vt_hi = ops.vt_hi;
+      g.epi.vt_lo = ops.vt_lo;
+      g.epi.ldt = ops.ldt;
+    } else {
+      g.epi.out = m->qkv;
+      g.epi.ldo = qkvw;
+    }
+    {
+      PhaseScope ps(m, FG_PHASE_GEMM_QKV, s, gemm_flops(g));
+      FG_TRY(gemm_tn(g, m->err, s));
+    }
+    if (!tc) {
+      // QK-norm + RoPE (embed.go:198-207)
+      PhaseScope ps(m, FG_PHASE_QK_NORM_ROPE, s, double(M) * (Hq + Hkv) * D * 8.0);
+      FG_TRY(qk_norm_rope(m->qkv, nullptr, M, Hq, Hkv, D, L.qgain, L.kgain, c.rms_norm_eps,
+                          m->rope_cos[L.rope], m->rope_sin[L.rope], T, s));
+    }
+    {
+      PhaseScope ps(m, FG_PHASE_ATTENTION, s, 0.0);
+      if (tc) {
+        FG_TRY(attention_tc_operands(a, ops, m->err, s));
       } else {
         FG_TRY(attention_simt(a, s));
       }

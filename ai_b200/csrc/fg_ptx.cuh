@@ -245,6 +245,21 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
   return d;
 }
 
+// The same descriptor for rows of SW bytes (128 or 64) written by TMA with
+// the matching swizzle: 8-row atoms 8·SW bytes apart, layout type
+// SWIZZLE_128B (2) or SWIZZLE_64B (4); the tile base must be 8·SW aligned.
+template <int SW>
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t saddr) {
+  static_assert(SW == 128 || SW == 64, "swizzle width");
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1u) << 16;
+  d |= static_cast<uint64_t>((8u * SW) >> 4) << 32;
+  d |= static_cast<uint64_t>(1u) << 46;
+  d |= static_cast<uint64_t>(SW == 128 ? 2u : 4u) << 61;
+  return d;
+}
+
 // Instruction descriptor: kind::tf32, FP32 accumulator, both operands K-major.
 __host__ __device__ constexpr uint32_t idesc_tf32(int m, int n) {
   return (1u << 4)                                 // D format: F32
