@@ -43,17 +43,24 @@ struct KParams {
 
 // BK fp32 of K per pipeline stage: 32 (128-byte swizzled rows) or 16
 // (64-byte rows: half the bytes per stage, so more stages in flight).
-template <int BN, bool SA, bool SB, int BK>
+// SA: A's low part is loaded by TMA; CV: it is computed in shared memory
+// from the A tile by converter warps (A is then read from memory once).
+template <int BN, bool SA, bool SB, int BK, bool CV = false>
 struct Cfg {
   static constexpr int kSwizzle = BK * 4;
+  static constexpr bool kAlo = SA || CV;
+  static constexpr int kThreads = CV ? 320 : 192;
   static constexpr uint32_t kABytes = kBM * BK * 4;
   static constexpr uint32_t kBBytes = BN * BK * 4;
-  static constexpr uint32_t kStageBytes = kABytes * (SA ? 2 : 1) + kBBytes * (SB ? 2 : 1);
-  static constexpr int kStagesRaw = (kSmemLimit - 2048) / kStageBytes;
+  static constexpr uint32_t kStageBytes = kABytes * (kAlo ? 2 : 1) + kBBytes * (SB ? 2 : 1);
+  static constexpr uint32_t kTmaBytes = kStageBytes - (CV ? kABytes : 0);
+  // per epilogue warp a padded [32 × 33] fp32 block for row-contiguous stores
+  static constexpr uint32_t kEpiStageBytes = 4 * 32 * 33 * 4;
+  static constexpr int kStagesRaw = (kSmemLimit - 2048 - int(kEpiStageBytes)) / kStageBytes;
   static constexpr int kMaxStages = BK == 16 ? 8 : 6;
   static constexpr int kStages = kStagesRaw > kMaxStages ? kMaxStages : kStagesRaw;
   static constexpr uint32_t kTmemCols = 2 * BN;
-  static constexpr size_t kSmemBytes = 1024 + size_t(kStages) * kStageBytes + 256;
+  static constexpr size_t kSmemBytes = 1024 + size_t(kStages) * kStageBytes + 256 + kEpiStageBytes;
   static_assert(kStages >= 2, "tile too large for shared memory");
   static_assert(BK == 16 || BK == 32, "stage depth");
 };
@@ -117,11 +124,61 @@ __device__ __forceinline__ void store_row32(float* dst, const float (&v)[32], in
   }
 }
 
+// A warp's [32 rows × 32 columns] fp32 block, one row per lane in v, is
+// written to dst (row of lane 0, first column) through the padded staging
+// tile `st` ([32][33], conflict-free both ways): each store instruction
+// then writes 32 consecutive floats of one row — one 128-byte segment —
+// instead of 32 rows' 16-byte pieces. rows/cols bound the valid block.
+__device__ __forceinline__ void warp_store_block(float* st, const float (&v)[32], float* dst,
+                                                 int64_t ld, int rows, int cols) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) st[lane * 33 + j] = v[j];
+  __syncwarp();
+  if (lane < cols) {
+#pragma unroll 4
+    for (int rr = 0; rr < 32; ++rr)
+      if (rr < rows) dst[int64_t(rr) * ld + lane] = st[rr * 33 + lane];
+  }
+  __syncwarp();
+}
+
+// The same block written as bf16 hi/lo parts (64-byte segments per store).
+__device__ __forceinline__ void warp_store_block_bf16(float* st, const float (&v)[32],
+                                                      __nv_bfloat16* hi, __nv_bfloat16* lo,
+                                                      int64_t ld, int rows) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) st[lane * 33 + j] = v[j];
+  __syncwarp();
+#pragma unroll 4
+  for (int rr = 0; rr < 32; ++rr) {
+    if (rr < rows) {
+      const float y = st[rr * 33 + lane];
+      const __nv_bfloat16 h = __float2bfloat16_rn(y);
+      hi[int64_t(rr) * ld + lane] = h;
+      lo[int64_t(rr) * ld + lane] = __float2bfloat16_rn(y - __bfloat162float(h));
+    }
+  }
+  __syncwarp();
+}
+
 __device__ __forceinline__ void store_bf16_split(__nv_bfloat16* hi, __nv_bfloat16* lo, int64_t off,
                                                  float y) {
   const __nv_bfloat16 h = __float2bfloat16_rn(y);
   hi[off] = h;
   lo[off] = __float2bfloat16_rn(y - __bfloat162float(h));
+}
+
+// Four 32-column accumulator chunks (TMEM column offsets c0..c3 from taddr)
+// under a single wait.
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, int c0, int c1, int c2, int c3,
+                                         uint32_t (&r)[4][32]) {
+  tmem_ld_32x32b_x32(taddr + uint32_t(c0), r[0]);
+  tmem_ld_32x32b_x32(taddr + uint32_t(c1), r[1]);
+  tmem_ld_32x32b_x32(taddr + uint32_t(c2), r[2]);
+  tmem_ld_32x32b_x32(taddr + uint32_t(c3), r[3]);
+  tmem_ld_wait();
 }
 
 // Epilogue of the QKV projection when it feeds the tensor-core attention:
@@ -132,34 +189,42 @@ __device__ __forceinline__ void store_bf16_split(__nv_bfloat16* hi, __nv_bfloat1
 // bf16 hi/lo written transposed per sequence (vt[(b·Hkv+hk)·256 + d][t]).
 // tcgen05.ld is warp-collective, so every lane loads even for rows ≥ M.
 __device__ __forceinline__ void qkv_attn_epilogue(const GemmEpilogue& e, uint32_t taddr, int tn,
-                                                  int row, bool row_ok, float rs) {
+                                                  int row, bool row_ok, float rs, float* st,
+                                                  int rows) {
   constexpr int D = 256, H2 = 128;
-  if (tn < e.Hq + e.Hkv) {
-    const bool is_q = tn < e.Hq;
-    const float* g = is_q ? e.qgain : e.kgain;
-    // pass 1: Σ y² over the head
+  // Fields in registers: read through the reference they would be re-read
+  // after every global store (the stores might alias them).
+  const int Hq = e.Hq, Hkv = e.Hkv, T = e.T;
+  if (tn < Hq + Hkv) {
+    const bool is_q = tn < Hq;
+    const float* const g = is_q ? e.qgain : e.kgain;
+    const float eps = e.eps;
+    const int t = row % T;
+    const float* const cs = e.rope_cos + int64_t(t) * H2;
+    const float* const sn = e.rope_sin + int64_t(t) * H2;
+    __nv_bfloat16* const hi = static_cast<__nv_bfloat16*>(is_q ? e.q_hi : e.k_hi);
+    __nv_bfloat16* const lo = static_cast<__nv_bfloat16*>(is_q ? e.q_lo : e.k_lo);
+    const int width = (is_q ? Hq : Hkv) * D;
+    const int head = is_q ? tn : tn - Hq;
+    // pass 1: Σ y² over the head, columns in order
     float ss = 0.f;
 #pragma unroll 1
-    for (int c0 = 0; c0 < D; c0 += 32) {
-      uint32_t r[32];
-      tmem_ld_32x32b_x32(taddr + uint32_t(c0), r);
-      tmem_ld_wait();
+    for (int h0 = 0; h0 < D; h0 += 128) {
+      uint32_t r[4][32];
+      tmem_ld4(taddr, h0, h0 + 32, h0 + 64, h0 + 96, r);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float y = __fmul_rn(__uint_as_float(r[j]), rs);
-        ss = __fadd_rn(ss, __fmul_rn(y, y));
-      }
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float y = __fmul_rn(__uint_as_float(r[q][j]), rs);
+          ss = __fadd_rn(ss, __fmul_rn(y, y));
+        }
     }
-    const float m = __fadd_rn(__fdiv_rn(ss, float(D)), e.eps);
+    const float m = __fadd_rn(__fdiv_rn(ss, float(D)), eps);
     const float inv = float(1.0 / sqrt(double(m)));
-    const int t = row % e.T;
-    const float* cs = e.rope_cos + int64_t(t) * H2;
-    const float* sn = e.rope_sin + int64_t(t) * H2;
-    __nv_bfloat16* hi = static_cast<__nv_bfloat16*>(is_q ? e.q_hi : e.k_hi);
-    __nv_bfloat16* lo = static_cast<__nv_bfloat16*>(is_q ? e.q_lo : e.k_lo);
-    const int width = (is_q ? e.Hq : e.Hkv) * D;
-    const int head = is_q ? tn : tn - e.Hq;
-    const int64_t base = int64_t(row) * width + int64_t(head) * D;
+    const int lane = threadIdx.x & 31;
+    // the warp's first row, first column of this head
+    const int64_t base0 = int64_t(row - lane) * width + int64_t(head) * D;
     // pass 2: normalise, rotate the pairs (i, i + 128), split, store
 #pragma unroll 1
     for (int c0 = 0; c0 < H2; c0 += 32) {
@@ -167,64 +232,46 @@ __device__ __forceinline__ void qkv_attn_epilogue(const GemmEpilogue& e, uint32_
       tmem_ld_32x32b_x32(taddr + uint32_t(c0), ra);
       tmem_ld_32x32b_x32(taddr + uint32_t(H2 + c0), rb);
       tmem_ld_wait();
-      if (row_ok) {
+      float y1[32], y2[32];
 #pragma unroll
-        for (int j0 = 0; j0 < 32; j0 += 8) {
-          uint32_t h1[4], l1[4], h2[4], l2[4];
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            float y1[2], y2[2];
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int j = j0 + 2 * q + u, i = c0 + j;
-              const float x1 = __fmul_rn(__fmul_rn(__fmul_rn(__uint_as_float(ra[j]), rs), inv), g[i]);
-              const float x2 = __fmul_rn(__fmul_rn(__fmul_rn(__uint_as_float(rb[j]), rs), inv), g[i + H2]);
-              const float c = cs[i], s = sn[i];
-              y1[u] = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
-              y2[u] = __fadd_rn(__fmul_rn(x1, s), __fmul_rn(x2, c));
-            }
-            const float a0 = bf16_round_f32(y1[0]), a1 = bf16_round_f32(y1[1]);
-            const float b0 = bf16_round_f32(y2[0]), b1 = bf16_round_f32(y2[1]);
-            h1[q] = pack_bf16x2(a0, a1);
-            l1[q] = pack_bf16x2(y1[0] - a0, y1[1] - a1);
-            h2[q] = pack_bf16x2(b0, b1);
-            l2[q] = pack_bf16x2(y2[0] - b0, y2[1] - b1);
-          }
-          const int64_t o1 = base + c0 + j0, o2 = o1 + H2;
-          *reinterpret_cast<uint4*>(hi + o1) = make_uint4(h1[0], h1[1], h1[2], h1[3]);
-          *reinterpret_cast<uint4*>(lo + o1) = make_uint4(l1[0], l1[1], l1[2], l1[3]);
-          *reinterpret_cast<uint4*>(hi + o2) = make_uint4(h2[0], h2[1], h2[2], h2[3]);
-          *reinterpret_cast<uint4*>(lo + o2) = make_uint4(l2[0], l2[1], l2[2], l2[3]);
-        }
+      for (int j = 0; j < 32; ++j) {
+        const int i = c0 + j;
+        const float x1 = __fmul_rn(__fmul_rn(__fmul_rn(__uint_as_float(ra[j]), rs), inv), g[i]);
+        const float x2 = __fmul_rn(__fmul_rn(__fmul_rn(__uint_as_float(rb[j]), rs), inv), g[i + H2]);
+        const float c = row_ok ? cs[i] : 0.f, s = row_ok ? sn[i] : 0.f;
+        y1[j] = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+        y2[j] = __fadd_rn(__fmul_rn(x1, s), __fmul_rn(x2, c));
       }
+      warp_store_block_bf16(st, y1, hi + base0 + c0, lo + base0 + c0, width, rows);
+      warp_store_block_bf16(st, y2, hi + base0 + H2 + c0, lo + base0 + H2 + c0, width, rows);
     }
   } else {
-    const int hk = tn - e.Hq - e.Hkv;
-    const int b = row / e.T, t = row % e.T;
-    __nv_bfloat16* hi = static_cast<__nv_bfloat16*>(e.vt_hi);
-    __nv_bfloat16* lo = static_cast<__nv_bfloat16*>(e.vt_lo);
-    const int64_t base = (int64_t(b) * e.Hkv + hk) * D * e.ldt + t;
+    const int hk = tn - Hq - Hkv;
+    const int b = row / T, t = row % T;
+    __nv_bfloat16* const hi = static_cast<__nv_bfloat16*>(e.vt_hi);
+    __nv_bfloat16* const lo = static_cast<__nv_bfloat16*>(e.vt_lo);
+    const int64_t ldt = e.ldt;
+    const int64_t base = (int64_t(b) * Hkv + hk) * D * ldt + t;
 #pragma unroll 1
     for (int c0 = 0; c0 < D; c0 += 32) {
       uint32_t r[32];
       tmem_ld_32x32b_x32(taddr + uint32_t(c0), r);
       tmem_ld_wait();
       if (row_ok) {
-#pragma unroll 8
+#pragma unroll
         for (int j = 0; j < 32; ++j)
-          store_bf16_split(hi, lo, base + int64_t(c0 + j) * e.ldt,
-                           __fmul_rn(__uint_as_float(r[j]), rs));
+          store_bf16_split(hi, lo, base + int64_t(c0 + j) * ldt, __fmul_rn(__uint_as_float(r[j]), rs));
       }
     }
   }
 }
 
-template <int BN, bool SA, bool SB, int BK>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int BN, bool SA, bool SB, int BK, bool CV>
+__global__ void __launch_bounds__(Cfg<BN, SA, SB, BK, CV>::kThreads, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mAlo,
                      const __grid_constant__ CUtensorMap mB, const __grid_constant__ CUtensorMap mBlo,
-                     const KParams p) {
-  using C = Cfg<BN, SA, SB, BK>;
+                     const __grid_constant__ KParams p) {
+  using C = Cfg<BN, SA, SB, BK, CV>;
   constexpr int S = C::kStages;
   constexpr int kSw = C::kSwizzle;
   constexpr uint32_t kIdesc = idesc_tf32(kBM, BN);
@@ -232,8 +279,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + size_t(S) * C::kStageBytes);
-  // bars[0..S) full, [S..2S) empty, [2S..2S+2) acc_full, [2S+2..2S+4) acc_empty, [2S+4] drain
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
+  // bars[0..S) full, [S..2S) empty, [2S..2S+2) acc_full, [2S+2..2S+4) acc_empty,
+  // [2S+4] drain, [2S+5..3S+5) A low part converted
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 3 * S + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -245,11 +293,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto accf_bar = [&](int a) { return smem_u32(&bars[2 * S + a]); };
   auto acce_bar = [&](int a) { return smem_u32(&bars[2 * S + 2 + a]); };
   const uint32_t drain_bar = smem_u32(&bars[2 * S + 4]);
+  auto conv_bar = [&](int s) { return smem_u32(&bars[2 * S + 5 + s]); };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
+      if (CV) mbar_init(conv_bar(s), 128);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(accf_bar(a), 1);
@@ -287,15 +337,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kb = 0; kb < p.nk; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1, abort_flag, p.err, kDevTimeoutEmpty)) break;
           const uint32_t fb = full_bar(stage);
-          mbar_arrive_expect_tx(fb, C::kStageBytes);
+          mbar_arrive_expect_tx(fb, C::kTmaBytes);
           armed[stage]++;
           uint32_t dst = smem_u32(smem + size_t(stage) * C::kStageBytes);
           tma_load_2d(dst, &mA, fb, kb * BK, tm * kBM);
           dst += C::kABytes;
-          if (SA) {
-            tma_load_2d(dst, &mAlo, fb, kb * BK, tm * kBM);
-            dst += C::kABytes;
-          }
+          if (SA) tma_load_2d(dst, &mAlo, fb, kb * BK, tm * kBM);
+          if (C::kAlo) dst += C::kABytes;
           tma_load_2d(dst, &mB, fb, kb * BK, tn * BN);
           dst += C::kBBytes;
           if (SB) tma_load_2d(dst, &mBlo, fb, kb * BK, tn * BN);
@@ -342,7 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + size_t(stage) * C::kStageBytes);
           const uint32_t alo_addr = a_addr + C::kABytes;
-          const uint32_t b_addr = a_addr + C::kABytes * (SA ? 2 : 1);
+          const uint32_t b_addr = a_addr + C::kABytes * (C::kAlo ? 2 : 1);
           const uint32_t blo_addr = b_addr + C::kBBytes;
 #pragma unroll
           for (int k = 0; k < BK / kUmmaK; ++k) {
@@ -352,6 +400,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_tf32(d_tmem, da, db, kIdesc, (kb | k) != 0 ? 1u : 0u);
             if (SB) mma_tf32(d_tmem, da, kmajor_desc<kSw>(blo_addr + koff), kIdesc, 1u);
             if (SA) mma_tf32(d_tmem, kmajor_desc<kSw>(alo_addr + koff), db, kIdesc, 1u);
+          }
+          if (CV) {
+            // low pass once the converter warps have written A's low part
+            if (!mbar_wait(conv_bar(stage), phase, abort_flag, p.err, kDevTimeoutFull)) {
+              ok = false;
+              issued = true;
+              break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int k = 0; k < BK / kUmmaK; ++k) {
+              const uint32_t koff = uint32_t(k * kUmmaK * 4);
+              mma_tf32(d_tmem, kmajor_desc<kSw>(alo_addr + koff), kmajor_desc<kSw>(b_addr + koff),
+                       kIdesc, 1u);
+            }
           }
           issued = true;
           mma_commit(empty_bar(stage));
@@ -375,13 +438,61 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+  } else if (CV && warp >= 6) {
+    // -------------------------------------------------- converters (warps 6..9)
+    // A tile [128 rows × BK fp32] as TMA swizzled it; the low part lands at
+    // the same byte offsets of the stage's A_lo slot, so it has the same
+    // swizzled layout the MMA descriptor expects.
+    const int ct = threadIdx.x - 192;  // 0..127
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int tile = blockIdx.x; tile < ntiles && !*abort_flag; tile += gridDim.x) {
+      bool ok = true;
+      for (int kb = 0; kb < p.nk; ++kb) {
+        if (!mbar_wait(full_bar(stage), phase, abort_flag, p.err, kDevTimeoutFull)) {
+          ok = false;
+          break;
+        }
+        const float4* src = reinterpret_cast<const float4*>(smem + size_t(stage) * C::kStageBytes);
+        float4* dst = reinterpret_cast<float4*>(smem + size_t(stage) * C::kStageBytes + C::kABytes);
+#pragma unroll
+        for (int q = 0; q < int(C::kABytes / 16 / 128); ++q) {
+          const float4 v = src[q * 128 + ct];
+          dst[q * 128 + ct] = make_float4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
+        }
+        fence_proxy_async_smem();  // generic-proxy writes → visible to the tensor core
+        mbar_arrive(conv_bar(stage));
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!ok) break;
+    }
   } else {
     // -------------------------------------------------- epilogue (warps 2..5)
     const int quad = warp & 3;
-    const int rloc = quad * 32 + lane;
     const GemmEpilogue& e = p.e;
-    const bool vec_out = (e.ldo % 4 == 0) && ((reinterpret_cast<uintptr_t>(e.out) & 15) == 0);
-    const bool vec_lo = e.out_lo && (e.ldo_lo % 4 == 0) && ((reinterpret_cast<uintptr_t>(e.out_lo) & 15) == 0);
+    float* st = reinterpret_cast<float*>(smem + size_t(S) * C::kStageBytes + 256) + (warp - 2) * 32 * 33;
+    // Fields in registers: read through the reference they would be re-read
+    // after every global store (the stores might alias them).
+    float* const out = e.out;
+    const int64_t ldo = e.ldo;
+    float* const out_lo = e.out_lo;
+    const int64_t ldo_lo = e.ldo_lo;
+    const float* const rowscale = e.rowscale;
+    const float* const bias = e.bias;
+    const float* const mul = e.mul;
+    const int64_t ldm = e.ldm;
+    const float* const resid = e.residual;
+    const int64_t ldr = e.ldr;
+    const int act = e.act;
+    const bool geglu = e.geglu != 0;
+    const bool qkv = BN == 256 && e.qkv_attn != 0;
+    const bool plain = !bias && !mul && !resid && act == FG_ACT_NONE;
+    const int Nout = p.Nout;
+    const bool vec_out = (ldo % 4 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
+    const bool vec_lo = out_lo && (ldo_lo % 4 == 0) && ((reinterpret_cast<uintptr_t>(out_lo) & 15) == 0);
     int local = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++local) {
       const int acc = local & 1;
@@ -390,13 +501,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!__all_sync(0xffffffffu, got)) break;  // warp-uniform before the collective tcgen05.ld
       tc_fence_after();
       const int tm = tile / p.ntn, tn = tile % p.ntn;
-      const int row = tm * kBM + rloc;
+      const int row0 = tm * kBM + quad * 32;  // the warp's first row
+      const int row = row0 + lane;
       const bool row_ok = row < p.M;
-      const float rs = (e.rowscale && row_ok) ? e.rowscale[row] : 1.f;
+      const int rows = max(0, min(32, p.M - row0));
+      const float rs = (rowscale && row_ok) ? rowscale[row] : 1.f;
       const uint32_t taddr = tmem_base + (uint32_t(quad * 32) << 16) + uint32_t(acc * BN);
-      if (BN == 256 && e.qkv_attn) {
-        qkv_attn_epilogue(e, taddr, tn, row, row_ok, rs);
-      } else if (e.geglu) {
+      if (qkv) {
+        qkv_attn_epilogue(e, taddr, tn, row, row_ok, rs, st, rows);
+      } else if (geglu) {
         // Tile columns [0, BN/2) are gate, [BN/2, BN) the matching up columns.
 #pragma unroll 1
         for (int c0 = 0; c0 < BN / 2; c0 += 32) {
@@ -405,47 +518,58 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld_32x32b_x32(taddr + uint32_t(BN / 2 + c0), ru);
           tmem_ld_wait();
           const int col0 = tn * (BN / 2) + c0;
-          const int ncols = min(32, p.Nout - col0);
-          if (row_ok && ncols > 0) {
-            float v[32], vl[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float g = __uint_as_float(rg[j]) * rs;
-              const float u = __uint_as_float(ru[j]) * rs;
-              const float o = gelu_tanh(g) * u;
-              v[j] = o;
-              vl[j] = tf32_lo(o);
-            }
-            store_row32(e.out + int64_t(row) * e.ldo + col0, v, ncols, vec_out);
-            if (e.out_lo) store_row32(e.out_lo + int64_t(row) * e.ldo_lo + col0, vl, ncols, vec_lo);
-          }
-        }
-      } else {
-#pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(taddr + uint32_t(c0), r);
-          tmem_ld_wait();
-          const int col0 = tn * BN + c0;
-          const int ncols = min(32, p.Nout - col0);
+          const int ncols = min(32, Nout - col0);
           if (row_ok && ncols > 0) {
             float v[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
-              float x = __uint_as_float(r[j]);
-              const int col = col0 + j;
-              if (e.bias && j < ncols) x = x + e.bias[col];
-              x = x * rs;
-              x = apply_act(x, e.act);
-              if (e.mul && j < ncols) x = x * e.mul[int64_t(row) * e.ldm + col];
-              if (e.residual && j < ncols) x = x + e.residual[int64_t(row) * e.ldr + col];
-              v[j] = x;
+              const float g = __uint_as_float(rg[j]) * rs;
+              const float u = __uint_as_float(ru[j]) * rs;
+              v[j] = gelu_tanh(g) * u;
             }
-            store_row32(e.out + int64_t(row) * e.ldo + col0, v, ncols, vec_out);
-            if (e.out_lo) {
+            store_row32(out + int64_t(row) * ldo + col0, v, ncols, vec_out);
+            if (out_lo) {
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] = tf32_lo(v[j]);
-              store_row32(e.out_lo + int64_t(row) * e.ldo_lo + col0, v, ncols, vec_lo);
+              store_row32(out_lo + int64_t(row) * ldo_lo + col0, v, ncols, vec_lo);
+            }
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int h0 = 0; h0 < BN; h0 += 64) {
+          uint32_t r[2][32];
+          tmem_ld_32x32b_x32(taddr + uint32_t(h0), r[0]);
+          tmem_ld_32x32b_x32(taddr + uint32_t(h0 + 32), r[1]);
+          tmem_ld_wait();
+          if (!row_ok) continue;
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            const int col0 = tn * BN + h0 + 32 * q;
+            const int ncols = min(32, Nout - col0);
+            if (ncols <= 0) break;
+            float v[32];
+            if (plain) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[q][j]) * rs;
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                float x = __uint_as_float(r[q][j]);
+                const int col = col0 + j;
+                if (bias && j < ncols) x = x + bias[col];
+                x = x * rs;
+                x = apply_act(x, act);
+                if (mul && j < ncols) x = x * mul[int64_t(row) * ldm + col];
+                if (resid && j < ncols) x = x + resid[int64_t(row) * ldr + col];
+                v[j] = x;
+              }
+            }
+            store_row32(out + int64_t(row) * ldo + col0, v, ncols, vec_out);
+            if (out_lo) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = tf32_lo(v[j]);
+              store_row32(out_lo + int64_t(row) * ldo_lo + col0, v, ncols, vec_lo);
             }
           }
         }
@@ -488,15 +612,15 @@ int make_map(CUtensorMap* m, const float* ptr, int64_t rows, int64_t cols, int64
   return FG_OK;
 }
 
-template <int BN, bool SA, bool SB, int BK>
+template <int BN, bool SA, bool SB, int BK, bool CV = false>
 int launch_variant(const GemmArgs& g, const KParams& kp, int* dev_err, cudaStream_t stream) {
-  using C = Cfg<BN, SA, SB, BK>;
+  using C = Cfg<BN, SA, SB, BK, CV>;
   CUtensorMap mA, mAlo, mB, mBlo;
   FG_TRY(make_map(&mA, g.A, g.M, g.K, g.lda, kBM, BK));
   FG_TRY(make_map(&mB, g.B, g.Nb, g.K, g.ldb, BN, BK));
   if (SA) FG_TRY(make_map(&mAlo, g.A_lo, g.M, g.K, g.lda, kBM, BK)); else mAlo = mA;
   if (SB) FG_TRY(make_map(&mBlo, g.B_lo, g.Nb, g.K, g.ldb, BN, BK)); else mBlo = mB;
-  auto kern = gemm_tf32_kernel<BN, SA, SB, BK>;
+  auto kern = gemm_tf32_kernel<BN, SA, SB, BK, CV>;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -506,46 +630,41 @@ int launch_variant(const GemmArgs& g, const KParams& kp, int* dev_err, cudaStrea
   }
   const int ntiles = kp.ntm * kp.ntn;
   const int grid = std::max(1, std::min(ntiles, sm_count()));
-  kern<<<grid, kThreads, C::kSmemBytes, stream>>>(mA, mAlo, mB, mBlo, kp);
+  kern<<<grid, C::kThreads, C::kSmemBytes, stream>>>(mA, mAlo, mB, mBlo, kp);
   FG_CUDA_TRY(cudaGetLastError());
   (void)dev_err;
   return FG_OK;
 }
 
-template <int BK>
+// A's low part: none (plain TF32), loaded (SA), or computed in shared memory (CV).
+template <int BN, bool SB>
+int launch_a_mode(const GemmArgs& g, const KParams& kp, int* dev_err, cudaStream_t stream) {
+  constexpr int BK = 32;
+  if (g.A_lo) return launch_variant<BN, true, SB, BK, false>(g, kp, dev_err, stream);
+  if (g.a_lo_smem) return launch_variant<BN, false, SB, BK, true>(g, kp, dev_err, stream);
+  return launch_variant<BN, false, SB, BK, false>(g, kp, dev_err, stream);
+}
+
+template <int BN>
+int launch_b_mode(const GemmArgs& g, const KParams& kp, int* dev_err, cudaStream_t stream) {
+  if (g.B_lo) return launch_a_mode<BN, true>(g, kp, dev_err, stream);
+  return launch_a_mode<BN, false>(g, kp, dev_err, stream);
+}
+
 int dispatch(const GemmArgs& g, KParams& kp, int* dev_err, cudaStream_t stream) {
-  const bool sa = g.A_lo != nullptr, sb = g.B_lo != nullptr;
-  kp.nk = (g.K + BK - 1) / BK;
+  kp.nk = (g.K + 31) / 32;
   if (g.epi.geglu) {
     kp.Nout = g.Nb / 2;
     kp.ntn = g.Nb / 256;
-    if (sa && sb) return launch_variant<256, true, true, BK>(g, kp, dev_err, stream);
-    if (sa) return launch_variant<256, true, false, BK>(g, kp, dev_err, stream);
-    if (sb) return launch_variant<256, false, true, BK>(g, kp, dev_err, stream);
-    return launch_variant<256, false, false, BK>(g, kp, dev_err, stream);
+    return launch_b_mode<256>(g, kp, dev_err, stream);
   }
   kp.Nout = g.Nb;
   if (g.Nb <= 128) {
     kp.ntn = 1;
-    if (sa && sb) return launch_variant<128, true, true, BK>(g, kp, dev_err, stream);
-    if (sa) return launch_variant<128, true, false, BK>(g, kp, dev_err, stream);
-    if (sb) return launch_variant<128, false, true, BK>(g, kp, dev_err, stream);
-    return launch_variant<128, false, false, BK>(g, kp, dev_err, stream);
+    return launch_b_mode<128>(g, kp, dev_err, stream);
   }
   kp.ntn = (g.Nb + 255) / 256;
-  if (sa && sb) return launch_variant<256, true, true, BK>(g, kp, dev_err, stream);
-  if (sa) return launch_variant<256, true, false, BK>(g, kp, dev_err, stream);
-  if (sb) return launch_variant<256, false, true, BK>(g, kp, dev_err, stream);
-  return launch_variant<256, false, false, BK>(g, kp, dev_err, stream);
-}
-
-// Stage depth: FG_GEMM_BK=16 selects 64-byte stages (more in flight).
-int stage_bk() {
-  static int bk = [] {
-    const char* v = std::getenv("FG_GEMM_BK");
-    return (v && std::atoi(v) == 16) ? 16 : 32;
-  }();
-  return bk;
+  return launch_b_mode<256>(g, kp, dev_err, stream);
 }
 
 }  // namespace
@@ -567,7 +686,7 @@ int gemm_tn(const GemmArgs& g, int* dev_err, cudaStream_t stream) {
   kp.e = g.epi;
   kp.err = dev_err;
   kp.ntm = (g.M + kBM - 1) / kBM;
-  return stage_bk() == 16 ? dispatch<16>(g, kp, dev_err, stream) : dispatch<32>(g, kp, dev_err, stream);
+  return dispatch(g, kp, dev_err, stream);
 }
 
 // ---------------------------------------------------------------- helpers

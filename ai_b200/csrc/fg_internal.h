@@ -101,6 +101,9 @@ struct GemmArgs {
   const float* B = nullptr;
   const float* B_lo = nullptr;
   int64_t ldb = 0;
+  // Split-TF32 without a stored A_lo: the kernel computes A's low part in
+  // shared memory from the A tile (A is read from memory once).
+  bool a_lo_smem = false;
   GemmEpilogue epi;
 };
 

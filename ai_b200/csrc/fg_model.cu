@@ -131,6 +131,9 @@ struct fg_model {
   void* attn_ws = nullptr;  // split-bf16 operands of the tensor-core attention
   size_t attn_ws_bytes = 0;
   bool attn_simt = false;   // FG_ATTENTION=simt selects the SIMT kernel
+  // FG_GEMM_ALO=global: producers write the split-TF32 low parts of the
+  // GEMM inputs to memory instead of the GEMM computing them in shared memory
+  bool alo_global = false;
   // host-API staging
   int32_t* d_ids = nullptr;
   int64_t d_ids_cap = 0;
@@ -451,6 +454,7 @@ GemmArgs make_gemm(int M, const float* A, const float* A_lo, int64_t lda, const 
   g.K = B.cols;
   g.A = A;
   g.A_lo = split ? A_lo : nullptr;
+  g.a_lo_smem = split && A_lo == nullptr;  // low part made in shared memory
   g.lda = lda;
   g.B = B.hi;
   g.B_lo = split ? B.lo : nullptr;
@@ -468,11 +472,16 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
   if (M > INT32_MAX) return set_error(FG_EINVAL, "batch too large");
   FG_TRY(ensure_workspace(m, M, B));
   const int qkvw = (Hq + 2 * Hkv) * D, attw = Hq * D;
-  float* x_lo = split ? m->x_lo : nullptr;
+  // Split-TF32 low parts of GEMM inputs: made in shared memory by the GEMM
+  // (default), or written to memory by their producers (FG_GEMM_ALO=global).
+  const bool lo_global = split && m->alo_global;
+  float* x_lo = lo_global ? m->x_lo : nullptr;
+  float* att_lo = lo_global ? m->att_lo : nullptr;
+  float* gu_lo = lo_global ? m->gu_lo : nullptr;
 
   const double act_bytes = double(M) * H * 4.0;
   {
-    PhaseScope ps(m, FG_PHASE_EMBED, s, act_bytes * (split ? 3 : 2) + double(M) * 8, 2);
+    PhaseScope ps(m, FG_PHASE_EMBED, s, act_bytes * (lo_global ? 3 : 2) + double(M) * 8, 2);
     eff_len_kernel<<<(B + 127) / 128, 128, 0, s>>>(lengths, B, T, m->eff_len);
     FG_CUDA_TRY(cudaGetLastError());
     const float emb_scale = float(std::sqrt(double(H)));
@@ -489,7 +498,7 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
     a.k = m->qkv + int64_t(Hq) * D;
     a.v = m->qkv + int64_t(Hq + Hkv) * D;
     a.out = m->att;
-    a.out_lo = split ? m->att_lo : nullptr;
+    a.out_lo = att_lo;
     a.qsb = int64_t(T) * qkvw; a.qsh = D; a.qst = qkvw;
     a.ksb = a.qsb; a.ksh = D; a.kst = qkvw;
     a.vsb = a.qsb; a.vsh = D; a.vst = qkvw;
@@ -561,7 +570,7 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
       }
     }
     // o0 = att · Wo   (embed.go:212-214)
-    g = make_gemm(int(M), m->att, m->att_lo, attw, L.wo, split);
+    g = make_gemm(int(M), m->att, att_lo, attw, L.wo, split);
     g.epi.out = m->tmp;
     g.epi.ldo = H;
     {
@@ -570,7 +579,7 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
     }
     // x += RMSNorm(o0)   (embed.go:216-220), and the FFN pre-norm factor
     {
-      PhaseScope ps(m, FG_PHASE_RESIDUAL, s, act_bytes * (split ? 4 : 3) + double(M) * 4);
+      PhaseScope ps(m, FG_PHASE_RESIDUAL, s, act_bytes * (lo_global ? 4 : 3) + double(M) * 4);
       FG_TRY(residual_postnorm(m->x, x_lo, m->tmp, L.post_attn, c.rms_norm_eps, m->rowscale,
                                nullptr, M, H, s));
     }
@@ -578,7 +587,7 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
     g = make_gemm(int(M), m->x, x_lo, H, L.wgu, split);
     g.epi.out = m->gu;
     g.epi.ldo = F;
-    g.epi.out_lo = split ? m->gu_lo : nullptr;
+    g.epi.out_lo = gu_lo;
     g.epi.ldo_lo = F;
     g.epi.rowscale = m->rowscale;
     g.epi.geglu = 1;
@@ -587,7 +596,7 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
       FG_TRY(gemm_tn(g, m->err, s));
     }
     // mlp0 = gu · Wd   (embed.go:229)
-    g = make_gemm(int(M), m->gu, m->gu_lo, F, L.wd, split);
+    g = make_gemm(int(M), m->gu, gu_lo, F, L.wd, split);
     g.epi.out = m->tmp;
     g.epi.ldo = H;
     {
@@ -596,7 +605,7 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
     }
     // x += RMSNorm(mlp0)   (embed.go:231-235); final norm on the last layer (embed.go:237)
     {
-      PhaseScope ps(m, FG_PHASE_RESIDUAL, s, act_bytes * ((split && !last) ? 4 : 3) + double(M) * 4);
+      PhaseScope ps(m, FG_PHASE_RESIDUAL, s, act_bytes * ((lo_global && !last) ? 4 : 3) + double(M) * 4);
       FG_TRY(residual_postnorm(m->x, x_lo, m->tmp, L.post_ffn, c.rms_norm_eps, m->rowscale,
                                last ? m->final_gain : nullptr, M, H, s));
     }
@@ -605,9 +614,9 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
 
   // pool (embed.go:381-404), head (embed.go:408-429), L2 (embed.go:472-475)
   PhaseScope ps(m, FG_PHASE_POOL_HEAD, s, act_bytes, 2 + int(m->dense.size()));
-  FG_TRY(mean_pool(m->x, m->eff_len, B, T, H, m->pooled, split ? m->pooled_lo : nullptr, s));
+  FG_TRY(mean_pool(m->x, m->eff_len, B, T, H, m->pooled, lo_global ? m->pooled_lo : nullptr, s));
   const float* cur = m->pooled;
-  const float* cur_lo = m->pooled_lo;
+  const float* cur_lo = lo_global ? m->pooled_lo : nullptr;
   int width = H;
   float* bufs[2] = {m->head_a, m->head_b};
   float* bufs_lo[2] = {m->head_a_lo, m->head_b_lo};
@@ -616,12 +625,12 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
     GemmArgs g = make_gemm(B, cur, cur_lo, width, d.w, split);
     g.epi.out = bufs[j & 1];
     g.epi.ldo = d.out;
-    g.epi.out_lo = split ? bufs_lo[j & 1] : nullptr;
+    g.epi.out_lo = lo_global ? bufs_lo[j & 1] : nullptr;
     g.epi.ldo_lo = d.out;
     g.epi.act = d.tanh ? kActTanh : FG_ACT_NONE;
     FG_TRY(gemm_tn(g, m->err, s));
     cur = bufs[j & 1];
-    cur_lo = bufs_lo[j & 1];
+    cur_lo = lo_global ? bufs_lo[j & 1] : nullptr;
     width = d.out;
   }
   if (dim > width) return set_error(FG_EINVAL, "gemma: Dim(%d) outside 1..%d", dim, width);
@@ -670,6 +679,8 @@ int fg_model_create(const fg_config* cfg, int device, fg_model** out) {
   m->cfg.rope_base = m->rope_base.data();
   const char* att = std::getenv("FG_ATTENTION");
   m->attn_simt = att && std::string(att) == "simt";
+  const char* alo = std::getenv("FG_GEMM_ALO");
+  m->alo_global = alo && std::string(alo) == "global";
   *out = m;
   return FG_OK;
 }
