@@ -39,7 +39,16 @@ struct KParams {
   int ntm, ntn, nk;
   GemmEpilogue e;
   int* err;
+  int tma_out, tma_out_lo;  // out / out_lo are written by TMA stores (maps mOut / mOutLo)
 };
+
+// Shared memory of each epilogue warp: two 4 KB boxes of [32 rows × 32
+// fp32], 128-byte swizzled and 1024-byte aligned, for TMA stores (one is
+// filled while the store of the other still reads it); the QKV epilogue
+// uses the first 4.2 KB as a padded [32 × 33] transpose block. The stage
+// ring comes first, then these 4 × 8 KB, then the mbarriers.
+constexpr uint32_t kEpiWarpBytes = 8192;
+constexpr uint32_t kEpiStageBytesAll = 4 * kEpiWarpBytes;
 
 // BK fp32 of K per pipeline stage: 32 (128-byte swizzled rows) or 16
 // (64-byte rows: half the bytes per stage, so more stages in flight).
@@ -54,13 +63,12 @@ struct Cfg {
   static constexpr uint32_t kBBytes = BN * BK * 4;
   static constexpr uint32_t kStageBytes = kABytes * (kAlo ? 2 : 1) + kBBytes * (SB ? 2 : 1);
   static constexpr uint32_t kTmaBytes = kStageBytes - (CV ? kABytes : 0);
-  // per epilogue warp a padded [32 × 33] fp32 block for row-contiguous stores
-  static constexpr uint32_t kEpiStageBytes = 4 * 32 * 33 * 4;
+  static constexpr uint32_t kEpiStageBytes = kEpiStageBytesAll;
   static constexpr int kStagesRaw = (kSmemLimit - 2048 - int(kEpiStageBytes)) / kStageBytes;
   static constexpr int kMaxStages = BK == 16 ? 8 : 6;
   static constexpr int kStages = kStagesRaw > kMaxStages ? kMaxStages : kStagesRaw;
   static constexpr uint32_t kTmemCols = 2 * BN;
-  static constexpr size_t kSmemBytes = 1024 + size_t(kStages) * kStageBytes + 256 + kEpiStageBytes;
+  static constexpr size_t kSmemBytes = 1024 + size_t(kStages) * kStageBytes + kEpiStageBytes + 256;
   static_assert(kStages >= 2, "tile too large for shared memory");
   static_assert(BK == 16 || BK == 32, "stage depth");
 };
@@ -199,9 +207,12 @@ __device__ __forceinline__ void qkv_attn_epilogue(const GemmEpilogue& e, uint32_
     const bool is_q = tn < Hq;
     const float* const g = is_q ? e.qgain : e.kgain;
     const float eps = e.eps;
+    // position-minor tables: the warp's 32 consecutive rows read one
+    // 128-byte segment per column instead of 32 scattered words
     const int t = row % T;
-    const float* const cs = e.rope_cos + int64_t(t) * H2;
-    const float* const sn = e.rope_sin + int64_t(t) * H2;
+    const int64_t rld = e.rope_ld;
+    const float* const cs = e.rope_cos + t;
+    const float* const sn = e.rope_sin + t;
     __nv_bfloat16* const hi = static_cast<__nv_bfloat16*>(is_q ? e.q_hi : e.k_hi);
     __nv_bfloat16* const lo = static_cast<__nv_bfloat16*>(is_q ? e.q_lo : e.k_lo);
     const int width = (is_q ? Hq : Hkv) * D;
@@ -238,7 +249,7 @@ __device__ __forceinline__ void qkv_attn_epilogue(const GemmEpilogue& e, uint32_
         const int i = c0 + j;
         const float x1 = __fmul_rn(__fmul_rn(__fmul_rn(__uint_as_float(ra[j]), rs), inv), g[i]);
         const float x2 = __fmul_rn(__fmul_rn(__fmul_rn(__uint_as_float(rb[j]), rs), inv), g[i + H2]);
-        const float c = row_ok ? cs[i] : 0.f, s = row_ok ? sn[i] : 0.f;
+        const float c = row_ok ? cs[i * rld] : 0.f, s = row_ok ? sn[i * rld] : 0.f;
         y1[j] = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
         y2[j] = __fadd_rn(__fmul_rn(x1, s), __fmul_rn(x2, c));
       }
@@ -266,10 +277,147 @@ __device__ __forceinline__ void qkv_attn_epilogue(const GemmEpilogue& e, uint32_
   }
 }
 
+// An epilogue warp's staging area (kEpiWarpBytes) and the number of TMA
+// store boxes it has issued (selects which of the two boxes is filled next).
+struct EpiStage {
+  uint8_t* base;
+  int n;
+};
+
+// The warp's [32 rows × 32 columns] fp32 block (row `lane` in v) written to
+// global memory at (row0, col0) by one TMA store: every lane puts its row
+// into the next 128-byte-swizzled staging box (16-byte chunk c of row r at
+// chunk c ^ (r % 8), conflict-free), then lane 0 issues the store, which
+// writes whole rows of 128 bytes and drops what lies outside the tensor.
+__device__ __forceinline__ void store_box_tma(const CUtensorMap* map, EpiStage& es, const float (&v)[32],
+                                              int col0, int row0, bool inside) {
+  const int lane = threadIdx.x & 31;
+  uint8_t* buf = es.base + (es.n & 1) * 4096;
+  if (lane == 0) tma_store_wait_read<1>();  // the store that last read this box is done with it
+  __syncwarp();
+  float4* rowp = reinterpret_cast<float4*>(buf + lane * 128);
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    rowp[c ^ (lane & 7)] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+  fence_proxy_async_smem();  // generic-proxy writes → visible to the TMA engine
+  __syncwarp();
+  if (lane == 0 && inside) {
+    tma_store_2d(map, smem_u32(buf), col0, row0);
+    tma_store_commit();
+  }
+  ++es.n;
+}
+
+// One accumulator tile through the epilogue, by one of the four epilogue
+// warps: its 32 TMEM lanes at `taddr` (BN columns) hold output rows
+// row0 .. row0+31 of N-tile tn. Results go out by TMA stores when the
+// launch prepared maps for them (p.tma_out / p.tma_out_lo), else by direct
+// row stores.
+template <int BN>
+__device__ __forceinline__ void epilogue_tile(const KParams& p, const CUtensorMap& mOut,
+                                              const CUtensorMap& mOutLo, uint32_t taddr, int row0,
+                                              int tn, EpiStage& es) {
+  const GemmEpilogue& e = p.e;
+  // Fields in registers: read through the reference they would be re-read
+  // after every global store (the stores might alias them).
+  float* const out = e.out;
+  const int64_t ldo = e.ldo;
+  float* const out_lo = e.out_lo;
+  const int64_t ldo_lo = e.ldo_lo;
+  const float* const rowscale = e.rowscale;
+  const float* const bias = e.bias;
+  const float* const mul = e.mul;
+  const int64_t ldm = e.ldm;
+  const float* const resid = e.residual;
+  const int64_t ldr = e.ldr;
+  const int act = e.act;
+  const bool geglu = e.geglu != 0;
+  const bool qkv = BN == 256 && e.qkv_attn != 0;
+  const bool plain = !bias && !mul && !resid && act == FG_ACT_NONE;
+  const bool tma = p.tma_out != 0, tma_lo = p.tma_out_lo != 0;
+  const int Nout = p.Nout, M = p.M;
+  const bool vec_out = (ldo % 4 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
+  const bool vec_lo = out_lo && (ldo_lo % 4 == 0) && ((reinterpret_cast<uintptr_t>(out_lo) & 15) == 0);
+  const int row = row0 + int(threadIdx.x & 31);
+  const bool row_ok = row < M;
+  const int rows = max(0, min(32, M - row0));
+  const float rs = (rowscale && row_ok) ? rowscale[row] : 1.f;
+  if (qkv) {
+    qkv_attn_epilogue(e, taddr, tn, row, row_ok, rs, reinterpret_cast<float*>(es.base), rows);
+  } else if (geglu) {
+    // Tile columns [0, BN/2) are gate, [BN/2, BN) the matching up columns.
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN / 2; c0 += 32) {
+      uint32_t rg[32], ru[32];
+      tmem_ld_32x32b_x32(taddr + uint32_t(c0), rg);
+      tmem_ld_32x32b_x32(taddr + uint32_t(BN / 2 + c0), ru);
+      tmem_ld_wait();
+      const int col0 = tn * (BN / 2) + c0;
+      const int ncols = min(32, Nout - col0);
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float g = __uint_as_float(rg[j]) * rs;
+        const float u = __uint_as_float(ru[j]) * rs;
+        v[j] = gelu_tanh(g) * u;
+      }
+      if (tma) store_box_tma(&mOut, es, v, col0, row0, ncols > 0 && rows > 0);
+      else if (row_ok && ncols > 0) store_row32(out + int64_t(row) * ldo + col0, v, ncols, vec_out);
+      if (out_lo) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = tf32_lo(v[j]);
+        if (tma_lo) store_box_tma(&mOutLo, es, v, col0, row0, ncols > 0 && rows > 0);
+        else if (row_ok && ncols > 0) store_row32(out_lo + int64_t(row) * ldo_lo + col0, v, ncols, vec_lo);
+      }
+    }
+  } else {
+#pragma unroll 1
+    for (int h0 = 0; h0 < BN; h0 += 64) {
+      uint32_t r[2][32];
+      tmem_ld_32x32b_x32(taddr + uint32_t(h0), r[0]);
+      tmem_ld_32x32b_x32(taddr + uint32_t(h0 + 32), r[1]);
+      tmem_ld_wait();
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int col0 = tn * BN + h0 + 32 * q;
+        const int ncols = min(32, Nout - col0);
+        if (ncols <= 0) break;  // warp-uniform
+        float v[32];
+        if (plain) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[q][j]) * rs;
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float x = __uint_as_float(r[q][j]);
+            const int col = col0 + j;
+            const bool in = row_ok && j < ncols;
+            if (bias && j < ncols) x = x + bias[col];
+            x = x * rs;
+            x = apply_act(x, act);
+            if (mul && in) x = x * mul[int64_t(row) * ldm + col];
+            if (resid && in) x = x + resid[int64_t(row) * ldr + col];
+            v[j] = x;
+          }
+        }
+        if (tma) store_box_tma(&mOut, es, v, col0, row0, rows > 0);
+        else if (row_ok) store_row32(out + int64_t(row) * ldo + col0, v, ncols, vec_out);
+        if (out_lo) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = tf32_lo(v[j]);
+          if (tma_lo) store_box_tma(&mOutLo, es, v, col0, row0, rows > 0);
+          else if (row_ok) store_row32(out_lo + int64_t(row) * ldo_lo + col0, v, ncols, vec_lo);
+        }
+      }
+    }
+  }
+}
+
 template <int BN, bool SA, bool SB, int BK, bool CV>
 __global__ void __launch_bounds__(Cfg<BN, SA, SB, BK, CV>::kThreads, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mAlo,
                      const __grid_constant__ CUtensorMap mB, const __grid_constant__ CUtensorMap mBlo,
+                     const __grid_constant__ CUtensorMap mOut, const __grid_constant__ CUtensorMap mOutLo,
                      const __grid_constant__ KParams p) {
   using C = Cfg<BN, SA, SB, BK, CV>;
   constexpr int S = C::kStages;
@@ -278,7 +426,8 @@ __global__ void __launch_bounds__(Cfg<BN, SA, SB, BK, CV>::kThreads, 1)
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + size_t(S) * C::kStageBytes);
+  uint8_t* epi_smem = smem + size_t(S) * C::kStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(epi_smem + C::kEpiStageBytes);
   // bars[0..S) full, [S..2S) empty, [2S..2S+2) acc_full, [2S+2..2S+4) acc_empty,
   // [2S+4] drain, [2S+5..3S+5) A low part converted
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 3 * S + 5);
@@ -472,27 +621,7 @@ __global__ void __launch_bounds__(Cfg<BN, SA, SB, BK, CV>::kThreads, 1)
   } else {
     // -------------------------------------------------- epilogue (warps 2..5)
     const int quad = warp & 3;
-    const GemmEpilogue& e = p.e;
-    float* st = reinterpret_cast<float*>(smem + size_t(S) * C::kStageBytes + 256) + (warp - 2) * 32 * 33;
-    // Fields in registers: read through the reference they would be re-read
-    // after every global store (the stores might alias them).
-    float* const out = e.out;
-    const int64_t ldo = e.ldo;
-    float* const out_lo = e.out_lo;
-    const int64_t ldo_lo = e.ldo_lo;
-    const float* const rowscale = e.rowscale;
-    const float* const bias = e.bias;
-    const float* const mul = e.mul;
-    const int64_t ldm = e.ldm;
-    const float* const resid = e.residual;
-    const int64_t ldr = e.ldr;
-    const int act = e.act;
-    const bool geglu = e.geglu != 0;
-    const bool qkv = BN == 256 && e.qkv_attn != 0;
-    const bool plain = !bias && !mul && !resid && act == FG_ACT_NONE;
-    const int Nout = p.Nout;
-    const bool vec_out = (ldo % 4 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15) == 0);
-    const bool vec_lo = out_lo && (ldo_lo % 4 == 0) && ((reinterpret_cast<uintptr_t>(out_lo) & 15) == 0);
+    EpiStage es{epi_smem + size_t(warp - 2) * kEpiWarpBytes, 0};
     int local = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++local) {
       const int acc = local & 1;
@@ -501,82 +630,13 @@ __global__ void __launch_bounds__(Cfg<BN, SA, SB, BK, CV>::kThreads, 1)
       if (!__all_sync(0xffffffffu, got)) break;  // warp-uniform before the collective tcgen05.ld
       tc_fence_after();
       const int tm = tile / p.ntn, tn = tile % p.ntn;
-      const int row0 = tm * kBM + quad * 32;  // the warp's first row
-      const int row = row0 + lane;
-      const bool row_ok = row < p.M;
-      const int rows = max(0, min(32, p.M - row0));
-      const float rs = (rowscale && row_ok) ? rowscale[row] : 1.f;
       const uint32_t taddr = tmem_base + (uint32_t(quad * 32) << 16) + uint32_t(acc * BN);
-      if (qkv) {
-        qkv_attn_epilogue(e, taddr, tn, row, row_ok, rs, st, rows);
-      } else if (geglu) {
-        // Tile columns [0, BN/2) are gate, [BN/2, BN) the matching up columns.
-#pragma unroll 1
-        for (int c0 = 0; c0 < BN / 2; c0 += 32) {
-          uint32_t rg[32], ru[32];
-          tmem_ld_32x32b_x32(taddr + uint32_t(c0), rg);
-          tmem_ld_32x32b_x32(taddr + uint32_t(BN / 2 + c0), ru);
-          tmem_ld_wait();
-          const int col0 = tn * (BN / 2) + c0;
-          const int ncols = min(32, Nout - col0);
-          if (row_ok && ncols > 0) {
-            float v[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float g = __uint_as_float(rg[j]) * rs;
-              const float u = __uint_as_float(ru[j]) * rs;
-              v[j] = gelu_tanh(g) * u;
-            }
-            store_row32(out + int64_t(row) * ldo + col0, v, ncols, vec_out);
-            if (out_lo) {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = tf32_lo(v[j]);
-              store_row32(out_lo + int64_t(row) * ldo_lo + col0, v, ncols, vec_lo);
-            }
-          }
-        }
-      } else {
-#pragma unroll 1
-        for (int h0 = 0; h0 < BN; h0 += 64) {
-          uint32_t r[2][32];
-          tmem_ld_32x32b_x32(taddr + uint32_t(h0), r[0]);
-          tmem_ld_32x32b_x32(taddr + uint32_t(h0 + 32), r[1]);
-          tmem_ld_wait();
-          if (!row_ok) continue;
-#pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            const int col0 = tn * BN + h0 + 32 * q;
-            const int ncols = min(32, Nout - col0);
-            if (ncols <= 0) break;
-            float v[32];
-            if (plain) {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[q][j]) * rs;
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                float x = __uint_as_float(r[q][j]);
-                const int col = col0 + j;
-                if (bias && j < ncols) x = x + bias[col];
-                x = x * rs;
-                x = apply_act(x, act);
-                if (mul && j < ncols) x = x * mul[int64_t(row) * ldm + col];
-                if (resid && j < ncols) x = x + resid[int64_t(row) * ldr + col];
-                v[j] = x;
-              }
-            }
-            store_row32(out + int64_t(row) * ldo + col0, v, ncols, vec_out);
-            if (out_lo) {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = tf32_lo(v[j]);
-              store_row32(out_lo + int64_t(row) * ldo_lo + col0, v, ncols, vec_lo);
-            }
-          }
-        }
-      }
+      epilogue_tile<BN>(p, mOut, mOutLo, taddr, tm * kBM + quad * 32, tn, es);
       tc_fence_before();
       mbar_arrive(acce_bar(acc));
     }
+    if (lane == 0) tma_store_wait_all();  // stores done before the CTA's shared memory goes away
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -585,6 +645,258 @@ __global__ void __launch_bounds__(Cfg<BN, SA, SB, BK, CV>::kThreads, 1)
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+// ------------------------------------------------------- CTA-pair kernel
+// The same GEMM on pairs of SMs (a cluster of two CTAs) with the pair MMA
+// (tcgen05.mma.cta_group::2, M = 256, N = 256): each CTA loads its 128 rows
+// of the A tile and its 128 rows of the 256-row B tile, so every B byte is
+// read from shared memory once for 256 output rows instead of 128. That
+// halves the B operand traffic through shared memory, which is what limits
+// the single-CTA kernel (A, A_lo and B reads by the tensor core plus the
+// TMA and converter traffic exceed the shared-memory bandwidth).
+//   warp 0      both CTAs: TMA producer into the CTA's own stage ring
+//   warp 1      both CTAs: TMEM allocation (pair); even CTA: MMA issuer
+//   warps 2..5  both CTAs: epilogue of the CTA's 128 accumulator rows
+//   warps 6..9  both CTAs: A_lo converter (CV) and stage-ready signal to
+//               the even CTA, whose MMA thread waits for both halves
+// Only TMA loads without multicast are used; the MMA completion is
+// signalled to both CTAs by a multicast tcgen05.commit.
+template <bool CV>
+struct PairCfg {
+  static constexpr int BN = 256, BK = 32;
+  static constexpr int kThreads = 320;
+  static constexpr uint32_t kABytes = 128 * BK * 4;  // this CTA's A rows
+  static constexpr uint32_t kBBytes = 128 * BK * 4;  // this CTA's half of the B rows
+  static constexpr uint32_t kStageBytes = kABytes * (CV ? 2 : 1) + kBBytes;
+  static constexpr uint32_t kTmaBytes = kABytes + kBBytes;
+  static constexpr uint32_t kEpiStageBytes = kEpiStageBytesAll;
+  static constexpr int kStagesRaw = (kSmemLimit - 2048 - int(kEpiStageBytes)) / kStageBytes;
+  static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
+  static constexpr uint32_t kTmemCols = 512;  // two 256-column accumulators
+  static constexpr size_t kSmemBytes = 1024 + size_t(kStages) * kStageBytes + kEpiStageBytes + 256;
+  static_assert(kStages >= 3, "stage ring too shallow");
+};
+
+template <bool CV>
+__global__ void __launch_bounds__(320, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mB,
+                     const __grid_constant__ CUtensorMap mOut, const __grid_constant__ CUtensorMap mOutLo,
+                     const __grid_constant__ KParams p) {
+  using C = PairCfg<CV>;
+  constexpr int S = C::kStages;
+  constexpr int BN = C::BN, BK = C::BK;
+  constexpr uint32_t kIdesc = idesc_tf32(256, BN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* epi_smem = smem + size_t(S) * C::kStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(epi_smem + C::kEpiStageBytes);
+  // bars[0..S) full (local TMA), [S..2S) empty, [2S..3S) ready (even CTA),
+  // [3S..3S+2) acc_full, [3S+2..3S+4) acc_empty (even CTA), [3S+4] drain
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 3 * S + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = int(blockIdx.x >> 1), npairs = int(gridDim.x >> 1);
+  const int ntiles = p.ntm * p.ntn;
+
+  auto full_bar = [&](int s) { return smem_u32(&bars[s]); };
+  auto empty_bar = [&](int s) { return smem_u32(&bars[S + s]); };
+  auto ready_bar = [&](int s) { return smem_u32(&bars[2 * S + s]); };
+  auto accf_bar = [&](int a) { return smem_u32(&bars[3 * S + a]); };
+  auto acce_bar = [&](int a) { return smem_u32(&bars[3 * S + 2 + a]); };
+  const uint32_t drain_bar = smem_u32(&bars[3 * S + 4]);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+      mbar_init(ready_bar(s), 8);  // 4 converter warps in each CTA
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(accf_bar(a), 1);
+      mbar_init(acce_bar(a), 8);  // 4 epilogue warps in each CTA
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&mA);
+    tma_prefetch_desc(&mB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_holder), C::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers initialised before any cross-CTA arrive
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------ TMA producer
+      int armed[S];
+#pragma unroll
+      for (int s = 0; s < S; ++s) armed[s] = 0;
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = pair; tile < ntiles && !*abort_flag; tile += npairs) {
+        const int tm = tile / p.ntn, tn = tile % p.ntn;
+        const int arow = tm * 256 + int(rank) * 128, brow = tn * BN + int(rank) * 128;
+        for (int kb = 0; kb < p.nk; ++kb) {
+          if (!mbar_wait_cluster(empty_bar(stage), phase ^ 1, abort_flag, p.err, kDevTimeoutEmpty)) break;
+          const uint32_t fb = full_bar(stage);
+          mbar_arrive_expect_tx(fb, C::kTmaBytes);
+          armed[stage]++;
+          const uint32_t dst = smem_u32(smem + size_t(stage) * C::kStageBytes);
+          tma_load_2d(dst, &mA, fb, kb * BK, arow);
+          tma_load_2d(dst + C::kABytes * (CV ? 2 : 1), &mB, fb, kb * BK, brow);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (*abort_flag) {
+        // Let every load this thread issued land before the CTA retires.
+        for (int s = 0; s < S; ++s) {
+          if (armed[s] == 0) continue;
+          const uint32_t par = uint32_t(armed[s] - 1) & 1u;
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(full_bar(s), par)) {
+            if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+              atomicCAS(p.err, 0, kDevTimeoutDrain);
+              break;
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ------------------------------------------------ MMA issuer (even CTA)
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool issued = false;
+      for (int tile = pair; tile < ntiles && !*abort_flag; tile += npairs, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_par = uint32_t(local >> 1) & 1u;
+        if (!mbar_wait_cluster(acce_bar(acc), acc_par ^ 1, abort_flag, p.err, kDevTimeoutAccEmpty)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + uint32_t(acc * BN);
+        bool ok = true;
+        for (int kb = 0; kb < p.nk; ++kb) {
+          if (!mbar_wait_cluster(ready_bar(stage), phase, abort_flag, p.err, kDevTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + size_t(stage) * C::kStageBytes);
+          const uint32_t alo_addr = a_addr + C::kABytes;
+          const uint32_t b_addr = a_addr + C::kABytes * (CV ? 2 : 1);
+#pragma unroll
+          for (int k = 0; k < BK / kUmmaK; ++k) {
+            const uint32_t koff = uint32_t(k * kUmmaK * 4);
+            mma_tf32_pair(d_tmem, kmajor_desc<128>(a_addr + koff), kmajor_desc<128>(b_addr + koff), kIdesc,
+                          (kb | k) != 0 ? 1u : 0u);
+          }
+          if (CV) {
+#pragma unroll
+            for (int k = 0; k < BK / kUmmaK; ++k) {
+              const uint32_t koff = uint32_t(k * kUmmaK * 4);
+              mma_tf32_pair(d_tmem, kmajor_desc<128>(alo_addr + koff), kmajor_desc<128>(b_addr + koff),
+                            kIdesc, 1u);
+            }
+          }
+          issued = true;
+          mma_commit_pair(empty_bar(stage), 0x3);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit_pair(accf_bar(acc), 0x3);
+      }
+      if (issued) {
+        // Every pair MMA issued above must finish before TMEM is released.
+        mma_commit_pair(drain_bar, 0x1);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(drain_bar, 0)) {
+          if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+            atomicCAS(p.err, 0, kDevTimeoutDrain);
+            break;
+          }
+        }
+      }
+    }
+  } else if (warp >= 6) {
+    // -------------------------------------------------- converters (warps 6..9)
+    const int ct = threadIdx.x - 192;  // 0..127
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int tile = pair; tile < ntiles && !*abort_flag; tile += npairs) {
+      bool ok = true;
+      for (int kb = 0; kb < p.nk; ++kb) {
+        if (!mbar_wait(full_bar(stage), phase, abort_flag, p.err, kDevTimeoutFull)) {
+          ok = false;
+          break;
+        }
+        if (CV) {
+          const float4* src = reinterpret_cast<const float4*>(smem + size_t(stage) * C::kStageBytes);
+          float4* dst = reinterpret_cast<float4*>(smem + size_t(stage) * C::kStageBytes + C::kABytes);
+#pragma unroll
+          for (int q = 0; q < int(C::kABytes / 16 / 128); ++q) {
+            const float4 v = src[q * 128 + ct];
+            dst[q * 128 + ct] = make_float4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
+          }
+          fence_proxy_async_smem();  // generic-proxy writes → visible to the tensor core
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(mapa_shared(ready_bar(stage), 0));
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!ok) break;
+    }
+  } else {
+    // -------------------------------------------------- epilogue (warps 2..5)
+    const int quad = warp & 3;
+    EpiStage es{epi_smem + size_t(warp - 2) * kEpiWarpBytes, 0};
+    int local = 0;
+    for (int tile = pair; tile < ntiles; tile += npairs, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_par = uint32_t(local >> 1) & 1u;
+      const bool got = mbar_wait_cluster(accf_bar(acc), acc_par, abort_flag, p.err, kDevTimeoutAccFull);
+      if (!__all_sync(0xffffffffu, got)) break;  // warp-uniform before the collective tcgen05.ld
+      tc_fence_after();
+      const int tm = tile / p.ntn, tn = tile % p.ntn;
+      const uint32_t taddr = tmem_base + (uint32_t(quad * 32) << 16) + uint32_t(acc * BN);
+      epilogue_tile<BN>(p, mOut, mOutLo, taddr, tm * 256 + int(rank) * 128 + quad * 32, tn, es);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(mapa_shared(acce_bar(acc), 0));
+    }
+    if (lane == 0) tma_store_wait_all();  // stores done before the CTA's shared memory goes away
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA releases TMEM or exits while its pair may still use it
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, C::kTmemCols);
   }
 }
 
@@ -612,14 +924,42 @@ int make_map(CUtensorMap* m, const float* ptr, int64_t rows, int64_t cols, int64
   return FG_OK;
 }
 
+// TMA-store maps for the epilogue's outputs ([32 × 32] fp32 boxes) where the
+// output allows them (16-byte aligned, row stride a multiple of 4 floats);
+// the attention-operand epilogue writes its bf16 parts itself.
+// FG_GEMM_TMA_STORE=0 selects direct row stores everywhere.
+int prepare_out_maps(const GemmArgs& g, KParams& kp, CUtensorMap* mOut, CUtensorMap* mOutLo) {
+  static const bool enabled = [] {
+    const char* v = std::getenv("FG_GEMM_TMA_STORE");
+    return !(v && v[0] == '0');
+  }();
+  auto ok = [](const float* ptr, int64_t ld) {
+    return ptr != nullptr && (reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && ld % 4 == 0;
+  };
+  kp.tma_out = 0;
+  kp.tma_out_lo = 0;
+  if (!enabled || g.epi.qkv_attn) return FG_OK;
+  if (ok(g.epi.out, g.epi.ldo)) {
+    FG_TRY(make_map(mOut, g.epi.out, g.M, kp.Nout, g.epi.ldo, 32, 32));
+    kp.tma_out = 1;
+  }
+  if (ok(g.epi.out_lo, g.epi.ldo_lo)) {
+    FG_TRY(make_map(mOutLo, g.epi.out_lo, g.M, kp.Nout, g.epi.ldo_lo, 32, 32));
+    kp.tma_out_lo = 1;
+  }
+  return FG_OK;
+}
+
 template <int BN, bool SA, bool SB, int BK, bool CV = false>
-int launch_variant(const GemmArgs& g, const KParams& kp, int* dev_err, cudaStream_t stream) {
+int launch_variant(const GemmArgs& g, KParams kp, int* dev_err, cudaStream_t stream) {
   using C = Cfg<BN, SA, SB, BK, CV>;
   CUtensorMap mA, mAlo, mB, mBlo;
   FG_TRY(make_map(&mA, g.A, g.M, g.K, g.lda, kBM, BK));
   FG_TRY(make_map(&mB, g.B, g.Nb, g.K, g.ldb, BN, BK));
   if (SA) FG_TRY(make_map(&mAlo, g.A_lo, g.M, g.K, g.lda, kBM, BK)); else mAlo = mA;
   if (SB) FG_TRY(make_map(&mBlo, g.B_lo, g.Nb, g.K, g.ldb, BN, BK)); else mBlo = mB;
+  CUtensorMap mOut = mA, mOutLo = mA;
+  FG_TRY(prepare_out_maps(g, kp, &mOut, &mOutLo));
   auto kern = gemm_tf32_kernel<BN, SA, SB, BK, CV>;
   static bool attr_set[64] = {false};
   int dev = 0;
@@ -630,10 +970,62 @@ int launch_variant(const GemmArgs& g, const KParams& kp, int* dev_err, cudaStrea
   }
   const int ntiles = kp.ntm * kp.ntn;
   const int grid = std::max(1, std::min(ntiles, sm_count()));
-  kern<<<grid, C::kThreads, C::kSmemBytes, stream>>>(mA, mAlo, mB, mBlo, kp);
+  kern<<<grid, C::kThreads, C::kSmemBytes, stream>>>(mA, mAlo, mB, mBlo, mOut, mOutLo, kp);
   FG_CUDA_TRY(cudaGetLastError());
   (void)dev_err;
   return FG_OK;
+}
+
+// CTA-pair kernel: 256-row M tiles, 256-column N tiles.
+template <bool CV>
+int launch_pair(const GemmArgs& g, KParams kp, int* dev_err, cudaStream_t stream) {
+  using C = PairCfg<CV>;
+  CUtensorMap mA, mB;
+  FG_TRY(make_map(&mA, g.A, g.M, g.K, g.lda, 128, 32));
+  FG_TRY(make_map(&mB, g.B, g.Nb, g.K, g.ldb, 128, 32));
+  CUtensorMap mOut = mA, mOutLo = mA;
+  FG_TRY(prepare_out_maps(g, kp, &mOut, &mOutLo));
+  kp.ntm = (g.M + 255) / 256;
+  auto kern = gemm_pair_kernel<CV>;
+  static bool attr_set[64] = {false};
+  static int max_pairs[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(C::kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (!attr_set[dev & 63]) {
+    FG_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(C::kSmemBytes)));
+    cfg.gridDim = dim3(2 * (sm_count() / 2));
+    int n = 0;
+    FG_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+    if (n < 1) return set_error(FG_ECUDA, "gemm: no CTA pair of this kernel fits on an SM pair");
+    max_pairs[dev & 63] = n;
+    attr_set[dev & 63] = true;
+  }
+  const int ntiles = kp.ntm * kp.ntn;
+  cfg.gridDim = dim3(2 * std::max(1, std::min(ntiles, max_pairs[dev & 63])));
+  FG_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, mA, mB, mOut, mOutLo, kp));
+  (void)dev_err;
+  return FG_OK;
+}
+
+// Pair kernel for 256-wide N tiles without stored low parts (M of at least
+// one pair tile); FG_GEMM_PAIR=0 selects the single-CTA kernel instead.
+bool use_pair(const GemmArgs& g) {
+  static const bool enabled = [] {
+    const char* v = std::getenv("FG_GEMM_PAIR");
+    return !(v && v[0] == '0');
+  }();
+  return enabled && g.A_lo == nullptr && g.B_lo == nullptr && g.M >= 256;
 }
 
 // A's low part: none (plain TF32), loaded (SA), or computed in shared memory (CV).
@@ -656,14 +1048,16 @@ int dispatch(const GemmArgs& g, KParams& kp, int* dev_err, cudaStream_t stream) 
   if (g.epi.geglu) {
     kp.Nout = g.Nb / 2;
     kp.ntn = g.Nb / 256;
-    return launch_b_mode<256>(g, kp, dev_err, stream);
+  } else {
+    kp.Nout = g.Nb;
+    if (g.Nb <= 128) {
+      kp.ntn = 1;
+      return launch_b_mode<128>(g, kp, dev_err, stream);
+    }
+    kp.ntn = (g.Nb + 255) / 256;
   }
-  kp.Nout = g.Nb;
-  if (g.Nb <= 128) {
-    kp.ntn = 1;
-    return launch_b_mode<128>(g, kp, dev_err, stream);
-  }
-  kp.ntn = (g.Nb + 255) / 256;
+  if (use_pair(g)) return g.a_lo_smem ? launch_pair<true>(g, kp, dev_err, stream)
+                                      : launch_pair<false>(g, kp, dev_err, stream);
   return launch_b_mode<256>(g, kp, dev_err, stream);
 }
 

@@ -82,8 +82,9 @@ struct GemmEpilogue {
   const float* qgain = nullptr;
   const float* kgain = nullptr;
   float eps = 0.f;
-  const float* rope_cos = nullptr;  // [>= T, 128]
+  const float* rope_cos = nullptr;  // position-minor: [128, rope_ld], entry (i, t) at i·rope_ld + t
   const float* rope_sin = nullptr;
+  int64_t rope_ld = 0;              // >= T
   void* q_hi = nullptr;  // bf16 [M, Hq·256]
   void* q_lo = nullptr;
   void* k_hi = nullptr;  // bf16 [M, Hkv·256]

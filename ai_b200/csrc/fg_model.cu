@@ -115,7 +115,8 @@ struct fg_model {
   std::vector<fg::Layer> layers;
   float* final_gain = nullptr;
   std::vector<fg::Dense> dense;
-  std::vector<float*> rope_cos, rope_sin;
+  std::vector<float*> rope_cos, rope_sin;    // [max_tokens, D/2]
+  std::vector<float*> rope_cosT, rope_sinT;  // the same, position-minor [D/2, max_tokens]
   std::vector<double> rope_bases;  // distinct bases, index = Layer::rope
   std::vector<void*> allocations;
 
@@ -325,6 +326,17 @@ int finalize(fg_model* m, int64_t max_tokens) {
       FG_TRY(upload(m, sn, &ds));
       m->rope_cos.push_back(dc);
       m->rope_sin.push_back(ds);
+      const size_t half = size_t(D) / 2, P = size_t(c.max_tokens);
+      std::vector<float> cst(cs.size()), snt(sn.size());
+      for (size_t t = 0; t < P; ++t)
+        for (size_t i = 0; i < half; ++i) {
+          cst[i * P + t] = cs[t * half + i];
+          snt[i * P + t] = sn[t * half + i];
+        }
+      FG_TRY(upload(m, cst, &dc));
+      FG_TRY(upload(m, snt, &ds));
+      m->rope_cosT.push_back(dc);
+      m->rope_sinT.push_back(ds);
     }
   }
 
@@ -538,8 +550,9 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
       g.epi.qgain = L.qgain;
       g.epi.kgain = L.kgain;
       g.epi.eps = c.rms_norm_eps;
-      g.epi.rope_cos = m->rope_cos[L.rope];
-      g.epi.rope_sin = m->rope_sin[L.rope];
+      g.epi.rope_cos = m->rope_cosT[L.rope];
+      g.epi.rope_sin = m->rope_sinT[L.rope];
+      g.epi.rope_ld = c.max_tokens;
       g.epi.q_hi = ops.q_hi;
       g.epi.q_lo = ops.q_lo;
       g.epi.k_hi = ops.k_hi;

@@ -88,6 +88,25 @@ def test_tf32_operands_are_truncated_by_the_tensor_core(cuda):
     assert np.array_equal(r1, r2), np.abs(r1 - r2).max()
 
 
+@pytest.mark.parametrize("m,k,n", [(256, 64, 256), (1000, 768, 768), (600, 256, 1280),
+                                   (513, 32, 2304), (300, 1152, 300)])
+def test_matmul_plain_tf32_equals_truncated_product(cuda, m, k, n):
+    """Plain TF32 with M >= 256 and N > 128 runs on SM pairs (256-row
+    tiles, ragged M and N edges included); the result is the float64
+    product of the TF32-truncated operands up to fp32 accumulation."""
+    from ai_b200 import tensor as T
+
+    rng = np.random.default_rng(11)
+    a = rng.standard_normal((m, k), dtype=np.float32)
+    w = rng.standard_normal((k, n), dtype=np.float32)
+    trunc = lambda v: (v.view(np.uint32) & np.uint32(0xFFFFE000)).view(np.float32)
+    want = trunc(a).astype(np.float64) @ trunc(w).astype(np.float64)
+    wt = _t(w.T.copy(), cuda).t()  # K-major weights: no copy on the way in
+    got = T.MatMul(_t(a, cuda), wt, precision=T.PREC_TF32).cpu().numpy()
+    ok = _gemm_tol(got, want, a, w)
+    assert ok.all(), f"max err {np.abs(got - want).max()} at {np.argwhere(~ok)[:3]}"
+
+
 def _gelu64(x):
     return 0.5 * x * (1 + np.tanh(0.7978845608028654 * (x + 0.044715 * x ** 3)))
 
@@ -112,6 +131,32 @@ def test_matmul_fused_epilogue_order(cuda, act):
     f = T.Fused(Bias=_t(bias, cuda), Act=act, Mul=_t(mul, cuda), RowScale=_t(rs, cuda),
                 Residual=_t(res, cuda))
     got = T.MatMulFused(_t(a, cuda), _t(w, cuda), f).cpu().numpy()
+    assert np.allclose(got, want, rtol=1e-4, atol=1e-4), np.abs(got - want).max()
+
+
+@pytest.mark.parametrize("act", [0, 1, 2])
+def test_matmul_fused_epilogue_on_sm_pairs(cuda, act):
+    """The same epilogue on the SM-pair kernel (plain TF32, M >= 256): each
+    CTA of a pair applies it to its own 128 rows of the 256-row tile."""
+    from ai_b200 import tensor as T
+
+    rng = np.random.default_rng(8)
+    m, k, n = 700, 96, 520
+    trunc = lambda v: (v.view(np.uint32) & np.uint32(0xFFFFE000)).view(np.float32)
+    a = rng.standard_normal((m, k), dtype=np.float32)
+    w = rng.standard_normal((k, n), dtype=np.float32)
+    bias = rng.standard_normal(n, dtype=np.float32)
+    rs = rng.uniform(0.5, 2, m).astype(np.float32)
+    mul = rng.standard_normal((m, n), dtype=np.float32)
+    res = rng.standard_normal((m, n), dtype=np.float32)
+    y = trunc(a).astype(np.float64) @ trunc(w).astype(np.float64) + bias
+    y = y * rs[:, None]
+    y = [y, np.maximum(y, 0), _gelu64(y)][act]
+    want = y * mul + res
+    f = T.Fused(Bias=_t(bias, cuda), Act=act, Mul=_t(mul, cuda), RowScale=_t(rs, cuda),
+                Residual=_t(res, cuda))
+    wt = _t(w.T.copy(), cuda).t()
+    got = T.MatMulFused(_t(a, cuda), wt, f, precision=T.PREC_TF32).cpu().numpy()
     assert np.allclose(got, want, rtol=1e-4, atol=1e-4), np.abs(got - want).max()
 
 
