@@ -39,7 +39,14 @@ struct KParams {
   int ntm, ntn, nk;
   GemmEpilogue e;
   int* err;
-  int tma_out, tma_out_lo;  // out / out_lo are written by TMA stores (maps mOut / mOutLo)
+  int tma_out, tma_out_lo;  // out / out_lo are written by TMA stores (maps m[0] / m[1])
+  int tma_qk;               // q / k attention operands are written by TMA stores (maps m[0..3])
+};
+
+// TMA-store maps of the epilogue outputs: fp32 out / out_lo in m[0] / m[1];
+// for the attention-operand epilogue the bf16 q_hi, q_lo, k_hi, k_lo.
+struct OutMaps {
+  CUtensorMap m[4];
 };
 
 // Shared memory of each epilogue warp: two 4 KB boxes of [32 rows × 32
@@ -189,6 +196,34 @@ __device__ __forceinline__ void tmem_ld4(uint32_t taddr, int c0, int c1, int c2,
   tmem_ld_wait();
 }
 
+// An epilogue warp's staging area (kEpiWarpBytes) and the number of TMA
+// store boxes it has issued (selects which of the two boxes is filled next).
+struct EpiStage {
+  uint8_t* base;
+  int n;
+};
+
+// bf16 parts of two fp32 values y0, y1, packed into a word each (y0 in the
+// low half): hi = RN(y), lo = RN(y - hi).
+__device__ __forceinline__ void split_pack_pair(float y0, float y1, uint32_t& hw, uint32_t& lw) {
+  const __nv_bfloat16 h0 = __float2bfloat16_rn(y0), h1 = __float2bfloat16_rn(y1);
+  const __nv_bfloat16 l0 = __float2bfloat16_rn(y0 - __bfloat162float(h0));
+  const __nv_bfloat16 l1 = __float2bfloat16_rn(y1 - __bfloat162float(h1));
+  hw = uint32_t(__bfloat16_as_ushort(h0)) | (uint32_t(__bfloat16_as_ushort(h1)) << 16);
+  lw = uint32_t(__bfloat16_as_ushort(l0)) | (uint32_t(__bfloat16_as_ushort(l1)) << 16);
+}
+
+// Half `hf` (16 bf16 = 32 bytes) of row `lane` of a [32 rows × 32 bf16] TMA
+// box with 64-byte swizzling: 16-byte chunk c of row r sits at chunk
+// c ^ ((r / 2) % 4), which spreads eight consecutive rows over all banks.
+__device__ __forceinline__ void put_half_row_bf16_sw64(uint8_t* box, int hf, const uint32_t (&w)[8]) {
+  const int lane = threadIdx.x & 31;
+  uint4* rowp = reinterpret_cast<uint4*>(box + lane * 64);
+  const int sw = (lane >> 1) & 3;
+  rowp[(2 * hf) ^ sw] = make_uint4(w[0], w[1], w[2], w[3]);
+  rowp[(2 * hf + 1) ^ sw] = make_uint4(w[4], w[5], w[6], w[7]);
+}
+
 // Epilogue of the QKV projection when it feeds the tensor-core attention:
 // the accumulator tile is one head (256 columns). q/k heads: y = rs·acc,
 // per-head RMSNorm with gain (attention.go:312-337: v·inv·g, inv from the
@@ -196,9 +231,10 @@ __device__ __forceinline__ void tmem_ld4(uint32_t taddr, int c0, int c1, int c2,
 // (rope.go:66-87), then bf16 hi/lo parts, token-major. v heads: rs·acc as
 // bf16 hi/lo written transposed per sequence (vt[(b·Hkv+hk)·256 + d][t]).
 // tcgen05.ld is warp-collective, so every lane loads even for rows ≥ M.
-__device__ __forceinline__ void qkv_attn_epilogue(const GemmEpilogue& e, uint32_t taddr, int tn,
-                                                  int row, bool row_ok, float rs, float* st,
-                                                  int rows) {
+__device__ __forceinline__ void qkv_attn_epilogue(const GemmEpilogue& e, const OutMaps& om, bool tma_qk,
+                                                  uint32_t taddr, int tn, int row, bool row_ok, float rs,
+                                                  EpiStage& es, int rows) {
+  float* const st = reinterpret_cast<float*>(es.base);
   constexpr int D = 256, H2 = 128;
   // Fields in registers: read through the reference they would be re-read
   // after every global store (the stores might alias them).
@@ -243,18 +279,53 @@ __device__ __forceinline__ void qkv_attn_epilogue(const GemmEpilogue& e, uint32_
       tmem_ld_32x32b_x32(taddr + uint32_t(c0), ra);
       tmem_ld_32x32b_x32(taddr + uint32_t(H2 + c0), rb);
       tmem_ld_wait();
-      float y1[32], y2[32];
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
+      // y1 = x1·c - x2·s, y2 = x1·s + x2·c for column j of the chunk
+      auto rot = [&](int j, float& y1, float& y2) {
         const int i = c0 + j;
         const float x1 = __fmul_rn(__fmul_rn(__fmul_rn(__uint_as_float(ra[j]), rs), inv), g[i]);
         const float x2 = __fmul_rn(__fmul_rn(__fmul_rn(__uint_as_float(rb[j]), rs), inv), g[i + H2]);
         const float c = row_ok ? cs[i * rld] : 0.f, s = row_ok ? sn[i * rld] : 0.f;
-        y1[j] = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
-        y2[j] = __fadd_rn(__fmul_rn(x1, s), __fmul_rn(x2, c));
+        y1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
+        y2 = __fadd_rn(__fmul_rn(x1, s), __fmul_rn(x2, c));
+      };
+      if (tma_qk) {
+        // four [32 × 32] bf16 boxes: y1 hi, y1 lo, y2 hi, y2 lo, filled 16 columns at a time
+        if (lane == 0) tma_store_wait_read<0>();  // the previous chunk's stores have read the boxes
+        __syncwarp();
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t w[4][8];  // y1 hi, y1 lo, y2 hi, y2 lo: 16 bf16 each
+#pragma unroll
+          for (int jj = 0; jj < 16; jj += 2) {
+            float a1, a2, b1, b2;
+            rot(hf * 16 + jj, a1, a2);
+            rot(hf * 16 + jj + 1, b1, b2);
+            split_pack_pair(a1, b1, w[0][jj / 2], w[1][jj / 2]);
+            split_pack_pair(a2, b2, w[2][jj / 2], w[3][jj / 2]);
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) put_half_row_bf16_sw64(es.base + q * 2048, hf, w[q]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && rows > 0) {
+          const CUtensorMap* mh = &om.m[is_q ? 0 : 2];
+          const CUtensorMap* ml = &om.m[is_q ? 1 : 3];
+          const uint32_t b = smem_u32(es.base);
+          const int col = head * D + c0, r0 = row - lane;
+          tma_store_2d(mh, b, col, r0);
+          tma_store_2d(ml, b + 2048, col, r0);
+          tma_store_2d(mh, b + 4096, col + H2, r0);
+          tma_store_2d(ml, b + 6144, col + H2, r0);
+          tma_store_commit();
+        }
+      } else {
+        float y1[32], y2[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) rot(j, y1[j], y2[j]);
+        warp_store_block_bf16(st, y1, hi + base0 + c0, lo + base0 + c0, width, rows);
+        warp_store_block_bf16(st, y2, hi + base0 + H2 + c0, lo + base0 + H2 + c0, width, rows);
       }
-      warp_store_block_bf16(st, y1, hi + base0 + c0, lo + base0 + c0, width, rows);
-      warp_store_block_bf16(st, y2, hi + base0 + H2 + c0, lo + base0 + H2 + c0, width, rows);
     }
   } else {
     const int hk = tn - Hq - Hkv;
@@ -276,13 +347,6 @@ __device__ __forceinline__ void qkv_attn_epilogue(const GemmEpilogue& e, uint32_
     }
   }
 }
-
-// An epilogue warp's staging area (kEpiWarpBytes) and the number of TMA
-// store boxes it has issued (selects which of the two boxes is filled next).
-struct EpiStage {
-  uint8_t* base;
-  int n;
-};
 
 // The warp's [32 rows × 32 columns] fp32 block (row `lane` in v) written to
 // global memory at (row0, col0) by one TMA store: every lane puts its row
@@ -314,9 +378,8 @@ __device__ __forceinline__ void store_box_tma(const CUtensorMap* map, EpiStage& 
 // launch prepared maps for them (p.tma_out / p.tma_out_lo), else by direct
 // row stores.
 template <int BN>
-__device__ __forceinline__ void epilogue_tile(const KParams& p, const CUtensorMap& mOut,
-                                              const CUtensorMap& mOutLo, uint32_t taddr, int row0,
-                                              int tn, EpiStage& es) {
+__device__ __forceinline__ void epilogue_tile(const KParams& p, const OutMaps& om, uint32_t taddr,
+                                              int row0, int tn, EpiStage& es) {
   const GemmEpilogue& e = p.e;
   // Fields in registers: read through the reference they would be re-read
   // after every global store (the stores might alias them).
@@ -343,7 +406,7 @@ __device__ __forceinline__ void epilogue_tile(const KParams& p, const CUtensorMa
   const int rows = max(0, min(32, M - row0));
   const float rs = (rowscale && row_ok) ? rowscale[row] : 1.f;
   if (qkv) {
-    qkv_attn_epilogue(e, taddr, tn, row, row_ok, rs, reinterpret_cast<float*>(es.base), rows);
+    qkv_attn_epilogue(e, om, p.tma_qk != 0, taddr, tn, row, row_ok, rs, es, rows);
   } else if (geglu) {
     // Tile columns [0, BN/2) are gate, [BN/2, BN) the matching up columns.
 #pragma unroll 1
@@ -361,12 +424,12 @@ __device__ __forceinline__ void epilogue_tile(const KParams& p, const CUtensorMa
         const float u = __uint_as_float(ru[j]) * rs;
         v[j] = gelu_tanh(g) * u;
       }
-      if (tma) store_box_tma(&mOut, es, v, col0, row0, ncols > 0 && rows > 0);
+      if (tma) store_box_tma(&om.m[0], es, v, col0, row0, ncols > 0 && rows > 0);
       else if (row_ok && ncols > 0) store_row32(out + int64_t(row) * ldo + col0, v, ncols, vec_out);
       if (out_lo) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = tf32_lo(v[j]);
-        if (tma_lo) store_box_tma(&mOutLo, es, v, col0, row0, ncols > 0 && rows > 0);
+        if (tma_lo) store_box_tma(&om.m[1], es, v, col0, row0, ncols > 0 && rows > 0);
         else if (row_ok && ncols > 0) store_row32(out_lo + int64_t(row) * ldo_lo + col0, v, ncols, vec_lo);
       }
     }
@@ -400,12 +463,12 @@ __device__ __forceinline__ void epilogue_tile(const KParams& p, const CUtensorMa
             v[j] = x;
           }
         }
-        if (tma) store_box_tma(&mOut, es, v, col0, row0, rows > 0);
+        if (tma) store_box_tma(&om.m[0], es, v, col0, row0, rows > 0);
         else if (row_ok) store_row32(out + int64_t(row) * ldo + col0, v, ncols, vec_out);
         if (out_lo) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = tf32_lo(v[j]);
-          if (tma_lo) store_box_tma(&mOutLo, es, v, col0, row0, rows > 0);
+          if (tma_lo) store_box_tma(&om.m[1], es, v, col0, row0, rows > 0);
           else if (row_ok) store_row32(out_lo + int64_t(row) * ldo_lo + col0, v, ncols, vec_lo);
         }
       }
@@ -417,7 +480,7 @@ template <int BN, bool SA, bool SB, int BK, bool CV>
 __global__ void __launch_bounds__(Cfg<BN, SA, SB, BK, CV>::kThreads, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mAlo,
                      const __grid_constant__ CUtensorMap mB, const __grid_constant__ CUtensorMap mBlo,
-                     const __grid_constant__ CUtensorMap mOut, const __grid_constant__ CUtensorMap mOutLo,
+                     const __grid_constant__ OutMaps om,
                      const __grid_constant__ KParams p) {
   using C = Cfg<BN, SA, SB, BK, CV>;
   constexpr int S = C::kStages;
@@ -631,7 +694,7 @@ __global__ void __launch_bounds__(Cfg<BN, SA, SB, BK, CV>::kThreads, 1)
       tc_fence_after();
       const int tm = tile / p.ntn, tn = tile % p.ntn;
       const uint32_t taddr = tmem_base + (uint32_t(quad * 32) << 16) + uint32_t(acc * BN);
-      epilogue_tile<BN>(p, mOut, mOutLo, taddr, tm * kBM + quad * 32, tn, es);
+      epilogue_tile<BN>(p, om, taddr, tm * kBM + quad * 32, tn, es);
       tc_fence_before();
       mbar_arrive(acce_bar(acc));
     }
@@ -682,7 +745,7 @@ struct PairCfg {
 template <bool CV>
 __global__ void __launch_bounds__(320, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mB,
-                     const __grid_constant__ CUtensorMap mOut, const __grid_constant__ CUtensorMap mOutLo,
+                     const __grid_constant__ OutMaps om,
                      const __grid_constant__ KParams p) {
   using C = PairCfg<CV>;
   constexpr int S = C::kStages;
@@ -882,7 +945,7 @@ __global__ void __launch_bounds__(320, 1)
       tc_fence_after();
       const int tm = tile / p.ntn, tn = tile % p.ntn;
       const uint32_t taddr = tmem_base + (uint32_t(quad * 32) << 16) + uint32_t(acc * BN);
-      epilogue_tile<BN>(p, mOut, mOutLo, taddr, tm * 256 + int(rank) * 128 + quad * 32, tn, es);
+      epilogue_tile<BN>(p, om, taddr, tm * 256 + int(rank) * 128 + quad * 32, tn, es);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(mapa_shared(acce_bar(acc), 0));
@@ -928,7 +991,20 @@ int make_map(CUtensorMap* m, const float* ptr, int64_t rows, int64_t cols, int64
 // output allows them (16-byte aligned, row stride a multiple of 4 floats);
 // the attention-operand epilogue writes its bf16 parts itself.
 // FG_GEMM_TMA_STORE=0 selects direct row stores everywhere.
-int prepare_out_maps(const GemmArgs& g, KParams& kp, CUtensorMap* mOut, CUtensorMap* mOutLo) {
+// Row-major [rows, cols] bf16 matrix, [32 × 32] boxes with 64-byte swizzling.
+int make_map_bf16(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int64_t ld) {
+  cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(ld) * 2};
+  cuuint32_t box[2] = {32u, 32u};
+  cuuint32_t es[2] = {1u, 1u};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(FG_ECUDA, "cuTensorMapEncodeTiled (bf16) failed (%d)", int(r));
+  return FG_OK;
+}
+
+int prepare_out_maps(const GemmArgs& g, KParams& kp, OutMaps* om) {
   static const bool enabled = [] {
     const char* v = std::getenv("FG_GEMM_TMA_STORE");
     return !(v && v[0] == '0');
@@ -938,13 +1014,27 @@ int prepare_out_maps(const GemmArgs& g, KParams& kp, CUtensorMap* mOut, CUtensor
   };
   kp.tma_out = 0;
   kp.tma_out_lo = 0;
-  if (!enabled || g.epi.qkv_attn) return FG_OK;
+  kp.tma_qk = 0;
+  if (!enabled) return FG_OK;
+  if (g.epi.qkv_attn) {
+    const GemmEpilogue& e = g.epi;
+    const void* ps[4] = {e.q_hi, e.q_lo, e.k_hi, e.k_lo};
+    for (const void* q : ps)
+      if (!q || (reinterpret_cast<uintptr_t>(q) & 15) != 0) return FG_OK;
+    const int64_t wq = int64_t(e.Hq) * 256, wk = int64_t(e.Hkv) * 256;
+    FG_TRY(make_map_bf16(&om->m[0], e.q_hi, g.M, wq, wq));
+    FG_TRY(make_map_bf16(&om->m[1], e.q_lo, g.M, wq, wq));
+    FG_TRY(make_map_bf16(&om->m[2], e.k_hi, g.M, wk, wk));
+    FG_TRY(make_map_bf16(&om->m[3], e.k_lo, g.M, wk, wk));
+    kp.tma_qk = 1;
+    return FG_OK;
+  }
   if (ok(g.epi.out, g.epi.ldo)) {
-    FG_TRY(make_map(mOut, g.epi.out, g.M, kp.Nout, g.epi.ldo, 32, 32));
+    FG_TRY(make_map(&om->m[0], g.epi.out, g.M, kp.Nout, g.epi.ldo, 32, 32));
     kp.tma_out = 1;
   }
   if (ok(g.epi.out_lo, g.epi.ldo_lo)) {
-    FG_TRY(make_map(mOutLo, g.epi.out_lo, g.M, kp.Nout, g.epi.ldo_lo, 32, 32));
+    FG_TRY(make_map(&om->m[1], g.epi.out_lo, g.M, kp.Nout, g.epi.ldo_lo, 32, 32));
     kp.tma_out_lo = 1;
   }
   return FG_OK;
@@ -958,8 +1048,9 @@ int launch_variant(const GemmArgs& g, KParams kp, int* dev_err, cudaStream_t str
   FG_TRY(make_map(&mB, g.B, g.Nb, g.K, g.ldb, BN, BK));
   if (SA) FG_TRY(make_map(&mAlo, g.A_lo, g.M, g.K, g.lda, kBM, BK)); else mAlo = mA;
   if (SB) FG_TRY(make_map(&mBlo, g.B_lo, g.Nb, g.K, g.ldb, BN, BK)); else mBlo = mB;
-  CUtensorMap mOut = mA, mOutLo = mA;
-  FG_TRY(prepare_out_maps(g, kp, &mOut, &mOutLo));
+  OutMaps om;
+  for (CUtensorMap& m : om.m) m = mA;
+  FG_TRY(prepare_out_maps(g, kp, &om));
   auto kern = gemm_tf32_kernel<BN, SA, SB, BK, CV>;
   static bool attr_set[64] = {false};
   int dev = 0;
@@ -970,7 +1061,7 @@ int launch_variant(const GemmArgs& g, KParams kp, int* dev_err, cudaStream_t str
   }
   const int ntiles = kp.ntm * kp.ntn;
   const int grid = std::max(1, std::min(ntiles, sm_count()));
-  kern<<<grid, C::kThreads, C::kSmemBytes, stream>>>(mA, mAlo, mB, mBlo, mOut, mOutLo, kp);
+  kern<<<grid, C::kThreads, C::kSmemBytes, stream>>>(mA, mAlo, mB, mBlo, om, kp);
   FG_CUDA_TRY(cudaGetLastError());
   (void)dev_err;
   return FG_OK;
@@ -983,8 +1074,9 @@ int launch_pair(const GemmArgs& g, KParams kp, int* dev_err, cudaStream_t stream
   CUtensorMap mA, mB;
   FG_TRY(make_map(&mA, g.A, g.M, g.K, g.lda, 128, 32));
   FG_TRY(make_map(&mB, g.B, g.Nb, g.K, g.ldb, 128, 32));
-  CUtensorMap mOut = mA, mOutLo = mA;
-  FG_TRY(prepare_out_maps(g, kp, &mOut, &mOutLo));
+  OutMaps om;
+  for (CUtensorMap& m : om.m) m = mA;
+  FG_TRY(prepare_out_maps(g, kp, &om));
   kp.ntm = (g.M + 255) / 256;
   auto kern = gemm_pair_kernel<CV>;
   static bool attr_set[64] = {false};
@@ -1013,7 +1105,7 @@ int launch_pair(const GemmArgs& g, KParams kp, int* dev_err, cudaStream_t stream
   }
   const int ntiles = kp.ntm * kp.ntn;
   cfg.gridDim = dim3(2 * std::max(1, std::min(ntiles, max_pairs[dev & 63])));
-  FG_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, mA, mB, mOut, mOutLo, kp));
+  FG_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, mA, mB, om, kp));
   (void)dev_err;
   return FG_OK;
 }
