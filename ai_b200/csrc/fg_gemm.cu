@@ -83,12 +83,13 @@ struct Cfg {
 // Eigen's rational tanh for float (the method the reference's kernels use,
 // internal/kernel/generic.go:309-360): odd degree-13 over even degree-6
 // polynomial after clamping to the point where it reaches ±1.
-__device__ __forceinline__ float tanh_rational(float x) {
-  if (x > -0.0004f && x < 0.0004f) return x;
-  if (x >= 9.f) return 1.f;
-  if (x <= -9.f) return -1.f;
+// Written without branches (the rational is always evaluated and the small
+// and saturated cases selected afterwards) so that the epilogue can keep
+// many independent elements in flight; the results are those of the
+// early-return form.
+__device__ __forceinline__ float tanh_rational(float x_in) {
   const float c = 7.99881172180175781f;
-  x = fminf(fmaxf(x, -c), c);
+  const float x = fminf(fmaxf(x_in, -c), c);
   const float x2 = x * x;
   float p = -2.76076847742355e-16f;
   p = p * x2 + 2.00018790482477e-13f;
@@ -102,7 +103,11 @@ __device__ __forceinline__ float tanh_rational(float x) {
   q = q * x2 + 1.18534705686654e-04f;
   q = q * x2 + 2.26843463243900e-03f;
   q = q * x2 + 4.89352518554385e-03f;
-  return p / q;
+  float r = p / q;
+  r = (x_in > -0.0004f && x_in < 0.0004f) ? x_in : r;
+  r = x_in >= 9.f ? 1.f : r;
+  r = x_in <= -9.f ? -1.f : r;
+  return r;
 }
 
 // tanh-GELU in the reference's operation order (internal/kernel/math.go:122-143):
