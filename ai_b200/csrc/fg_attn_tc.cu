@@ -62,6 +62,7 @@ struct Params {
   float* out_lo;
   int64_t osb, osh, ost;
   int* err;
+  int tma_out, tma_out_lo;  // out / out_lo written by TMA stores (maps mO / mOlo)
 };
 
 __device__ __forceinline__ bool waitb(uint32_t bar, uint32_t par, volatile int* ab, int* err, int code) {
@@ -72,7 +73,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap mQ0, const __grid_constant__ CUtensorMap mQ1,
                    const __grid_constant__ CUtensorMap mK0, const __grid_constant__ CUtensorMap mK1,
                    const __grid_constant__ CUtensorMap mV0, const __grid_constant__ CUtensorMap mV1,
-                   const Params p) {
+                   const __grid_constant__ CUtensorMap mO, const __grid_constant__ CUtensorMap mOlo,
+                   const __grid_constant__ Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;                       // [part][chunk] 16 KB each
@@ -329,18 +331,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int q = 0; q < 4; ++q) tmem_ld_32x32b_x32(tS + uint32_t(q * 32), sr[q]);
       tmem_ld_wait();
       const int lo_c = vlo - key0, hi_c = vhi - key0;  // visible columns [lo_c, hi_c)
-      float mt = -FLT_MAX;
-      bool any = false;
+      // row maximum over the visible columns, eight independent chains
+      float mt8[8];
 #pragma unroll
-      for (int q = 0; q < 4; ++q)
+      for (int u = 0; u < 8; ++u) mt8[u] = -FLT_MAX;
+      const bool full_row = lo_c <= 0 && hi_c >= kKT;
+      if (full_row) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int col = q * 32 + e;
-          if (col >= lo_c && col < hi_c) {
-            mt = fmaxf(mt, __uint_as_float(sr[q][e]));
-            any = true;
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) mt8[e & 7] = fmaxf(mt8[e & 7], __uint_as_float(sr[q][e]));
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const int col = q * 32 + e;
+            if (col >= lo_c && col < hi_c) mt8[e & 7] = fmaxf(mt8[e & 7], __uint_as_float(sr[q][e]));
           }
-        }
+      }
+      const float mt = fmaxf(fmaxf(fmaxf(mt8[0], mt8[1]), fmaxf(mt8[2], mt8[3])),
+                             fmaxf(fmaxf(mt8[4], mt8[5]), fmaxf(mt8[6], mt8[7])));
+      const bool any = lo_c < hi_c && lo_c < kKT && hi_c > 0;
       float factor = 1.f;
       if (any) {
         if (!have) {
@@ -375,7 +387,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       l *= factor;
       const float mc = m * c;
       // probabilities, split into packed bf16 hi / lo, written over S
-      float psum = 0.f;
+      float ps8[8];  // eight independent partial sums
+#pragma unroll
+      for (int u = 0; u < 8; ++u) ps8[u] = 0.f;
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         uint32_t hw[16], lw[16];
@@ -386,7 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (have && col >= lo_c && col < hi_c) a = ex2_approx(fmaf(__uint_as_float(sr[q][2 * e]), c, -mc));
           if (have && col + 1 >= lo_c && col + 1 < hi_c)
             bb = ex2_approx(fmaf(__uint_as_float(sr[q][2 * e + 1]), c, -mc));
-          psum += a + bb;
+          ps8[e & 7] += a + bb;
           const float ah = bf16_round_f32(a), bh = bf16_round_f32(bb);
           hw[e] = pack_bf16x2(ah, bh);
           lw[e] = pack_bf16x2(a - ah, bb - bh);
@@ -394,7 +408,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_st_32x32b_x16(tS + uint32_t(q * 16), hw);
         tmem_st_32x32b_x16(tS + uint32_t(64 + q * 16), lw);
       }
-      l += psum;
+      l += ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(bar(9 + sb));
@@ -405,25 +419,71 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const bool row_ok = i < p.T;
       const float inv = (i < qlen && l > 0.f) ? 1.f / l : 0.f;
-      float* o = obase + int64_t(i) * p.ost;
-      float* ol = olbase ? olbase + int64_t(i) * p.ost : nullptr;
+      if (p.tma_out) {
+        // The warp's 32 rows × 256 columns as eight [32 × 32] boxes in its
+        // 32 KB of the Q region (every MMA that read Q has completed), then
+        // TMA stores; rows past the sequence end fall outside the map.
+        uint8_t* stg = sQ + size_t(warp - 2) * 32768;
+        const int tw = i0 + quad * 32;
+        const int parts = olbase ? 2 : 1;
 #pragma unroll 1
-      for (int ch = 0; ch < 8; ++ch) {
-        uint32_t ov[32];
-        tmem_ld_32x32b_x32(tO + lane_off + uint32_t(ch * 32), ov);
-        tmem_ld_wait();
-        if (row_ok) {
-          float4* o4 = reinterpret_cast<float4*>(o + ch * 32);
-          float4* l4 = ol ? reinterpret_cast<float4*>(ol + ch * 32) : nullptr;
+        for (int part = 0; part < parts; ++part) {
+          if (part == 1) {
+            if (lane == 0) tma_store_wait_read<0>();  // the hi boxes have been read
+            __syncwarp();
+          }
+#pragma unroll 1
+          for (int ch = 0; ch < 8; ch += 2) {
+            uint32_t ov[2][32];
+            tmem_ld_32x32b_x32(tO + lane_off + uint32_t(ch * 32), ov[0]);
+            tmem_ld_32x32b_x32(tO + lane_off + uint32_t(ch * 32 + 32), ov[1]);
+            tmem_ld_wait();
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            float4 v;
-            v.x = __uint_as_float(ov[4 * e]) * inv;
-            v.y = __uint_as_float(ov[4 * e + 1]) * inv;
-            v.z = __uint_as_float(ov[4 * e + 2]) * inv;
-            v.w = __uint_as_float(ov[4 * e + 3]) * inv;
-            o4[e] = v;
-            if (l4) l4[e] = make_float4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
+            for (int u = 0; u < 2; ++u) {
+              float4* rowp = reinterpret_cast<float4*>(stg + (ch + u) * 4096 + lane * 128);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                float4 v;
+                v.x = __uint_as_float(ov[u][4 * e]) * inv;
+                v.y = __uint_as_float(ov[u][4 * e + 1]) * inv;
+                v.z = __uint_as_float(ov[u][4 * e + 2]) * inv;
+                v.w = __uint_as_float(ov[u][4 * e + 3]) * inv;
+                if (part == 1) v = make_float4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
+                rowp[e ^ (lane & 7)] = v;  // 128-byte swizzle: chunk e of row r at e ^ (r % 8)
+              }
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && tw < p.T) {
+            for (int ch = 0; ch < 8; ++ch)
+              tma_store_3d(part ? &mOlo : &mO, smem_u32(stg + ch * 4096), h * kD + ch * 32, tw, b);
+            tma_store_commit();
+          }
+        }
+        if (lane == 0) tma_store_wait_all();
+        __syncwarp();
+      } else {
+        float* o = obase + int64_t(i) * p.ost;
+        float* ol = olbase ? olbase + int64_t(i) * p.ost : nullptr;
+#pragma unroll 1
+        for (int ch = 0; ch < 8; ++ch) {
+          uint32_t ov[32];
+          tmem_ld_32x32b_x32(tO + lane_off + uint32_t(ch * 32), ov);
+          tmem_ld_wait();
+          if (row_ok) {
+            float4* o4 = reinterpret_cast<float4*>(o + ch * 32);
+            float4* l4 = ol ? reinterpret_cast<float4*>(ol + ch * 32) : nullptr;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              float4 v;
+              v.x = __uint_as_float(ov[4 * e]) * inv;
+              v.y = __uint_as_float(ov[4 * e + 1]) * inv;
+              v.z = __uint_as_float(ov[4 * e + 2]) * inv;
+              v.w = __uint_as_float(ov[4 * e + 3]) * inv;
+              o4[e] = v;
+              if (l4) l4[e] = make_float4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
+            }
           }
         }
       }
@@ -507,6 +567,20 @@ int make_map_bf16(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, i
   return FG_OK;
 }
 
+// fp32 output viewed as [B][T][cols] (row stride ost, sequence stride osb,
+// in elements), [1 × 32 × 32] boxes with 128-byte swizzling.
+int make_map_out3d(CUtensorMap* m, const float* ptr, int B, int T, int64_t cols, int64_t ost, int64_t osb) {
+  cuuint64_t dims[3] = {cuuint64_t(cols), cuuint64_t(T), cuuint64_t(B)};
+  cuuint64_t strides[2] = {cuuint64_t(ost) * 4, cuuint64_t(osb) * 4};
+  cuuint32_t box[3] = {32u, 32u, 1u};
+  cuuint32_t es[3] = {1u, 1u, 1u};
+  CUresult r = g_encode_bf16(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(ptr), dims, strides, box,
+                             es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(FG_ECUDA, "cuTensorMapEncodeTiled (attention output) failed (%d)", int(r));
+  return FG_OK;
+}
+
 }  // namespace
 
 size_t attn_tc_workspace_bytes(int B, int T, int S, int Hq, int Hkv) {
@@ -576,6 +650,21 @@ int attention_tc_operands(const AttnArgs& a, const AttnOperands& o, int* err, cu
   prm.osh = a.osh;
   prm.ost = a.ost;
   prm.err = err;
+  // Output as a [B][T][cols] tensor with row stride ost: TMA stores when
+  // the heads are contiguous 256-column blocks and the strides allow it.
+  CUtensorMap mo = mq0, mol = mq0;
+  auto tma_ok = [&](const float* ptr) {
+    return ptr && (reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && a.osh == kD && a.ost % 4 == 0 &&
+           a.osb % 4 == 0 && a.ost >= int64_t(Hq) * kD && a.osb >= int64_t(T) * a.ost;
+  };
+  prm.tma_out = 0;
+  prm.tma_out_lo = 0;
+  if (tma_ok(a.out) && (a.out_lo == nullptr || tma_ok(a.out_lo))) {
+    FG_TRY(make_map_out3d(&mo, a.out, B, T, Hq * kD, a.ost, a.osb));
+    if (a.out_lo) FG_TRY(make_map_out3d(&mol, a.out_lo, B, T, Hq * kD, a.ost, a.osb));
+    prm.tma_out = 1;
+    prm.tma_out_lo = a.out_lo ? 1 : 0;
+  }
   static bool attr[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -585,7 +674,7 @@ int attention_tc_operands(const AttnArgs& a, const AttnOperands& o, int* err, cu
   }
   if ((T + kQ - 1) / kQ > 65535 || B > 65535) return set_error(FG_EINVAL, "attention grid too large");
   dim3 grid(unsigned((T + kQ - 1) / kQ), unsigned(Hq), unsigned(B));
-  attn_tc_kernel<<<grid, kThreads, kSmem, s>>>(mq0, mq1, mk0, mk1, mv0, mv1, prm);
+  attn_tc_kernel<<<grid, kThreads, kSmem, s>>>(mq0, mq1, mk0, mk1, mv0, mv1, mo, mol, prm);
   FG_CUDA_TRY(cudaGetLastError());
   return FG_OK;
 }
