@@ -80,9 +80,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sQ = smem;                       // [part][chunk] 16 KB each
   uint8_t* sRing = smem + kQBytes;          // [stage][part] 16 KB each
   uint64_t* bars = reinterpret_cast<uint64_t*>(sRing + kStages * kStageBytes);
-  // bars: 0 q_full | 1..3 kv_full | 4..6 kv_empty | 7,8 s_full | 9,10 p_full |
-  //       11,12 s_free | 13 o_prog | 14 o_final | 15 drain
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 16);
+  // bars: 0 Q d-chunk 0 | 1..3 kv_full | 4..6 kv_empty | 7,8 s_full | 9,10 p_full |
+  //       11,12 s_free | 13 o_prog | 14 o_final | 15 drain | 16..18 Q d-chunks 1..3
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 20);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -116,11 +116,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int ntiles = (kend + kKT - 1) / kKT - kt0;
 
   auto bar = [&](int k) { return smem_u32(&bars[k]); };
-  const uint32_t q_full = bar(0), s_full0 = bar(7), p_full0 = bar(9), s_free0 = bar(11);
+  // Q arrives per 64-column d-chunk (hi and lo), so the first score MMAs
+  // start when their chunk has landed rather than after all 128 KB.
+  auto q_bar = [&](int c) { return c == 0 ? bar(0) : bar(15 + c); };
+  const uint32_t s_full0 = bar(7), p_full0 = bar(9), s_free0 = bar(11);
   const uint32_t o_prog = bar(13), o_final = bar(14), drain = bar(15);
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
+    for (int c = 0; c < 4; ++c) mbar_init(q_bar(c), 1);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(bar(1 + s), 1);
       mbar_init(bar(4 + s), 1);
@@ -153,10 +156,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&mK0);
       tma_prefetch_desc(&mV0);
       const int qrow = b * p.T + i0;
-      mbar_arrive_expect_tx(q_full, kQBytes);
       for (int c = 0; c < 4; ++c) {
-        tma_load_2d(smem_u32(sQ + (0 * 4 + c) * kChunk), &mQ0, q_full, h * kD + c * 64, qrow);
-        tma_load_2d(smem_u32(sQ + (1 * 4 + c) * kChunk), &mQ1, q_full, h * kD + c * 64, qrow);
+        mbar_arrive_expect_tx(q_bar(c), 2 * kChunk);
+        tma_load_2d(smem_u32(sQ + (0 * 4 + c) * kChunk), &mQ0, q_bar(c), h * kD + c * 64, qrow);
+        tma_load_2d(smem_u32(sQ + (1 * 4 + c) * kChunk), &mQ1, q_bar(c), h * kD + c * 64, qrow);
       }
       int armed[kStages] = {0, 0, 0};
       int stage = 0;
@@ -198,9 +201,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           while (!mbar_try_wait(bar(1 + s), uint32_t(armed[s] - 1) & 1u))
             if (globaltimer_ns() - t0 > kWaitTimeoutNs) break;
         }
-        const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(q_full, 0))
-          if (globaltimer_ns() - t0 > kWaitTimeoutNs) break;
+        for (int c = 0; c < 4; ++c) {
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(q_bar(c), 0))
+            if (globaltimer_ns() - t0 > kWaitTimeoutNs) break;
+        }
       }
     }
   } else if (warp == 1) {
@@ -208,9 +213,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ------------------------------------------------------------ MMA issuer
       int stage = 0;
       uint32_t phase = 0;
-      bool ok = waitb(q_full, 0, abort_flag, p.err, kDevTimeoutFull);
+      bool ok = true;
       bool issued = false;
-      tc_fence_after();
       auto pv = [&](int jj) {
         const int sb = jj & 1;
         if (!waitb(bar(9 + sb), uint32_t(jj >> 1) & 1u, abort_flag, p.err, kDevTimeoutAccFull)) return false;
@@ -224,14 +228,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t v1 = v0 + kChunk;
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
-              const uint32_t col = uint32_t(kh * 32 + kk * 8);
+              // keys [16m, 16m + 16): P chunk m / 2, hi at its first 16
+              // columns, lo at the next 16 (see the softmax's pass 2)
+              const int mk = kh * 4 + kk;
+              const uint32_t hcol = uint32_t(32 * (mk >> 1) + 8 * (mk & 1));
               const uint64_t b0 = sw128_kmajor_desc(v0 + kk * 32);
               const uint64_t b1 = sw128_kmajor_desc(v1 + kk * 32);
               const uint32_t d = tO + uint32_t(dh * 128);
               const uint32_t first = (jj == 0 && kh == 0 && kk == 0) ? 0u : 1u;
-              mma_bf16_ts(d, tP + col, b0, kIdesc, first);        // p_hi · v_hi
-              mma_bf16_ts(d, tP + col, b1, kIdesc, 1u);           // p_hi · v_lo
-              mma_bf16_ts(d, tP + 64 + col, b0, kIdesc, 1u);      // p_lo · v_hi
+              mma_bf16_ts(d, tP + hcol, b0, kIdesc, first);       // p_hi · v_hi
+              mma_bf16_ts(d, tP + hcol, b1, kIdesc, 1u);          // p_hi · v_lo
+              mma_bf16_ts(d, tP + hcol + 16, b0, kIdesc, 1u);     // p_lo · v_hi
             }
             mma_commit(bar(4 + stage));
             if (++stage == kStages) {
@@ -255,6 +262,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const uint32_t tS = tmem + uint32_t(sb * 128);
         for (int c = 0; c < 4 && ok; ++c) {
+          if (j == 0 && !waitb(q_bar(c), 0, abort_flag, p.err, kDevTimeoutFull)) {
+            ok = false;
+            break;
+          }
           if (!waitb(bar(1 + stage), phase, abort_flag, p.err, kDevTimeoutFull)) {
             ok = false;
             break;
@@ -326,29 +337,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       const uint32_t tS = tmem + lane_off + uint32_t(sb * 128);
-      uint32_t sr[4][32];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) tmem_ld_32x32b_x32(tS + uint32_t(q * 32), sr[q]);
-      tmem_ld_wait();
       const int lo_c = vlo - key0, hi_c = vhi - key0;  // visible columns [lo_c, hi_c)
-      // row maximum over the visible columns, eight independent chains
+      const bool full_row = lo_c <= 0 && hi_c >= kKT;
+      // pass 1: row maximum over the visible columns, two 64-column halves,
+      // eight independent chains (few live registers leave room for the
+      // long-latency exponentials and conversions of pass 2 to overlap)
       float mt8[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) mt8[u] = -FLT_MAX;
-      const bool full_row = lo_c <= 0 && hi_c >= kKT;
-      if (full_row) {
+#pragma unroll 1
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t sr[2][32];
+        tmem_ld_32x32b_x32(tS + uint32_t(hh * 64), sr[0]);
+        tmem_ld_32x32b_x32(tS + uint32_t(hh * 64 + 32), sr[1]);
+        tmem_ld_wait();
+        if (full_row) {
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
+          for (int q = 0; q < 2; ++q)
 #pragma unroll
-          for (int e = 0; e < 32; ++e) mt8[e & 7] = fmaxf(mt8[e & 7], __uint_as_float(sr[q][e]));
-      } else {
+            for (int e = 0; e < 32; ++e) mt8[e & 7] = fmaxf(mt8[e & 7], __uint_as_float(sr[q][e]));
+        } else {
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
+          for (int q = 0; q < 2; ++q)
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int col = q * 32 + e;
-            if (col >= lo_c && col < hi_c) mt8[e & 7] = fmaxf(mt8[e & 7], __uint_as_float(sr[q][e]));
-          }
+            for (int e = 0; e < 32; ++e) {
+              const int col = hh * 64 + q * 32 + e;
+              if (col >= lo_c && col < hi_c) mt8[e & 7] = fmaxf(mt8[e & 7], __uint_as_float(sr[q][e]));
+            }
+        }
       }
       const float mt = fmaxf(fmaxf(fmaxf(mt8[0], mt8[1]), fmaxf(mt8[2], mt8[3])),
                              fmaxf(fmaxf(mt8[4], mt8[5]), fmaxf(mt8[6], mt8[7])));
@@ -386,27 +402,46 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       l *= factor;
       const float mc = m * c;
-      // probabilities, split into packed bf16 hi / lo, written over S
+      // pass 2: probabilities, split into packed bf16 hi / lo. The 32-column
+      // chunk q of S is overwritten by its own P: hi (16 columns of bf16
+      // pairs) at columns 32q.., lo at 32q+16.., so S is read in 64-column
+      // halves that no earlier store has touched.
       float ps8[8];  // eight independent partial sums
 #pragma unroll
       for (int u = 0; u < 8; ++u) ps8[u] = 0.f;
+      const bool all_vis = have && full_row;
+#pragma unroll 1
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t sr[2][32];
+        tmem_ld_32x32b_x32(tS + uint32_t(hh * 64), sr[0]);
+        tmem_ld_32x32b_x32(tS + uint32_t(hh * 64 + 32), sr[1]);
+        tmem_ld_wait();
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        uint32_t hw[16], lw[16];
+        for (int q = 0; q < 2; ++q) {
+          uint32_t hw[16], lw[16];
 #pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int col = q * 32 + 2 * e;
-          float a = 0.f, bb = 0.f;
-          if (have && col >= lo_c && col < hi_c) a = ex2_approx(fmaf(__uint_as_float(sr[q][2 * e]), c, -mc));
-          if (have && col + 1 >= lo_c && col + 1 < hi_c)
-            bb = ex2_approx(fmaf(__uint_as_float(sr[q][2 * e + 1]), c, -mc));
-          ps8[e & 7] += a + bb;
-          const float ah = bf16_round_f32(a), bh = bf16_round_f32(bb);
-          hw[e] = pack_bf16x2(ah, bh);
-          lw[e] = pack_bf16x2(a - ah, bb - bh);
+          for (int e = 0; e < 16; ++e) {
+            const int col = hh * 64 + q * 32 + 2 * e;
+            float a, bb;
+            if (all_vis) {
+              a = ex2_approx(fmaf(__uint_as_float(sr[q][2 * e]), c, -mc));
+              bb = ex2_approx(fmaf(__uint_as_float(sr[q][2 * e + 1]), c, -mc));
+            } else {
+              a = (have && col >= lo_c && col < hi_c) ? ex2_approx(fmaf(__uint_as_float(sr[q][2 * e]), c, -mc)) : 0.f;
+              bb = (have && col + 1 >= lo_c && col + 1 < hi_c)
+                       ? ex2_approx(fmaf(__uint_as_float(sr[q][2 * e + 1]), c, -mc))
+                       : 0.f;
+            }
+            ps8[e & 7] += a + bb;
+            const uint32_t h2 = pack_bf16x2(a, bb);  // RN bf16 of both, a in the low half
+            const float ah = __uint_as_float(h2 << 16), bh = __uint_as_float(h2 & 0xffff0000u);
+            hw[e] = h2;
+            lw[e] = pack_bf16x2(a - ah, bb - bh);
+          }
+          const uint32_t cq = uint32_t((hh * 2 + q) * 32);
+          tmem_st_32x32b_x16(tS + cq, hw);
+          tmem_st_32x32b_x16(tS + cq + 16, lw);
         }
-        tmem_st_32x32b_x16(tS + uint32_t(q * 16), hw);
-        tmem_st_32x32b_x16(tS + uint32_t(64 + q * 16), lw);
       }
       l += ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
       tmem_st_wait();
@@ -461,7 +496,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_store_commit();
           }
         }
-        if (lane == 0) tma_store_wait_all();
+        if (lane == 0) tma_store_wait_read<0>();  // the boxes are read; the writes complete on their own
         __syncwarp();
       } else {
         float* o = obase + int64_t(i) * p.ost;

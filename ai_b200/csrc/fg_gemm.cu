@@ -703,7 +703,7 @@ __global__ void __launch_bounds__(Cfg<BN, SA, SB, BK, CV>::kThreads, 1)
       tc_fence_before();
       mbar_arrive(acce_bar(acc));
     }
-    if (lane == 0) tma_store_wait_all();  // stores done before the CTA's shared memory goes away
+    if (lane == 0) tma_store_wait_read<0>();  // staging read before the CTA's shared memory goes away
     __syncwarp();
   }
 
@@ -955,7 +955,7 @@ __global__ void __launch_bounds__(320, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(mapa_shared(acce_bar(acc), 0));
     }
-    if (lane == 0) tma_store_wait_all();  // stores done before the CTA's shared memory goes away
+    if (lane == 0) tma_store_wait_read<0>();  // staging read before the CTA's shared memory goes away
     __syncwarp();
   }
 
