@@ -48,7 +48,7 @@ constexpr uint32_t kChunk = 128 * 64 * 2;           // [128 rows × 64 bf16] = 1
 constexpr uint32_t kQBytes = 2 * 4 * kChunk;        // Q hi/lo × 4 d-chunks = 128 KB
 constexpr uint32_t kStageBytes = 2 * kChunk;        // hi + lo chunk = 32 KB
 constexpr size_t kSmem = 1024 + kQBytes + kStages * kStageBytes + 256;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;  // producer, MMA issuer, 8 softmax warps
 constexpr uint32_t kIdesc = idesc_bf16(128, 128);
 constexpr float kRescaleLog2 = 8.f;  // rescale O when the max grows by more than 2^8
 
@@ -130,7 +130,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int k = 0; k < 2; ++k) {
       mbar_init(bar(7 + k), 1);
-      mbar_init(bar(9 + k), 128);
+      mbar_init(bar(9 + k), 256);
       mbar_init(bar(11 + k), 1);
     }
     mbar_init(o_prog, 1);
@@ -312,7 +312,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // -------------------------------------------------------------- softmax
+    // Two warps per TMEM lane quadrant (warps w and w + 4 hold the same 32
+    // query rows): both find the row maximum over all 128 columns of S (the
+    // same value, so the same running max and rescale decisions without an
+    // exchange); each then handles half of the columns — exponentials for
+    // 64 columns of S, rescaling and output for 128 columns of O.
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r = quad * 32 + lane;
     const int i = i0 + r;
     const uint32_t lane_off = uint32_t(quad * 32) << 16;
@@ -325,7 +331,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float c = p.scale_log2;
     float m = -FLT_MAX;
     bool have = false;
-    float l = 0.f;
+    float l = 0.f;  // this warp's columns only; the halves are added at the end
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
       const int sb = j & 1;
@@ -339,6 +345,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t tS = tmem + lane_off + uint32_t(sb * 128);
       const int lo_c = vlo - key0, hi_c = vhi - key0;  // visible columns [lo_c, hi_c)
       const bool full_row = lo_c <= 0 && hi_c >= kKT;
+      const int span = max(0, hi_c - lo_c);  // col is visible iff unsigned(col - lo_c) < span
       // pass 1: row maximum over the visible columns, two 64-column halves,
       // eight independent chains (few live registers leave room for the
       // long-latency exponentials and conversions of pass 2 to overlap)
@@ -362,7 +369,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
               const int col = hh * 64 + q * 32 + e;
-              if (col >= lo_c && col < hi_c) mt8[e & 7] = fmaxf(mt8[e & 7], __uint_as_float(sr[q][e]));
+              const bool in = unsigned(col - lo_c) < unsigned(span);
+              mt8[e & 7] = fmaxf(mt8[e & 7], in ? __uint_as_float(sr[q][e]) : -FLT_MAX);
             }
         }
       }
@@ -379,7 +387,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           m = mt;
         }
       }
-      // O rows rescale: the whole warp takes part if any lane needs it
+      // O rows rescale (this warp's 128 columns): the whole warp takes part
+      // if any lane needs it
       const bool need = factor != 1.f;
       if (__any_sync(0xffffffffu, need) && j > 0) {
         const bool done = waitb(o_prog, uint32_t(j - 1) & 1u, abort_flag, p.err, kDevTimeoutAccFull);
@@ -389,9 +398,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
 #pragma unroll 1
-        for (int ch = 0; ch < 8; ++ch) {
+        for (int ch = 0; ch < 4; ++ch) {
           uint32_t ov[32];
-          const uint32_t ta = tO + lane_off + uint32_t(ch * 32);
+          const uint32_t ta = tO + lane_off + uint32_t(half * 128 + ch * 32);
           tmem_ld_32x32b_x32(ta, ov);
           tmem_ld_wait();
 #pragma unroll
@@ -402,16 +411,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       l *= factor;
       const float mc = m * c;
-      // pass 2: probabilities, split into packed bf16 hi / lo. The 32-column
-      // chunk q of S is overwritten by its own P: hi (16 columns of bf16
-      // pairs) at columns 32q.., lo at 32q+16.., so S is read in 64-column
-      // halves that no earlier store has touched.
+      // pass 2: probabilities of this warp's 64 columns, split into packed
+      // bf16 hi / lo. The 32-column chunk q of S is overwritten by its own
+      // P: hi (16 columns of bf16 pairs) at columns 32q.., lo at 32q+16..
       float ps8[8];  // eight independent partial sums
 #pragma unroll
       for (int u = 0; u < 8; ++u) ps8[u] = 0.f;
       const bool all_vis = have && full_row;
-#pragma unroll 1
-      for (int hh = 0; hh < 2; ++hh) {
+      {
+        const int hh = half;
         uint32_t sr[2][32];
         tmem_ld_32x32b_x32(tS + uint32_t(hh * 64), sr[0]);
         tmem_ld_32x32b_x32(tS + uint32_t(hh * 64 + 32), sr[1]);
@@ -427,10 +435,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               a = ex2_approx(fmaf(__uint_as_float(sr[q][2 * e]), c, -mc));
               bb = ex2_approx(fmaf(__uint_as_float(sr[q][2 * e + 1]), c, -mc));
             } else {
-              a = (have && col >= lo_c && col < hi_c) ? ex2_approx(fmaf(__uint_as_float(sr[q][2 * e]), c, -mc)) : 0.f;
-              bb = (have && col + 1 >= lo_c && col + 1 < hi_c)
-                       ? ex2_approx(fmaf(__uint_as_float(sr[q][2 * e + 1]), c, -mc))
-                       : 0.f;
+              // masked scores become -inf, whose exponential is exactly 0
+              const float s0 = unsigned(col - lo_c) < unsigned(span) ? __uint_as_float(sr[q][2 * e]) : -INFINITY;
+              const float s1 = unsigned(col + 1 - lo_c) < unsigned(span) ? __uint_as_float(sr[q][2 * e + 1]) : -INFINITY;
+              a = have ? ex2_approx(fmaf(s0, c, -mc)) : 0.f;
+              bb = have ? ex2_approx(fmaf(s1, c, -mc)) : 0.f;
             }
             ps8[e & 7] += a + bb;
             const uint32_t h2 = pack_bf16x2(a, bb);  // RN bf16 of both, a in the low half
@@ -452,13 +461,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool fin = ok && waitb(o_final, 0, abort_flag, p.err, kDevTimeoutAccFull);
     if (__all_sync(0xffffffffu, fin)) {
       tc_fence_after();
+      // row sum = both halves' sums (l of the other warp of the quadrant,
+      // through the K/V ring, free now that every MMA has completed)
+      float* red = reinterpret_cast<float*>(sRing);
+      red[(half * 4 + quad) * 32 + lane] = l;
+      asm volatile("bar.sync %0, 64;" ::"r"(1 + quad) : "memory");
+      const float l_lo = red[quad * 32 + lane], l_hi = red[(4 + quad) * 32 + lane];
+      const float lsum = l_lo + l_hi;  // same order in both warps
       const bool row_ok = i < p.T;
-      const float inv = (i < qlen && l > 0.f) ? 1.f / l : 0.f;
+      const float inv = (i < qlen && lsum > 0.f) ? 1.f / lsum : 0.f;
+      const int col_base = half * 128;  // this warp's output columns
       if (p.tma_out) {
-        // The warp's 32 rows × 256 columns as eight [32 × 32] boxes in its
-        // 32 KB of the Q region (every MMA that read Q has completed), then
+        // The warp's 32 rows × 128 columns as four [32 × 32] boxes in its
+        // 16 KB of the Q region (every MMA that read Q has completed), then
         // TMA stores; rows past the sequence end fall outside the map.
-        uint8_t* stg = sQ + size_t(warp - 2) * 32768;
+        uint8_t* stg = sQ + size_t(warp - 2) * 16384;
         const int tw = i0 + quad * 32;
         const int parts = olbase ? 2 : 1;
 #pragma unroll 1
@@ -468,10 +485,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
           }
 #pragma unroll 1
-          for (int ch = 0; ch < 8; ch += 2) {
+          for (int ch = 0; ch < 4; ch += 2) {
             uint32_t ov[2][32];
-            tmem_ld_32x32b_x32(tO + lane_off + uint32_t(ch * 32), ov[0]);
-            tmem_ld_32x32b_x32(tO + lane_off + uint32_t(ch * 32 + 32), ov[1]);
+            tmem_ld_32x32b_x32(tO + lane_off + uint32_t(col_base + ch * 32), ov[0]);
+            tmem_ld_32x32b_x32(tO + lane_off + uint32_t(col_base + ch * 32 + 32), ov[1]);
             tmem_ld_wait();
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
@@ -491,20 +508,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0 && tw < p.T) {
-            for (int ch = 0; ch < 8; ++ch)
-              tma_store_3d(part ? &mOlo : &mO, smem_u32(stg + ch * 4096), h * kD + ch * 32, tw, b);
+            for (int ch = 0; ch < 4; ++ch)
+              tma_store_3d(part ? &mOlo : &mO, smem_u32(stg + ch * 4096), h * kD + col_base + ch * 32, tw, b);
             tma_store_commit();
           }
         }
         if (lane == 0) tma_store_wait_read<0>();  // the boxes are read; the writes complete on their own
         __syncwarp();
       } else {
-        float* o = obase + int64_t(i) * p.ost;
-        float* ol = olbase ? olbase + int64_t(i) * p.ost : nullptr;
+        float* o = obase + int64_t(i) * p.ost + col_base;
+        float* ol = olbase ? olbase + int64_t(i) * p.ost + col_base : nullptr;
 #pragma unroll 1
-        for (int ch = 0; ch < 8; ++ch) {
+        for (int ch = 0; ch < 4; ++ch) {
           uint32_t ov[32];
-          tmem_ld_32x32b_x32(tO + lane_off + uint32_t(ch * 32), ov);
+          tmem_ld_32x32b_x32(tO + lane_off + uint32_t(col_base + ch * 32), ov);
           tmem_ld_wait();
           if (row_ok) {
             float4* o4 = reinterpret_cast<float4*>(o + ch * 32);

@@ -211,11 +211,9 @@ struct EpiStage {
 // bf16 parts of two fp32 values y0, y1, packed into a word each (y0 in the
 // low half): hi = RN(y), lo = RN(y - hi).
 __device__ __forceinline__ void split_pack_pair(float y0, float y1, uint32_t& hw, uint32_t& lw) {
-  const __nv_bfloat16 h0 = __float2bfloat16_rn(y0), h1 = __float2bfloat16_rn(y1);
-  const __nv_bfloat16 l0 = __float2bfloat16_rn(y0 - __bfloat162float(h0));
-  const __nv_bfloat16 l1 = __float2bfloat16_rn(y1 - __bfloat162float(h1));
-  hw = uint32_t(__bfloat16_as_ushort(h0)) | (uint32_t(__bfloat16_as_ushort(h1)) << 16);
-  lw = uint32_t(__bfloat16_as_ushort(l0)) | (uint32_t(__bfloat16_as_ushort(l1)) << 16);
+  hw = pack_bf16x2(y0, y1);  // one paired round-to-nearest conversion
+  const float h0 = __uint_as_float(hw << 16), h1 = __uint_as_float(hw & 0xffff0000u);
+  lw = pack_bf16x2(y0 - h0, y1 - h1);
 }
 
 // Half `hf` (16 bf16 = 32 bytes) of row `lane` of a [32 rows × 32 bf16] TMA
