@@ -280,7 +280,7 @@ def run_ours(args, rank, local_rank, world, cfg):
     if tp.exists():
         traffic = json.loads(tp.read_text()).get("bytes_per_launch")
     roofline = {
-        "bound": "tensor", "kernel": "gemm_tf32_kernel (all encoder projections)",
+        "bound": "tensor", "kernel": "gemm_pair_kernel (tcgen05 cta_group::2 split-TF32, all encoder projections)",
         "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s",
         "frac": achieved / tf32_peak if achieved else None, "traffic": traffic,
         "peak_source": f"{pk['source']} bf16 sustained {pk['bf16_sustained']} TFLOP/s / 2 "
