@@ -1,0 +1,125 @@
+"""Parity at BASELINE.json's full sizes, through properties that do not
+depend on size, plus the float64 oracle on sampled sequences:
+
+- config 2 (256 x 512): two runs are bitwise equal; every embedding has
+  unit norm; sequences embedded alone equal their rows in the full batch;
+  sampled sequences match the oracle (cosine >= 0.99999, max-abs <= 1e-4).
+- config 3 (8192 ragged sequences, lengths 16..2048, through the batching
+  of Model.embed_ids): unit norms, and the shortest, a middle and the
+  longest sequence match the oracle.
+- config 5 (32 x 2048): a 2048-token sequence matches the oracle; two runs
+  are bitwise equal.
+- config 4 (MatMul sweep, M = 65536): split-TF32 against a float64 product
+  (torch on the GPU as the checker) for A·B and A·Wᵀ (a transposed view).
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+COS_MIN = 0.99999
+MAXABS = 1e-4
+
+
+def _cmp(got, want):
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    if got.ndim == 1:
+        got, want = got[None], want[None]
+    cos = (got * want).sum(1) / np.linalg.norm(got, axis=1) / np.linalg.norm(want, axis=1)
+    return float(cos.min()), float(np.abs(got - want).max())
+
+
+@pytest.fixture(scope="module")
+def full():
+    from ai_b200 import gemma
+    from ai_b200 import synthetic as S
+    from oracle import oracle as O
+
+    cfg = dict(S.EMBEDDINGGEMMA_300M)
+    w = S.make_weights(cfg, seed=0)
+    model = gemma.from_synthetic(cfg, w, device=0, max_batch_tokens=256 * 512)
+    orc = O.from_bf16(cfg, w)
+    yield model, orc
+    model.close()
+
+
+def _oracle(orc, seq):
+    from oracle import oracle as O
+
+    ids = np.asarray(seq, np.int32)[None]
+    return orc.embed_padded(ids, np.array([ids.shape[1]], np.int32), mode=O.F64)[0]
+
+
+def test_config2_full_batch_properties(full):
+    from ai_b200 import synthetic as S
+
+    model, orc = full
+    ids = S.make_ids(256, 512, 1)
+    lengths = np.full(256, 512, np.int32)
+    e1 = model.embed_padded(ids, lengths)
+    e2 = model.embed_padded(ids, lengths)
+    assert np.array_equal(e1, e2), "two runs differ"
+    assert np.all(np.isfinite(e1))
+    assert np.allclose(np.linalg.norm(e1.astype(np.float64), axis=1), 1.0, atol=1e-5)
+    for k in (0, 137, 255):
+        alone = model.embed_padded(ids[k:k + 1], lengths[k:k + 1])[0]
+        assert np.abs(alone - e1[k]).max() <= 1e-6, k
+    for k in (0, 255):
+        c, m = _cmp(e1[k], _oracle(orc, ids[k]))
+        print(f"config 2 seq {k}: cos {c:.9f} maxabs {m:.2e}")
+        assert c >= COS_MIN and m <= MAXABS
+
+
+def test_config3_ragged_full_set(full):
+    from ai_b200 import synthetic as S
+
+    model, orc = full
+    seqs, lengths = S.make_ragged(8192, 16, 2048, 2)
+    emb = np.stack(model.embed_ids(seqs))
+    assert emb.shape == (8192, 768)
+    assert np.all(np.isfinite(emb))
+    assert np.allclose(np.linalg.norm(emb.astype(np.float64), axis=1), 1.0, atol=1e-5)
+    order = np.argsort(lengths, kind="stable")
+    for k in (order[0], order[len(order) // 2], order[-1]):
+        c, m = _cmp(emb[k], _oracle(orc, seqs[k]))
+        print(f"config 3 seq {k} (length {lengths[k]}): cos {c:.9f} maxabs {m:.2e}")
+        assert c >= COS_MIN and m <= MAXABS
+
+
+def test_config5_long_context(full):
+    from ai_b200 import synthetic as S
+
+    model, orc = full
+    ids = S.make_ids(32, 2048, 4)
+    lengths = np.full(32, 2048, np.int32)
+    e1 = model.embed_padded(ids, lengths)
+    e2 = model.embed_padded(ids, lengths)
+    assert np.array_equal(e1, e2)
+    c, m = _cmp(e1[5], _oracle(orc, ids[5]))
+    print(f"config 5 seq 5: cos {c:.9f} maxabs {m:.2e}")
+    assert c >= COS_MIN and m <= MAXABS
+
+
+@pytest.mark.parametrize("k,n", [(768, 3072), (1152, 768)])
+@pytest.mark.parametrize("transposed", [False, True])
+def test_config4_matmul_sweep_full_m(cuda, k, n, transposed):
+    import torch
+
+    from ai_b200 import tensor as T
+
+    g = torch.Generator(device=cuda).manual_seed(3)
+    m = 65536
+    a = torch.randn(m, k, generator=g, device=cuda, dtype=torch.float32)
+    if transposed:
+        w = torch.randn(n, k, generator=g, device=cuda, dtype=torch.float32).t()  # [k, n] view, no copy
+    else:
+        w = torch.randn(k, n, generator=g, device=cuda, dtype=torch.float32)
+    got = T.MatMul(a, w)
+    want = a.double() @ w.double()
+    err = (got.double() - want).abs()
+    scale = a.double().norm(dim=1)[:, None] * w.double().norm(dim=0)[None, :]
+    ok = (err <= 1e-4 * (1 + want.abs())) | (err <= 1e-5 * scale)
+    print(f"M={m} K={k} N={n} T={transposed}: max|err| {err.max().item():.3e} "
+          f"max err/(|a||w|) {(err / scale).max().item():.3e}")
+    assert bool(ok.all())
