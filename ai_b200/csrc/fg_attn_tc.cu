@@ -81,7 +81,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sRing = smem + kQBytes;          // [stage][part] 16 KB each
   uint64_t* bars = reinterpret_cast<uint64_t*>(sRing + kStages * kStageBytes);
   // bars: 0 Q d-chunk 0 | 1..3 kv_full | 4..6 kv_empty | 7,8 s_full | 9,10 p_full |
-  //       11,12 s_free | 13 o_prog | 14 o_final | 15 drain | 16..18 Q d-chunks 1..3
+  //       11,12 s_free | 13 o_prog | 14 o_final | 15 drain | 16..18 Q d-chunks 1..3 |
+  //       19 row-sum halves exchanged
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 20);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
@@ -136,6 +137,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(o_prog, 1);
     mbar_init(o_final, 1);
     mbar_init(drain, 1);
+    mbar_init(bar(19), 8);  // row-sum halves written, one arrive per softmax warp
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -465,7 +467,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       // through the K/V ring, free now that every MMA has completed)
       float* red = reinterpret_cast<float*>(sRing);
       red[(half * 4 + quad) * 32 + lane] = l;
-      asm volatile("bar.sync %0, 64;" ::"r"(1 + quad) : "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(19));  // a bounded wait, unlike a named barrier, cannot hang
+      waitb(bar(19), 0, abort_flag, p.err, kDevTimeoutAccFull);
       const float l_lo = red[quad * 32 + lane], l_hi = red[(4 + quad) * 32 + lane];
       const float lsum = l_lo + l_hi;  // same order in both warps
       const bool row_ok = i < p.T;
