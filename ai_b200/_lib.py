@@ -34,7 +34,11 @@ MAX_DENSE = 4
 
 # Phases of fg_model_read_profile (include/fgemma.h FG_PHASE_*).
 PHASES = ["embed", "gemm_qkv", "qk_norm_rope", "attention", "gemm_o", "residual",
-          "gemm_gate_up", "gemm_down", "pool_head"]
+          "gemm_gate_up", "gemm_down", "pool_head", "widen"]
+
+# fg_model_set_weight_residency modes
+WEIGHTS_F32 = 0
+WEIGHTS_BF16 = 1
 
 # Every symbol include/fgemma.h declares, with (restype, argtypes).
 _i64 = C.c_int64
@@ -92,6 +96,8 @@ SIGNATURES = {
     "fg_model_create": (C.c_int, [C.POINTER(Config), C.c_int, C.POINTER(_vp)]),
     "fg_model_set_weight": (C.c_int, [_vp, C.c_char_p, C.c_int, C.POINTER(_i64), C.c_int, _vp]),
     "fg_model_finalize": (C.c_int, [_vp, _i64]),
+    "fg_model_set_weight_residency": (C.c_int, [_vp, C.c_int]),
+    "fg_model_weight_bytes": (C.c_int64, [_vp]),
     "fg_embed_ids": (C.c_int, [_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp]),
     "fg_embed_ids_device": (C.c_int, [_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp]),
     "fg_model_check": (C.c_int, [_vp]),

@@ -31,8 +31,23 @@ __device__ __forceinline__ float sq_acc(float acc, float v) { return __fadd_rn(a
 constexpr int kWarpsPerBlock = 8;
 
 // ---------------------------------------------------------------- gather
-template <int C4>
-__global__ void __launch_bounds__(256) embed_kernel(const float* __restrict__ table, int64_t vocab,
+// Row `id` of the table, chunk c of a lane: 4 consecutive values.
+template <typename TT>
+__device__ __forceinline__ float4 table_chunk(const TT* table, int64_t id, int n, int i4);
+template <>
+__device__ __forceinline__ float4 table_chunk<float>(const float* table, int64_t id, int n, int i4) {
+  return __ldg(reinterpret_cast<const float4*>(table + id * n) + i4);
+}
+template <>
+__device__ __forceinline__ float4 table_chunk<uint16_t>(const uint16_t* table, int64_t id, int n, int i4) {
+  // bf16 → fp32 is exact: the bf16 bits are the fp32's upper half
+  const uint2 h = __ldg(reinterpret_cast<const uint2*>(table + id * n) + i4);
+  return make_float4(__uint_as_float(h.x << 16), __uint_as_float(h.x & 0xffff0000u),
+                     __uint_as_float(h.y << 16), __uint_as_float(h.y & 0xffff0000u));
+}
+
+template <int C4, typename TT>
+__global__ void __launch_bounds__(256) embed_kernel(const TT* __restrict__ table, int64_t vocab,
                                                     const int32_t* __restrict__ ids,
                                                     const int32_t* __restrict__ lengths, int B, int T,
                                                     int n, float emb_scale, float eps,
@@ -59,11 +74,10 @@ __global__ void __launch_bounds__(256) embed_kernel(const float* __restrict__ ta
     if (lane == 0) atomicCAS(err, 0, kDevBadArgs);
     id = 0;
   }
-  const float4* src = reinterpret_cast<const float4*>(table + id * n);
   float ss = 0.f;
 #pragma unroll
   for (int c = 0; c < C4; ++c) {
-    float4 v = __ldg(src + lane + 32 * c);
+    float4 v = table_chunk<TT>(table, id, n, lane + 32 * c);
     v.x = __fmul_rn(v.x, emb_scale);
     v.y = __fmul_rn(v.y, emb_scale);
     v.z = __fmul_rn(v.z, emb_scale);
@@ -302,15 +316,22 @@ int grid_for(int64_t tasks, int per_block) {
 
 }  // namespace
 
-int embed_gather(const float* table, int64_t vocab, const int32_t* ids, const int32_t* lengths,
-                 int B, int T, int hidden, float emb_scale, float eps, float* x, float* x_lo,
-                 float* rowscale, int* err, cudaStream_t s) {
+int embed_gather(const float* table, const uint16_t* table_bf16, int64_t vocab, const int32_t* ids,
+                 const int32_t* lengths, int B, int T, int hidden, float emb_scale, float eps, float* x,
+                 float* x_lo, float* rowscale, int* err, cudaStream_t s) {
   const int64_t rows = int64_t(B) * T;
   if (rows == 0) return FG_OK;
   const int grid = grid_for(rows, kWarpsPerBlock);
   switch (hidden / 128) {
-#define FG_EMB(C) \
-  case C: embed_kernel<C><<<grid, 256, 0, s>>>(table, vocab, ids, lengths, B, T, hidden, emb_scale, eps, x, x_lo, rowscale, err); break;
+#define FG_EMB(C)                                                                                   \
+  case C:                                                                                           \
+    if (table_bf16)                                                                                 \
+      embed_kernel<C, uint16_t><<<grid, 256, 0, s>>>(table_bf16, vocab, ids, lengths, B, T, hidden, \
+                                                     emb_scale, eps, x, x_lo, rowscale, err);       \
+    else                                                                                            \
+      embed_kernel<C, float><<<grid, 256, 0, s>>>(table, vocab, ids, lengths, B, T, hidden,         \
+                                                  emb_scale, eps, x, x_lo, rowscale, err);          \
+    break;
     FG_EMB(1) FG_EMB(2) FG_EMB(3) FG_EMB(4) FG_EMB(5) FG_EMB(6) FG_EMB(7) FG_EMB(8)
 #undef FG_EMB
     default:

@@ -10,10 +10,12 @@ namespace fg {
 // layer's folded pre-norm factor rowscale = 1/√(Σx²/n + eps)
 // (matmul_fused.go:125-143, embed.go:432-438). ids/lengths are [B·T]/[B];
 // positions at or past max(len, 1) are written as zeros; a length-0
-// sequence embeds the pad id 0 at position 0.
-int embed_gather(const float* table, int64_t vocab, const int32_t* ids, const int32_t* lengths,
-                 int B, int T, int hidden, float emb_scale, float eps, float* x, float* x_lo,
-                 float* rowscale, int* dev_err, cudaStream_t s);
+// sequence embeds the pad id 0 at position 0. The table is fp32, or bf16
+// (`table_bf16`, used when non-null) widened exactly as it is read
+// (safetensors/convert.go:31-38 widens the same bits once at load).
+int embed_gather(const float* table, const uint16_t* table_bf16, int64_t vocab, const int32_t* ids,
+                 const int32_t* lengths, int B, int T, int hidden, float emb_scale, float eps, float* x,
+                 float* x_lo, float* rowscale, int* dev_err, cudaStream_t s);
 
 // Per-head RMSNorm of q and k with their gains (attention.go:292-337), then
 // rotate-half RoPE with the layer's cos/sin tables [T, D/2] (rope.go:66-87),

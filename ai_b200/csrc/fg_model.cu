@@ -27,6 +27,7 @@
 
 #include "fg_internal.h"
 #include "fg_kernels.cuh"
+#include "fg_ptx.cuh"
 
 namespace fg {
 
@@ -83,8 +84,20 @@ struct DevMat {
   int rows = 0, cols = 0;
 };
 
+// A projection resident as bf16 (FG_WEIGHTS_BF16): [rows, cols] bits and
+// the pre-norm gain folded into its columns at widening (null: none).
+struct Bf16Mat {
+  uint16_t* w = nullptr;
+  const float* gain = nullptr;
+  bool lo = false;  // the folded values have non-zero split-TF32 low parts
+};
+
 struct Layer {
   DevMat wqkv, wo, wgu, wd;
+  bool resident_bf16 = false;  // the four below hold the weights; the DevMats are the workspace
+  Bf16Mat bqkv, bo, bgu, bd;
+  float* g_in = nullptr;  // pre-attention and pre-FFN gains (1 + w)
+  float* g_pf = nullptr;
   float* qgain = nullptr;
   float* kgain = nullptr;
   float* post_attn = nullptr;
@@ -111,7 +124,8 @@ struct fg_model {
   bool finalized = false;
 
   // device weights
-  float* embed = nullptr;
+  float* embed = nullptr;             // fp32 table, or
+  uint16_t* embed_bf16 = nullptr;     // the bf16 table when every entry is bf16-exact
   std::vector<fg::Layer> layers;
   float* final_gain = nullptr;
   std::vector<fg::Dense> dense;
@@ -135,6 +149,11 @@ struct fg_model {
   // FG_GEMM_ALO=global: producers write the split-TF32 low parts of the
   // GEMM inputs to memory instead of the GEMM computing them in shared memory
   bool alo_global = false;
+  int weight_mode = FG_WEIGHTS_F32;
+  size_t weight_bytes = 0;  // device bytes allocated by finalize before the activation workspace
+  size_t alloc_bytes = 0;
+  // FG_WEIGHTS_BF16: one layer's widened fp32 projections (hi and low parts)
+  fg::DevMat ws_qkv, ws_o, ws_gu, ws_d;
   // host-API staging
   int32_t* d_ids = nullptr;
   int64_t d_ids_cap = 0;
@@ -168,6 +187,7 @@ int dev_alloc(fg_model* m, void** p, size_t bytes) {
     return set_error(FG_ENOMEM, "device allocation of %zu bytes failed", bytes);
   }
   m->allocations.push_back(*p);
+  m->alloc_bytes += bytes;
   return FG_OK;
 }
 
@@ -185,6 +205,99 @@ int upload(fg_model* m, const std::vector<float>& h, float** out) {
   return FG_OK;
 }
 
+// The embedding table stays resident in bf16 (half the bytes: 403 MB
+// instead of 805 MB for EmbeddingGemma's 262144 × 768) when every entry is
+// a widened bf16 — always so for a bf16 checkpoint — and the gather widens
+// it exactly; otherwise it is kept in fp32. FG_EMBED_BF16=0 keeps fp32.
+int upload_table(fg_model* m, const std::vector<float>& h, float** f32, uint16_t** b16) {
+  *f32 = nullptr;
+  *b16 = nullptr;
+  const char* env = std::getenv("FG_EMBED_BF16");
+  bool exact = !(env && env[0] == '0');
+  for (size_t i = 0; exact && i < h.size(); ++i) {
+    uint32_t u;
+    std::memcpy(&u, &h[i], 4);
+    exact = (u & 0xffffu) == 0;
+  }
+  if (!exact) return upload(m, h, f32);
+  std::vector<uint16_t> hb(h.size());
+  for (size_t i = 0; i < h.size(); ++i) {
+    uint32_t u;
+    std::memcpy(&u, &h[i], 4);
+    hb[i] = uint16_t(u >> 16);
+  }
+  FG_TRY(dev_alloc_t(m, b16, hb.size()));
+  FG_CUDA_TRY(cudaMemcpy(*b16, hb.data(), hb.size() * sizeof(uint16_t), cudaMemcpyHostToDevice));
+  return FG_OK;
+}
+
+// bf16 bits of h when every value is a widened bf16 (else false).
+bool pack_bf16(const float* h, size_t n, std::vector<uint16_t>& out) {
+  out.resize(n);
+  for (size_t i = 0; i < n; ++i) {
+    uint32_t u;
+    std::memcpy(&u, &h[i], 4);
+    if (u & 0xffffu) return false;
+    out[i] = uint16_t(u >> 16);
+  }
+  return true;
+}
+
+// Whether W'[r][c] = W[r][c]·g[c] (the fold, in fp32) has a non-zero
+// split-TF32 low part anywhere. tf32 keeps the top 10 mantissa bits.
+bool fold_has_lo(const float* w, const std::vector<float>* g, int64_t rows, int64_t cols) {
+  for (int64_t r = 0; r < rows; ++r)
+    for (int64_t c = 0; c < cols; ++c) {
+      const float v = g ? w[r * cols + c] * (*g)[size_t(c)] : w[r * cols + c];
+      uint32_t u;
+      std::memcpy(&u, &v, 4);
+      if (u & 0x1fffu) return true;
+    }
+  return false;
+}
+
+struct WidenJob {
+  const uint16_t* w;
+  const float* gain;
+  float* hi;
+  float* lo;
+  int64_t n4;  // groups of 4 values
+  int cols;    // a multiple of 4
+};
+struct WidenJobs {
+  WidenJob j[4];
+};
+
+// Widens bf16 projections, folds the pre-norm gain into their columns and
+// splits them for split-TF32, the same fp32 operations upload_mat performs
+// on the host-folded weights (fold: w·g; split_tf32: hi = tf32(v),
+// lo = v − hi), so the GEMM sees identical operands. blockIdx.y = job.
+__global__ void __launch_bounds__(256) widen_fold_kernel(WidenJobs jobs) {
+  const WidenJob J = jobs.j[blockIdx.y];
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < J.n4;
+       i += int64_t(gridDim.x) * blockDim.x) {
+    const uint2 h = __ldg(reinterpret_cast<const uint2*>(J.w) + i);
+    float v[4] = {__uint_as_float(h.x << 16), __uint_as_float(h.x & 0xffff0000u),
+                  __uint_as_float(h.y << 16), __uint_as_float(h.y & 0xffff0000u)};
+    if (J.gain) {
+      const int c = int((i * 4) % J.cols);
+      const float4 g = __ldg(reinterpret_cast<const float4*>(J.gain + c));
+      v[0] = __fmul_rn(v[0], g.x);
+      v[1] = __fmul_rn(v[1], g.y);
+      v[2] = __fmul_rn(v[2], g.z);
+      v[3] = __fmul_rn(v[3], g.w);
+    }
+    float4 hi, lo;
+    hi.x = tf32_hi(v[0]); hi.y = tf32_hi(v[1]); hi.z = tf32_hi(v[2]); hi.w = tf32_hi(v[3]);
+    reinterpret_cast<float4*>(J.hi)[i] = hi;
+    if (J.lo) {
+      lo.x = __fsub_rn(v[0], hi.x); lo.y = __fsub_rn(v[1], hi.y);
+      lo.z = __fsub_rn(v[2], hi.z); lo.w = __fsub_rn(v[3], hi.w);
+      reinterpret_cast<float4*>(J.lo)[i] = lo;
+    }
+  }
+}
+
 // Uploads a K-major [rows, cols] fp32 matrix and its split-TF32 parts.
 int upload_mat(fg_model* m, const std::vector<float>& h, int rows, int cols, DevMat* out) {
   float* raw = nullptr;
@@ -200,6 +313,7 @@ int upload_mat(fg_model* m, const std::vector<float>& h, int rows, int cols, Dev
   FG_CUDA_TRY(cudaMemcpy(&any, flag, sizeof(int), cudaMemcpyDeviceToHost));
   if (!any) {  // bf16-exact weights: no low pass, release the buffer
     FG_CUDA_TRY(cudaFree(lo));
+    m->alloc_bytes -= h.size() * sizeof(float);
     m->allocations.erase(std::find(m->allocations.begin(), m->allocations.end(), static_cast<void*>(lo)));
     lo = nullptr;
   }
@@ -235,12 +349,15 @@ std::vector<float> plus_one(const HostTensor& t) {
   return g;
 }
 
-// Folds a pre-norm gain into a [out, in] projection: W'[n][k] = W[n][k]·g[k]
-// (the reference's diag(g)·Wᵀ on the transposed weight, model.go:206-222).
-void fold_into(const HostTensor& w, const std::vector<float>& g, float* dst) {
-  const int64_t rows = w.shape[0], cols = w.shape[1];
+// Folds a pre-norm gain into [rows, cols] projection rows: W'[n][k] =
+// W[n][k]·g[k] (the reference's diag(g)·Wᵀ on the transposed weight,
+// model.go:206-222).
+std::vector<float> fold(const std::vector<float>& w, const std::vector<float>& g, int64_t cols) {
+  std::vector<float> out(w.size());
+  const int64_t rows = int64_t(w.size()) / cols;
   for (int64_t r = 0; r < rows; ++r)
-    for (int64_t c = 0; c < cols; ++c) dst[r * cols + c] = w.data[r * cols + c] * g[c];
+    for (int64_t c = 0; c < cols; ++c) out[r * cols + c] = w[r * cols + c] * g[c];
+  return out;
 }
 
 void rope_table(double base, int T, int D, std::vector<float>& c, std::vector<float>& s) {
@@ -309,7 +426,7 @@ int finalize(fg_model* m, int64_t max_tokens) {
 
   const HostTensor* t = nullptr;
   FG_TRY(need(m, "embed_tokens.weight", {c.vocab_size, H}, &t));
-  FG_TRY(upload(m, t->data, &m->embed));
+  FG_TRY(upload_table(m, t->data, &m->embed, &m->embed_bf16));
 
   // distinct rope bases
   for (int l = 0; l < c.num_layers; ++l) {
@@ -364,22 +481,44 @@ int finalize(fg_model* m, int64_t max_tokens) {
 
     const std::vector<float> g_in = plus_one(*in_norm), g_pf = plus_one(*pf_norm);
     const int64_t qkv_rows = (Hq + 2 * Hkv) * D;
-    std::vector<float> wqkv(size_t(qkv_rows * H));
-    fold_into(*wq, g_in, wqkv.data());
-    fold_into(*wk, g_in, wqkv.data() + Hq * D * H);
-    fold_into(*wv, g_in, wqkv.data() + (Hq + Hkv) * D * H);
-    FG_TRY(upload_mat(m, wqkv, int(qkv_rows), int(H), &L.wqkv));
-    FG_TRY(upload_mat(m, wo->data, int(H), int(Hq * D), &L.wo));
-
-    std::vector<float> gate(size_t(F * H)), up(size_t(F * H)), gu(size_t(2 * F * H));
-    fold_into(*wg, g_pf, gate.data());
-    fold_into(*wu, g_pf, up.data());
+    // q|k|v rows and gate/up rows interleaved in blocks of 128 (the GeGLU
+    // epilogue's pairing), before any fold
+    std::vector<float> rqkv(size_t(qkv_rows * H)), rgu(size_t(2 * F * H));
+    std::memcpy(rqkv.data(), wq->data.data(), size_t(Hq * D * H) * 4);
+    std::memcpy(rqkv.data() + Hq * D * H, wk->data.data(), size_t(Hkv * D * H) * 4);
+    std::memcpy(rqkv.data() + (Hq + Hkv) * D * H, wv->data.data(), size_t(Hkv * D * H) * 4);
     for (int64_t j = 0; j < F / 128; ++j) {
-      std::memcpy(gu.data() + (2 * j) * 128 * H, gate.data() + j * 128 * H, size_t(128 * H) * 4);
-      std::memcpy(gu.data() + (2 * j + 1) * 128 * H, up.data() + j * 128 * H, size_t(128 * H) * 4);
+      std::memcpy(rgu.data() + (2 * j) * 128 * H, wg->data.data() + j * 128 * H, size_t(128 * H) * 4);
+      std::memcpy(rgu.data() + (2 * j + 1) * 128 * H, wu->data.data() + j * 128 * H, size_t(128 * H) * 4);
     }
-    FG_TRY(upload_mat(m, gu, int(2 * F), int(H), &L.wgu));
-    FG_TRY(upload_mat(m, wd->data, int(H), int(F), &L.wd));
+    std::vector<uint16_t> bqkv, bo, bgu, bd;
+    L.resident_bf16 = m->weight_mode == FG_WEIGHTS_BF16 && pack_bf16(rqkv.data(), rqkv.size(), bqkv) &&
+                      pack_bf16(wo->data.data(), wo->data.size(), bo) &&
+                      pack_bf16(rgu.data(), rgu.size(), bgu) && pack_bf16(wd->data.data(), wd->data.size(), bd);
+    if (L.resident_bf16) {
+      auto put = [&](const std::vector<uint16_t>& b, const float* gain, bool lo, Bf16Mat* out) -> int {
+        FG_TRY(dev_alloc_t(m, &out->w, b.size()));
+        FG_CUDA_TRY(cudaMemcpy(out->w, b.data(), b.size() * 2, cudaMemcpyHostToDevice));
+        out->gain = gain;
+        out->lo = lo;
+        return FG_OK;
+      };
+      FG_TRY(upload(m, g_in, &L.g_in));
+      FG_TRY(upload(m, g_pf, &L.g_pf));
+      FG_TRY(put(bqkv, L.g_in, fold_has_lo(rqkv.data(), &g_in, qkv_rows, H), &L.bqkv));
+      FG_TRY(put(bo, nullptr, false, &L.bo));
+      FG_TRY(put(bgu, L.g_pf, fold_has_lo(rgu.data(), &g_pf, 2 * F, H), &L.bgu));
+      FG_TRY(put(bd, nullptr, false, &L.bd));
+      L.wqkv = DevMat{nullptr, nullptr, int(qkv_rows), int(H)};
+      L.wo = DevMat{nullptr, nullptr, int(H), int(Hq * D)};
+      L.wgu = DevMat{nullptr, nullptr, int(2 * F), int(H)};
+      L.wd = DevMat{nullptr, nullptr, int(H), int(F)};
+    } else {
+      FG_TRY(upload_mat(m, fold(rqkv, g_in, H), int(qkv_rows), int(H), &L.wqkv));
+      FG_TRY(upload_mat(m, wo->data, int(H), int(Hq * D), &L.wo));
+      FG_TRY(upload_mat(m, fold(rgu, g_pf, H), int(2 * F), int(H), &L.wgu));
+      FG_TRY(upload_mat(m, wd->data, int(H), int(F), &L.wd));
+    }
 
     FG_TRY(upload(m, plus_one(*qn), &L.qgain));
     FG_TRY(upload(m, plus_one(*kn), &L.kgain));
@@ -405,6 +544,27 @@ int finalize(fg_model* m, int64_t max_tokens) {
     prev = d.out;
   }
   m->host.clear();
+  bool any_bf16 = false, lo_qkv = false, lo_gu = false;
+  for (const Layer& L : m->layers) {
+    any_bf16 |= L.resident_bf16;
+    lo_qkv |= L.resident_bf16 && L.bqkv.lo;
+    lo_gu |= L.resident_bf16 && L.bgu.lo;
+  }
+  if (any_bf16) {
+    const Layer& L0 = m->layers[0];
+    auto ws = [&](const DevMat& shape, bool lo, DevMat* out) -> int {
+      *out = DevMat{nullptr, nullptr, shape.rows, shape.cols};
+      const size_t n = size_t(shape.rows) * shape.cols;
+      FG_TRY(dev_alloc_t(m, &out->hi, n));
+      if (lo) FG_TRY(dev_alloc_t(m, &out->lo, n));
+      return FG_OK;
+    };
+    FG_TRY(ws(L0.wqkv, lo_qkv, &m->ws_qkv));
+    FG_TRY(ws(L0.wo, false, &m->ws_o));
+    FG_TRY(ws(L0.wgu, lo_gu, &m->ws_gu));
+    FG_TRY(ws(L0.wd, false, &m->ws_d));
+  }
+  m->weight_bytes = m->alloc_bytes;
   FG_TRY(ensure_workspace(m, std::max<int64_t>(max_tokens, 1), 1));
   FG_CUDA_TRY(cudaDeviceSynchronize());
   m->finalized = true;
@@ -493,17 +653,41 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
 
   const double act_bytes = double(M) * H * 4.0;
   {
-    PhaseScope ps(m, FG_PHASE_EMBED, s, act_bytes * (lo_global ? 3 : 2) + double(M) * 8, 2);
+    // table rows read (2 or 4 B per value) + x (+ x_lo) written + ids and rowscale
+    const double row_read = double(M) * H * (m->embed_bf16 ? 2.0 : 4.0);
+    PhaseScope ps(m, FG_PHASE_EMBED, s, row_read + act_bytes * (lo_global ? 2 : 1) + double(M) * 8, 2);
     eff_len_kernel<<<(B + 127) / 128, 128, 0, s>>>(lengths, B, T, m->eff_len);
     FG_CUDA_TRY(cudaGetLastError());
     const float emb_scale = float(std::sqrt(double(H)));
-    FG_TRY(embed_gather(m->embed, c.vocab_size, ids, lengths, B, T, H, emb_scale, c.rms_norm_eps,
+    FG_TRY(embed_gather(m->embed, m->embed_bf16, c.vocab_size, ids, lengths, B, T, H, emb_scale, c.rms_norm_eps,
                         m->x, x_lo, m->rowscale, m->err, s));
   }
 
   for (int l = 0; l < c.num_layers; ++l) {
     const Layer& L = m->layers[l];
     const bool last = l == c.num_layers - 1;
+    // The layer's projections: resident fp32, or bf16 widened now into the
+    // one-layer workspace (the previous layer's GEMMs, earlier on the same
+    // stream, have finished reading it).
+    DevMat Wqkv = L.wqkv, Wo = L.wo, Wgu = L.wgu, Wd = L.wd;
+    if (L.resident_bf16) {
+      Wqkv = DevMat{m->ws_qkv.hi, L.bqkv.lo ? m->ws_qkv.lo : nullptr, L.wqkv.rows, L.wqkv.cols};
+      Wo = DevMat{m->ws_o.hi, nullptr, L.wo.rows, L.wo.cols};
+      Wgu = DevMat{m->ws_gu.hi, L.bgu.lo ? m->ws_gu.lo : nullptr, L.wgu.rows, L.wgu.cols};
+      Wd = DevMat{m->ws_d.hi, nullptr, L.wd.rows, L.wd.cols};
+      WidenJobs jobs{};
+      const Bf16Mat* src[4] = {&L.bqkv, &L.bo, &L.bgu, &L.bd};
+      const DevMat* dst[4] = {&Wqkv, &Wo, &Wgu, &Wd};
+      double bytes = 0;
+      for (int i = 0; i < 4; ++i) {
+        const int64_t n = int64_t(dst[i]->rows) * dst[i]->cols;
+        jobs.j[i] = WidenJob{src[i]->w, src[i]->gain, dst[i]->hi, dst[i]->lo, n / 4, dst[i]->cols};
+        bytes += double(n) * (2 + 4 + (dst[i]->lo ? 4 : 0)) + (src[i]->gain ? dst[i]->cols * 4.0 : 0.0);
+      }
+      PhaseScope ps(m, FG_PHASE_WIDEN, s, bytes);
+      widen_fold_kernel<<<dim3(4 * 148, 4), 256, 0, s>>>(jobs);
+      FG_CUDA_TRY(cudaGetLastError());
+    }
     // attention arguments (embed.go:209, attention.go:130)
     AttnArgs a{};
     a.q = m->qkv;
@@ -539,7 +723,7 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
       FG_TRY(attn_tc_carve(m->attn_ws, B, T, T, Hq, Hkv, &ops));
     }
     // q|k|v = rowscale ⊙ (x · Wqkv'ᵀ)   (embed.go:193-197)
-    GemmArgs g = make_gemm(int(M), m->x, x_lo, H, L.wqkv, split);
+    GemmArgs g = make_gemm(int(M), m->x, x_lo, H, Wqkv, split);
     g.epi.rowscale = m->rowscale;
     if (tc) {
       // + QK-norm and RoPE (embed.go:198-207) in the epilogue
@@ -583,7 +767,7 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
       }
     }
     // o0 = att · Wo   (embed.go:212-214)
-    g = make_gemm(int(M), m->att, att_lo, attw, L.wo, split);
+    g = make_gemm(int(M), m->att, att_lo, attw, Wo, split);
     g.epi.out = m->tmp;
     g.epi.ldo = H;
     {
@@ -597,7 +781,7 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
                                nullptr, M, H, s));
     }
     // gu = GELU(rs·x·Wg') ⊙ (rs·x·Wu')   (embed.go:224-227)
-    g = make_gemm(int(M), m->x, x_lo, H, L.wgu, split);
+    g = make_gemm(int(M), m->x, x_lo, H, Wgu, split);
     g.epi.out = m->gu;
     g.epi.ldo = F;
     g.epi.out_lo = gu_lo;
@@ -609,7 +793,7 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
       FG_TRY(gemm_tn(g, m->err, s));
     }
     // mlp0 = gu · Wd   (embed.go:229)
-    g = make_gemm(int(M), m->gu, gu_lo, F, L.wd, split);
+    g = make_gemm(int(M), m->gu, gu_lo, F, Wd, split);
     g.epi.out = m->tmp;
     g.epi.ldo = H;
     {
@@ -694,8 +878,27 @@ int fg_model_create(const fg_config* cfg, int device, fg_model** out) {
   m->attn_simt = att && std::string(att) == "simt";
   const char* alo = std::getenv("FG_GEMM_ALO");
   m->alo_global = alo && std::string(alo) == "global";
+  const char* wm = std::getenv("FG_WEIGHTS");
+  if (wm && std::string(wm) == "bf16") m->weight_mode = FG_WEIGHTS_BF16;
   *out = m;
   return FG_OK;
+}
+
+int fg_model_set_weight_residency(fg_model* m, int mode) {
+  clear_error();
+  if (!m) return set_error(FG_EINVAL, "fg_model_set_weight_residency: null model");
+  if (m->finalized) return set_error(FG_ESTATE, "fg_model_set_weight_residency after finalize");
+  if (mode != FG_WEIGHTS_F32 && mode != FG_WEIGHTS_BF16)
+    return set_error(FG_EINVAL, "fg_model_set_weight_residency: unknown mode %d", mode);
+  m->weight_mode = mode;
+  return FG_OK;
+}
+
+int64_t fg_model_weight_bytes(fg_model* m) {
+  clear_error();
+  if (!m) return set_error(FG_EINVAL, "fg_model_weight_bytes: null model");
+  if (!m->finalized) return set_error(FG_ESTATE, "fg_model_weight_bytes before finalize");
+  return int64_t(m->weight_bytes);
 }
 
 int fg_model_set_weight(fg_model* m, const char* name, int dtype, const int64_t* shape, int ndim,

@@ -146,6 +146,16 @@ def BatchTokens(n: int) -> Option:
     return f
 
 
+def WeightsBF16() -> Option:
+    """Keep the bf16 projections resident as bf16 on the device and widen
+    each layer's just before use (fg_model_set_weight_residency): half the
+    weight bytes, identical embeddings. The reference lists this as open
+    work (TODO.md: "bf16 weight storage expanded during GEMM packing")."""
+    def f(m):
+        m.weight_residency = _lib.WEIGHTS_BF16
+    return f
+
+
 @dataclass
 class DenseSpec:
     w: np.ndarray          # [out, in] float32 or bf16 bits
@@ -210,6 +220,7 @@ class Model:
         self.batch_tokens = 8192
         self.scale = 1.0 / math.sqrt(cfg.query_pre_attn_scalar)
         self.dense = list(dense)
+        self.weight_residency = _lib.WEIGHTS_F32
         for o in options:
             o(self)
         lib = _lib.lib()
@@ -241,6 +252,7 @@ class Model:
         _lib.check(lib.fg_model_create(C.byref(fc), device, C.byref(h)))
         self._h = h
         try:
+            _lib.check(lib.fg_model_set_weight_residency(self._h, int(self.weight_residency)))
             for name, (dt, arr) in weights.items():
                 self._set(name, dt, arr)
             for j, d in enumerate(self.dense):
@@ -263,6 +275,12 @@ class Model:
     def Dim(self) -> int:
         """Embedding width before Matryoshka truncation (model.go:336-344)."""
         return int(self.dense[-1].shape[0]) if self.dense else self.cfg.hidden_size
+
+    def weight_bytes(self) -> int:
+        """Device bytes held by the weights (fg_model_weight_bytes)."""
+        n = _lib.lib().fg_model_weight_bytes(self._h)
+        _lib.check(int(n) if n < 0 else 0)
+        return int(n)
 
     def close(self) -> None:
         if getattr(self, "_h", None):

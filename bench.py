@@ -185,7 +185,8 @@ def run_ours(args, rank, local_rank, world, cfg):
                                 device_id=dev)
     prec = gemma.PREC_TF32 if args.precision == "tf32" else gemma.PREC_SPLIT_TF32
     w = S.make_weights(cfg, seed=0)
-    model = gemma.from_synthetic(cfg, w, device=local_rank, max_batch_tokens=BATCH * SEQ)
+    opts = [gemma.WeightsBF16()] if args.weights == "bf16" else []
+    model = gemma.from_synthetic(cfg, w, device=local_rank, max_batch_tokens=BATCH * SEQ, options=opts)
     dim = model.Dim()
     ids_np = S.make_ids(BATCH, SEQ, 1 if rank == 0 else 1000 + rank)
     len_np = np.full(BATCH, SEQ, np.int32)
@@ -315,6 +316,8 @@ def run_ours(args, rank, local_rank, world, cfg):
                        "global_batch": BATCH * world, "seq_len": SEQ,
                        "parallelism": f"replicas x{world} + NCCL gather of embeddings onto rank 0" if world > 1 else "single GPU",
                        "precision": args.precision,
+                       "weights_resident": args.weights,
+                       "weight_bytes": model.weight_bytes(),
                        "l2_flush": "none: inputs larger than L2 (weights 1.2 GB, activations > 4 GB per step)"},
             "tokens_per_s": value * SEQ,
             "attention_tflops": (attn * BATCH * args.steps / (attn_ms / 1e3) / 1e12) if attn_ms else None,
@@ -342,6 +345,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--precision", choices=["split_tf32", "tf32"], default="split_tf32")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--weights", choices=["f32", "bf16"], default="f32",
+                    help="projection weights resident in fp32 (default) or bf16, widened per layer")
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="sequences per GPU (default 256; smaller only for profiling runs)")
     ap.add_argument("--seq", type=int, default=SEQ, help="tokens per sequence (default 512)")

@@ -136,6 +136,25 @@ int fg_model_set_weight(fg_model* m, const char* name, int dtype, const int64_t*
  * max_batch_tokens sizes the device workspace (B·T of the largest call). */
 int fg_model_finalize(fg_model* m, int64_t max_batch_tokens);
 
+/* Device residency of the encoder's projection weights, chosen before
+ * fg_model_finalize (no counterpart in the reference, whose TODO.md lists
+ * "bf16 weight storage expanded during GEMM packing (halves the 1.2 GB)";
+ * its bf16 widening is safetensors/convert.go:31-38).
+ * FG_WEIGHTS_F32 (default): the gain-folded fp32 projections and their
+ * split-TF32 low parts stay resident. FG_WEIGHTS_BF16: every bf16-exact
+ * projection stays resident as bf16 beside its fp32 pre-norm gain, and each
+ * layer's are widened, folded and split into one layer's fp32 workspace on
+ * the stream just before that layer's GEMMs — the same operands bit for
+ * bit, so the embeddings are identical. A layer with a projection that is
+ * not bf16-exact stays fp32. Returns FG_ESTATE after finalize. */
+#define FG_WEIGHTS_F32 0
+#define FG_WEIGHTS_BF16 1
+int fg_model_set_weight_residency(fg_model* m, int mode);
+
+/* Device bytes the model's weights occupy (embedding table, projections and
+ * their low parts, gains, RoPE tables, the widening workspace). */
+int64_t fg_model_weight_bytes(fg_model* m);
+
 /* Embeds B sequences of ids, right-padded to T, and writes [B, dim] float
  * embeddings (mean-pooled, Dense head, Matryoshka-narrowed, L2-normalised)
  * in input order. Host buffers; synchronous. Same semantics as
@@ -172,7 +191,8 @@ void fg_model_destroy(fg_model* m);
 #define FG_PHASE_GEMM_GATE_UP 6
 #define FG_PHASE_GEMM_DOWN 7
 #define FG_PHASE_POOL_HEAD 8
-#define FG_NUM_PHASES 9
+#define FG_PHASE_WIDEN 9 /* bf16-resident projections widened per layer */
+#define FG_NUM_PHASES 10
 int fg_model_set_profiling(fg_model* m, int enable);
 int fg_model_read_profile(fg_model* m, double* ms, int64_t* launches, double* work, int n);
 

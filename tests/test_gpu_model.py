@@ -129,6 +129,76 @@ def test_length_zero_and_one(small):
     assert c >= COS_MIN and m <= MAXABS, (c, m)
 
 
+def test_embedding_table_bf16_residency(small, monkeypatch):
+    """A bf16-exact table is kept as bf16 on the device and widened in the
+    gather: the result is bitwise the fp32-resident table's
+    (FG_EMBED_BF16=0). A table that is not bf16-exact stays fp32 and
+    matches the oracle on the same weights."""
+    from ai_b200 import _lib, gemma
+    from ai_b200 import synthetic as S
+    from oracle import oracle as O
+
+    cfg, w, model, orc = small
+    ids = S.make_ids(3, 64, 5, cfg["vocab_size"])
+    lengths = np.array([64, 17, 40], np.int32)
+    base = model.embed_padded(ids, lengths)
+    monkeypatch.setenv("FG_EMBED_BF16", "0")
+    m32 = gemma.from_synthetic(cfg, w, device=0, max_batch_tokens=8192)
+    try:
+        assert np.array_equal(m32.embed_padded(ids, lengths), base)
+    finally:
+        m32.close()
+    monkeypatch.delenv("FG_EMBED_BF16")
+
+    wf = {k: S.bf16_to_f32(v) for k, v in w.items()}
+    t = wf["embed_tokens.weight"]
+    noise = np.random.default_rng(9).standard_normal(t.shape).astype(np.float32)
+    wf["embed_tokens.weight"] = (t * (1 + 1e-3 * noise)).astype(np.float32)
+    assert np.any(wf["embed_tokens.weight"].view(np.uint32) & 0xFFFF)
+    body = {k: (_lib.DT_BF16, v) for k, v in w.items() if not k.startswith("dense.")}
+    body["embed_tokens.weight"] = (_lib.DT_F32, wf["embed_tokens.weight"])
+    dense = [gemma.DenseSpec(w[f"dense.{j}.linear.weight"], _lib.DT_BF16)
+             for j in range(len([k for k in w if k.startswith("dense.")]))]
+    mf = gemma.Model(gemma.config_from_dict(cfg), body, dense, True, device=0, max_batch_tokens=8192)
+    try:
+        got = mf.embed_padded(ids, lengths)
+    finally:
+        mf.close()
+    ref = O.OracleModel(cfg, wf).embed_padded(ids, lengths, mode=O.F64)
+    c, m = _cmp(got, ref)
+    assert c >= COS_MIN and m <= MAXABS, (c, m)
+    assert not np.array_equal(got, base)
+
+
+@pytest.mark.parametrize("norm_std", [0.0, 0.1])
+def test_bf16_resident_projections_are_bitwise_identical(norm_std):
+    """gemma.WeightsBF16(): projections resident as bf16, widened, gain-folded
+    and split per layer on the device, give the same embeddings bit for bit
+    as the fp32-resident weights, in split-TF32 and plain TF32, with zero
+    norm weights (folded weights bf16-exact, no low parts) and non-zero ones
+    (folded weights with low parts); the weights take fewer device bytes."""
+    from ai_b200 import _lib, gemma
+    from ai_b200 import synthetic as S
+
+    cfg = S.small_config(layers=3, vocab=2048)
+    w = S.make_weights(cfg, seed=31, norm_std=norm_std)
+    ids = S.make_ids(4, 96, 6, cfg["vocab_size"])
+    lengths = np.array([96, 50, 1, 77], np.int32)
+    m32 = gemma.from_synthetic(cfg, w, device=0, max_batch_tokens=4096)
+    m16 = gemma.from_synthetic(cfg, w, device=0, max_batch_tokens=4096, options=[gemma.WeightsBF16()])
+    try:
+        for prec in (_lib.PREC_SPLIT_TF32, _lib.PREC_TF32):
+            a = m32.embed_padded(ids, lengths, precision=prec)
+            b = m16.embed_padded(ids, lengths, precision=prec)
+            assert np.array_equal(a, b), prec
+        b32, b16 = m32.weight_bytes(), m16.weight_bytes()
+        print(f"norm_std {norm_std}: weight bytes fp32 {b32}, bf16 {b16}")
+        assert b16 < b32
+    finally:
+        m32.close()
+        m16.close()
+
+
 def test_batch_invariance(small):
     """A sequence embeds the same alone and inside a padded batch
     (models/gemma/gemma_test.go:117-135 asks ≥ 0.9999)."""
