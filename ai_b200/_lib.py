@@ -114,6 +114,11 @@ SIGNATURES = {
     "fg_rope": (C.c_int, [_vp, _i64, C.c_int, C.c_int, C.c_double, _vp, _vp, _vp]),
     "fg_attention": (C.c_int, [_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                C.c_int, _vp, C.c_int, C.c_float, _vp, C.c_int, _vp]),
+    "fg_normalize_rows": (C.c_int, [_i64, _i64, _vp, _i64, _vp, _i64, _vp]),
+    "fg_similarities": (C.c_int, [_i64, _i64, _i64, _vp, _i64, _vp, _i64, _vp, _i64, C.c_int, _vp]),
+    "fg_nearest": (C.c_int, [_i64, _i64, _i64, _vp, _i64, _vp, _i64, _vp, _vp, C.c_int, _vp]),
+    "fg_kmeans": (C.c_int, [_i64, _i64, _vp, _i64, C.c_int, C.c_int, C.c_uint64, _vp, _vp, _vp, _vp,
+                            C.POINTER(C.c_int), C.c_int, _vp]),
 }
 
 

@@ -28,6 +28,7 @@ SOURCES = [
     "fg_ops.cu",
     "fg_model.cu",
     "fg_noalloc.cu",
+    "fg_cluster.cu",
 ]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

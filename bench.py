@@ -337,6 +337,84 @@ def run_ours(args, rank, local_rank, world, cfg):
         dist.destroy_process_group()
 
 
+def run_cluster(args):
+    """--workload cluster: the consumer of the embeddings on one GPU —
+    cluster.Nearest at the reference's TestNearestSpeed size (50 000 unit
+    rows × 768 against 40 centres, cluster_test.go:65-79) timed on the
+    device with CUDA events, and cluster.KMeans (k = 40, 20 rounds) timed
+    end to end through its host call; the CPU restatement (oracle/cluster.py,
+    numpy float64 products on all host threads) beside both."""
+    import torch
+
+    from ai_b200 import cluster as CL
+    from oracle import cluster as OC
+
+    dev = torch.device("cuda:0")
+    n, d, k = 50000, 768, 40
+    rng = np.random.default_rng(12)
+    groups = OC.normalize(rng.standard_normal((k, d)).astype(np.float32))
+    xs = OC.normalize((groups[np.arange(n) % k] + 0.1 * rng.standard_normal((n, d))).astype(np.float32))
+    cs = OC.normalize(rng.standard_normal((k, d)).astype(np.float32))
+    x = torch.from_numpy(xs).to(dev)
+    c = torch.from_numpy(cs).to(dev)
+    idx = torch.empty(n, dtype=torch.int32, device=dev)
+    sim = torch.empty(n, dtype=torch.float32, device=dev)
+    lib = __import__("ai_b200._lib", fromlist=["lib"]).lib()
+    stream = torch.cuda.current_stream(dev)
+
+    def nearest():
+        rc = lib.fg_nearest(n, k, d, x.data_ptr(), d, c.data_ptr(), d, idx.data_ptr(), sim.data_ptr(),
+                            0, stream.cuda_stream)
+        assert rc == 0
+    for _ in range(max(args.warmup, 3)):
+        nearest()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = max(args.steps, 20)
+    clocks = ClockSampler([0])
+    clocks.start()
+    e0.record(stream)
+    for _ in range(reps):
+        nearest()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / reps
+    algo_bytes = n * d * 4 + k * d * 4 + n * 8  # rows read once, centres, index + similarity written
+    pk = peaks()
+    gbs = algo_bytes / (ms / 1e3) / 1e9
+    t0 = time.perf_counter()
+    want_i, _ = OC.nearest(xs, cs)
+    cpu_nearest_ms = (time.perf_counter() - t0) * 1e3
+    agree = float(np.mean(idx.cpu().numpy() == want_i))
+
+    t0 = time.perf_counter()
+    res = CL.KMeans(x, k, 20, 1)
+    torch.cuda.synchronize()
+    km_ms = (time.perf_counter() - t0) * 1e3
+    t0 = time.perf_counter()
+    ref = OC.kmeans(xs, k, 20, 1)
+    cpu_km_ms = (time.perf_counter() - t0) * 1e3
+    line = {
+        "metric": "cluster.Nearest rows/s, 50000 x 768 against 40 centres", "value": n / (ms / 1e3),
+        "unit": "rows/s", "n_gpus": 1, "steps": reps, "warmup": max(args.warmup, 3), "ms_per_step": ms,
+        "higher_is_better": True, "dtype": "f32 (split-TF32 product)", "data": "synthetic: 40 noisy groups of unit rows, seed 12",
+        "config": {"workload": "cluster: Nearest 50000 x 768 vs 40 centres; KMeans k=40, 20 rounds, seed 1",
+                   "l2_flush": "none: the rows (154 MB) exceed L2"},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": gbs / pk["hbm_gbs"], "traffic": None,
+                     "note": f"algorithmic bytes {algo_bytes} per call ({pk['source']} peak)"},
+        "nearest_index_agreement_with_oracle": agree,
+        "kmeans": {"ms": km_ms, "iterations": res.Iterations, "inertia": res.Inertia(),
+                   "oracle_iterations": ref.iterations, "oracle_inertia": ref.inertia(),
+                   "assignment_equal": bool(np.array_equal(np.asarray(res.Assignment), ref.assignment))},
+        "cpu_baseline": {"nearest_ms": cpu_nearest_ms, "kmeans_ms": cpu_km_ms, "kind": "port",
+                         "cores": os.cpu_count(), "sample": "the same inputs, oracle/cluster.py (numpy)"},
+        "clocks": clk,
+    }
+    print(json.dumps(line))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -350,7 +428,12 @@ def main():
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="sequences per GPU (default 256; smaller only for profiling runs)")
     ap.add_argument("--seq", type=int, default=SEQ, help="tokens per sequence (default 512)")
+    ap.add_argument("--workload", choices=["encoder", "cluster"], default="encoder",
+                    help="encoder (the headline, default) or cluster (Nearest / KMeans on one GPU)")
     args = ap.parse_args()
+    if args.workload == "cluster":
+        run_cluster(args)
+        return
     globals().update(BATCH=args.batch, SEQ=args.seq)
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

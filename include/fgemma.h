@@ -252,6 +252,40 @@ int fg_attention(const float* q, const float* k, const float* v, int B, int Hq, 
                  int S, int D, const int32_t* key_lengths, int window, float scale, float* out,
                  int precision, void* stream);
 
+/* ---- cluster: the consumer of the embeddings (cluster/cluster.go) ------ */
+/* Device pointers, row-major with leading dimensions; `precision` as for
+ * fg_matmul (the similarity products run on the split-TF32 GEMM). */
+
+/* out = every row of x [n, d] scaled to unit length; rows of length zero
+ * stay zero — cluster.Normalize (cluster.go:19-28). out may equal x. */
+int fg_normalize_rows(int64_t n, int64_t d, const float* x, int64_t ldx, float* out, int64_t ldo,
+                      void* stream);
+
+/* out [q, n] = queries [q, d] · docs [n, d]ᵀ, the cosine similarities of
+ * unit-length rows — cluster.Similarities (cluster.go:185-190). */
+int fg_similarities(int64_t q, int64_t n, int64_t d, const float* queries, int64_t ldq, const float* docs,
+                    int64_t ldd, float* out, int64_t ldo, int precision, void* stream);
+
+/* For every row of x [n, d], the index of the most similar of the k
+ * centres [k, d] (the first on ties, as tensor.Argmax) and that similarity
+ * — cluster.Nearest (cluster.go:136-148). Asynchronous on the stream. */
+int fg_nearest(int64_t n, int64_t k, int64_t d, const float* x, int64_t ldx, const float* centres, int64_t ldc,
+               int32_t* index, float* similarity, int precision, void* stream);
+
+/* k-means of the unit-length rows of x [n, d] by cosine similarity —
+ * cluster.KMeans (cluster.go:43-133): k-means++ seeding driven by Go's
+ * math/rand/v2 PCG seeded (seed, seed ^ 0x9e3779b97f4a7c15), then up to
+ * `iters` rounds of assignment (one product + row argmax) and centre update
+ * (row sums in row order, empty centres restarted on the worst-fitting row,
+ * renormalised), stopping after a round in which no row changed centre
+ * (from the second round on). Writes centres [k, d] (unit length, leading
+ * dimension d), assignment [n], similarity [n] (each row's similarity to
+ * its centre), sizes [k] and *iterations. k outside 1..n is FG_EINVAL (the
+ * reference panics). Synchronous. */
+int fg_kmeans(int64_t n, int64_t d, const float* x, int64_t ldx, int k, int iters, uint64_t seed,
+              float* centres, int32_t* assignment, float* similarity, int32_t* sizes, int* iterations,
+              int precision, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
