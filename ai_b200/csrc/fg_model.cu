@@ -634,6 +634,51 @@ GemmArgs make_gemm(int M, const float* A, const float* A_lo, int64_t lda, const 
   return g;
 }
 
+struct Batch {
+  int start, count, T;  // positions [start, start+count) of the order; padded length T ≥ 1
+};
+
+// The batching of (*Model).Embed (embed.go:46-74): indices stably sorted by
+// length (sortIndex, model.go:412), then greedy batches in that order, a
+// batch closing when admitting the next sequence would make its padded
+// size max_len·count exceed the budget.
+void plan_batches(const int* len, int nseq, int64_t budget, std::vector<int>& order, std::vector<Batch>& batches) {
+  order.resize(static_cast<size_t>(nseq));
+  for (int i = 0; i < nseq; ++i) order[size_t(i)] = i;
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return len[a] < len[b]; });
+  batches.clear();
+  int start = 0, count = 0, max_len = 0;
+  for (int k = 0; k < nseq; ++k) {
+    const int l = len[order[size_t(k)]];
+    int nm = std::max(max_len, l);
+    if (count > 0 && int64_t(nm) * (count + 1) > budget) {
+      batches.push_back({start, count, std::max(max_len, 1)});
+      start = k;
+      count = 0;
+      max_len = 0;
+      nm = l;
+    }
+    ++count;
+    max_len = nm;
+  }
+  if (count > 0) batches.push_back({start, count, std::max(max_len, 1)});
+}
+
+// The tensor-core attention's operand workspace, grown (never shrunk) to
+// `need` bytes; growing waits for the work already queued on `s`.
+int grow_attn_ws(fg_model* m, size_t need, cudaStream_t s) {
+  if (need <= m->attn_ws_bytes) return FG_OK;
+  if (m->attn_ws) {
+    FG_CUDA_TRY(cudaStreamSynchronize(s));
+    FG_CUDA_TRY(cudaFree(m->attn_ws));
+    m->attn_ws = nullptr;
+    m->attn_ws_bytes = 0;
+  }
+  FG_CUDA_TRY(cudaMalloc(&m->attn_ws, need));
+  m->attn_ws_bytes = need;
+  return FG_OK;
+}
+
 int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int T, int dim,
             int precision, float* out, cudaStream_t s) {
   const fg_config& c = m->cfg;
@@ -709,17 +754,7 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
     const bool tc = !m->attn_simt && attn_tc_supported(a);
     AttnOperands ops{};
     if (tc) {
-      const size_t need = attn_tc_workspace_bytes(B, T, T, Hq, Hkv);
-      if (need > m->attn_ws_bytes) {
-        if (m->attn_ws) {
-          FG_CUDA_TRY(cudaStreamSynchronize(s));
-          FG_CUDA_TRY(cudaFree(m->attn_ws));
-          m->attn_ws = nullptr;
-          m->attn_ws_bytes = 0;
-        }
-        FG_CUDA_TRY(cudaMalloc(&m->attn_ws, need));
-        m->attn_ws_bytes = need;
-      }
+      FG_TRY(grow_attn_ws(m, attn_tc_workspace_bytes(B, T, T, Hq, Hkv), s));
       FG_TRY(attn_tc_carve(m->attn_ws, B, T, T, Hq, Hkv, &ops));
     }
     // q|k|v = rowscale ⊙ (x · Wqkv'ᵀ)   (embed.go:193-197)
@@ -1003,6 +1038,148 @@ int fg_embed_ids(fg_model* m, const int32_t* ids, const int32_t* lengths, int B,
   FG_TRY(fg_embed_ids_device(m, m->d_ids, m->d_len, B, T, dim, precision, m->d_out, m->stream));
   FG_CUDA_TRY(cudaMemcpyAsync(out, m->d_out, size_t(nout) * 4, cudaMemcpyDeviceToHost, m->stream));
   FG_CUDA_TRY(cudaStreamSynchronize(m->stream));
+  return fg_model_check(m);
+}
+
+int fg_plan_batches(const int32_t* lengths, int nseq, int64_t batch_tokens, int32_t* order, int32_t* batch_end) {
+  clear_error();
+  if (nseq < 0 || batch_tokens < 1) return set_error(FG_EINVAL, "fg_plan_batches: bad arguments");
+  if (nseq == 0) return 0;
+  if (!lengths || !order || !batch_end) return set_error(FG_EINVAL, "fg_plan_batches: null buffer");
+  std::vector<int> len(lengths, lengths + nseq), ord;
+  for (int l : len)
+    if (l < 0) return set_error(FG_EINVAL, "fg_plan_batches: negative length");
+  std::vector<Batch> batches;
+  plan_batches(len.data(), nseq, batch_tokens, ord, batches);
+  for (int i = 0; i < nseq; ++i) order[i] = ord[size_t(i)];
+  for (size_t b = 0; b < batches.size(); ++b) batch_end[b] = batches[b].start + batches[b].count;
+  return int(batches.size());
+}
+
+int fg_embed_many(fg_model* m, const int32_t* ids, const int64_t* offsets, int nseq, int max_tokens,
+                  int64_t batch_tokens, int dim, int precision, float* out) {
+  clear_error();
+  if (!m) return set_error(FG_EINVAL, "null model");
+  if (!m->finalized) return set_error(FG_ESTATE, "embed before fg_model_finalize");
+  if (nseq < 0) return set_error(FG_EINVAL, "negative sequence count");
+  if (nseq == 0) return FG_OK;
+  if (!offsets || !out) return set_error(FG_EINVAL, "null buffer");
+  if (batch_tokens < 1) return set_error(FG_EINVAL, "batch_tokens %lld < 1", (long long)batch_tokens);
+  if (precision != FG_PREC_SPLIT_TF32 && precision != FG_PREC_TF32)
+    return set_error(FG_EINVAL, "unknown precision %d", precision);
+  const int full = model_dim(m);
+  if (dim < 1 || dim > full) return set_error(FG_EINVAL, "gemma: Dim(%d) outside 1..%d", dim, full);
+  const int cap_t = m->cfg.max_tokens;
+  const int max_t = (max_tokens > 0 && max_tokens < cap_t) ? max_tokens : cap_t;
+  // truncate (embed.go:38-40), validate
+  std::vector<int> len(static_cast<size_t>(nseq));
+  if (offsets[0] < 0) return set_error(FG_EINVAL, "offsets[0] = %lld < 0", (long long)offsets[0]);
+  for (int i = 0; i < nseq; ++i) {
+    const int64_t n = offsets[i + 1] - offsets[i];
+    if (n < 0) return set_error(FG_EINVAL, "offsets decrease at sequence %d", i);
+    len[size_t(i)] = int(std::min<int64_t>(n, max_t));
+    if (len[size_t(i)] > 0 && !ids) return set_error(FG_EINVAL, "null ids");
+    for (int t = 0; t < len[size_t(i)]; ++t) {
+      const int32_t id = ids[offsets[i] + t];
+      if (id < 0 || id >= m->cfg.vocab_size)
+        return set_error(FG_EINVAL, "token id %d at [%d, %d] outside the vocabulary", id, i, t);
+    }
+  }
+  std::vector<int> order;
+  std::vector<Batch> batches;
+  plan_batches(len.data(), nseq, batch_tokens, order, batches);
+  int64_t max_bt = 0;
+  int max_b = 0;
+  size_t attn_need = 0;
+  for (const Batch& b : batches) {
+    max_bt = std::max<int64_t>(max_bt, int64_t(b.count) * b.T);
+    max_b = std::max(max_b, b.count);
+    if (!m->attn_simt && m->cfg.head_dim == 256)
+      attn_need = std::max(attn_need, attn_tc_workspace_bytes(b.count, b.T, b.T, m->cfg.num_heads, m->cfg.num_kv_heads));
+  }
+  FG_CUDA_TRY(cudaSetDevice(m->device));
+  if (!m->stream) FG_CUDA_TRY(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
+  cudaStream_t s = m->stream;
+  FG_TRY(ensure_workspace(m, max_bt, max_b));
+  FG_TRY(grow_attn_ws(m, attn_need, s));
+
+  // Two slots of pinned staging and device buffers: batch i+1 is packed and
+  // copied in (copy stream) while batch i runs (the model's stream), and
+  // batch i−1's embeddings are scattered into `out` meanwhile.
+  struct Slot {
+    int32_t *h_ids = nullptr, *h_len = nullptr, *d_ids = nullptr, *d_len = nullptr;
+    float *h_out = nullptr, *d_out = nullptr;
+    cudaEvent_t h2d = nullptr, done = nullptr;
+  } slot[2];
+  cudaStream_t cs = nullptr;
+  int rc = FG_OK;
+  auto cuda_ok = [&](cudaError_t e, const char* what) {
+    if (e != cudaSuccess && rc == FG_OK) rc = set_error(FG_ECUDA, "fg_embed_many: %s failed: %s", what, cudaGetErrorString(e));
+    return rc == FG_OK;
+  };
+  bool ok = cuda_ok(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking), "stream");
+  for (int k = 0; k < 2 && ok; ++k) {
+    Slot& q = slot[k];
+    ok = cuda_ok(cudaHostAlloc(reinterpret_cast<void**>(&q.h_ids), size_t(max_bt) * 4, cudaHostAllocDefault), "pinned ids") &&
+         cuda_ok(cudaHostAlloc(reinterpret_cast<void**>(&q.h_len), size_t(max_b) * 4, cudaHostAllocDefault), "pinned lengths") &&
+         cuda_ok(cudaHostAlloc(reinterpret_cast<void**>(&q.h_out), size_t(max_b) * dim * 4, cudaHostAllocDefault), "pinned out") &&
+         cuda_ok(cudaMalloc(&q.d_ids, size_t(max_bt) * 4), "ids") && cuda_ok(cudaMalloc(&q.d_len, size_t(max_b) * 4), "lengths") &&
+         cuda_ok(cudaMalloc(&q.d_out, size_t(max_b) * dim * 4), "out") &&
+         cuda_ok(cudaEventCreateWithFlags(&q.h2d, cudaEventDisableTiming), "event") &&
+         cuda_ok(cudaEventCreateWithFlags(&q.done, cudaEventDisableTiming), "event");
+  }
+  auto scatter = [&](int bi) {
+    const Batch& b = batches[size_t(bi)];
+    const Slot& q = slot[bi & 1];
+    for (int r = 0; r < b.count; ++r)
+      std::memcpy(out + int64_t(order[size_t(b.start + r)]) * dim, q.h_out + int64_t(r) * dim, size_t(dim) * 4);
+  };
+  const int nb = int(batches.size());
+  for (int bi = 0; bi < nb && ok; ++bi) {
+    const Batch& b = batches[size_t(bi)];
+    Slot& q = slot[bi & 1];
+    for (int r = 0; r < b.count; ++r) {
+      const int i = order[size_t(b.start + r)];
+      const int l = len[size_t(i)];
+      int32_t* row = q.h_ids + int64_t(r) * b.T;
+      if (l) std::memcpy(row, ids + offsets[i], size_t(l) * 4);
+      std::memset(row + l, 0, size_t(b.T - l) * 4);  // right-padded with id 0 (embed.go:124-130)
+      q.h_len[r] = l;
+    }
+    ok = cuda_ok(cudaStreamWaitEvent(cs, q.done, 0), "wait") &&  // the slot's previous batch is finished
+         cuda_ok(cudaMemcpyAsync(q.d_ids, q.h_ids, size_t(b.count) * b.T * 4, cudaMemcpyHostToDevice, cs), "copy in") &&
+         cuda_ok(cudaMemcpyAsync(q.d_len, q.h_len, size_t(b.count) * 4, cudaMemcpyHostToDevice, cs), "copy in") &&
+         cuda_ok(cudaEventRecord(q.h2d, cs), "record") && cuda_ok(cudaStreamWaitEvent(s, q.h2d, 0), "wait");
+    if (!ok) break;
+    rc = forward(m, q.d_ids, q.d_len, b.count, b.T, dim, precision, q.d_out, s);
+    ok = rc == FG_OK &&
+         cuda_ok(cudaMemcpyAsync(q.h_out, q.d_out, size_t(b.count) * dim * 4, cudaMemcpyDeviceToHost, s), "copy out") &&
+         cuda_ok(cudaEventRecord(q.done, s), "record");
+    if (ok && bi > 0) {
+      ok = cuda_ok(cudaEventSynchronize(slot[(bi - 1) & 1].done), "sync");
+      if (ok) scatter(bi - 1);
+    }
+  }
+  if (ok) {
+    ok = cuda_ok(cudaEventSynchronize(slot[(nb - 1) & 1].done), "sync");
+    if (ok) scatter(nb - 1);
+  }
+  cudaStreamSynchronize(s);
+  if (cs) {
+    cudaStreamSynchronize(cs);
+    cudaStreamDestroy(cs);
+  }
+  for (Slot& q : slot) {
+    if (q.h_ids) cudaFreeHost(q.h_ids);
+    if (q.h_len) cudaFreeHost(q.h_len);
+    if (q.h_out) cudaFreeHost(q.h_out);
+    if (q.d_ids) cudaFree(q.d_ids);
+    if (q.d_len) cudaFree(q.d_len);
+    if (q.d_out) cudaFree(q.d_out);
+    if (q.h2d) cudaEventDestroy(q.h2d);
+    if (q.done) cudaEventDestroy(q.done);
+  }
+  if (rc != FG_OK) return rc;
   return fg_model_check(m);
 }
 

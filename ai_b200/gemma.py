@@ -357,38 +357,48 @@ class Model:
 
     def embed_ids(self, seqs: Sequence[Sequence[int]], Dim: Optional[int] = None,
                   precision: int = PREC_SPLIT_TF32) -> List[np.ndarray]:
-        """(*Model).Embed (embed.go:15-80) from token ids."""
+        """(*Model).Embed (embed.go:15-80) from token ids: truncation, the
+        stable length sort, greedy batches under BatchTokens and the
+        overlapped host/GPU pipeline all run in fg_embed_many."""
         dim = self.Dim()
         if Dim is not None and Dim != 0:
             if Dim < 1 or Dim > dim:
                 raise GemmaError(f"gemma: Dim({Dim}) outside 1..{dim}")
             dim = Dim
-        ids = [list(s)[: self.max_tokens] for s in seqs]
-        lengths = [len(s) for s in ids]
-        order = sorted(range(len(ids)), key=lambda i: lengths[i])  # stable, like sort.SliceStable
-        out: List[Optional[np.ndarray]] = [None] * len(ids)
-        batch: List[int] = []
-        max_len = 0
+        n = len(seqs)
+        if n == 0:
+            return []
+        lens = np.fromiter((len(s) for s in seqs), dtype=np.int64, count=n)
+        offsets = np.zeros(n + 1, dtype=np.int64)
+        np.cumsum(lens, out=offsets[1:])
+        flat = np.zeros(max(int(offsets[-1]), 1), dtype=np.int32)
+        for i, s in enumerate(seqs):
+            if lens[i]:
+                flat[offsets[i]:offsets[i + 1]] = s
+        out = np.empty((n, dim), dtype=np.float32)
+        _lib.check(_lib.lib().fg_embed_many(self._h, flat.ctypes.data_as(C.c_void_p),
+                                            offsets.ctypes.data_as(C.c_void_p), n, int(self.max_tokens),
+                                            int(self.batch_tokens), dim, precision,
+                                            out.ctypes.data_as(C.c_void_p)))
+        return list(out)
 
-        def flush():
-            if not batch:
-                return
-            emb = self.embed_batch([ids[i] for i in batch], dim, precision)
-            for bi, idx in enumerate(batch):
-                out[idx] = emb[bi]
-            batch.clear()
 
-        for idx in order:
-            l = lengths[idx]
-            new_max = max(max_len, l)
-            if batch and new_max * (len(batch) + 1) > self.batch_tokens:
-                flush()
-                max_len = 0
-                new_max = l
-            batch.append(idx)
-            max_len = new_max
-        flush()
-        return out  # type: ignore[return-value]
+def plan_batches(lengths: Sequence[int], batch_tokens: int) -> Tuple[List[int], List[List[int]]]:
+    """The batching Model.embed_ids runs (fg_plan_batches): the indices in
+    stable length order and the batches as lists of indices."""
+    n = len(lengths)
+    ln = np.ascontiguousarray(lengths, dtype=np.int32)
+    order = np.zeros(max(n, 1), np.int32)
+    ends = np.zeros(max(n, 1), np.int32)
+    nb = _lib.lib().fg_plan_batches(ln.ctypes.data_as(C.c_void_p), n, int(batch_tokens),
+                                    order.ctypes.data_as(C.c_void_p), ends.ctypes.data_as(C.c_void_p))
+    _lib.check(min(nb, 0))
+    o = order[:n].tolist()
+    batches, start = [], 0
+    for e in ends[:nb].tolist():
+        batches.append(o[start:e])
+        start = e
+    return o, batches
 
 
 def Load(d, *options: Option, device: int = 0, max_batch_tokens: int = 8192) -> Model:

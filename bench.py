@@ -337,6 +337,88 @@ def run_ours(args, rank, local_rank, world, cfg):
         dist.destroy_process_group()
 
 
+def run_ragged(args, rank, local_rank, world, cfg):
+    """--workload ragged: benchmark config 3 — 8192 sequences, lengths
+    uniform in [16, 2048] (seed 2) — end to end through the public API on
+    host buffers: each rank embeds its cost-balanced contiguous slice of the
+    length-sorted batch with Model.embed_ids (fg_embed_many: greedy batches
+    under BatchTokens, packing and copies overlapped with the forward) and
+    the embeddings meet on rank 0 in one NCCL gather (replicas.py). A step
+    is the whole 8192-sequence batch; timed on the host around the
+    synchronous calls, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from ai_b200 import gemma, replicas
+    from ai_b200 import synthetic as S
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    prec = gemma.PREC_TF32 if args.precision == "tf32" else gemma.PREC_SPLIT_TF32
+    budget = 131072
+    w = S.make_weights(cfg, seed=0)
+    model = gemma.from_synthetic(cfg, w, device=local_rank, max_batch_tokens=budget,
+                                 options=[gemma.BatchTokens(budget)])
+    seqs, lengths = S.make_ragged(8192, 16, 2048, 2)
+    tokens = int(np.sum(lengths))
+
+    def step():
+        if world > 1:
+            return replicas.embed_replicated(model, seqs, group=None, device=dev)
+        return np.stack(model.embed_ids(seqs))
+
+    def timed():
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        t0 = time.perf_counter()
+        r = step()
+        torch.cuda.synchronize(dev)
+        el = time.perf_counter() - t0
+        if world > 1:
+            t = torch.tensor([el], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            el = float(t.item())
+        return r, el
+
+    for _ in range(max(args.warmup, 1)):
+        step()
+    times = []
+    sampler = ClockSampler(list(range(world)) if rank == 0 else [])
+    if rank == 0:
+        sampler.start()
+    res = None
+    for _ in range(max(args.steps, 1)):
+        res, el = timed()
+        times.append(el)
+    clk = sampler.stop() if rank == 0 else None
+    if rank == 0:
+        sec = statistics.median(times)
+        ok = res is not None and res.shape == (8192, model.Dim()) and bool(np.all(np.isfinite(res)))
+        line = {
+            "metric": "EmbeddingGemma embeddings/s, config 3 ragged (8192 seqs, lengths 16..2048)",
+            "value": 8192 / sec, "unit": "embeddings/s", "n_gpus": world, "steps": len(times),
+            "warmup": max(args.warmup, 1), "ms_per_step": sec * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic: random-init weights (seed 0), ragged ids seed 2",
+            "config": {"workload": "config 3: 8192 sequences, lengths uniform in [16, 2048], right-padded",
+                       "batch_tokens": budget, "valid_tokens": tokens,
+                       "parallelism": f"replicas x{world} on cost-balanced slices + NCCL gather onto rank 0"
+                       if world > 1 else "single GPU",
+                       "timing": "host wall clock around the synchronous public calls (ids on the host "
+                                 "to embeddings on rank 0's host), median of steps, max over ranks"},
+            "tokens_per_s": tokens / sec, "all_finite": ok, "clocks": clk,
+        }
+        print(json.dumps(line))
+    model.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def run_cluster(args):
     """--workload cluster: the consumer of the embeddings on one GPU —
     cluster.Nearest at the reference's TestNearestSpeed size (50 000 unit
@@ -428,8 +510,9 @@ def main():
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="sequences per GPU (default 256; smaller only for profiling runs)")
     ap.add_argument("--seq", type=int, default=SEQ, help="tokens per sequence (default 512)")
-    ap.add_argument("--workload", choices=["encoder", "cluster"], default="encoder",
-                    help="encoder (the headline, default) or cluster (Nearest / KMeans on one GPU)")
+    ap.add_argument("--workload", choices=["encoder", "ragged", "cluster"], default="encoder",
+                    help="encoder (config 2, the headline, default), ragged (config 3 end to end) "
+                         "or cluster (Nearest / KMeans on one GPU)")
     args = ap.parse_args()
     if args.workload == "cluster":
         run_cluster(args)
@@ -445,6 +528,8 @@ def main():
     cfg = dict(S.EMBEDDINGGEMMA_300M)
     if args.impl == "reference":
         run_reference(args, rank, world, cfg)
+    elif args.workload == "ragged":
+        run_ragged(args, rank, local_rank, world, cfg)
     else:
         run_ours(args, rank, local_rank, world, cfg)
 

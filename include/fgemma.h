@@ -164,6 +164,26 @@ int64_t fg_model_weight_bytes(fg_model* m);
 int fg_embed_ids(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int T, int dim,
                  int precision, float* out);
 
+/* (*Model).Embed (models/gemma/embed.go:15-80) after tokenisation, with the
+ * host work overlapped with the GPU's. Sequence i is ids[offsets[i] ..
+ * offsets[i+1]) (offsets has nseq + 1 entries), truncated to max_tokens
+ * (embed.go:38-40; 0 or more than the model's limit = the model's limit).
+ * The sequences are stably sorted by length (sortIndex, model.go:412) and
+ * cut into greedy batches whose padded size max_len·count stays within
+ * batch_tokens (embed.go:58-74; a longer single sequence runs alone), each
+ * right-padded with id 0. While one batch runs on the GPU the next is
+ * packed into pinned memory and copied in on a second stream, and the
+ * previous batch's embeddings are copied out and placed. out is
+ * [nseq, dim] in the caller's order. Synchronous. */
+int fg_embed_many(fg_model* m, const int32_t* ids, const int64_t* offsets, int nseq, int max_tokens,
+                  int64_t batch_tokens, int dim, int precision, float* out);
+
+/* fg_embed_many's batching alone, on the host (no device work): lengths
+ * [nseq] → order [nseq] (indices stably sorted by length) and batch_end
+ * [number of batches ≤ nseq] (each batch's end position in order). Returns
+ * the number of batches, or a negative status. */
+int fg_plan_batches(const int32_t* lengths, int nseq, int64_t batch_tokens, int32_t* order, int32_t* batch_end);
+
 /* As fg_embed_ids with device buffers on the model's device, asynchronous
  * on `stream` (a cudaStream_t, NULL = default stream). */
 int fg_embed_ids_device(fg_model* m, const int32_t* d_ids, const int32_t* d_lengths, int B, int T,

@@ -242,6 +242,33 @@ def test_embed_ids_batches_and_restores_order(small):
     assert c >= COS_MIN and m <= MAXABS
 
 
+def test_embed_ids_pipeline_equals_batch_by_batch(small):
+    """fg_embed_many (batches packed and copied in while the previous one
+    runs) gives, bit for bit, what running each planned batch alone gives;
+    truncation to MaxTokens (embed.go:38-40) and empty sequences included."""
+    from ai_b200 import gemma
+    from ai_b200 import synthetic as S
+
+    cfg, w, model, orc = small
+    seqs, _ = S.make_ragged(37, 1, 400, 17, cfg["vocab_size"])
+    seqs[3] = []
+    seqs[20] = list(seqs[20]) * 3  # longer than the budget: runs alone
+    model.batch_tokens = 1000
+    model.max_tokens = 700
+    try:
+        got = np.stack(model.embed_ids(seqs))
+        cut = [list(s)[:700] for s in seqs]
+        _, batches = gemma.plan_batches([len(s) for s in cut], 1000)
+        want = np.zeros_like(got)
+        for b in batches:
+            want[b] = model.embed_batch([cut[i] for i in b])
+    finally:
+        model.batch_tokens = 8192
+        model.max_tokens = 2048
+    assert len(batches) > 5
+    assert np.array_equal(got, want)
+
+
 def test_errors_are_reported_not_fatal(small):
     from ai_b200 import _lib, gemma
 

@@ -89,40 +89,27 @@ def test_load_config_and_head_from_a_model_dir(tmp_path):
     assert np.array_equal(st["embed_tokens.weight"][1], w["embed_tokens.weight"])
 
 
-class _FakeModel:
-    """Model.embed_ids with embed_batch recorded instead of run."""
-
-    def __init__(self, batch_tokens, max_tokens=2048):
-        from ai_b200 import gemma
-
-        self.batch_tokens = batch_tokens
-        self.max_tokens = max_tokens
-        self.calls = []
-        self.embed_ids = gemma.Model.embed_ids.__get__(self)
-
-    def Dim(self):
-        return 4
-
-    def embed_batch(self, seqs, dim, precision):
-        self.calls.append([len(s) for s in seqs])
-        return np.array([[len(s), s[0] if s else -1, 0, 0] for s in seqs], np.float32)
-
-
 def test_embed_batches_by_length_under_the_token_budget():
+    """fg_embed_many's batching (embed.go:46-74), on the host only."""
+    from ai_b200 import gemma
+
     lengths = [5, 3, 9, 3, 1, 7]
-    seqs = [[i] * n for i, n in enumerate(lengths)]
-    m = _FakeModel(batch_tokens=12)
-    out = m.embed_ids(seqs)
+    order, batches = gemma.plan_batches(lengths, 12)
     # stable ascending order: 1, 3, 3, 5, 7, 9; maxLen·(n+1) ≤ 12
-    assert m.calls == [[1, 3, 3], [5], [7], [9]]
-    for i, n in enumerate(lengths):
-        assert out[i][0] == n and out[i][1] == i
-
-
-def test_embed_truncates_to_max_tokens():
-    m = _FakeModel(batch_tokens=8192, max_tokens=4)
-    out = m.embed_ids([[1] * 10])
-    assert out[0][0] == 4
+    assert order == [4, 1, 3, 0, 5, 2]
+    assert [[lengths[i] for i in b] for b in batches] == [[1, 3, 3], [5], [7], [9]]
+    # a sequence longer than the budget runs alone; empty input, zero lengths
+    assert gemma.plan_batches([20, 2, 2], 8)[1] == [[1, 2], [0]]
+    assert gemma.plan_batches([], 8) == ([], [])
+    assert gemma.plan_batches([0, 0, 0], 2)[1] == [[0, 1, 2]]
+    rng = np.random.default_rng(3)
+    ln = rng.integers(0, 600, 500).tolist()
+    order, batches = gemma.plan_batches(ln, 4096)
+    assert sorted(order) == list(range(500))
+    assert [ln[i] for i in order] == sorted(ln)
+    assert sum(batches, []) == order
+    for b in batches:
+        assert len(b) == 1 or max(ln[i] for i in b) * len(b) <= 4096
 
 
 def test_tensor_ops_reject_bad_shapes_before_any_device_call():
