@@ -82,6 +82,11 @@ class Config(C.Structure):
         ("dense_out", C.c_int * MAX_DENSE),
         ("dense_tanh", C.c_int * MAX_DENSE),
         ("l2_normalize", C.c_int),
+        ("variant", C.c_int),
+        ("layer_head_dim", C.POINTER(C.c_int)),
+        ("layer_kv_heads", C.POINTER(C.c_int)),
+        ("ple_dim", C.c_int),
+        ("embedding_dim", C.c_int),
     ]
 
 

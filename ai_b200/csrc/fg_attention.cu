@@ -21,13 +21,15 @@ namespace fg {
 namespace {
 
 constexpr int kBQ = 64;
-constexpr int kBKV = 32;
 
+// Key tile: 32 keys up to head_dim 256; 16 keys at 512 so that the Q tile
+// and the K/V tiles fit in shared memory (203 KB).
 template <int DP>
 struct AttnSmem {
+  static constexpr int kKV = DP > 256 ? 16 : 32;
   static constexpr int kLd = DP + 4;
-  static constexpr size_t kFloats = size_t(kBQ) * kLd + 2 * size_t(kBKV) * kLd +
-                                    size_t(kBQ) * (kBKV + 1) + 2 * kBQ;
+  static constexpr size_t kFloats = size_t(kBQ) * kLd + 2 * size_t(kKV) * kLd +
+                                    size_t(kBQ) * (kKV + 1) + 2 * kBQ;
   static constexpr size_t kBytes = kFloats * 4;
 };
 
@@ -54,6 +56,8 @@ template <int DP>
 __global__ void __launch_bounds__(256, 1) attn_simt_kernel(const AttnArgs a) {
   using SM = AttnSmem<DP>;
   constexpr int LD = SM::kLd;
+  constexpr int kBKV = SM::kKV;
+  constexpr int KK = kBKV / 8;  // keys per thread in the score phase
   constexpr int NJ = DP / 64;  // float4 column groups per thread in the P·V phase
   extern __shared__ float4 smem4[];
   float* sm = reinterpret_cast<float*>(smem4);
@@ -128,11 +132,11 @@ __global__ void __launch_bounds__(256, 1) attn_simt_kernel(const AttnArgs a) {
     }
     __syncthreads();
 
-    float sc[2][4];
+    float sc[2][KK];
 #pragma unroll
     for (int r = 0; r < 2; ++r)
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) sc[r][kk] = 0.f;
+      for (int kk = 0; kk < KK; ++kk) sc[r][kk] = 0.f;
     const float* q0p = Qs + (2 * ty) * LD;
     const float* q1p = q0p + LD;
 #pragma unroll 4
@@ -140,7 +144,7 @@ __global__ void __launch_bounds__(256, 1) attn_simt_kernel(const AttnArgs a) {
       const float4 q0 = *reinterpret_cast<const float4*>(q0p + d);
       const float4 q1 = *reinterpret_cast<const float4*>(q1p + d);
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
+      for (int kk = 0; kk < KK; ++kk) {
         const float4 kv = *reinterpret_cast<const float4*>(Ks + (tx + 8 * kk) * LD + d);
         sc[0][kk] = fmaf(q0.x, kv.x, sc[0][kk]);
         sc[0][kk] = fmaf(q0.y, kv.y, sc[0][kk]);
@@ -156,11 +160,11 @@ __global__ void __launch_bounds__(256, 1) attn_simt_kernel(const AttnArgs a) {
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
       const int i = i0 + 2 * ty + r;
-      bool vis[4];
+      bool vis[KK];
       float tmax = -FLT_MAX;
       bool tany = false;
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
+      for (int kk = 0; kk < KK; ++kk) {
         const int j = j0 + tx + 8 * kk;
         vis[kk] = j < klen && (a.window <= 0 || (i - j < a.window && j - i < a.window));
         if (vis[kk]) {
@@ -182,7 +186,7 @@ __global__ void __launch_bounds__(256, 1) attn_simt_kernel(const AttnArgs a) {
       }
       float psum = 0.f;
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
+      for (int kk = 0; kk < KK; ++kk) {
         const float p = (vis[kk] && any_r[r]) ? expf(a.scale * (sc[r][kk] - m_r[r])) : 0.f;
         Ps[(2 * ty + r) * (kBKV + 1) + tx + 8 * kk] = p;
         psum += p;
@@ -321,11 +325,12 @@ int attention_simt(const AttnArgs& a, cudaStream_t s) {
   if (a.B == 0 || a.T == 0) return FG_OK;
   if (a.Hkv <= 0 || a.Hq % a.Hkv != 0)
     return set_error(FG_EINVAL, "attention: %d query heads not a multiple of %d key/value heads", a.Hq, a.Hkv);
-  if (a.D <= 0 || a.D > 256) return set_error(FG_EINVAL, "attention: head dimension %d unsupported (1..256)", a.D);
+  if (a.D <= 0 || a.D > 512) return set_error(FG_EINVAL, "attention: head dimension %d unsupported (1..512)", a.D);
   if (a.T > 65535 * kBQ || a.Hq > 65535 || a.B > 65535) return set_error(FG_EINVAL, "attention: grid too large");
   if (a.D <= 64) return launch_attn<64>(a, s);
   if (a.D <= 128) return launch_attn<128>(a, s);
-  return launch_attn<256>(a, s);
+  if (a.D <= 256) return launch_attn<256>(a, s);
+  return launch_attn<512>(a, s);
 }
 
 }  // namespace fg

@@ -95,12 +95,15 @@ __global__ void __launch_bounds__(256) embed_kernel(const TT* __restrict__ table
 
 // ------------------------------------------------------- QK-norm + RoPE
 // One warp per (row, head). Heads [0, Hq) are queries, [Hq, Hq+Hkv) keys,
-// [Hq+Hkv, Hq+2Hkv) values (only split when a lo buffer is given).
+// [Hq+Hkv, Hq+2Hkv) values: RMS-normalised with vgain when one is given
+// (EmbeddingGemma 2's weight-free v_norm, embed.go:300), and split when a
+// lo buffer is given; no RoPE on values.
 constexpr int kMaxPairs = 8;  // D ≤ 512
 __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
     float* __restrict__ qkv, float* __restrict__ qkv_lo, int64_t rows, int Hq, int Hkv, int D,
-    int heads_done, const float* __restrict__ qgain, const float* __restrict__ kgain, float eps,
-    const float* __restrict__ cos_t, const float* __restrict__ sin_t, int T) {
+    int heads_done, const float* __restrict__ qgain, const float* __restrict__ kgain,
+    const float* __restrict__ vgain, float eps, const float* __restrict__ cos_t,
+    const float* __restrict__ sin_t, int T) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t task = int64_t(blockIdx.x) * kWarpsPerBlock + warp;
   if (task >= rows * heads_done) return;
@@ -110,11 +113,12 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
   const int width = (Hq + 2 * Hkv) * D;
   float* v = qkv + row * width + int64_t(head) * D;
   float* vl = qkv_lo ? qkv_lo + row * width + int64_t(head) * D : nullptr;
-  if (head >= Hq + Hkv) {  // value head: split only
+  const bool value = head >= Hq + Hkv;
+  if (value && !vgain) {  // value head: split only
     for (int i = lane; i < D; i += 32) vl[i] = tf32_lo(v[i]);
     return;
   }
-  const float* g = head < Hq ? qgain : kgain;
+  const float* g = value ? vgain : (head < Hq ? qgain : kgain);
   float a[kMaxPairs], b2[kMaxPairs];
   float ss = 0.f;
 #pragma unroll
@@ -134,6 +138,23 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
   for (int p = 0; p < kMaxPairs; ++p) ss = sq_acc(ss, b2[p]);
   ss = warp_sum(ss);
   const float inv = rms_inv(ss, D, eps);
+  if (value) {
+#pragma unroll
+    for (int p = 0; p < kMaxPairs; ++p) {
+      const int i = lane + 32 * p;
+      if (i < half) {
+        const float y1 = __fmul_rn(__fmul_rn(a[p], inv), g[i]);
+        const float y2 = __fmul_rn(__fmul_rn(b2[p], inv), g[i + half]);
+        v[i] = y1;
+        v[i + half] = y2;
+        if (vl) {
+          vl[i] = tf32_lo(y1);
+          vl[i + half] = tf32_lo(y2);
+        }
+      }
+    }
+    return;
+  }
   const int t = int(row % T);
   const float* c = cos_t + int64_t(t) * half;
   const float* s = sin_t + int64_t(t) * half;
@@ -161,7 +182,7 @@ template <int C4>
 __global__ void __launch_bounds__(256) residual_postnorm_kernel(
     float* __restrict__ x, float* __restrict__ x_lo, const float* __restrict__ o,
     const float* __restrict__ gain, float eps, float* __restrict__ rowscale,
-    const float* __restrict__ fgain, int64_t rows, int n) {
+    const float* __restrict__ fgain, int64_t rows, int n, float scalar) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row = int64_t(blockIdx.x) * kWarpsPerBlock + warp;
   if (row >= rows) return;
@@ -189,6 +210,11 @@ __global__ void __launch_bounds__(256) residual_postnorm_kernel(
     xx.y = __fadd_rn(xx.y, __fmul_rn(__fmul_rn(ov[c].y, inv_o), g.y));
     xx.z = __fadd_rn(xx.z, __fmul_rn(__fmul_rn(ov[c].z, inv_o), g.z));
     xx.w = __fadd_rn(xx.w, __fmul_rn(__fmul_rn(ov[c].w, inv_o), g.w));
+    // EmbeddingGemma 2's layer scalar (embed.go:370-371); 1 elsewhere (exact)
+    xx.x = __fmul_rn(xx.x, scalar);
+    xx.y = __fmul_rn(xx.y, scalar);
+    xx.z = __fmul_rn(xx.z, scalar);
+    xx.w = __fmul_rn(xx.w, scalar);
     xv[c] = xx;
     ssx = sq_acc(ssx, xx.x);
     ssx = sq_acc(ssx, xx.y);
@@ -267,8 +293,9 @@ __global__ void row_sumsq_kernel(const float* __restrict__ x, int64_t rows, int6
   if (lane == 0) out[row] = ss;
 }
 
-__global__ void rmsnorm_kernel(const float* __restrict__ x, int64_t rows, int64_t n,
-                               const float* __restrict__ g, float eps, float* __restrict__ out) {
+// out may equal x (each row is read in full before it is written).
+__global__ void rmsnorm_kernel(const float* x, int64_t rows, int64_t n, const float* __restrict__ g,
+                               float eps, float* out) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row = int64_t(blockIdx.x) * kWarpsPerBlock + warp;
   if (row >= rows) return;
@@ -342,27 +369,27 @@ int embed_gather(const float* table, const uint16_t* table_bf16, int64_t vocab, 
 }
 
 int qk_norm_rope(float* qkv, float* qkv_lo, int64_t rows, int Hq, int Hkv, int D,
-                 const float* qgain, const float* kgain, float eps, const float* cos_t,
-                 const float* sin_t, int T, cudaStream_t s) {
+                 const float* qgain, const float* kgain, const float* vgain, float eps,
+                 const float* cos_t, const float* sin_t, int T, cudaStream_t s) {
   if (rows == 0) return FG_OK;
   if (D % 2 != 0 || D / 2 > 32 * kMaxPairs)
     return set_error(FG_EINVAL, "head_dim %d unsupported (even, at most 512)", D);
-  const int heads = Hq + Hkv + (qkv_lo ? Hkv : 0);
+  const int heads = Hq + Hkv + ((qkv_lo || vgain) ? Hkv : 0);
   const int grid = grid_for(rows * heads, kWarpsPerBlock);
-  qk_norm_rope_kernel<<<grid, 256, 0, s>>>(qkv, qkv_lo, rows, Hq, Hkv, D, heads, qgain, kgain, eps,
-                                           cos_t, sin_t, T);
+  qk_norm_rope_kernel<<<grid, 256, 0, s>>>(qkv, qkv_lo, rows, Hq, Hkv, D, heads, qgain, kgain, vgain,
+                                           eps, cos_t, sin_t, T);
   FG_CUDA_TRY(cudaGetLastError());
   return FG_OK;
 }
 
 int residual_postnorm(float* x, float* x_lo, const float* o, const float* gain, float eps,
                       float* rowscale, const float* final_gain, int64_t rows, int n,
-                      cudaStream_t s) {
+                      cudaStream_t s, float scalar) {
   if (rows == 0) return FG_OK;
   const int grid = grid_for(rows, kWarpsPerBlock);
   switch (n / 128) {
 #define FG_RES(C) \
-  case C: residual_postnorm_kernel<C><<<grid, 256, 0, s>>>(x, x_lo, o, gain, eps, rowscale, final_gain, rows, n); break;
+  case C: residual_postnorm_kernel<C><<<grid, 256, 0, s>>>(x, x_lo, o, gain, eps, rowscale, final_gain, rows, n, scalar); break;
     FG_RES(1) FG_RES(2) FG_RES(3) FG_RES(4) FG_RES(5) FG_RES(6) FG_RES(7) FG_RES(8)
 #undef FG_RES
     default:

@@ -22,17 +22,18 @@ int embed_gather(const float* table, const uint16_t* table_bf16, int64_t vocab, 
 // in place on the token-major qkv buffer [B·T, (Hq+2·Hkv)·D]; v untouched.
 // Optional lo buffer (same layout) receives split-TF32 low parts of q, k, v.
 int qk_norm_rope(float* qkv, float* qkv_lo, int64_t rows, int Hq, int Hkv, int D,
-                 const float* qgain, const float* kgain, float eps, const float* cos_t,
-                 const float* sin_t, int T, cudaStream_t s);
+                 const float* qgain, const float* kgain, const float* vgain, float eps,
+                 const float* cos_t, const float* sin_t, int T, cudaStream_t s);
 
 // x ← x + RMSNorm(o, gain) (embed.go:216-220, 231-235), then the next
 // pre-norm factor rowscale = 1/√(Σx²/n + eps). x_lo (optional) receives the
-// split-TF32 low part of the new x. When final_gain is given, x is replaced
-// by RMSNorm(x_new, final_gain) instead (embed.go:237) and rowscale/x_lo are
-// not written.
+// split-TF32 low part of the new x. x_new is (x + RMSNorm(o, gain))·scalar
+// (EmbeddingGemma 2's layer scalar, embed.go:370-371; 1 = plain residual).
+// When final_gain is given, x is replaced by RMSNorm(x_new, final_gain)
+// instead (embed.go:237) and rowscale/x_lo are not written.
 int residual_postnorm(float* x, float* x_lo, const float* o, const float* gain, float eps,
                       float* rowscale, const float* final_gain, int64_t rows, int n,
-                      cudaStream_t s);
+                      cudaStream_t s, float scalar = 1.0f);
 
 // pooled[b] = mean over t < max(len_b, 1) of h[b, t] (embed.go:381-404);
 // pooled_lo (optional) gets its split-TF32 low part.

@@ -103,6 +103,14 @@ struct Layer {
   float* post_attn = nullptr;
   float* post_ffn = nullptr;
   int rope = 0;  // index into the model's rope tables
+  // EmbeddingGemma 2 (encode2, embed.go:247-377): this layer's head geometry,
+  // the PLE block's gate [P, H] and projection [H, P], the weight-free
+  // v_norm (ones), the PLE post-norm and the layer scalar
+  int D = 0, Hkv = 0;
+  DevMat wpg, wpp;
+  float* vgain = nullptr;
+  float* ple_post = nullptr;
+  float scalar = 1.f;
 };
 
 struct Dense {
@@ -154,6 +162,15 @@ struct fg_model {
   size_t alloc_bytes = 0;
   // FG_WEIGHTS_BF16: one layer's widened fp32 projections (hi and low parts)
   fg::DevMat ws_qkv, ws_o, ws_gu, ws_d;
+  // EmbeddingGemma 2: per-layer geometry, the per-layer-embedding projection
+  // [L·P, H] and its norm, the embedding projection [E, H], and their
+  // workspaces (ple [tokens, L·P], the constant 1/√H row scale, the PLE
+  // block's gated activations [tokens, P])
+  std::vector<int> head_dim_l, kv_l;
+  std::vector<int> rope_dims;  // head dim of each rope table (index = Layer::rope)
+  fg::DevMat ple_proj, emb_proj;
+  float* ple_gain = nullptr;
+  float *ple_buf = nullptr, *ple_scale = nullptr, *gbuf = nullptr;
   // host-API staging
   int32_t* d_ids = nullptr;
   int64_t d_ids_cap = 0;
@@ -383,9 +400,12 @@ int ensure_workspace(fg_model* m, int64_t tokens, int batch) {
   const fg_config& c = m->cfg;
   if (tokens > m->cap_tokens) {
     if (m->x) return set_error(FG_EINVAL, "batch of %lld tokens exceeds the workspace (%lld)", (long long)tokens, (long long)m->cap_tokens);
-    const int64_t H = c.hidden_size, D = c.head_dim;
-    const int64_t qkvw = int64_t(c.num_heads + 2 * c.num_kv_heads) * D;
-    const int64_t attw = int64_t(c.num_heads) * D;
+    const int64_t H = c.hidden_size;
+    int64_t qkvw = 0, attw = 0;  // widest layer (EmbeddingGemma 2's differ)
+    for (int l = 0; l < c.num_layers; ++l) {
+      qkvw = std::max<int64_t>(qkvw, int64_t(c.num_heads + 2 * m->kv_l[size_t(l)]) * m->head_dim_l[size_t(l)]);
+      attw = std::max<int64_t>(attw, int64_t(c.num_heads) * m->head_dim_l[size_t(l)]);
+    }
     const int64_t F = c.intermediate_size;
     FG_TRY(dev_alloc_t(m, &m->x, tokens * H));
     FG_TRY(dev_alloc_t(m, &m->x_lo, tokens * H));
@@ -396,10 +416,20 @@ int ensure_workspace(fg_model* m, int64_t tokens, int batch) {
     FG_TRY(dev_alloc_t(m, &m->gu, tokens * F));
     FG_TRY(dev_alloc_t(m, &m->gu_lo, tokens * F));
     FG_TRY(dev_alloc_t(m, &m->tmp, tokens * std::max(H, attw)));
+    if (c.variant == 2) {
+      const int64_t P = c.ple_dim, L = c.num_layers;
+      FG_TRY(dev_alloc_t(m, &m->ple_buf, tokens * L * P));
+      FG_TRY(dev_alloc_t(m, &m->gbuf, tokens * P));
+      FG_TRY(dev_alloc_t(m, &m->ple_scale, tokens));
+      // pl·(1/√hidden) as a row scale of the product (embed.go:270)
+      const float inv = float(1.0 / std::sqrt(double(H)));
+      std::vector<float> hs(static_cast<size_t>(tokens), inv);
+      FG_CUDA_TRY(cudaMemcpy(m->ple_scale, hs.data(), hs.size() * sizeof(float), cudaMemcpyHostToDevice));
+    }
     m->cap_tokens = tokens;
   }
   if (batch > m->cap_batch) {
-    int widest = c.hidden_size;
+    int widest = std::max(c.hidden_size, c.variant == 2 ? c.embedding_dim : 0);
     for (auto& d : m->dense) widest = std::max(widest, std::max(d.in, d.out));
     const int64_t nb = std::max(batch, 1);
     FG_TRY(dev_alloc_t(m, &m->pooled, nb * c.hidden_size));
@@ -414,7 +444,126 @@ int ensure_workspace(fg_model* m, int64_t tokens, int batch) {
   return FG_OK;
 }
 
+// The weights EmbeddingGemma 2's Load reads (model.go:142-205 with the
+// variant-2 additions), folded as there: norms multiply by the stored
+// weight, the input norm folds into Wq/Wk/Wv and the pre-FFN norm into
+// Wgate/Wup (model.go:206-222).
+int finalize_v2(fg_model* m, int64_t max_tokens) {
+  const fg_config& c = m->cfg;
+  const int64_t H = c.hidden_size, Hq = c.num_heads, F = c.intermediate_size;
+  const int64_t L = c.num_layers, P = c.ple_dim, E = c.embedding_dim;
+  if (F % 128 != 0) return set_error(FG_EINVAL, "intermediate_size %lld must be a multiple of 128", (long long)F);
+  if (H % 128 != 0 || H > 1024) return set_error(FG_EINVAL, "hidden_size %lld must be a multiple of 128 up to 1024", (long long)H);
+  FG_CUDA_TRY(cudaSetDevice(m->device));
+  FG_TRY(device_error_word(&m->err));
+  const HostTensor* t = nullptr;
+  FG_TRY(need(m, "embed_tokens.weight", {c.vocab_size, H}, &t));
+  FG_TRY(upload_table(m, t->data, &m->embed, &m->embed_bf16));
+
+  // rope tables per distinct (base, head dim)
+  auto rope_index = [&](double base, int D, int* out) -> int {
+    for (size_t i = 0; i < m->rope_bases.size(); ++i)
+      if (m->rope_bases[i] == base && m->rope_dims[i] == D) {
+        *out = int(i);
+        return FG_OK;
+      }
+    std::vector<float> cs, sn;
+    rope_table(base, c.max_tokens, D, cs, sn);
+    float *dc = nullptr, *ds = nullptr;
+    FG_TRY(upload(m, cs, &dc));
+    FG_TRY(upload(m, sn, &ds));
+    m->rope_cos.push_back(dc);
+    m->rope_sin.push_back(ds);
+    m->rope_bases.push_back(base);
+    m->rope_dims.push_back(D);
+    *out = int(m->rope_bases.size()) - 1;
+    return FG_OK;
+  };
+  auto gain = [&](const std::string& name, int64_t n, float** out) -> int {
+    const HostTensor* g = nullptr;
+    FG_TRY(need(m, name, {n}, &g));
+    return upload(m, g->data, out);
+  };
+
+  m->layers.resize(size_t(L));
+  for (int l = 0; l < L; ++l) {
+    const std::string p = "layers." + std::to_string(l) + ".";
+    Layer& Ly = m->layers[size_t(l)];
+    const int64_t D = m->head_dim_l[size_t(l)], Hkv = m->kv_l[size_t(l)];
+    Ly.D = int(D);
+    Ly.Hkv = int(Hkv);
+    FG_TRY(rope_index(m->rope_base[l], int(D), &Ly.rope));
+    const HostTensor *in_norm, *pf_norm, *wq, *wk, *wv, *wo, *wg, *wu, *wd, *pg, *pp;
+    FG_TRY(need(m, p + "input_layernorm.weight", {H}, &in_norm));
+    FG_TRY(need(m, p + "pre_feedforward_layernorm.weight", {H}, &pf_norm));
+    FG_TRY(need(m, p + "self_attn.q_proj.weight", {Hq * D, H}, &wq));
+    FG_TRY(need(m, p + "self_attn.k_proj.weight", {Hkv * D, H}, &wk));
+    FG_TRY(need(m, p + "self_attn.v_proj.weight", {Hkv * D, H}, &wv));
+    FG_TRY(need(m, p + "self_attn.o_proj.weight", {H, Hq * D}, &wo));
+    FG_TRY(need(m, p + "mlp.gate_proj.weight", {F, H}, &wg));
+    FG_TRY(need(m, p + "mlp.up_proj.weight", {F, H}, &wu));
+    FG_TRY(need(m, p + "mlp.down_proj.weight", {H, F}, &wd));
+    FG_TRY(need(m, p + "ple_block.per_layer_input_gate.weight", {P, H}, &pg));
+    FG_TRY(need(m, p + "ple_block.per_layer_projection.weight", {H, P}, &pp));
+    const HostTensor* sc = find(m, p + "layer_scalar");
+    if (!sc || sc->data.size() != 1) return set_error(FG_EINVAL, "gemma: weight %slayer_scalar not found (one value)", p.c_str());
+    Ly.scalar = sc->data[0];
+
+    const std::vector<float>& g_in = in_norm->data;  // no 1 + w in EmbeddingGemma 2
+    const std::vector<float>& g_pf = pf_norm->data;
+    std::vector<float> rqkv(size_t((Hq + 2 * Hkv) * D * H)), rgu(size_t(2 * F * H));
+    std::memcpy(rqkv.data(), wq->data.data(), size_t(Hq * D * H) * 4);
+    std::memcpy(rqkv.data() + Hq * D * H, wk->data.data(), size_t(Hkv * D * H) * 4);
+    std::memcpy(rqkv.data() + (Hq + Hkv) * D * H, wv->data.data(), size_t(Hkv * D * H) * 4);
+    for (int64_t j = 0; j < F / 128; ++j) {
+      std::memcpy(rgu.data() + (2 * j) * 128 * H, wg->data.data() + j * 128 * H, size_t(128 * H) * 4);
+      std::memcpy(rgu.data() + (2 * j + 1) * 128 * H, wu->data.data() + j * 128 * H, size_t(128 * H) * 4);
+    }
+    FG_TRY(upload_mat(m, fold(rqkv, g_in, H), int((Hq + 2 * Hkv) * D), int(H), &Ly.wqkv));
+    FG_TRY(upload_mat(m, wo->data, int(H), int(Hq * D), &Ly.wo));
+    FG_TRY(upload_mat(m, fold(rgu, g_pf, H), int(2 * F), int(H), &Ly.wgu));
+    FG_TRY(upload_mat(m, wd->data, int(H), int(F), &Ly.wd));
+    FG_TRY(upload_mat(m, pg->data, int(P), int(H), &Ly.wpg));
+    FG_TRY(upload_mat(m, pp->data, int(H), int(P), &Ly.wpp));
+    FG_TRY(gain(p + "self_attn.q_norm.weight", D, &Ly.qgain));
+    FG_TRY(gain(p + "self_attn.k_norm.weight", D, &Ly.kgain));
+    FG_TRY(upload(m, std::vector<float>(size_t(D), 1.0f), &Ly.vgain));  // v_norm has no weight
+    FG_TRY(gain(p + "post_attention_layernorm.weight", H, &Ly.post_attn));
+    FG_TRY(gain(p + "post_feedforward_layernorm.weight", H, &Ly.post_ffn));
+    FG_TRY(gain(p + "ple_block.post_per_layer_input_norm.weight", H, &Ly.ple_post));
+  }
+  FG_TRY(gain("norm.weight", H, &m->final_gain));
+  const HostTensor *pm, *ep;
+  FG_TRY(need(m, "ple.per_layer_model_projection.weight", {L * P, H}, &pm));
+  FG_TRY(upload_mat(m, pm->data, int(L * P), int(H), &m->ple_proj));
+  FG_TRY(gain("ple.per_layer_projection_norm.weight", P, &m->ple_gain));
+  FG_TRY(need(m, "embedding_projection.weight", {E, H}, &ep));
+  FG_TRY(upload_mat(m, ep->data, int(E), int(H), &m->emb_proj));
+
+  int prev = int(E);
+  for (int j = 0; j < c.num_dense; ++j) {
+    const HostTensor* w = nullptr;
+    FG_TRY(need(m, "dense." + std::to_string(j) + ".linear.weight", {c.dense_out[j], c.dense_in[j]}, &w));
+    if (c.dense_in[j] != prev) return set_error(FG_EINVAL, "dense layer %d takes %d features, previous gives %d", j, c.dense_in[j], prev);
+    if (c.dense_in[j] % 4 != 0) return set_error(FG_EINVAL, "dense layer %d input width must be a multiple of 4", j);
+    Dense d;
+    d.in = c.dense_in[j];
+    d.out = c.dense_out[j];
+    d.tanh = c.dense_tanh[j] != 0;
+    FG_TRY(upload_mat(m, w->data, d.out, d.in, &d.w));
+    m->dense.push_back(d);
+    prev = d.out;
+  }
+  m->host.clear();
+  m->weight_bytes = m->alloc_bytes;
+  FG_TRY(ensure_workspace(m, std::max<int64_t>(max_tokens, 1), 1));
+  FG_CUDA_TRY(cudaDeviceSynchronize());
+  m->finalized = true;
+  return FG_OK;
+}
+
 int finalize(fg_model* m, int64_t max_tokens) {
+  if (m->cfg.variant == 2) return finalize_v2(m, max_tokens);
   const fg_config& c = m->cfg;
   const int64_t H = c.hidden_size, D = c.head_dim, Hq = c.num_heads, Hkv = c.num_kv_heads;
   const int64_t F = c.intermediate_size;
@@ -679,8 +828,174 @@ int grow_attn_ws(fg_model* m, size_t need, cudaStream_t s) {
   return FG_OK;
 }
 
+// EmbeddingGemma 2's text tower (encode2From, embed.go:247-377), then pool,
+// embedding projection, Dense head and L2 (embed.go:381-475). Per layer:
+// Q/K/V (row-scaled product) → q/k RMSNorm + RoPE and the weight-free
+// v_norm → attention with unscaled scores (tensor cores at head_dim 256,
+// the SIMT kernel at the global layers' 512) → O → x += RMSNorm(o) → GeGLU
+// FFN → x += RMSNorm(mlp) → PLE block g = GELU(x·Wgate)⊙ple_l, y = g·Wproj
+// → x = (x + RMSNorm(y))·scalar; the final norm is fused into the last
+// residual kernel.
+int forward_v2(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int T, int dim,
+               int precision, float* out, cudaStream_t s) {
+  const fg_config& c = m->cfg;
+  const bool split = precision == FG_PREC_SPLIT_TF32;
+  const int H = c.hidden_size, Hq = c.num_heads, F = c.intermediate_size;
+  const int L = c.num_layers, P = c.ple_dim, E = c.embedding_dim;
+  const int64_t M = int64_t(B) * T;
+  if (M > INT32_MAX) return set_error(FG_EINVAL, "batch too large");
+  FG_TRY(ensure_workspace(m, M, B));
+  const double act_bytes = double(M) * H * 4.0;
+  {
+    const double row_read = double(M) * H * (m->embed_bf16 ? 2.0 : 4.0);
+    PhaseScope ps(m, FG_PHASE_EMBED, s, row_read + act_bytes + double(M) * 8, 2);
+    eff_len_kernel<<<(B + 127) / 128, 128, 0, s>>>(lengths, B, T, m->eff_len);
+    FG_CUDA_TRY(cudaGetLastError());
+    const float emb_scale = float(std::sqrt(double(H)));
+    FG_TRY(embed_gather(m->embed, m->embed_bf16, c.vocab_size, ids, lengths, B, T, H, emb_scale, c.rms_norm_eps,
+                        m->x, nullptr, m->rowscale, m->err, s));
+  }
+  // per-layer embeddings once per pass: RMSNorm_P((x·Wple)·(1/√H)) (embed.go:270-275)
+  {
+    GemmArgs g = make_gemm(int(M), m->x, nullptr, H, m->ple_proj, split);
+    g.epi.out = m->ple_buf;
+    g.epi.ldo = int64_t(L) * P;
+    g.epi.rowscale = m->ple_scale;
+    PhaseScope ps(m, FG_PHASE_GEMM_QKV, s, gemm_flops(g));
+    FG_TRY(gemm_tn(g, m->err, s));
+    FG_TRY(rmsnorm(m->ple_buf, M * L, P, m->ple_gain, c.rms_norm_eps, m->ple_buf, s));
+  }
+  for (int l = 0; l < L; ++l) {
+    const Layer& Ly = m->layers[size_t(l)];
+    const bool last = l == L - 1;
+    const int D = Ly.D, Hkv = Ly.Hkv;
+    const int qkvw = (Hq + 2 * Hkv) * D, attw = Hq * D;
+    AttnArgs a{};
+    a.q = m->qkv;
+    a.k = m->qkv + int64_t(Hq) * D;
+    a.v = m->qkv + int64_t(Hq + Hkv) * D;
+    a.out = m->att;
+    a.out_lo = nullptr;
+    a.qsb = int64_t(T) * qkvw; a.qsh = D; a.qst = qkvw;
+    a.ksb = a.qsb; a.ksh = D; a.kst = qkvw;
+    a.vsb = a.qsb; a.vsh = D; a.vst = qkvw;
+    a.osb = int64_t(T) * attw; a.osh = D; a.ost = attw;
+    a.B = B; a.Hq = Hq; a.Hkv = Hkv; a.T = T; a.S = T; a.D = D;
+    a.klen = m->eff_len;
+    a.qlen = m->eff_len;
+    a.window = (c.window > 0 && m->sliding[size_t(l)]) ? c.window : 0;
+    a.scale = c.attn_scale;
+    // q|k|v = rowscale ⊙ (x · Wqkv'ᵀ)   (embed.go:285-288)
+    GemmArgs g = make_gemm(int(M), m->x, nullptr, H, Ly.wqkv, split);
+    g.epi.rowscale = m->rowscale;
+    g.epi.out = m->qkv;
+    g.epi.ldo = qkvw;
+    {
+      PhaseScope ps(m, FG_PHASE_GEMM_QKV, s, gemm_flops(g));
+      FG_TRY(gemm_tn(g, m->err, s));
+    }
+    {
+      // q/k RMSNorm + RoPE, v RMSNorm (embed.go:289-317)
+      PhaseScope ps(m, FG_PHASE_QK_NORM_ROPE, s, double(M) * (Hq + 2 * Hkv) * D * 8.0);
+      FG_TRY(qk_norm_rope(m->qkv, nullptr, M, Hq, Hkv, D, Ly.qgain, Ly.kgain, Ly.vgain, c.rms_norm_eps,
+                          m->rope_cos[size_t(Ly.rope)], m->rope_sin[size_t(Ly.rope)], T, s));
+    }
+    {
+      PhaseScope ps(m, FG_PHASE_ATTENTION, s, 0.0);
+      if (!m->attn_simt && attn_tc_supported(a)) {
+        const size_t need = attn_tc_workspace_bytes(B, T, T, Hq, Hkv);
+        FG_TRY(grow_attn_ws(m, need, s));
+        FG_TRY(attention_tc(a, m->attn_ws, m->attn_ws_bytes, m->err, s));
+      } else {
+        FG_TRY(attention_simt(a, s));
+      }
+    }
+    // o0 = att · Wo; x += RMSNorm(o0)   (embed.go:336-343)
+    g = make_gemm(int(M), m->att, nullptr, attw, Ly.wo, split);
+    g.epi.out = m->tmp;
+    g.epi.ldo = H;
+    {
+      PhaseScope ps(m, FG_PHASE_GEMM_O, s, gemm_flops(g));
+      FG_TRY(gemm_tn(g, m->err, s));
+    }
+    {
+      PhaseScope ps(m, FG_PHASE_RESIDUAL, s, act_bytes * 3 + double(M) * 4);
+      FG_TRY(residual_postnorm(m->x, nullptr, m->tmp, Ly.post_attn, c.rms_norm_eps, m->rowscale, nullptr, M, H, s));
+    }
+    // FFN as in encode (embed.go:345-357)
+    g = make_gemm(int(M), m->x, nullptr, H, Ly.wgu, split);
+    g.epi.out = m->gu;
+    g.epi.ldo = F;
+    g.epi.rowscale = m->rowscale;
+    g.epi.geglu = 1;
+    {
+      PhaseScope ps(m, FG_PHASE_GEMM_GATE_UP, s, gemm_flops(g));
+      FG_TRY(gemm_tn(g, m->err, s));
+    }
+    g = make_gemm(int(M), m->gu, nullptr, F, Ly.wd, split);
+    g.epi.out = m->tmp;
+    g.epi.ldo = H;
+    {
+      PhaseScope ps(m, FG_PHASE_GEMM_DOWN, s, gemm_flops(g));
+      FG_TRY(gemm_tn(g, m->err, s));
+    }
+    {
+      PhaseScope ps(m, FG_PHASE_RESIDUAL, s, act_bytes * 3 + double(M) * 4);
+      FG_TRY(residual_postnorm(m->x, nullptr, m->tmp, Ly.post_ffn, c.rms_norm_eps, m->rowscale, nullptr, M, H, s));
+    }
+    // PLE block: g = GELU(x·Wgate) ⊙ ple_l; y0 = g·Wproj;
+    // x = (x + RMSNorm(y0))·scalar   (embed.go:359-371)
+    g = make_gemm(int(M), m->x, nullptr, H, Ly.wpg, split);
+    g.epi.out = m->gbuf;
+    g.epi.ldo = P;
+    g.epi.act = FG_ACT_GELU;
+    g.epi.mul = m->ple_buf + int64_t(l) * P;
+    g.epi.ldm = int64_t(L) * P;
+    {
+      PhaseScope ps(m, FG_PHASE_GEMM_GATE_UP, s, gemm_flops(g));
+      FG_TRY(gemm_tn(g, m->err, s));
+    }
+    g = make_gemm(int(M), m->gbuf, nullptr, P, Ly.wpp, split);
+    g.epi.out = m->tmp;
+    g.epi.ldo = H;
+    {
+      PhaseScope ps(m, FG_PHASE_GEMM_DOWN, s, gemm_flops(g));
+      FG_TRY(gemm_tn(g, m->err, s));
+    }
+    {
+      PhaseScope ps(m, FG_PHASE_RESIDUAL, s, act_bytes * 3 + double(M) * 4);
+      FG_TRY(residual_postnorm(m->x, nullptr, m->tmp, Ly.ple_post, c.rms_norm_eps, m->rowscale,
+                               last ? m->final_gain : nullptr, M, H, s, Ly.scalar));
+    }
+  }
+  // pool, embedding projection, Dense head, L2 (embed.go:381-475)
+  PhaseScope ps(m, FG_PHASE_POOL_HEAD, s, act_bytes, 3 + int(m->dense.size()));
+  FG_TRY(mean_pool(m->x, m->eff_len, B, T, H, m->pooled, nullptr, s));
+  float* bufs[2] = {m->head_a, m->head_b};
+  GemmArgs g = make_gemm(B, m->pooled, nullptr, H, m->emb_proj, split);
+  g.epi.out = bufs[0];
+  g.epi.ldo = E;
+  FG_TRY(gemm_tn(g, m->err, s));
+  const float* cur = bufs[0];
+  int width = E;
+  for (size_t j = 0; j < m->dense.size(); ++j) {
+    const Dense& d = m->dense[j];
+    g = make_gemm(B, cur, nullptr, width, d.w, split);
+    g.epi.out = bufs[(j + 1) & 1];
+    g.epi.ldo = d.out;
+    g.epi.act = d.tanh ? kActTanh : FG_ACT_NONE;
+    FG_TRY(gemm_tn(g, m->err, s));
+    cur = bufs[(j + 1) & 1];
+    width = d.out;
+  }
+  if (dim > width) return set_error(FG_EINVAL, "gemma: Dim(%d) outside 1..%d", dim, width);
+  FG_TRY(l2_normalize(cur, width, B, dim, c.l2_normalize, out, s));
+  return FG_OK;
+}
+
 int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int T, int dim,
             int precision, float* out, cudaStream_t s) {
+  if (m->cfg.variant == 2) return forward_v2(m, ids, lengths, B, T, dim, precision, out, s);
   const fg_config& c = m->cfg;
   const bool split = precision == FG_PREC_SPLIT_TF32;
   const int H = c.hidden_size, D = c.head_dim, Hq = c.num_heads, Hkv = c.num_kv_heads;
@@ -790,7 +1105,7 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
     if (!tc) {
       // QK-norm + RoPE (embed.go:198-207)
       PhaseScope ps(m, FG_PHASE_QK_NORM_ROPE, s, double(M) * (Hq + Hkv) * D * 8.0);
-      FG_TRY(qk_norm_rope(m->qkv, nullptr, M, Hq, Hkv, D, L.qgain, L.kgain, c.rms_norm_eps,
+      FG_TRY(qk_norm_rope(m->qkv, nullptr, M, Hq, Hkv, D, L.qgain, L.kgain, nullptr, c.rms_norm_eps,
                           m->rope_cos[L.rope], m->rope_sin[L.rope], T, s));
     }
     {
@@ -870,7 +1185,10 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
   return FG_OK;
 }
 
+// (*Model).Dim (model.go:336-344): the embedding projection's width for
+// EmbeddingGemma 2, else the last Dense layer's, else hidden.
 int model_dim(const fg_model* m) {
+  if (m->cfg.variant == 2) return m->cfg.embedding_dim;
   return m->cfg.num_dense > 0 ? m->cfg.dense_out[m->cfg.num_dense - 1] : m->cfg.hidden_size;
 }
 
@@ -894,6 +1212,21 @@ int fg_model_create(const fg_config* cfg, int device, fg_model** out) {
     return set_error(FG_EINVAL, "gemma: %d query heads not a multiple of %d key/value heads", c.num_heads, c.num_kv_heads);
   if (c.num_dense < 0 || c.num_dense > FG_MAX_DENSE) return set_error(FG_EINVAL, "gemma: %d dense layers", c.num_dense);
   if (!c.sliding || !c.rope_base) return set_error(FG_EINVAL, "gemma: per-layer sliding / rope_base arrays missing");
+  if (c.variant != 0 && c.variant != 2) return set_error(FG_EINVAL, "gemma: unknown variant %d", c.variant);
+  if (c.variant == 2) {
+    if (c.ple_dim <= 0 || c.ple_dim % 4 != 0 || c.embedding_dim <= 0 || c.embedding_dim % 4 != 0)
+      return set_error(FG_EINVAL, "gemma: embedding_gemma2 needs hidden_size_per_layer_input and embedding_dim (multiples of 4)");
+    for (int l = 0; l < c.num_layers; ++l) {
+      const int D = c.layer_head_dim ? c.layer_head_dim[l] : c.head_dim;
+      const int kv = c.layer_kv_heads ? c.layer_kv_heads[l] : c.num_kv_heads;
+      if (D <= 0 || D % 4 != 0 || D > 512)
+        return set_error(FG_EINVAL, "gemma: layer %d head_dim %d unsupported (multiple of 4, at most 512)", l, D);
+      if (kv <= 0 || c.num_heads % kv != 0)
+        return set_error(FG_EINVAL, "gemma: layer %d: %d query heads not a multiple of %d key/value heads", l, c.num_heads, kv);
+    }
+  } else if (c.layer_head_dim || c.layer_kv_heads) {
+    return set_error(FG_EINVAL, "gemma: per-layer head geometry is an embedding_gemma2 setting");
+  }
   int ndev = 0;
   if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) {
     cudaGetLastError();
@@ -909,6 +1242,12 @@ int fg_model_create(const fg_config* cfg, int device, fg_model** out) {
   m->rope_base.assign(c.rope_base, c.rope_base + c.num_layers);
   m->cfg.sliding = m->sliding.data();
   m->cfg.rope_base = m->rope_base.data();
+  for (int l = 0; l < c.num_layers; ++l) {
+    m->head_dim_l.push_back(c.layer_head_dim ? c.layer_head_dim[l] : c.head_dim);
+    m->kv_l.push_back(c.layer_kv_heads ? c.layer_kv_heads[l] : c.num_kv_heads);
+  }
+  m->cfg.layer_head_dim = m->head_dim_l.data();
+  m->cfg.layer_kv_heads = m->kv_l.data();
   const char* att = std::getenv("FG_ATTENTION");
   m->attn_simt = att && std::string(att) == "simt";
   const char* alo = std::getenv("FG_GEMM_ALO");

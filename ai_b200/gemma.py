@@ -65,9 +65,18 @@ class Config:
     use_bidirectional_attention: bool = False
     max_position_embeddings: int = 0
     rope_scaling: object = None
+    # EmbeddingGemma 2 only (config.go:38-45): variant 2, else 0
+    variant: int = 0
+    hidden_size_per_layer_input: int = 0
+    embedding_dim: int = 0
+    per_layer_config: Optional[dict] = None
+    rope_parameters: Optional[dict] = None
 
     def window(self) -> int:
-        """Attend when |i − j| < window() (config.go:331-339)."""
+        """Attend when |i − j| < window() (config.go:331-339). EmbeddingGemma 2
+        configures an inclusive radius, so its bound is one more."""
+        if self.variant == 2:
+            return self.sliding_window + 1
         if self.use_bidirectional_attention:
             return self.sliding_window // 2 + 1
         return self.sliding_window
@@ -75,8 +84,25 @@ class Config:
     def is_sliding(self, l: int) -> bool:
         return self.layer_types[l] == "sliding_attention"
 
+    def _override(self, l: int) -> dict:
+        pl = self.per_layer_config or {}
+        return pl.get(f"{l:02d}", pl.get(str(l), {})) or {}
+
+    def head_dim_of(self, l: int) -> int:
+        """Config.headDim(l) (config.go:314-320)."""
+        return int(self._override(l).get("head_dim") or self.head_dim)
+
+    def kv_heads_of(self, l: int) -> int:
+        """Config.kvHeads(l) (config.go:322-328)."""
+        return int(self._override(l).get("num_key_value_heads") or self.num_key_value_heads)
+
     def rope_base(self, l: int) -> float:
-        """Local base on sliding layers, global theta otherwise (config.go:346-362)."""
+        """Local base on sliding layers, global theta otherwise (config.go:346-362);
+        EmbeddingGemma 2 reads rope_parameters per layer type."""
+        if self.variant == 2:
+            rp = (self.rope_parameters or {}).get(self.layer_types[l]) or {}
+            if rp.get("rope_theta"):
+                return float(rp["rope_theta"])
         if self.is_sliding(l):
             return self.rope_local_base_freq if self.rope_local_base_freq != 0 else 10000.0
         return self.rope_theta if self.rope_theta != 0 else 10000.0
@@ -100,10 +126,47 @@ class Config:
                              f"{self.num_hidden_layers} layers")
 
 
+def _fill_variant2(c: Config) -> Config:
+    """fillVariant2 (config.go:249-297): EmbeddingGemma 2's defaults and checks."""
+    c.variant = 2
+    if not c.layer_types:
+        c.layer_types = ["full_attention" if (i + 1) % 6 == 0 else "sliding_attention"
+                         for i in range(c.num_hidden_layers)]
+    if c.per_layer_config is None:
+        c.per_layer_config = {f"{i:02d}": {"head_dim": 512, "num_key_value_heads": 1}
+                              for i, t in enumerate(c.layer_types) if t == "full_attention"}
+    if c.rope_parameters is None:
+        c.rope_parameters = {"sliding_attention": {"rope_theta": 10000.0, "rope_type": "default"},
+                             "full_attention": {"rope_theta": 1000000.0, "rope_type": "default"}}
+    for t, rp in c.rope_parameters.items():
+        if rp.get("rope_type") not in (None, "", "default"):
+            raise GemmaError(f"gemma: rope_type {rp.get('rope_type')!r} for {t} not supported")
+    if c.embedding_dim == 0:
+        c.embedding_dim = 768
+    if c.hidden_size_per_layer_input == 0:
+        raise GemmaError("gemma: embedding_gemma2 config without hidden_size_per_layer_input")
+    c.validate()
+    for l in range(c.num_hidden_layers):
+        if c.head_dim_of(l) % 2 != 0:
+            raise GemmaError(f"gemma: layer {l} head_dim {c.head_dim_of(l)} must be even for RoPE")
+        if c.num_attention_heads % c.kv_heads_of(l) != 0:
+            raise GemmaError(f"gemma: layer {l}: {c.num_attention_heads} query heads not a multiple of "
+                             f"{c.kv_heads_of(l)} key/value heads")
+    return c
+
+
 def config_from_dict(raw: dict) -> Config:
-    """LoadConfig's parsing and defaults (config.go:178-227)."""
+    """LoadConfig's parsing and defaults (config.go:178-227); an
+    embedding_gemma2 checkpoint's text model is read from text_config
+    (config.go:174-207; its vision and audio towers are not run here)."""
     if raw.get("model_type") == "embedding_gemma2":
-        raise GemmaError("gemma: embedding_gemma2 checkpoints are outside this encoder path")
+        c = Config()
+        text = raw.get("text_config") or {}
+        for f in c.__dataclass_fields__:
+            if f in text and text[f] is not None and f != "variant":
+                setattr(c, f, text[f])
+        c.rope_scaling = text.get("rope_scaling")
+        return _fill_variant2(c)
     c = Config()
     for f in c.__dataclass_fields__:
         if f in raw and raw[f] is not None:
@@ -218,7 +281,12 @@ class Model:
         self.device = device
         self.max_tokens = min(cfg.max_position_embeddings or 2048, 2048)
         self.batch_tokens = 8192
-        self.scale = 1.0 / math.sqrt(cfg.query_pre_attn_scalar)
+        if cfg.variant == 2:
+            # scores unscaled, the model card's 8192-token context (model.go:105-109)
+            self.scale = 1.0
+            self.max_tokens = min(cfg.max_position_embeddings or 8192, 8192)
+        else:
+            self.scale = 1.0 / math.sqrt(cfg.query_pre_attn_scalar)
         self.dense = list(dense)
         self.weight_residency = _lib.WEIGHTS_F32
         for o in options:
@@ -248,6 +316,14 @@ class Model:
             fc.dense_out[j], fc.dense_in[j] = int(d.shape[0]), int(d.shape[1])
             fc.dense_tanh[j] = int(d.tanh)
         fc.l2_normalize = int(l2)
+        if cfg.variant == 2:
+            self._hd = (C.c_int * L)(*[cfg.head_dim_of(l) for l in range(L)])
+            self._kv = (C.c_int * L)(*[cfg.kv_heads_of(l) for l in range(L)])
+            fc.variant = 2
+            fc.layer_head_dim = self._hd
+            fc.layer_kv_heads = self._kv
+            fc.ple_dim = cfg.hidden_size_per_layer_input
+            fc.embedding_dim = cfg.embedding_dim
         h = C.c_void_p()
         _lib.check(lib.fg_model_create(C.byref(fc), device, C.byref(h)))
         self._h = h
@@ -274,6 +350,8 @@ class Model:
 
     def Dim(self) -> int:
         """Embedding width before Matryoshka truncation (model.go:336-344)."""
+        if self.cfg.variant == 2:
+            return self.cfg.embedding_dim
         return int(self.dense[-1].shape[0]) if self.dense else self.cfg.hidden_size
 
     def weight_bytes(self) -> int:

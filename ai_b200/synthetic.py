@@ -118,6 +118,122 @@ def make_weights(cfg: dict = EMBEDDINGGEMMA_300M, seed: int = 0, norm_std: float
     return out
 
 
+# EmbeddingGemma 2's text tower, shaped as the reference's config test
+# (models/gemma/gemma2_test.go TestConfig2): 12 layers of width 512, layers 5
+# and 11 global with 512-wide heads and one KV head, per-layer inputs of 512,
+# a 768-wide embedding projection.
+EMBEDDINGGEMMA2_TEXT = {
+    "hidden_size": 512,
+    "intermediate_size": 2048,
+    "num_hidden_layers": 12,
+    "num_attention_heads": 4,
+    "num_key_value_heads": 2,
+    "head_dim": 256,
+    "vocab_size": 262144,
+    "sliding_window": 512,
+    "rms_norm_eps": 1e-06,
+    "hidden_activation": "gelu_pytorch_tanh",
+    "hidden_size_per_layer_input": 512,
+    "embedding_dim": 768,
+    "max_position_embeddings": 8192,
+    "per_layer_config": {"05": {"head_dim": 512, "num_key_value_heads": 1},
+                         "11": {"head_dim": 512, "num_key_value_heads": 1}},
+    "rope_parameters": {"full_attention": {"rope_theta": 1000000.0, "rope_type": "default"},
+                        "sliding_attention": {"rope_theta": 10000.0, "rope_type": "default"}},
+}
+
+
+def eg2_config(text: dict = EMBEDDINGGEMMA2_TEXT) -> dict:
+    """An embedding_gemma2 config.json (text tower only)."""
+    return {"model_type": "embedding_gemma2", "text_config": dict(text)}
+
+
+def eg2_small_config(layers: int = 3, hidden: int = 256, vocab: int = 4096, window: int = 48,
+                     full=(1,), ple: int = 128, emb: int = 192) -> dict:
+    """A small EmbeddingGemma 2 for tests: `full` layers global with 512-wide
+    heads and one KV head, the others sliding (radius `window`) with 256-wide
+    heads and two KV heads."""
+    t = dict(EMBEDDINGGEMMA2_TEXT)
+    t.update({"hidden_size": hidden, "intermediate_size": 512, "num_hidden_layers": layers,
+              "vocab_size": vocab, "sliding_window": window, "hidden_size_per_layer_input": ple,
+              "embedding_dim": emb,
+              "layer_types": ["full_attention" if l in full else "sliding_attention" for l in range(layers)],
+              "per_layer_config": {f"{l:02d}": {"head_dim": 512, "num_key_value_heads": 1} for l in full}})
+    return eg2_config(t)
+
+
+def _eg2_geometry(t: dict, l: int) -> Tuple[int, int]:
+    o = (t.get("per_layer_config") or {}).get(f"{l:02d}", {})
+    return int(o.get("head_dim") or t["head_dim"]), int(o.get("num_key_value_heads") or t["num_key_value_heads"])
+
+
+def weight_specs_eg2(cfg: dict, head=()) -> List[Tuple[str, Tuple[int, ...], str]]:
+    """EmbeddingGemma 2's text-tower weights (model.go:142-205): kind 'w' =
+    N(0,0.02²), 'n' = a norm that multiplies by its weight (1 + noise),
+    'q' = a q/k norm, 's' = the layer scalar."""
+    t = cfg["text_config"]
+    H, F, Hq, V = t["hidden_size"], t["intermediate_size"], t["num_attention_heads"], t["vocab_size"]
+    L, P, E = t["num_hidden_layers"], t["hidden_size_per_layer_input"], t.get("embedding_dim") or 768
+    specs = [("embed_tokens.weight", (V, H), "w")]
+    for l in range(L):
+        D, Hkv = _eg2_geometry(t, l)
+        p = f"layers.{l}."
+        specs += [
+            (p + "self_attn.q_proj.weight", (Hq * D, H), "w"),
+            (p + "self_attn.k_proj.weight", (Hkv * D, H), "w"),
+            (p + "self_attn.v_proj.weight", (Hkv * D, H), "w"),
+            (p + "self_attn.o_proj.weight", (H, Hq * D), "w"),
+            (p + "mlp.gate_proj.weight", (F, H), "w"),
+            (p + "mlp.up_proj.weight", (F, H), "w"),
+            (p + "mlp.down_proj.weight", (H, F), "w"),
+            (p + "ple_block.per_layer_input_gate.weight", (P, H), "w"),
+            (p + "ple_block.per_layer_projection.weight", (H, P), "w"),
+            (p + "input_layernorm.weight", (H,), "n"),
+            (p + "post_attention_layernorm.weight", (H,), "n"),
+            (p + "pre_feedforward_layernorm.weight", (H,), "n"),
+            (p + "post_feedforward_layernorm.weight", (H,), "n"),
+            (p + "self_attn.q_norm.weight", (D,), "q"),
+            (p + "self_attn.k_norm.weight", (D,), "q"),
+            (p + "ple_block.post_per_layer_input_norm.weight", (H,), "n"),
+            (p + "layer_scalar", (1,), "s"),
+        ]
+    specs += [("norm.weight", (H,), "n"),
+              ("ple.per_layer_model_projection.weight", (L * P, H), "w"),
+              ("ple.per_layer_projection_norm.weight", (P,), "n"),
+              ("embedding_projection.weight", (E, H), "w")]
+    for j, (i, o) in enumerate(head):
+        specs.append((f"dense.{j}.linear.weight", (o, i), "w"))
+    return specs
+
+
+def make_weights_eg2(cfg: dict, seed: int = 0, norm_std: float = 0.1, head=()) -> Dict[str, np.ndarray]:
+    """Random-init EmbeddingGemma 2 weights as bfloat16 bits: matrices
+    ~N(0, 0.02²) from default_rng(seed) in weight_specs_eg2 order; norms
+    1 + N(0, norm_std²), q/k norms D^(-1/4)·(1 + N(0, norm_std²)) and layer
+    scalars uniform in [0.5, 1.5) from default_rng(seed + 1000).
+
+    The scores are not scaled in this architecture (model.go:105-109), so a
+    trained model's q/k norm weights keep q·k of order one; unit q/k gains
+    would give logits of order √D, a near-argmax softmax, and a random
+    model that amplifies every rounding difference by orders of magnitude.
+    D^(-1/4) on each side restores logits of order one."""
+    rng = np.random.default_rng(seed)
+    nrng = np.random.default_rng(seed + 1000)
+    out = {}
+    for name, shape, kind in weight_specs_eg2(cfg, head):
+        if kind == "w":
+            x = rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02)
+        elif kind == "n":
+            x = np.float32(1) + nrng.standard_normal(shape, dtype=np.float32) * np.float32(norm_std)
+        elif kind == "q":
+            x = (np.float32(1) + nrng.standard_normal(shape, dtype=np.float32) * np.float32(norm_std)) \
+                * np.float32(shape[0] ** -0.25)
+        else:
+            x = nrng.uniform(0.5, 1.5, shape).astype(np.float32)
+        out[name] = bf16_round(x.astype(np.float32))
+    return out
+
+
 def make_ids(batch: int, seq: int, seed: int, vocab: int = 262144) -> np.ndarray:
     """[batch, seq] int32 ids: BOS first, the rest uniform in [3, vocab)."""
     rng = np.random.default_rng(seed)

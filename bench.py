@@ -419,6 +419,81 @@ def run_ragged(args, rank, local_rank, world, cfg):
         dist.destroy_process_group()
 
 
+def eg2_work(t: dict, T: int):
+    """Algorithmic FLOPs of one EmbeddingGemma 2 sequence of T valid tokens:
+    the projections (Q/K/V/O, GeGLU, the PLE projection and each layer's PLE
+    gate and projection) and the attention's allowed (query, key) pairs."""
+    H, F, Hq, L, P = (t["hidden_size"], t["intermediate_size"], t["num_attention_heads"],
+                      t["num_hidden_layers"], t["hidden_size_per_layer_input"])
+    from ai_b200.gemma import config_from_dict
+
+    c = config_from_dict({"model_type": "embedding_gemma2", "text_config": t})
+    w = c.window()
+    i = np.arange(T)
+    local = int(np.sum(np.minimum(T - 1, i + w - 1) - np.maximum(0, i - w + 1) + 1)) if T > w else T * T
+    linear = 2 * H * L * P * T  # per-layer-embedding projection
+    attn = 0
+    for l in range(L):
+        D, kv = c.head_dim_of(l), c.kv_heads_of(l)
+        linear += 2 * T * (H * (Hq + 2 * kv) * D + Hq * D * H + 3 * H * F + 2 * H * P)
+        attn += 4 * Hq * D * (local if c.is_sliding(l) else T * T)
+    return linear, attn
+
+
+def run_eg2(args):
+    """--workload eg2: EmbeddingGemma 2's text tower (the 12-layer shape of
+    the reference's config test, random-init weights seed 0) at 256 × 512
+    tokens on one GPU, inputs resident, device-timed with CUDA events."""
+    import torch
+
+    from ai_b200 import gemma
+    from ai_b200 import synthetic as S
+
+    dev = torch.device("cuda", 0)
+    cfg = S.eg2_config()
+    w = S.make_weights_eg2(cfg, seed=0)
+    model = gemma.from_synthetic(cfg, w, device=0, max_batch_tokens=BATCH * SEQ)
+    dim = model.Dim()
+    ids = torch.from_numpy(S.make_ids(BATCH, SEQ, 1)).to(dev)
+    lens = torch.from_numpy(np.full(BATCH, SEQ, np.int32)).to(dev)
+    out = torch.empty((BATCH, dim), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(args.warmup, 3)):
+        model.embed_device(ids, lens, BATCH, SEQ, dim, out, stream)
+    model.check()
+    model.read_profile()
+    model.set_profiling(True)
+    torch.cuda.synchronize()
+    clocks = ClockSampler([0])
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        model.embed_device(ids, lens, BATCH, SEQ, dim, out, stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    model.check()
+    prof = model.read_profile()
+    linear, attn = eg2_work(cfg["text_config"], SEQ)
+    flops = (linear + attn) * BATCH
+    line = {
+        "metric": "EmbeddingGemma 2 (text tower) embeddings/s at 256x512 tok, 1 B200", "value": BATCH / (ms / 1e3),
+        "unit": "embeddings/s", "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3),
+        "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: random-init EmbeddingGemma 2-shaped weights (seed 0), ids seed 1",
+        "config": {"workload": "EmbeddingGemma 2 text tower: 12 layers, hidden 512, 4 heads; sliding layers "
+                               "256-wide heads x2 KV, global layers 5/11 512-wide x1 KV; PLE 512; out 768; "
+                               "256 x 512 tokens", "l2_flush": "none: activations exceed L2"},
+        "tflops_algorithmic": flops / (ms / 1e3) / 1e12,
+        "phases_ms_per_step": {p: round(v["ms"] / args.steps, 3) for p, v in prof.items()},
+        "clocks": clk,
+    }
+    print(json.dumps(line))
+    model.close()
+
+
 def run_cluster(args):
     """--workload cluster: the consumer of the embeddings on one GPU —
     cluster.Nearest at the reference's TestNearestSpeed size (50 000 unit
@@ -510,12 +585,16 @@ def main():
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="sequences per GPU (default 256; smaller only for profiling runs)")
     ap.add_argument("--seq", type=int, default=SEQ, help="tokens per sequence (default 512)")
-    ap.add_argument("--workload", choices=["encoder", "ragged", "cluster"], default="encoder",
-                    help="encoder (config 2, the headline, default), ragged (config 3 end to end) "
-                         "or cluster (Nearest / KMeans on one GPU)")
+    ap.add_argument("--workload", choices=["encoder", "ragged", "cluster", "eg2"], default="encoder",
+                    help="encoder (config 2, the headline, default), ragged (config 3 end to end), "
+                         "cluster (Nearest / KMeans on one GPU) or eg2 (EmbeddingGemma 2 text tower)")
     args = ap.parse_args()
     if args.workload == "cluster":
         run_cluster(args)
+        return
+    if args.workload == "eg2":
+        globals().update(BATCH=args.batch, SEQ=args.seq)
+        run_eg2(args)
         return
     globals().update(BATCH=args.batch, SEQ=args.seq)
     rank = int(os.environ.get("RANK", "0"))

@@ -87,7 +87,7 @@ typedef struct fg_config {
   int window;
   float rms_norm_eps;
   float attn_scale;
-  int max_tokens;          /* sequence cap (model.go:98-104), ≤ 2048 */
+  int max_tokens;          /* sequence cap (model.go:98-109): ≤ 2048, ≤ 8192 for variant 2 */
   const int* sliding;      /* [num_layers] */
   const double* rope_base; /* [num_layers] */
   int num_dense;
@@ -95,6 +95,15 @@ typedef struct fg_config {
   int dense_out[FG_MAX_DENSE];
   int dense_tanh[FG_MAX_DENSE];
   int l2_normalize;        /* Normalize module present (model.go:262-263, 305-306) */
+  /* EmbeddingGemma 2's text tower (encode2, embed.go:247-377; config.go
+   * 286-362): variant = 2, else 0. Its norms multiply by the stored weight
+   * (no 1 + w, model.go:128-139); attn_scale is 1 (model.go:105-109);
+   * window = sliding_window + 1 (config.go:331-339). */
+  int variant;
+  const int* layer_head_dim;  /* [num_layers] Config.headDim(l); NULL = head_dim everywhere */
+  const int* layer_kv_heads;  /* [num_layers] Config.kvHeads(l); NULL = num_kv_heads */
+  int ple_dim;                /* hidden_size_per_layer_input (variant 2) */
+  int embedding_dim;          /* embedding_projection output width (variant 2) */
 } fg_config;
 
 typedef struct fg_model fg_model;
