@@ -379,12 +379,17 @@ def run_ragged(args, rank, local_rank, world, cfg):
         r = step()
         torch.cuda.synchronize(dev)
         el = time.perf_counter() - t0
+        per_rank = [el]
         if world > 1:
             t = torch.tensor([el], device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            el = float(t.item())
+            parts = [torch.zeros_like(t) for _ in range(world)]
+            dist.all_gather(parts, t)
+            per_rank = [float(p.item()) for p in parts]
+            el = max(per_rank)
+        rank_times.append(per_rank)
         return r, el
 
+    rank_times = []
     for _ in range(max(args.warmup, 1)):
         step()
     times = []
@@ -412,6 +417,7 @@ def run_ragged(args, rank, local_rank, world, cfg):
                        "timing": "host wall clock around the synchronous public calls (ids on the host "
                                  "to embeddings on rank 0's host), median of steps, max over ranks"},
             "tokens_per_s": tokens / sec, "all_finite": ok, "clocks": clk,
+            "rank_ms_last_step": [round(x * 1e3, 1) for x in rank_times[-1]],
         }
         print(json.dumps(line))
     model.close()
