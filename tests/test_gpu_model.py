@@ -199,6 +199,29 @@ def test_bf16_resident_projections_are_bitwise_identical(norm_std):
         m16.close()
 
 
+def test_stored_low_parts_equal_shared_memory_low_parts(monkeypatch):
+    """FG_GEMM_ALO=global (the producers write A's split-TF32 low parts and
+    the SM-pair GEMM loads them by TMA) computes the same products as the
+    default (the GEMM makes them in shared memory): bitwise equal."""
+    from ai_b200 import gemma
+    from ai_b200 import synthetic as S
+
+    cfg = S.small_config(layers=3, vocab=2048)
+    w = S.make_weights(cfg, seed=41, norm_std=0.0)
+    ids = S.make_ids(6, 128, 12, cfg["vocab_size"])
+    lengths = np.array([128, 100, 1, 77, 128, 64], np.int32)
+    m1 = gemma.from_synthetic(cfg, w, device=0, max_batch_tokens=4096)
+    monkeypatch.setenv("FG_GEMM_ALO", "global")
+    m2 = gemma.from_synthetic(cfg, w, device=0, max_batch_tokens=4096)
+    try:
+        a, b = m1.embed_padded(ids, lengths), m2.embed_padded(ids, lengths)
+        print(f"stored vs shared-memory low parts: max |diff| {np.abs(a - b).max():.3e}")
+        assert np.array_equal(a, b)
+    finally:
+        m1.close()
+        m2.close()
+
+
 def test_batch_invariance(small):
     """A sequence embeds the same alone and inside a padded batch
     (models/gemma/gemma_test.go:117-135 asks ≥ 0.9999)."""
