@@ -77,29 +77,33 @@ __global__ void fill_kernel(float* p, int64_t n, float v) {
 
 // Per row of sim [n, k]: the first column holding the maximum (a NaN in
 // column 0 keeps column 0, later NaNs are skipped, as tensor.Argmax's
-// `v > best` scan does) and its value. With `assign` the previous index is
-// compared (changed rows counted) and overwritten; `sizes` counts rows per
-// column.
+// `v > best` scan does) and its value. LPR lanes share a row (LPR = 32 /
+// rows per warp), each scanning columns sub, sub + LPR, …; with `index`
+// holding the previous assignment, changed rows are counted before it is
+// overwritten; `sizes` counts rows per column.
+template <int LPR>
 __global__ void __launch_bounds__(256) argmax_rows_kernel(const float* __restrict__ sim, int64_t lds, int64_t n,
                                                           int k, int32_t* __restrict__ index,
                                                           float* __restrict__ value, int32_t* __restrict__ changed,
                                                           int32_t* __restrict__ sizes) {
-  const int lane = threadIdx.x & 31;
-  const int64_t row = int64_t(blockIdx.x) * kRowWarps + (threadIdx.x >> 5);
-  if (row >= n) return;
-  const float* s = sim + row * lds;
-  const float first = s[0];
+  constexpr int kRowsPerWarp = 32 / LPR;
+  const int lane = threadIdx.x & 31, sub = lane % LPR;
+  const int64_t row = (int64_t(blockIdx.x) * kRowWarps + (threadIdx.x >> 5)) * kRowsPerWarp + lane / LPR;
+  const bool live = row < n;
+  const float* s = sim + (live ? row : 0) * lds;
   float best = -INFINITY;
   int bi = -1;
-  for (int j = lane; j < k; j += 32) {
-    const float v = s[j];
-    if (v > best || (bi < 0 && v == best)) {  // v == -inf still claims the slot
-      best = v;
-      bi = j;
+  if (live) {
+    for (int j = sub; j < k; j += LPR) {
+      const float v = s[j];
+      if (v > best || (bi < 0 && v == best)) {  // v == -inf still claims the slot
+        best = v;
+        bi = j;
+      }
     }
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
+  for (int o = LPR / 2; o > 0; o >>= 1) {
     const float ob = __shfl_xor_sync(0xffffffffu, best, o);
     const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
     if (oi >= 0 && (bi < 0 || ob > best || (ob == best && oi < bi))) {
@@ -107,18 +111,31 @@ __global__ void __launch_bounds__(256) argmax_rows_kernel(const float* __restric
       bi = oi;
     }
   }
+  if (!live || sub != 0) return;
+  const float first = s[0];
   if (isnan(first) || bi < 0) {  // column 0 is the answer when nothing beats it
     best = first;
     bi = 0;
   }
-  if (lane == 0) {
-    if (changed) {
-      if (index[row] != bi) atomicAdd(changed, 1);
-    }
-    index[row] = bi;
-    value[row] = best;
-    if (sizes) atomicAdd(&sizes[bi], 1);
-  }
+  if (changed && index[row] != bi) atomicAdd(changed, 1);
+  index[row] = bi;
+  value[row] = best;
+  if (sizes) atomicAdd(&sizes[bi], 1);
+}
+
+int argmax_rows(const float* sim, int64_t lds, int64_t n, int k, int32_t* index, float* value,
+                int32_t* changed, int32_t* sizes, cudaStream_t s) {
+  auto grid = [&](int rows_per_warp) { return int((n + int64_t(kRowWarps) * rows_per_warp - 1) / (int64_t(kRowWarps) * rows_per_warp)); };
+  if (k <= 16)
+    argmax_rows_kernel<4><<<grid(8), 256, 0, s>>>(sim, lds, n, k, index, value, changed, sizes);
+  else if (k <= 64)
+    argmax_rows_kernel<8><<<grid(4), 256, 0, s>>>(sim, lds, n, k, index, value, changed, sizes);
+  else if (k <= 256)
+    argmax_rows_kernel<16><<<grid(2), 256, 0, s>>>(sim, lds, n, k, index, value, changed, sizes);
+  else
+    argmax_rows_kernel<32><<<grid(1), 256, 0, s>>>(sim, lds, n, k, index, value, changed, sizes);
+  FG_CUDA_TRY(cudaGetLastError());
+  return FG_OK;
 }
 
 __global__ void iota_kernel(int32_t* p, int64_t n) {
@@ -351,9 +368,7 @@ int fg_nearest(int64_t n, int64_t k, int64_t d, const float* x, int64_t ldx, con
   float* sim = nullptr;
   FG_TRY(ds.alloc(&sim, size_t(n * lds)));
   FG_TRY(similarities(x, ldx, n, d, centres, ldc, k, sim, lds, precision, ds, s));
-  argmax_rows_kernel<<<row_grid(n), 256, 0, s>>>(sim, lds, n, int(k), index, similarity, nullptr, nullptr);
-  FG_CUDA_TRY(cudaGetLastError());
-  return FG_OK;
+  return argmax_rows(sim, lds, n, int(k), index, similarity, nullptr, nullptr, s);
 }
 
 int fg_kmeans(int64_t n, int64_t d, const float* x, int64_t ldx, int k, int iters, uint64_t seed,
@@ -439,8 +454,7 @@ int fg_kmeans(int64_t n, int64_t d, const float* x, int64_t ldx, int k, int iter
     FG_TRY(similarities(x, ldx, n, d, centres, d, k, sim, lds, precision, ds, s));
     FG_CUDA_TRY(cudaMemsetAsync(changed, 0, sizeof(int32_t), s));
     FG_CUDA_TRY(cudaMemsetAsync(sizes, 0, size_t(k) * sizeof(int32_t), s));
-    argmax_rows_kernel<<<row_grid(n), 256, 0, s>>>(sim, lds, n, k, assignment, similarity, changed, sizes);
-    FG_CUDA_TRY(cudaGetLastError());
+    FG_TRY(argmax_rows(sim, lds, n, k, assignment, similarity, changed, sizes, s));
     // centre update: rows stably sorted by centre, summed in row order
     FG_CUDA_TRY(cub::DeviceRadixSort::SortPairs(sort_tmp, sort_bytes, keys, keys_out, rows_in, rows, n, 0,
                                                 end_bit, s));
