@@ -275,6 +275,11 @@ __device__ __forceinline__ void qkv_attn_epilogue(const GemmEpilogue& e, const O
     const int lane = threadIdx.x & 31;
     // the warp's first row, first column of this head
     const int64_t base0 = int64_t(row - lane) * width + int64_t(head) * D;
+    // the head's gains spread over the lanes (g[32k + lane] in gq[k]) and
+    // taken by shuffle: the same for every row, so no per-element loads
+    float gq[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) gq[k] = g[32 * k + lane];
     // pass 2: normalise, rotate the pairs (i, i + 128), split, store
 #pragma unroll 1
     for (int c0 = 0; c0 < H2; c0 += 32) {
@@ -282,11 +287,15 @@ __device__ __forceinline__ void qkv_attn_epilogue(const GemmEpilogue& e, const O
       tmem_ld_32x32b_x32(taddr + uint32_t(c0), ra);
       tmem_ld_32x32b_x32(taddr + uint32_t(H2 + c0), rb);
       tmem_ld_wait();
+      const int qq = c0 >> 5;
+      const float ga = qq == 0 ? gq[0] : qq == 1 ? gq[1] : qq == 2 ? gq[2] : gq[3];
+      const float gb = qq == 0 ? gq[4] : qq == 1 ? gq[5] : qq == 2 ? gq[6] : gq[7];
       // y1 = x1·c - x2·s, y2 = x1·s + x2·c for column j of the chunk
       auto rot = [&](int j, float& y1, float& y2) {
         const int i = c0 + j;
-        const float x1 = __fmul_rn(__fmul_rn(__fmul_rn(__uint_as_float(ra[j]), rs), inv), g[i]);
-        const float x2 = __fmul_rn(__fmul_rn(__fmul_rn(__uint_as_float(rb[j]), rs), inv), g[i + H2]);
+        const float g1 = __shfl_sync(0xffffffffu, ga, j), g2 = __shfl_sync(0xffffffffu, gb, j);
+        const float x1 = __fmul_rn(__fmul_rn(__fmul_rn(__uint_as_float(ra[j]), rs), inv), g1);
+        const float x2 = __fmul_rn(__fmul_rn(__fmul_rn(__uint_as_float(rb[j]), rs), inv), g2);
         const float c = row_ok ? cs[i * rld] : 0.f, s = row_ok ? sn[i * rld] : 0.f;
         y1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
         y2 = __fadd_rn(__fmul_rn(x1, s), __fmul_rn(x2, c));
