@@ -418,6 +418,7 @@ def run_ragged(args, rank, local_rank, world, cfg):
                                  "to embeddings on rank 0's host), median of steps, max over ranks"},
             "tokens_per_s": tokens / sec, "all_finite": ok, "clocks": clk,
             "rank_ms_last_step": [round(x * 1e3, 1) for x in rank_times[-1]],
+            "step_ms": [round(x * 1e3, 1) for x in times],
         }
         print(json.dumps(line))
     model.close()
