@@ -1,5 +1,5 @@
-// Flash attention on the tcgen05 tensor cores for head_dim 256, fp32 inputs
-// carried as split-bf16 operands.
+// Flash attention on the tcgen05 tensor cores for head_dim 256 and 512,
+// fp32 inputs carried as split-bf16 operands.
 //
 // Replaces attentionFused / AttentionBlock (tensor/attention.go:130-287,
 // internal/blas/attention.go:61-136) on the encoder path. Every fp32
@@ -23,6 +23,11 @@
 //               running max with lazy rescaling (O is rescaled in TMEM only
 //               when the max grows by more than 2^8), P = exp2 written back
 //               over S as packed bf16 hi/lo; the final 1/Σ and the store.
+// Head_dim 512 (EmbeddingGemma 2's global layers): Q (256 KB as split
+// bf16) does not fit beside the ring, so its d-chunks are streamed through
+// the ring with the K chunks they meet, and each CTA produces one 256-wide
+// half of the output (O in TMEM stays 256 columns), the two halves of a
+// head being two CTAs (blockIdx.y = 2·head + half) that both compute S.
 // Key tiles outside a query tile's window or past the sequence length are
 // never loaded. Masked keys get weight exactly 0, as the reference's
 // flushing exp gives them (internal/kernel/generic.go:283-291).
@@ -42,7 +47,7 @@ PFN_cuTensorMapEncodeTiled_v12000 g_encode_bf16 = nullptr;
 
 constexpr int kQ = 128;    // query rows per CTA
 constexpr int kKT = 128;   // keys per tile
-constexpr int kD = 256;    // head dimension
+constexpr int kD = 256;    // output columns per CTA (the head dimension, or half of 512)
 constexpr int kStages = 3;
 constexpr uint32_t kChunk = 128 * 64 * 2;           // [128 rows × 64 bf16] = 16 KB
 constexpr uint32_t kQBytes = 2 * 4 * kChunk;        // Q hi/lo × 4 d-chunks = 128 KB
@@ -65,10 +70,14 @@ struct Params {
   int tma_out, tma_out_lo;  // out / out_lo written by TMA stores (maps mO / mOlo)
 };
 
+// NC 64-column d-chunks per head (4: head_dim 256, Q resident; 8: head_dim
+// 512, Q streamed, QS).
+
 __device__ __forceinline__ bool waitb(uint32_t bar, uint32_t par, volatile int* ab, int* err, int code) {
   return mbar_wait(bar, par, ab, err, code);
 }
 
+template <int NC, bool QS>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap mQ0, const __grid_constant__ CUtensorMap mQ1,
                    const __grid_constant__ CUtensorMap mK0, const __grid_constant__ CUtensorMap mK1,
@@ -86,14 +95,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 20);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
-  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  constexpr int Dh = NC * 64;  // head dimension
+  const int qt = blockIdx.x, b = blockIdx.z;
+  const int h = QS ? int(blockIdx.y >> 1) : int(blockIdx.y);
+  const int oh = QS ? int(blockIdx.y & 1) : 0;  // output half of a 512-wide head
   const int hk = h / (p.Hq / p.Hkv);
   const int i0 = qt * kQ;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qlen = p.qlen ? min(p.qlen[b], p.T) : p.T;
   const int klen = p.klen ? max(0, min(p.klen[b], p.S)) : p.S;
-  float* obase = p.out + b * p.osb + h * p.osh;
-  float* olbase = p.out_lo ? p.out_lo + b * p.osb + h * p.osh : nullptr;
+  float* obase = p.out + b * p.osb + h * p.osh + oh * kD;
+  float* olbase = p.out_lo ? p.out_lo + b * p.osb + h * p.osh + oh * kD : nullptr;
   int kbeg = 0, kend = klen;
   if (p.window > 0) {
     kbeg = max(0, i0 - p.window + 1);
@@ -158,10 +170,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&mK0);
       tma_prefetch_desc(&mV0);
       const int qrow = b * p.T + i0;
-      for (int c = 0; c < 4; ++c) {
-        mbar_arrive_expect_tx(q_bar(c), 2 * kChunk);
-        tma_load_2d(smem_u32(sQ + (0 * 4 + c) * kChunk), &mQ0, q_bar(c), h * kD + c * 64, qrow);
-        tma_load_2d(smem_u32(sQ + (1 * 4 + c) * kChunk), &mQ1, q_bar(c), h * kD + c * 64, qrow);
+      if (!QS) {
+        for (int c = 0; c < 4; ++c) {
+          mbar_arrive_expect_tx(q_bar(c), 2 * kChunk);
+          tma_load_2d(smem_u32(sQ + (0 * 4 + c) * kChunk), &mQ0, q_bar(c), h * Dh + c * 64, qrow);
+          tma_load_2d(smem_u32(sQ + (1 * 4 + c) * kChunk), &mQ1, q_bar(c), h * Dh + c * 64, qrow);
+        }
       }
       int armed[kStages] = {0, 0, 0};
       int stage = 0;
@@ -183,11 +197,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       auto load_k = [&](int j) {
         const int key0 = (kt0 + j) * kKT;
-        for (int c = 0; c < 4 && ok; ++c) ok = next(&mK0, &mK1, hk * kD + c * 64, b * p.S + key0);
+        for (int c = 0; c < NC && ok; ++c) {
+          if (QS) ok = next(&mQ0, &mQ1, h * Dh + c * 64, qrow);  // Q chunk c, then the K chunk it meets
+          if (ok) ok = next(&mK0, &mK1, hk * Dh + c * 64, b * p.S + key0);
+        }
       };
       auto load_v = [&](int j) {
         const int key0 = (kt0 + j) * kKT;
-        const int vrow = (b * p.Hkv + hk) * kD;
+        const int vrow = (b * p.Hkv + hk) * Dh + oh * kD;
         for (int dh = 0; dh < 2 && ok; ++dh)
           for (int kh = 0; kh < 2 && ok; ++kh) ok = next(&mV0, &mV1, key0 + kh * 64, vrow + dh * 128);
       };
@@ -203,7 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           while (!mbar_try_wait(bar(1 + s), uint32_t(armed[s] - 1) & 1u))
             if (globaltimer_ns() - t0 > kWaitTimeoutNs) break;
         }
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < (QS ? 0 : 4); ++c) {
           const uint64_t t0 = globaltimer_ns();
           while (!mbar_try_wait(q_bar(c), 0))
             if (globaltimer_ns() - t0 > kWaitTimeoutNs) break;
@@ -263,10 +280,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
         }
         const uint32_t tS = tmem + uint32_t(sb * 128);
-        for (int c = 0; c < 4 && ok; ++c) {
-          if (j == 0 && !waitb(q_bar(c), 0, abort_flag, p.err, kDevTimeoutFull)) {
-            ok = false;
-            break;
+        for (int c = 0; c < NC && ok; ++c) {
+          uint32_t q0, q1;
+          int qstage = 0;
+          if (QS) {
+            // the Q chunk occupies the ring stage before its K chunk
+            if (!waitb(bar(1 + stage), phase, abort_flag, p.err, kDevTimeoutFull)) {
+              ok = false;
+              break;
+            }
+            qstage = stage;
+            q0 = smem_u32(sRing + stage * kStageBytes);
+            q1 = q0 + kChunk;
+            if (++stage == kStages) {
+              stage = 0;
+              phase ^= 1;
+            }
+          } else {
+            if (j == 0 && !waitb(q_bar(c), 0, abort_flag, p.err, kDevTimeoutFull)) {
+              ok = false;
+              break;
+            }
+            q0 = smem_u32(sQ + c * kChunk);
+            q1 = smem_u32(sQ + (4 + c) * kChunk);
           }
           if (!waitb(bar(1 + stage), phase, abort_flag, p.err, kDevTimeoutFull)) {
             ok = false;
@@ -275,8 +311,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint32_t k0 = smem_u32(sRing + stage * kStageBytes);
           const uint32_t k1 = k0 + kChunk;
-          const uint32_t q0 = smem_u32(sQ + c * kChunk);
-          const uint32_t q1 = smem_u32(sQ + (4 + c) * kChunk);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             const uint64_t a0 = sw128_kmajor_desc(q0 + kk * 32);
@@ -288,6 +322,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_bf16_ss(tS, a1, b0, kIdesc, 1u);                       // q_lo · k_hi
           }
           issued = true;
+          if (QS) mma_commit(bar(4 + qstage));
           mma_commit(bar(4 + stage));
           if (++stage == kStages) {
             stage = 0;
@@ -513,7 +548,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0 && tw < p.T) {
             for (int ch = 0; ch < 4; ++ch)
-              tma_store_3d(part ? &mOlo : &mO, smem_u32(stg + ch * 4096), h * kD + col_base + ch * 32, tw, b);
+              tma_store_3d(part ? &mOlo : &mO, smem_u32(stg + ch * 4096), h * Dh + oh * kD + col_base + ch * 32, tw, b);
             tma_store_commit();
           }
         }
@@ -558,17 +593,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Split of q or k (strided [B, H, T, D] element offsets b·sb + h·sh + t·st)
 // into token-major bf16 hi/lo [B·T, H·D]: one thread per 2 elements.
 __global__ void split_bf16_rows_kernel(const float* __restrict__ src, int64_t sb, int64_t sh,
-                                       int64_t st, int B, int T, int H,
+                                       int64_t st, int B, int T, int H, int D,
                                        __nv_bfloat16* __restrict__ hi,
                                        __nv_bfloat16* __restrict__ lo) {
-  const int cols = H * kD;
+  const int cols = H * D;
   const int64_t rows = int64_t(B) * T;
   const int64_t total = rows * (cols / 2);
   for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < total;
        e += int64_t(gridDim.x) * blockDim.x) {
     const int64_t r = e / (cols / 2);
     const int cc = int(e % (cols / 2)) * 2;
-    const int b = int(r / T), t = int(r % T), hd = cc / kD, d = cc % kD;
+    const int b = int(r / T), t = int(r % T), hd = cc / D, d = cc % D;
     const float2 v = *reinterpret_cast<const float2*>(src + b * sb + hd * sh + t * st + d);
     const __nv_bfloat16 h0 = __float2bfloat16_rn(v.x), h1 = __float2bfloat16_rn(v.y);
     __nv_bfloat162 hh;
@@ -639,10 +674,10 @@ int make_map_out3d(CUtensorMap* m, const float* ptr, int B, int T, int64_t cols,
 
 }  // namespace
 
-size_t attn_tc_workspace_bytes(int B, int T, int S, int Hq, int Hkv) {
+size_t attn_tc_workspace_bytes(int B, int T, int S, int Hq, int Hkv, int D) {
   const int64_t ldt = (S + 7) / 8 * 8;
-  return size_t(B) * T * Hq * kD * 2 * 2 + size_t(B) * S * Hkv * kD * 2 * 2 +
-         size_t(B) * Hkv * kD * ldt * 2 * 2 + 8 * 256;
+  return size_t(B) * T * Hq * D * 2 * 2 + size_t(B) * S * Hkv * D * 2 * 2 +
+         size_t(B) * Hkv * D * ldt * 2 * 2 + 8 * 256;
 }
 
 bool attn_tc_supported(const AttnArgs& a) {
@@ -652,11 +687,12 @@ bool attn_tc_supported(const AttnArgs& a) {
   const bool out_al = (reinterpret_cast<uintptr_t>(a.out) & 15) == 0 &&
                       ((a.osb | a.osh | a.ost) % 4) == 0 &&
                       (!a.out_lo || (reinterpret_cast<uintptr_t>(a.out_lo) & 15) == 0);
-  return a.D == kD && a.Hkv > 0 && a.Hq % a.Hkv == 0 && al && out_al && a.T > 0 && a.S > 0 &&
+  return (a.D == 256 || a.D == 512) && a.Hkv > 0 && a.Hq % a.Hkv == 0 && al && out_al && a.T > 0 && a.S > 0 &&
          int64_t(a.B) * a.T < (int64_t(1) << 31) && int64_t(a.B) * a.S < (int64_t(1) << 31);
 }
 
-int attn_tc_carve(void* ws, int B, int T, int S, int Hq, int Hkv, AttnOperands* o) {
+int attn_tc_carve(void* ws, int B, int T, int S, int Hq, int Hkv, AttnOperands* o, int D) {
+  const int kD = D;  // the head dimension for the layout below
   const int64_t ldt = (S + 7) / 8 * 8;
   const int64_t MQ = int64_t(B) * T, MK = int64_t(B) * S;
   auto align = [](uint8_t* q) { return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(q) + 255) & ~uintptr_t(255)); };
@@ -679,17 +715,18 @@ int attn_tc_carve(void* ws, int B, int T, int S, int Hq, int Hkv, AttnOperands* 
 int attention_tc_operands(const AttnArgs& a, const AttnOperands& o, int* err, cudaStream_t s) {
   const int B = a.B, T = a.T, S = a.S, Hq = a.Hq, Hkv = a.Hkv;
   if (B == 0) return FG_OK;
-  if (a.D != kD || Hkv <= 0 || Hq % Hkv != 0 || T <= 0 || S <= 0)
+  if ((a.D != 256 && a.D != 512) || Hkv <= 0 || Hq % Hkv != 0 || T <= 0 || S <= 0)
     return set_error(FG_EINVAL, "tensor-core attention: unsupported shape");
+  const int Dh = a.D;
   FG_TRY(tensor_map_encoder(&g_encode_bf16));
   const int64_t MQ = int64_t(B) * T, MK = int64_t(B) * S;
   CUtensorMap mq0, mq1, mk0, mk1, mv0, mv1;
-  FG_TRY(make_map_bf16(&mq0, o.q_hi, MQ, Hq * kD, Hq * kD, 128));
-  FG_TRY(make_map_bf16(&mq1, o.q_lo, MQ, Hq * kD, Hq * kD, 128));
-  FG_TRY(make_map_bf16(&mk0, o.k_hi, MK, Hkv * kD, Hkv * kD, 128));
-  FG_TRY(make_map_bf16(&mk1, o.k_lo, MK, Hkv * kD, Hkv * kD, 128));
-  FG_TRY(make_map_bf16(&mv0, o.vt_hi, int64_t(B) * Hkv * kD, S, o.ldt, 128));
-  FG_TRY(make_map_bf16(&mv1, o.vt_lo, int64_t(B) * Hkv * kD, S, o.ldt, 128));
+  FG_TRY(make_map_bf16(&mq0, o.q_hi, MQ, Hq * Dh, Hq * Dh, 128));
+  FG_TRY(make_map_bf16(&mq1, o.q_lo, MQ, Hq * Dh, Hq * Dh, 128));
+  FG_TRY(make_map_bf16(&mk0, o.k_hi, MK, Hkv * Dh, Hkv * Dh, 128));
+  FG_TRY(make_map_bf16(&mk1, o.k_lo, MK, Hkv * Dh, Hkv * Dh, 128));
+  FG_TRY(make_map_bf16(&mv0, o.vt_hi, int64_t(B) * Hkv * Dh, S, o.ldt, 128));
+  FG_TRY(make_map_bf16(&mv1, o.vt_lo, int64_t(B) * Hkv * Dh, S, o.ldt, 128));
   Params prm;
   prm.B = B;
   prm.T = T;
@@ -710,27 +747,35 @@ int attention_tc_operands(const AttnArgs& a, const AttnOperands& o, int* err, cu
   // the heads are contiguous 256-column blocks and the strides allow it.
   CUtensorMap mo = mq0, mol = mq0;
   auto tma_ok = [&](const float* ptr) {
-    return ptr && (reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && a.osh == kD && a.ost % 4 == 0 &&
-           a.osb % 4 == 0 && a.ost >= int64_t(Hq) * kD && a.osb >= int64_t(T) * a.ost;
+    return ptr && (reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && a.osh == Dh && a.ost % 4 == 0 &&
+           a.osb % 4 == 0 && a.ost >= int64_t(Hq) * Dh && a.osb >= int64_t(T) * a.ost;
   };
   prm.tma_out = 0;
   prm.tma_out_lo = 0;
   if (tma_ok(a.out) && (a.out_lo == nullptr || tma_ok(a.out_lo))) {
-    FG_TRY(make_map_out3d(&mo, a.out, B, T, Hq * kD, a.ost, a.osb));
-    if (a.out_lo) FG_TRY(make_map_out3d(&mol, a.out_lo, B, T, Hq * kD, a.ost, a.osb));
+    FG_TRY(make_map_out3d(&mo, a.out, B, T, Hq * Dh, a.ost, a.osb));
+    if (a.out_lo) FG_TRY(make_map_out3d(&mol, a.out_lo, B, T, Hq * Dh, a.ost, a.osb));
     prm.tma_out = 1;
     prm.tma_out_lo = a.out_lo ? 1 : 0;
   }
-  static bool attr[64] = {false};
+  static bool attr[64][2] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!attr[dev & 63]) {
-    FG_CUDA_TRY(cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmem)));
-    attr[dev & 63] = true;
+  const int wide = Dh == 512 ? 1 : 0;
+  if (!attr[dev & 63][wide]) {
+    if (wide)
+      FG_CUDA_TRY(cudaFuncSetAttribute(attn_tc_kernel<8, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmem)));
+    else
+      FG_CUDA_TRY(cudaFuncSetAttribute(attn_tc_kernel<4, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmem)));
+    attr[dev & 63][wide] = true;
   }
-  if ((T + kQ - 1) / kQ > 65535 || B > 65535) return set_error(FG_EINVAL, "attention grid too large");
-  dim3 grid(unsigned((T + kQ - 1) / kQ), unsigned(Hq), unsigned(B));
-  attn_tc_kernel<<<grid, kThreads, kSmem, s>>>(mq0, mq1, mk0, mk1, mv0, mv1, mo, mol, prm);
+  if ((T + kQ - 1) / kQ > 65535 || B > 65535 || Hq * (wide + 1) > 65535)
+    return set_error(FG_EINVAL, "attention grid too large");
+  dim3 grid(unsigned((T + kQ - 1) / kQ), unsigned(Hq * (wide + 1)), unsigned(B));
+  if (wide)
+    attn_tc_kernel<8, true><<<grid, kThreads, kSmem, s>>>(mq0, mq1, mk0, mk1, mv0, mv1, mo, mol, prm);
+  else
+    attn_tc_kernel<4, false><<<grid, kThreads, kSmem, s>>>(mq0, mq1, mk0, mk1, mv0, mv1, mo, mol, prm);
   FG_CUDA_TRY(cudaGetLastError());
   return FG_OK;
 }
@@ -739,17 +784,18 @@ int attention_tc(const AttnArgs& a, void* ws, size_t ws_bytes, int* err, cudaStr
   if (!attn_tc_supported(a)) return set_error(FG_EINVAL, "tensor-core attention: unsupported shape or alignment");
   const int B = a.B, T = a.T, S = a.S, Hq = a.Hq, Hkv = a.Hkv;
   if (B == 0) return FG_OK;
-  if (ws_bytes < attn_tc_workspace_bytes(B, T, S, Hq, Hkv))
+  const int Dh = a.D;
+  if (ws_bytes < attn_tc_workspace_bytes(B, T, S, Hq, Hkv, Dh))
     return set_error(FG_EINVAL, "attention workspace too small");
   AttnOperands o;
-  FG_TRY(attn_tc_carve(ws, B, T, S, Hq, Hkv, &o));
+  FG_TRY(attn_tc_carve(ws, B, T, S, Hq, Hkv, &o, Dh));
   const int64_t MQ = int64_t(B) * T, MK = int64_t(B) * S;
   auto bf = [](void* p) { return static_cast<__nv_bfloat16*>(p); };
   auto grid_of = [](int64_t n) { return int(std::min<int64_t>((n + 255) / 256, int64_t(sm_count()) * 16)); };
-  split_bf16_rows_kernel<<<grid_of(MQ * Hq * kD / 2), 256, 0, s>>>(a.q, a.qsb, a.qsh, a.qst, B, T, Hq, bf(o.q_hi), bf(o.q_lo));
-  split_bf16_rows_kernel<<<grid_of(MK * Hkv * kD / 2), 256, 0, s>>>(a.k, a.ksb, a.ksh, a.kst, B, S, Hkv, bf(o.k_hi), bf(o.k_lo));
-  dim3 tg(unsigned((S + 31) / 32), unsigned(kD / 32), unsigned(B * Hkv));
-  transpose_v_kernel<<<tg, dim3(32, 8), 0, s>>>(a.v, a.vsb, a.vsh, a.vst, B, S, Hkv, kD, bf(o.vt_hi), bf(o.vt_lo), o.ldt);
+  split_bf16_rows_kernel<<<grid_of(MQ * Hq * Dh / 2), 256, 0, s>>>(a.q, a.qsb, a.qsh, a.qst, B, T, Hq, Dh, bf(o.q_hi), bf(o.q_lo));
+  split_bf16_rows_kernel<<<grid_of(MK * Hkv * Dh / 2), 256, 0, s>>>(a.k, a.ksb, a.ksh, a.kst, B, S, Hkv, Dh, bf(o.k_hi), bf(o.k_lo));
+  dim3 tg(unsigned((S + 31) / 32), unsigned(Dh / 32), unsigned(B * Hkv));
+  transpose_v_kernel<<<tg, dim3(32, 8), 0, s>>>(a.v, a.vsb, a.vsh, a.vst, B, S, Hkv, Dh, bf(o.vt_hi), bf(o.vt_lo), o.ldt);
   FG_CUDA_TRY(cudaGetLastError());
   return attention_tc_operands(a, o, err, s);
 }

@@ -81,13 +81,14 @@ struct AttnArgs {
 };
 int attention_simt(const AttnArgs& a, cudaStream_t s);
 
-// The same attention on the tcgen05 tensor cores (head_dim 256, split-bf16
-// operands); ws must hold attn_tc_workspace_bytes() for the shapes.
-size_t attn_tc_workspace_bytes(int B, int T, int S, int Hq, int Hkv);
+// The same attention on the tcgen05 tensor cores (head_dim 256 or 512,
+// split-bf16 operands); ws must hold attn_tc_workspace_bytes() for the
+// shapes and head dimension D.
+size_t attn_tc_workspace_bytes(int B, int T, int S, int Hq, int Hkv, int D = 256);
 bool attn_tc_supported(const AttnArgs& a);
 int attention_tc(const AttnArgs& a, void* ws, size_t ws_bytes, int* err, cudaStream_t s);
 // The split-bf16 operands as the tensor-core kernel reads them: q, k
-// token-major [B·T, H·256], Vᵀ per sequence [B·Hkv·256, ldt keys].
+// token-major [B·T, H·D], Vᵀ per sequence [B·Hkv·D, ldt keys].
 struct AttnOperands {
   void* q_hi;
   void* q_lo;
@@ -98,7 +99,7 @@ struct AttnOperands {
   int64_t ldt;
 };
 // Carves ws (attn_tc_workspace_bytes) into the operand buffers.
-int attn_tc_carve(void* ws, int B, int T, int S, int Hq, int Hkv, AttnOperands* o);
+int attn_tc_carve(void* ws, int B, int T, int S, int Hq, int Hkv, AttnOperands* o, int D = 256);
 // Attention on operands already split (e.g. by the QKV GEMM's epilogue);
 // a's q/k/v pointers are not read.
 int attention_tc_operands(const AttnArgs& a, const AttnOperands& o, int* err, cudaStream_t s);

@@ -903,7 +903,7 @@ int forward_v2(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, i
     {
       PhaseScope ps(m, FG_PHASE_ATTENTION, s, 0.0);
       if (!m->attn_simt && attn_tc_supported(a)) {
-        const size_t need = attn_tc_workspace_bytes(B, T, T, Hq, Hkv);
+        const size_t need = attn_tc_workspace_bytes(B, T, T, Hq, Hkv, D);
         FG_TRY(grow_attn_ws(m, need, s));
         FG_TRY(attention_tc(a, m->attn_ws, m->attn_ws_bytes, m->err, s));
       } else {

@@ -217,7 +217,7 @@ int fg_attention(const float* q, const float* k, const float* v, int B, int Hq, 
   if (!(att && std::string(att) == "simt") && attn_tc_supported(a)) {
     int* err = nullptr;
     FG_TRY(device_error_word(&err));
-    const size_t need = attn_tc_workspace_bytes(B, T, S, Hq, Hkv);
+    const size_t need = attn_tc_workspace_bytes(B, T, S, Hq, Hkv, D);
     StreamScratch scratch(s);
     FG_TRY(scratch.alloc(need));
     FG_TRY(attention_tc(a, scratch.p, need, err, s));

@@ -192,6 +192,8 @@ def _naive_attention(q, k, v, lens, window, scale):
     (2, 2, 2, 33, 7, 3, 0, False),
     (1, 2, 1, 65, 1753, 256, 0, True),
     (2, 3, 1, 512, 512, 64, 128, True),
+    (2, 4, 1, 300, 300, 512, 0, True),     # head_dim 512: tensor cores, Q streamed
+    (1, 4, 2, 700, 700, 512, 257, False),
 ])
 def test_attention_vs_naive_float64(cuda, B, Hq, Hkv, T, S, D, window, padded):
     from ai_b200 import tensor as TT
@@ -290,6 +292,21 @@ def test_attention_running_max_rescale(cuda):
     want = _naive_attention(q, k, v, None, 0, 1 / 16)
     got = TT.AttentionScaled(_t(q, cuda), _t(k, cuda), _t(v, cuda), None, 0, 1 / 16).cpu().numpy()
     assert np.abs(got - want).max() <= 1e-4, np.abs(got - want).max()
+
+
+def test_attention_tensor_core_matches_simt_head_dim_512(cuda, monkeypatch):
+    from ai_b200 import tensor as TT
+    import torch
+
+    rng = np.random.default_rng(10)
+    q = rng.standard_normal((2, 4, 260, 512), dtype=np.float32)
+    k = rng.standard_normal((2, 2, 260, 512), dtype=np.float32)
+    v = rng.standard_normal((2, 2, 260, 512), dtype=np.float32)
+    lens = torch.tensor([260, 131], dtype=torch.int32)
+    tc = TT.AttentionScaled(_t(q, cuda), _t(k, cuda), _t(v, cuda), lens, 100, 1 / 32).cpu().numpy()
+    monkeypatch.setenv("FG_ATTENTION", "simt")
+    simt = TT.AttentionScaled(_t(q, cuda), _t(k, cuda), _t(v, cuda), lens, 100, 1 / 32).cpu().numpy()
+    assert np.abs(tc - simt).max() <= 1e-4
 
 
 def test_attention_tensor_core_matches_simt(cuda, monkeypatch):
