@@ -747,16 +747,18 @@ __global__ void __launch_bounds__(Cfg<BN, SA, SB, BK, CV>::kThreads, 1)
 // Only TMA loads without multicast are used; the MMA completion is
 // signalled to both CTAs by a multicast tcgen05.commit.
 // CV: A's low part computed in shared memory by the converter warps; SA:
-// loaded by TMA from a stored low part; neither: plain TF32.
-template <bool CV, bool SA = false>
+// loaded by TMA from a stored low part; neither: plain TF32. SB: B's low
+// part (weights that are not TF32-exact, e.g. folded with non-zero norm
+// gains) loaded by TMA, adding the A·B_lo pass. Stage: A | A_lo | B | B_lo.
+template <bool CV, bool SA = false, bool SB = false>
 struct PairCfg {
   static constexpr int BN = 256, BK = 32;
   static constexpr int kThreads = 320;
   static constexpr bool kLo = CV || SA;
   static constexpr uint32_t kABytes = 128 * BK * 4;  // this CTA's A rows
   static constexpr uint32_t kBBytes = 128 * BK * 4;  // this CTA's half of the B rows
-  static constexpr uint32_t kStageBytes = kABytes * (kLo ? 2 : 1) + kBBytes;
-  static constexpr uint32_t kTmaBytes = kABytes * (SA ? 2 : 1) + kBBytes;
+  static constexpr uint32_t kStageBytes = kABytes * (kLo ? 2 : 1) + kBBytes * (SB ? 2 : 1);
+  static constexpr uint32_t kTmaBytes = kABytes * (SA ? 2 : 1) + kBBytes * (SB ? 2 : 1);
   static constexpr uint32_t kEpiStageBytes = kEpiStageBytesAll;
   static constexpr int kStagesRaw = (kSmemLimit - 2048 - int(kEpiStageBytes)) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
@@ -765,12 +767,12 @@ struct PairCfg {
   static_assert(kStages >= 3, "stage ring too shallow");
 };
 
-template <bool CV, bool SA = false>
+template <bool CV, bool SA = false, bool SB = false>
 __global__ void __launch_bounds__(320, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mAlo,
-                     const __grid_constant__ CUtensorMap mB, const __grid_constant__ OutMaps om,
-                     const __grid_constant__ KParams p) {
-  using C = PairCfg<CV, SA>;
+                     const __grid_constant__ CUtensorMap mB, const __grid_constant__ CUtensorMap mBlo,
+                     const __grid_constant__ OutMaps om, const __grid_constant__ KParams p) {
+  using C = PairCfg<CV, SA, SB>;
   constexpr int S = C::kStages;
   constexpr int BN = C::BN, BK = C::BK;
   constexpr uint32_t kIdesc = idesc_tf32(256, BN);
@@ -815,6 +817,7 @@ __global__ void __launch_bounds__(320, 1)
     tma_prefetch_desc(&mA);
     tma_prefetch_desc(&mB);
     if (SA) tma_prefetch_desc(&mAlo);
+    if (SB) tma_prefetch_desc(&mBlo);
   }
   if (warp == 1) {
     tmem_alloc_pair(smem_u32(tmem_holder), C::kTmemCols);
@@ -846,6 +849,7 @@ __global__ void __launch_bounds__(320, 1)
           tma_load_2d(dst, &mA, fb, kb * BK, arow);
           if (SA) tma_load_2d(dst + C::kABytes, &mAlo, fb, kb * BK, arow);
           tma_load_2d(dst + C::kABytes * (C::kLo ? 2 : 1), &mB, fb, kb * BK, brow);
+          if (SB) tma_load_2d(dst + C::kABytes * (C::kLo ? 2 : 1) + C::kBBytes, &mBlo, fb, kb * BK, brow);
           if (++stage == S) {
             stage = 0;
             phase ^= 1;
@@ -890,11 +894,14 @@ __global__ void __launch_bounds__(320, 1)
           const uint32_t a_addr = smem_u32(smem + size_t(stage) * C::kStageBytes);
           const uint32_t alo_addr = a_addr + C::kABytes;
           const uint32_t b_addr = a_addr + C::kABytes * (C::kLo ? 2 : 1);
+          const uint32_t blo_addr = b_addr + C::kBBytes;
 #pragma unroll
           for (int k = 0; k < BK / kUmmaK; ++k) {
             const uint32_t koff = uint32_t(k * kUmmaK * 4);
-            mma_tf32_pair(d_tmem, kmajor_desc<128>(a_addr + koff), kmajor_desc<128>(b_addr + koff), kIdesc,
-                          (kb | k) != 0 ? 1u : 0u);
+            const uint64_t da = kmajor_desc<128>(a_addr + koff);
+            mma_tf32_pair(d_tmem, da, kmajor_desc<128>(b_addr + koff), kIdesc, (kb | k) != 0 ? 1u : 0u);
+            // A·B_lo interleaved as in the single-CTA kernel, so both give equal sums
+            if (SB) mma_tf32_pair(d_tmem, da, kmajor_desc<128>(blo_addr + koff), kIdesc, 1u);
           }
           if (C::kLo) {
 #pragma unroll
@@ -1093,18 +1100,19 @@ int launch_variant(const GemmArgs& g, KParams kp, int* dev_err, cudaStream_t str
 }
 
 // CTA-pair kernel: 256-row M tiles, 256-column N tiles.
-template <bool CV, bool SA = false>
+template <bool CV, bool SA = false, bool SB = false>
 int launch_pair(const GemmArgs& g, KParams kp, int* dev_err, cudaStream_t stream) {
-  using C = PairCfg<CV, SA>;
-  CUtensorMap mA, mAlo, mB;
+  using C = PairCfg<CV, SA, SB>;
+  CUtensorMap mA, mAlo, mB, mBlo;
   FG_TRY(make_map(&mA, g.A, g.M, g.K, g.lda, 128, 32));
   if (SA) FG_TRY(make_map(&mAlo, g.A_lo, g.M, g.K, g.lda, 128, 32)); else mAlo = mA;
   FG_TRY(make_map(&mB, g.B, g.Nb, g.K, g.ldb, 128, 32));
+  if (SB) FG_TRY(make_map(&mBlo, g.B_lo, g.Nb, g.K, g.ldb, 128, 32)); else mBlo = mB;
   OutMaps om;
   for (CUtensorMap& m : om.m) m = mA;
   FG_TRY(prepare_out_maps(g, kp, &om));
   kp.ntm = (g.M + 255) / 256;
-  auto kern = gemm_pair_kernel<CV, SA>;
+  auto kern = gemm_pair_kernel<CV, SA, SB>;
   static bool attr_set[64] = {false};
   static int max_pairs[64] = {0};
   int dev = 0;
@@ -1131,19 +1139,19 @@ int launch_pair(const GemmArgs& g, KParams kp, int* dev_err, cudaStream_t stream
   }
   const int ntiles = kp.ntm * kp.ntn;
   cfg.gridDim = dim3(2 * std::max(1, std::min(ntiles, max_pairs[dev & 63])));
-  FG_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, mA, mAlo, mB, om, kp));
+  FG_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, mA, mAlo, mB, mBlo, om, kp));
   (void)dev_err;
   return FG_OK;
 }
 
-// Pair kernel for 256-wide N tiles without a stored B low part (M of at
-// least one pair tile); FG_GEMM_PAIR=0 selects the single-CTA kernel instead.
+// Pair kernel for 256-wide N tiles (M of at least one pair tile);
+// FG_GEMM_PAIR=0 selects the single-CTA kernel instead.
 bool use_pair(const GemmArgs& g) {
   static const bool enabled = [] {
     const char* v = std::getenv("FG_GEMM_PAIR");
     return !(v && v[0] == '0');
   }();
-  return enabled && g.B_lo == nullptr && g.M >= 256;
+  return enabled && g.M >= 256;
 }
 
 // A's low part: none (plain TF32), loaded (SA), or computed in shared memory (CV).
@@ -1175,8 +1183,14 @@ int dispatch(const GemmArgs& g, KParams& kp, int* dev_err, cudaStream_t stream) 
     kp.ntn = (g.Nb + 255) / 256;
   }
   if (use_pair(g)) {
-    if (g.A_lo) return launch_pair<false, true>(g, kp, dev_err, stream);
-    return g.a_lo_smem ? launch_pair<true>(g, kp, dev_err, stream) : launch_pair<false>(g, kp, dev_err, stream);
+    if (g.B_lo) {
+      if (g.A_lo) return launch_pair<false, true, true>(g, kp, dev_err, stream);
+      if (g.a_lo_smem) return launch_pair<true, false, true>(g, kp, dev_err, stream);
+      // B_lo without any A low part: the single-CTA kernel below
+    } else {
+      if (g.A_lo) return launch_pair<false, true>(g, kp, dev_err, stream);
+      return g.a_lo_smem ? launch_pair<true>(g, kp, dev_err, stream) : launch_pair<false>(g, kp, dev_err, stream);
+    }
   }
   return launch_b_mode<256>(g, kp, dev_err, stream);
 }
