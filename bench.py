@@ -184,7 +184,7 @@ def run_ours(args, rank, local_rank, world, cfg):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
     prec = gemma.PREC_TF32 if args.precision == "tf32" else gemma.PREC_SPLIT_TF32
-    w = S.make_weights(cfg, seed=0)
+    w = S.make_weights(cfg, seed=0, norm_std=args.norm_std)
     opts = [gemma.WeightsBF16()] if args.weights == "bf16" else []
     model = gemma.from_synthetic(cfg, w, device=local_rank, max_batch_tokens=BATCH * SEQ, options=opts)
     dim = model.Dim()
@@ -317,6 +317,7 @@ def run_ours(args, rank, local_rank, world, cfg):
                        "parallelism": f"replicas x{world} + NCCL gather of embeddings onto rank 0" if world > 1 else "single GPU",
                        "precision": args.precision,
                        "weights_resident": args.weights,
+                       "norm_std": args.norm_std,
                        "weight_bytes": model.weight_bytes(),
                        "l2_flush": "none: inputs larger than L2 (weights 1.2 GB, activations > 4 GB per step)"},
             "tokens_per_s": value * SEQ,
@@ -587,6 +588,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--precision", choices=["split_tf32", "tf32"], default="split_tf32")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--norm-std", type=float, default=0.0,
+                    help="RMSNorm weights ~N(0, s^2) instead of the spec's zeros (checkpoint-like: the "
+                         "folded projections then carry split-TF32 low parts, a third GEMM pass)")
     ap.add_argument("--weights", choices=["f32", "bf16"], default="f32",
                     help="projection weights resident in fp32 (default) or bf16, widened per layer")
     ap.add_argument("--batch", type=int, default=BATCH,
