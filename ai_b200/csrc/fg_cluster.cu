@@ -293,26 +293,32 @@ struct DevScratch {
 // unit length by contract). The product runs on the split-TF32 tensor-core
 // GEMM with A = x read in place (its low part made in shared memory) when
 // x's rows are 16-byte aligned, else through fg_matmul's packing.
+// `cbuf` (optional, 2·k·round4(d) floats) holds the centres' split parts;
+// without it they go to scratch from `ds`.
 int similarities(const float* x, int64_t ldx, int64_t n, int64_t d, const float* c, int64_t ldc, int64_t k,
-                 float* sim, int64_t lds, int precision, DevScratch& ds, cudaStream_t s) {
-  const bool split = precision == FG_PREC_SPLIT_TF32;
+                 float* sim, int64_t lds, int precision, DevScratch& ds, cudaStream_t s,
+                 float* cbuf = nullptr) {
   const bool a_direct = (reinterpret_cast<uintptr_t>(x) & 15) == 0 && ldx % 4 == 0;
   if (!a_direct || n > INT32_MAX || d > INT32_MAX || k > INT32_MAX)
     return fg_matmul(n, k, d, x, ldx, c, ldc, 1, sim, lds, nullptr, precision, s);
   int* err = nullptr;
   FG_TRY(device_error_word(&err));
   const int64_t dp = round_up4(d);
-  float *bhi = nullptr, *blo = nullptr;
-  FG_TRY(ds.alloc(&bhi, size_t(k * dp)));
-  if (split) FG_TRY(ds.alloc(&blo, size_t(k * dp)));
-  FG_TRY(split_copy_2d(c, ldc, k, d, bhi, blo, dp, split ? 1 : 0, s));
+  const bool lo_pass = precision == FG_PREC_SPLIT_TF32;
+  float *bhi = cbuf, *blo = cbuf ? cbuf + k * dp : nullptr;
+  if (!bhi) {
+    FG_TRY(ds.alloc(&bhi, size_t(k * dp)));
+    if (lo_pass) FG_TRY(ds.alloc(&blo, size_t(k * dp)));
+  }
+  if (!lo_pass) blo = nullptr;
+  FG_TRY(split_copy_2d(c, ldc, k, d, bhi, blo, dp, lo_pass ? 1 : 0, s));
   GemmArgs g;
   g.M = int(n);
   g.Nb = int(k);
   g.K = int(d);
   g.A = x;
   g.lda = ldx;
-  g.a_lo_smem = split;
+  g.a_lo_smem = lo_pass;
   g.B = bhi;
   g.B_lo = blo;
   g.ldb = dp;
@@ -396,6 +402,8 @@ int fg_kmeans(int64_t n, int64_t d, const float* x, int64_t ldx, int k, int iter
   FG_TRY(ds.alloc(&rows, size_t(n)));
   FG_TRY(ds.alloc(&keys_out, size_t(n)));
   FG_TRY(ds.alloc(&worst_d, 1));
+  float* cbuf = nullptr;  // the centres' split parts, reused every round
+  FG_TRY(ds.alloc(&cbuf, size_t(2 * k) * size_t(round_up4(d))));
   // sort keys: the assignment, non-negative, read as unsigned
   const uint32_t* keys = reinterpret_cast<const uint32_t*>(assignment);
   int end_bit = 1;
@@ -451,7 +459,7 @@ int fg_kmeans(int64_t n, int64_t d, const float* x, int64_t ldx, int k, int iter
   for (int it = 1; it <= iters; ++it) {
     *iterations = it;
     // assignment: one product and a row argmax (cluster.go:88-99)
-    FG_TRY(similarities(x, ldx, n, d, centres, d, k, sim, lds, precision, ds, s));
+    FG_TRY(similarities(x, ldx, n, d, centres, d, k, sim, lds, precision, ds, s, cbuf));
     FG_CUDA_TRY(cudaMemsetAsync(changed, 0, sizeof(int32_t), s));
     FG_CUDA_TRY(cudaMemsetAsync(sizes, 0, size_t(k) * sizeof(int32_t), s));
     FG_TRY(argmax_rows(sim, lds, n, k, assignment, similarity, changed, sizes, s));
