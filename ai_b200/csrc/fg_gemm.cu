@@ -346,6 +346,25 @@ __device__ __forceinline__ void qkv_attn_epilogue(const GemmEpilogue& e, const O
     __nv_bfloat16* const lo = static_cast<__nv_bfloat16*>(e.vt_lo);
     const int64_t ldt = e.ldt;
     const int64_t base = (int64_t(b) * Hkv + hk) * D * ldt + t;
+    // EmbeddingGemma 2's weight-free v_norm (embed.go:300): y·inv, inv from
+    // Σ y² over the head as for q and k; 1 (exact) without it
+    float vinv = 1.f;
+    if (e.vnorm) {
+      float ss = 0.f;
+#pragma unroll 1
+      for (int h0 = 0; h0 < D; h0 += 128) {
+        uint32_t r4[4][32];
+        tmem_ld4(taddr, h0, h0 + 32, h0 + 64, h0 + 96, r4);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float y = __fmul_rn(__uint_as_float(r4[q][j]), rs);
+            ss = __fadd_rn(ss, __fmul_rn(y, y));
+          }
+      }
+      vinv = float(1.0 / sqrt(double(__fadd_rn(__fdiv_rn(ss, float(D)), e.eps))));
+    }
 #pragma unroll 1
     for (int c0 = 0; c0 < D; c0 += 32) {
       uint32_t r[32];
@@ -354,7 +373,8 @@ __device__ __forceinline__ void qkv_attn_epilogue(const GemmEpilogue& e, const O
       if (row_ok) {
 #pragma unroll
         for (int j = 0; j < 32; ++j)
-          store_bf16_split(hi, lo, base + int64_t(c0 + j) * ldt, __fmul_rn(__uint_as_float(r[j]), rs));
+          store_bf16_split(hi, lo, base + int64_t(c0 + j) * ldt,
+                           __fmul_rn(__fmul_rn(__uint_as_float(r[j]), rs), vinv));
       }
     }
   }

@@ -78,6 +78,7 @@ struct GemmEpilogue {
   // hi/lo; for v heads: rs·acc written transposed as bf16 hi/lo
   // vt[(b·Hkv + hk)·256 + d][t]. `out` is unused in this mode.
   int qkv_attn = 0;
+  int vnorm = 0;  // v heads RMS-normalised (weight-free, EmbeddingGemma 2) before their split
   int Hq = 0, Hkv = 0, T = 0;
   const float* qgain = nullptr;
   const float* kgain = nullptr;

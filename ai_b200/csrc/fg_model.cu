@@ -474,6 +474,21 @@ int finalize_v2(fg_model* m, int64_t max_tokens) {
     FG_TRY(upload(m, sn, &ds));
     m->rope_cos.push_back(dc);
     m->rope_sin.push_back(ds);
+    // position-minor copies for the fused QKV epilogue (256-wide heads)
+    float *dcT = nullptr, *dsT = nullptr;
+    if (D == 256) {
+      const int64_t P = c.max_tokens, half = D / 2;
+      std::vector<float> cst(cs.size()), snt(sn.size());
+      for (int64_t t = 0; t < P; ++t)
+        for (int64_t i = 0; i < half; ++i) {
+          cst[i * P + t] = cs[t * half + i];
+          snt[i * P + t] = sn[t * half + i];
+        }
+      FG_TRY(upload(m, cst, &dcT));
+      FG_TRY(upload(m, snt, &dsT));
+    }
+    m->rope_cosT.push_back(dcT);
+    m->rope_sinT.push_back(dsT);
     m->rope_bases.push_back(base);
     m->rope_dims.push_back(D);
     *out = int(m->rope_bases.size()) - 1;
@@ -885,16 +900,44 @@ int forward_v2(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, i
     a.qlen = m->eff_len;
     a.window = (c.window > 0 && m->sliding[size_t(l)]) ? c.window : 0;
     a.scale = c.attn_scale;
-    // q|k|v = rowscale ⊙ (x · Wqkv'ᵀ)   (embed.go:285-288)
+    // q|k|v = rowscale ⊙ (x · Wqkv'ᵀ)   (embed.go:285-288); on the
+    // 256-wide layers the epilogue also applies the q/k norms, RoPE and the
+    // v_norm and writes the tensor-core attention's operands
+    const bool tc = !m->attn_simt && attn_tc_supported(a);
+    const bool fused = tc && D == 256 && m->rope_cosT[size_t(Ly.rope)] != nullptr;
+    AttnOperands ops{};
+    if (tc) FG_TRY(grow_attn_ws(m, attn_tc_workspace_bytes(B, T, T, Hq, Hkv, D), s));
     GemmArgs g = make_gemm(int(M), m->x, nullptr, H, Ly.wqkv, split);
     g.epi.rowscale = m->rowscale;
-    g.epi.out = m->qkv;
-    g.epi.ldo = qkvw;
+    if (fused) {
+      FG_TRY(attn_tc_carve(m->attn_ws, B, T, T, Hq, Hkv, &ops));
+      g.epi.qkv_attn = 1;
+      g.epi.vnorm = 1;
+      g.epi.Hq = Hq;
+      g.epi.Hkv = Hkv;
+      g.epi.T = T;
+      g.epi.qgain = Ly.qgain;
+      g.epi.kgain = Ly.kgain;
+      g.epi.eps = c.rms_norm_eps;
+      g.epi.rope_cos = m->rope_cosT[size_t(Ly.rope)];
+      g.epi.rope_sin = m->rope_sinT[size_t(Ly.rope)];
+      g.epi.rope_ld = c.max_tokens;
+      g.epi.q_hi = ops.q_hi;
+      g.epi.q_lo = ops.q_lo;
+      g.epi.k_hi = ops.k_hi;
+      g.epi.k_lo = ops.k_lo;
+      g.epi.vt_hi = ops.vt_hi;
+      g.epi.vt_lo = ops.vt_lo;
+      g.epi.ldt = ops.ldt;
+    } else {
+      g.epi.out = m->qkv;
+      g.epi.ldo = qkvw;
+    }
     {
       PhaseScope ps(m, FG_PHASE_GEMM_QKV, s, gemm_flops(g));
       FG_TRY(gemm_tn(g, m->err, s));
     }
-    {
+    if (!fused) {
       // q/k RMSNorm + RoPE, v RMSNorm (embed.go:289-317)
       PhaseScope ps(m, FG_PHASE_QK_NORM_ROPE, s, double(M) * (Hq + 2 * Hkv) * D * 8.0);
       FG_TRY(qk_norm_rope(m->qkv, nullptr, M, Hq, Hkv, D, Ly.qgain, Ly.kgain, Ly.vgain, c.rms_norm_eps,
@@ -902,9 +945,9 @@ int forward_v2(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, i
     }
     {
       PhaseScope ps(m, FG_PHASE_ATTENTION, s, 0.0);
-      if (!m->attn_simt && attn_tc_supported(a)) {
-        const size_t need = attn_tc_workspace_bytes(B, T, T, Hq, Hkv, D);
-        FG_TRY(grow_attn_ws(m, need, s));
+      if (fused) {
+        FG_TRY(attention_tc_operands(a, ops, m->err, s));
+      } else if (tc) {
         FG_TRY(attention_tc(a, m->attn_ws, m->attn_ws_bytes, m->err, s));
       } else {
         FG_TRY(attention_simt(a, s));
