@@ -18,6 +18,11 @@
 // Split-TF32 accumulates A·B + A·B_lo + A_lo·B into the same accumulator;
 // an operand whose low part is identically zero (bf16-exact weights) has
 // no low pass, which changes nothing in the result.
+// Split-fp16 (pair kernel only): when B has an exact fp16 form under a
+// power-of-two scale (bf16 weights: 8 significant bits), A is cut into two
+// fp16 parts under a per-row power-of-two scale and the product is
+// A_hi·B + A_lo·B in kind::f16 — the same 22 bits of A as split-TF32, exact
+// products, at the fp16 rate (twice TF32's).
 #include <algorithm>
 #include <cstdlib>
 #include <cudaTypedefs.h>
@@ -41,7 +46,24 @@ struct KParams {
   int* err;
   int tma_out, tma_out_lo;  // out / out_lo are written by TMA stores (maps m[0] / m[1])
   int tma_qk;               // q / k attention operands are written by TMA stores (maps m[0..3])
+  // Split-fp16 pair kernel: A·2^e_r and B·2^b_exp in fp16 (see a_row_exp);
+  // the epilogue multiplies each row by 2^-(e_r + b_exp), which is exact.
+  int h16;
+  int a_exp, a_exp_rs, b_exp;
+  float a_norm_k;  // sqrt(K): max|a_r| <= sqrt(K) / rowscale[r]
 };
+
+// Exponent e_r of A row r in the split-fp16 product: |a_r|·2^e_r < 2^14, so
+// both fp16 parts are finite and every element down to 2^-17 of the bound
+// keeps 22 significant bits. Static (p.a_exp, from a bound on the whole
+// operand) or, with p.a_exp_rs, from the row's RMS scale rs = 1/sqrt(ms +
+// eps): max|a_r| <= sqrt(K·ms) < sqrt(K)/rs.
+__device__ __forceinline__ int a_row_exp(const KParams& p, int row) {
+  if (!p.a_exp_rs) return p.a_exp;
+  const float rs = row < p.M ? p.e.rowscale[row] : 1.f;
+  const int e = 13 - ilogbf(p.a_norm_k / rs);
+  return max(-60, min(60, e));
+}
 
 // TMA-store maps of the epilogue outputs: fp32 out / out_lo in m[0] / m[1];
 // for the attention-operand epilogue the bf16 q_hi, q_lo, k_hi, k_lo.
@@ -436,7 +458,11 @@ __device__ __forceinline__ void epilogue_tile(const KParams& p, const OutMaps& o
   const int row = row0 + int(threadIdx.x & 31);
   const bool row_ok = row < M;
   const int rows = max(0, min(32, M - row0));
-  const float rs = (rowscale && row_ok) ? rowscale[row] : 1.f;
+  float rs = (rowscale && row_ok) ? rowscale[row] : 1.f;
+  // split-fp16: undo the operands' power-of-two scales (exact); applied to
+  // the accumulator first where a bias is added before the row scale
+  const float fac = p.h16 ? pow2f(-(a_row_exp(p, row) + p.b_exp)) : 1.f;
+  if (!bias) rs *= fac;
   if (qkv) {
     qkv_attn_epilogue(e, om, p.tma_qk != 0, taddr, tn, row, row_ok, rs, es, rows);
   } else if (geglu) {
@@ -485,6 +511,7 @@ __device__ __forceinline__ void epilogue_tile(const KParams& p, const OutMaps& o
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             float x = __uint_as_float(r[q][j]);
+            if (bias) x *= fac;
             const int col = col0 + j;
             const bool in = row_ok && j < ncols;
             if (bias && j < ncols) x = x + bias[col];
@@ -770,14 +797,27 @@ __global__ void __launch_bounds__(Cfg<BN, SA, SB, BK, CV>::kThreads, 1)
 // loaded by TMA from a stored low part; neither: plain TF32. SB: B's low
 // part (weights that are not TF32-exact, e.g. folded with non-zero norm
 // gains) loaded by TMA, adding the A·B_lo pass. Stage: A | A_lo | B | B_lo.
-template <bool CV, bool SA = false, bool SB = false>
+//
+// H16 (split-fp16, with CV): the converters write A·2^e_r as two fp16 parts
+// (hi = a's top 11 significant bits, lo = fp16(a − hi): 22 significant
+// bits, as split-TF32 keeps) as two 64-byte-swizzled [128 × 32] tiles over
+// the fp32 A tile they came from (same 16 KB), B arrives as fp16 (B·2^b
+// exactly: bf16-exact weights), and each stage is 2 × 2 pair MMAs of
+// kind::f16 (K = 16) instead of 2 × 4 of kind::tf32 (K = 8) — half the
+// tensor-pipe time for the same products. Stage: A (then A_hi | A_lo) | B,
+// 24 KB, so 8 stages are in flight.
+template <bool CV, bool SA = false, bool SB = false, bool H16 = false>
 struct PairCfg {
+  static_assert(!H16 || (CV && !SA && !SB), "split-fp16 takes A's parts from the converters");
   static constexpr int BN = 256, BK = 32;
   static constexpr int kThreads = 320;
   static constexpr bool kLo = CV || SA;
   static constexpr uint32_t kABytes = 128 * BK * 4;  // this CTA's A rows
-  static constexpr uint32_t kBBytes = 128 * BK * 4;  // this CTA's half of the B rows
-  static constexpr uint32_t kStageBytes = kABytes * (kLo ? 2 : 1) + kBBytes * (SB ? 2 : 1);
+  static constexpr uint32_t kBBytes = 128 * BK * (H16 ? 2 : 4);  // this CTA's half of the B rows
+  static constexpr uint32_t kPartBytes = 128 * BK * 2;  // one fp16 part of A (H16), in A's place
+  static constexpr uint32_t kStageBytes =
+      H16 ? kABytes + kBBytes : kABytes * (kLo ? 2 : 1) + kBBytes * (SB ? 2 : 1);
+  static constexpr uint32_t kBOffset = H16 ? kABytes : kABytes * (kLo ? 2 : 1);
   static constexpr uint32_t kTmaBytes = kABytes * (SA ? 2 : 1) + kBBytes * (SB ? 2 : 1);
   static constexpr uint32_t kEpiStageBytes = kEpiStageBytesAll;
   static constexpr int kStagesRaw = (kSmemLimit - 2048 - int(kEpiStageBytes)) / kStageBytes;
@@ -787,15 +827,15 @@ struct PairCfg {
   static_assert(kStages >= 3, "stage ring too shallow");
 };
 
-template <bool CV, bool SA = false, bool SB = false>
+template <bool CV, bool SA = false, bool SB = false, bool H16 = false>
 __global__ void __launch_bounds__(320, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mAlo,
                      const __grid_constant__ CUtensorMap mB, const __grid_constant__ CUtensorMap mBlo,
                      const __grid_constant__ OutMaps om, const __grid_constant__ KParams p) {
-  using C = PairCfg<CV, SA, SB>;
+  using C = PairCfg<CV, SA, SB, H16>;
   constexpr int S = C::kStages;
   constexpr int BN = C::BN, BK = C::BK;
-  constexpr uint32_t kIdesc = idesc_tf32(256, BN);
+  constexpr uint32_t kIdesc = H16 ? idesc_f16(256, BN) : idesc_tf32(256, BN);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -868,8 +908,8 @@ __global__ void __launch_bounds__(320, 1)
           const uint32_t dst = smem_u32(smem + size_t(stage) * C::kStageBytes);
           tma_load_2d(dst, &mA, fb, kb * BK, arow);
           if (SA) tma_load_2d(dst + C::kABytes, &mAlo, fb, kb * BK, arow);
-          tma_load_2d(dst + C::kABytes * (C::kLo ? 2 : 1), &mB, fb, kb * BK, brow);
-          if (SB) tma_load_2d(dst + C::kABytes * (C::kLo ? 2 : 1) + C::kBBytes, &mBlo, fb, kb * BK, brow);
+          tma_load_2d(dst + C::kBOffset, &mB, fb, kb * BK, brow);
+          if (SB) tma_load_2d(dst + C::kBOffset + C::kBBytes, &mBlo, fb, kb * BK, brow);
           if (++stage == S) {
             stage = 0;
             phase ^= 1;
@@ -913,8 +953,19 @@ __global__ void __launch_bounds__(320, 1)
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + size_t(stage) * C::kStageBytes);
           const uint32_t alo_addr = a_addr + C::kABytes;
-          const uint32_t b_addr = a_addr + C::kABytes * (C::kLo ? 2 : 1);
+          const uint32_t b_addr = a_addr + C::kBOffset;
           const uint32_t blo_addr = b_addr + C::kBBytes;
+          if constexpr (H16) {
+            // hi·B then lo·B, K = 16 fp16 (32 bytes of the 64-byte rows) per MMA
+            const uint32_t hi_addr = a_addr, lo_addr = a_addr + C::kPartBytes;
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k)
+              mma_f16_pair(d_tmem, kmajor_desc<64>(hi_addr + k * 32), kmajor_desc<64>(b_addr + k * 32), kIdesc,
+                           (kb | k) != 0 ? 1u : 0u);
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k)
+              mma_f16_pair(d_tmem, kmajor_desc<64>(lo_addr + k * 32), kmajor_desc<64>(b_addr + k * 32), kIdesc, 1u);
+          } else {
 #pragma unroll
           for (int k = 0; k < BK / kUmmaK; ++k) {
             const uint32_t koff = uint32_t(k * kUmmaK * 4);
@@ -930,6 +981,7 @@ __global__ void __launch_bounds__(320, 1)
               mma_tf32_pair(d_tmem, kmajor_desc<128>(alo_addr + koff), kmajor_desc<128>(b_addr + koff),
                             kIdesc, 1u);
             }
+          }
           }
           issued = true;
           mma_commit_pair(empty_bar(stage), 0x3);
@@ -958,6 +1010,61 @@ __global__ void __launch_bounds__(320, 1)
     const int ct = threadIdx.x - 192;  // 0..127
     int stage = 0;
     uint32_t phase = 0;
+    if constexpr (H16) {
+      // Row ct of the CTA's 128 A rows: the fp32 row (128-byte swizzled:
+      // 16-byte chunk c at c ^ (ct & 7)) is read whole, all 128 threads
+      // meet, then its fp16 hi and lo rows (64-byte swizzled: chunk j at
+      // j ^ ((ct >> 1) & 3)) go over the tile. Every exit is decided
+      // together (the AND of the named barrier), so no thread is left
+      // waiting at it.
+      for (int tile = pair; tile < ntiles; tile += npairs) {
+        bool ok = true;
+        const float sc = pow2f(a_row_exp(p, (tile / p.ntn) * 256 + int(rank) * 128 + ct));
+        for (int kb = 0; kb < p.nk; ++kb) {
+          const bool got = mbar_wait(full_bar(stage), phase, abort_flag, p.err, kDevTimeoutFull);
+          uint8_t* base = smem + size_t(stage) * C::kStageBytes;
+          float4 v[8];
+          if (got) {
+            const float4* src = reinterpret_cast<const float4*>(base) + ct * 8;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) v[c] = src[c ^ (ct & 7)];
+          }
+          if (!named_bar_and(1, 128, got)) {
+            ok = false;
+            break;
+          }
+          uint4* dhi = reinterpret_cast<uint4*>(base) + ct * 4;
+          uint4* dlo = reinterpret_cast<uint4*>(base + C::kPartBytes) + ct * 4;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float4 v0 = v[2 * j], v1 = v[2 * j + 1];
+            const float a[8] = {v0.x * sc, v0.y * sc, v0.z * sc, v0.w * sc,
+                                v1.x * sc, v1.y * sc, v1.z * sc, v1.w * sc};
+            // hi: a's top 11 significant bits (exact in fp16 above 2^-14,
+            // rounded on the subnormal grid below: 2^-25 at most, 2^-39 of
+            // the row bound); lo = a − hi (exact), rounded to fp16
+            uint32_t h[4], l[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const float h0 = tf32_hi(a[2 * q]), h1 = tf32_hi(a[2 * q + 1]);
+              h[q] = pack_f16x2(h0, h1);
+              l[q] = pack_f16x2(a[2 * q] - h0, a[2 * q + 1] - h1);
+            }
+            const int pj = j ^ ((ct >> 1) & 3);
+            dhi[pj] = make_uint4(h[0], h[1], h[2], h[3]);
+            dlo[pj] = make_uint4(l[0], l[1], l[2], l[3]);
+          }
+          fence_proxy_async_smem();  // generic-proxy writes → visible to the tensor core
+          __syncwarp();
+          if (lane == 0) mbar_arrive_remote(mapa_shared(ready_bar(stage), 0));
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+      }
+    } else {
     for (int tile = pair; tile < ntiles && !*abort_flag; tile += npairs) {
       bool ok = true;
       for (int kb = 0; kb < p.nk; ++kb) {
@@ -983,6 +1090,7 @@ __global__ void __launch_bounds__(320, 1)
         }
       }
       if (!ok) break;
+    }
     }
   } else {
     // -------------------------------------------------- epilogue (warps 2..5)
@@ -1056,6 +1164,22 @@ int make_map_bf16(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, i
   return FG_OK;
 }
 
+// Row-major [rows, cols] fp16 matrix, [box_rows × 32] boxes with 64-byte
+// swizzling (the split-fp16 B operand).
+int make_map_f16(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) != 0 || ld % 8 != 0)
+    return set_error(FG_EINVAL, "fp16 GEMM operand %p / row stride %lld not 16-byte aligned", ptr, (long long)ld);
+  cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(ld) * 2};
+  cuuint32_t box[2] = {32u, cuuint32_t(box_rows)};
+  cuuint32_t es[2] = {1u, 1u};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(FG_ECUDA, "cuTensorMapEncodeTiled (fp16) failed (%d)", int(r));
+  return FG_OK;
+}
+
 int prepare_out_maps(const GemmArgs& g, KParams& kp, OutMaps* om) {
   static const bool enabled = [] {
     const char* v = std::getenv("FG_GEMM_TMA_STORE");
@@ -1120,19 +1244,21 @@ int launch_variant(const GemmArgs& g, KParams kp, int* dev_err, cudaStream_t str
 }
 
 // CTA-pair kernel: 256-row M tiles, 256-column N tiles.
-template <bool CV, bool SA = false, bool SB = false>
+template <bool CV, bool SA = false, bool SB = false, bool H16 = false>
 int launch_pair(const GemmArgs& g, KParams kp, int* dev_err, cudaStream_t stream) {
-  using C = PairCfg<CV, SA, SB>;
+  using C = PairCfg<CV, SA, SB, H16>;
   CUtensorMap mA, mAlo, mB, mBlo;
   FG_TRY(make_map(&mA, g.A, g.M, g.K, g.lda, 128, 32));
   if (SA) FG_TRY(make_map(&mAlo, g.A_lo, g.M, g.K, g.lda, 128, 32)); else mAlo = mA;
-  FG_TRY(make_map(&mB, g.B, g.Nb, g.K, g.ldb, 128, 32));
+  if (H16) FG_TRY(make_map_f16(&mB, g.B16, g.Nb, g.K, g.ldb, 128));
+  else FG_TRY(make_map(&mB, g.B, g.Nb, g.K, g.ldb, 128, 32));
   if (SB) FG_TRY(make_map(&mBlo, g.B_lo, g.Nb, g.K, g.ldb, 128, 32)); else mBlo = mB;
   OutMaps om;
   for (CUtensorMap& m : om.m) m = mA;
   FG_TRY(prepare_out_maps(g, kp, &om));
   kp.ntm = (g.M + 255) / 256;
-  auto kern = gemm_pair_kernel<CV, SA, SB>;
+  kp.h16 = H16 ? 1 : 0;
+  auto kern = gemm_pair_kernel<CV, SA, SB, H16>;
   static bool attr_set[64] = {false};
   static int max_pairs[64] = {0};
   int dev = 0;
@@ -1203,6 +1329,9 @@ int dispatch(const GemmArgs& g, KParams& kp, int* dev_err, cudaStream_t stream) 
     kp.ntn = (g.Nb + 255) / 256;
   }
   if (use_pair(g)) {
+    // split-fp16 where B has an exact fp16 form and A's parts are made here
+    if (g.B16 && g.a_lo_smem && !g.A_lo && (g.ldb % 8) == 0 && (!g.a_exp_rs || g.epi.rowscale))
+      return launch_pair<true, false, false, true>(g, kp, dev_err, stream);
     if (g.B_lo) {
       if (g.A_lo) return launch_pair<false, true, true>(g, kp, dev_err, stream);
       if (g.a_lo_smem) return launch_pair<true, false, true>(g, kp, dev_err, stream);
@@ -1234,6 +1363,11 @@ int gemm_tn(const GemmArgs& g, int* dev_err, cudaStream_t stream) {
   kp.e = g.epi;
   kp.err = dev_err;
   kp.ntm = (g.M + kBM - 1) / kBM;
+  kp.h16 = 0;
+  kp.a_exp = g.a_exp;
+  kp.a_exp_rs = g.a_exp_rs;
+  kp.b_exp = g.b_exp;
+  kp.a_norm_k = sqrtf(float(g.K));
   return dispatch(g, kp, dev_err, stream);
 }
 

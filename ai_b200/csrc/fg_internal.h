@@ -106,6 +106,14 @@ struct GemmArgs {
   // Split-TF32 without a stored A_lo: the kernel computes A's low part in
   // shared memory from the A tile (A is read from memory once).
   bool a_lo_smem = false;
+  // Split-fp16 (with a_lo_smem, M >= 256): B16 = the fp16 bits of B·2^b_exp,
+  // exact; A's rows are scaled by 2^e_r (a_exp, or from the epilogue's
+  // rowscale when a_exp_rs) so that |A|·2^e_r < 2^14. The products are
+  // A_hi·B + A_lo·B in kind::f16; the epilogue undoes the scales exactly.
+  const uint16_t* B16 = nullptr;
+  int b_exp = 0;
+  int a_exp = 0;
+  int a_exp_rs = 0;
   GemmEpilogue epi;
 };
 

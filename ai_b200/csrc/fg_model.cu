@@ -82,6 +82,10 @@ struct DevMat {
   float* hi = nullptr;
   float* lo = nullptr;  // null when every low part is zero
   int rows = 0, cols = 0;
+  // fp16 bits of hi·2^h16_exp when that is exact for every value (the
+  // split-fp16 GEMM's B operand), else null
+  uint16_t* h16 = nullptr;
+  int h16_exp = 0;
 };
 
 // A projection resident as bf16 (FG_WEIGHTS_BF16): [rows, cols] bits and
@@ -111,6 +115,10 @@ struct Layer {
   float* vgain = nullptr;
   float* ple_post = nullptr;
   float scalar = 1.f;
+  // split-fp16 exponents of the O and down projections' inputs, from
+  // bounds on the attention output and the gated activations (ok: finite)
+  int att_exp = 0, gu_exp = 0;
+  bool att_ok = false, gu_ok = false;
 };
 
 struct Dense {
@@ -157,6 +165,9 @@ struct fg_model {
   // FG_GEMM_ALO=global: producers write the split-TF32 low parts of the
   // GEMM inputs to memory instead of the GEMM computing them in shared memory
   bool alo_global = false;
+  // split-fp16 encoder GEMMs where the weights have an exact fp16 form
+  // (FG_GEMM_H16=0: split-TF32 everywhere)
+  bool h16 = true;
   int weight_mode = FG_WEIGHTS_F32;
   size_t weight_bytes = 0;  // device bytes allocated by finalize before the activation workspace
   size_t alloc_bytes = 0;
@@ -316,6 +327,54 @@ __global__ void __launch_bounds__(256) widen_fold_kernel(WidenJobs jobs) {
 }
 
 // Uploads a K-major [rows, cols] fp32 matrix and its split-TF32 parts.
+// The fp16 bits of v when v is exactly an fp16 value (normal or subnormal).
+bool f16_exact(float v, uint16_t* out) {
+  uint32_t u;
+  std::memcpy(&u, &v, 4);
+  const uint32_t sign = (u >> 31) << 15, ex = (u >> 23) & 0xffu, mant = u & 0x7fffffu;
+  if (ex == 0) {
+    *out = uint16_t(sign);
+    return mant == 0;  // fp32 subnormals are far below fp16's range
+  }
+  if (ex == 0xffu) return false;
+  const int e = int(ex) - 127;
+  if (e > 15) return false;
+  if (e >= -14) {
+    if (mant & 0x1fffu) return false;
+    *out = uint16_t(sign | (uint32_t(e + 15) << 10) | (mant >> 13));
+    return true;
+  }
+  const int sh = -e - 1;  // value = ((1 << 23) | mant) · 2^(e − 23) = m16 · 2^−24
+  if (sh > 24) return false;
+  const uint32_t sig = (1u << 23) | mant;
+  if (sig & ((1u << sh) - 1)) return false;
+  *out = uint16_t(sign | (sig >> sh));
+  return true;
+}
+
+// Exponent e with bound·2^e in [2^13, 2^14) (a split-fp16 operand scale), or
+// false when the bound is not a positive finite number.
+bool h16_exponent(double bound, int* e) {
+  if (!(bound > 0) || !std::isfinite(bound)) return false;
+  *e = 13 - std::ilogb(bound);
+  return *e > -100 && *e < 100;
+}
+
+// hi·2^e as fp16 bits, e from the largest |value|, when exact for all.
+int upload_h16(fg_model* m, const std::vector<float>& h, DevMat* out) {
+  double mx = 0;
+  for (float v : h) mx = std::max(mx, double(std::fabs(v)));
+  int e = 0;
+  if (!h16_exponent(mx, &e)) return FG_OK;
+  std::vector<uint16_t> b(h.size());
+  for (size_t i = 0; i < h.size(); ++i)
+    if (!f16_exact(std::ldexp(h[i], e), &b[i])) return FG_OK;
+  FG_TRY(dev_alloc_t(m, &out->h16, b.size()));
+  FG_CUDA_TRY(cudaMemcpy(out->h16, b.data(), b.size() * 2, cudaMemcpyHostToDevice));
+  out->h16_exp = e;
+  return FG_OK;
+}
+
 int upload_mat(fg_model* m, const std::vector<float>& h, int rows, int cols, DevMat* out) {
   float* raw = nullptr;
   FG_TRY(upload(m, h, &raw));
@@ -338,7 +397,20 @@ int upload_mat(fg_model* m, const std::vector<float>& h, int rows, int cols, Dev
   out->lo = lo;
   out->rows = rows;
   out->cols = cols;
+  // a weight with a low part is not fp16-exact (it has more than 11 bits)
+  if (m->h16 && !lo) FG_TRY(upload_h16(m, h, out));
   return FG_OK;
+}
+
+// sqrt(Σ_c (w[r][c]·g[c])²) of row r of a [rows, cols] matrix folded with
+// the column gain g (fp32 products, as the fold stores them).
+double folded_row_norm(const float* w, const std::vector<float>& g, int64_t r, int64_t cols) {
+  double s = 0;
+  for (int64_t c = 0; c < cols; ++c) {
+    const double v = double(w[r * cols + c] * g[size_t(c)]);
+    s += v * v;
+  }
+  return std::sqrt(s);
 }
 
 const HostTensor* find(fg_model* m, const std::string& name) {
@@ -682,6 +754,24 @@ int finalize(fg_model* m, int64_t max_tokens) {
       FG_TRY(upload_mat(m, wo->data, int(H), int(Hq * D), &L.wo));
       FG_TRY(upload_mat(m, fold(rgu, g_pf, H), int(2 * F), int(H), &L.wgu));
       FG_TRY(upload_mat(m, wd->data, int(H), int(F), &L.wd));
+      if (m->h16) {
+        // Bounds for the split-fp16 scales of the O and down inputs. With
+        // rs = 1/sqrt(mean(x²) + eps), ‖rs·x‖ < sqrt(H), so each projection
+        // output is below sqrt(H)·‖W'_row‖ (Cauchy-Schwarz): v, hence the
+        // attention output (convex combinations of v rows); gate and up,
+        // hence GELU(g)·u (|GELU(g)| <= max(|g|, 0.17)).
+        const double sh = std::sqrt(double(H));
+        double bv = 0, bgu = 0;
+        for (int64_t r = (Hq + Hkv) * D; r < qkv_rows; ++r)
+          bv = std::max(bv, sh * folded_row_norm(rqkv.data(), g_in, r, H));
+        for (int64_t k = 0; k < F; ++k) {
+          const double bg = sh * folded_row_norm(wg->data.data(), g_pf, k, H);
+          const double bu = sh * folded_row_norm(wu->data.data(), g_pf, k, H);
+          bgu = std::max(bgu, std::max(bg, 0.2) * bu);
+        }
+        L.att_ok = h16_exponent(bv * 1.01, &L.att_exp);
+        L.gu_ok = h16_exponent(bgu * 1.01, &L.gu_exp);
+      }
     }
 
     FG_TRY(upload(m, plus_one(*qn), &L.qgain));
@@ -1053,6 +1143,16 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
   float* x_lo = lo_global ? m->x_lo : nullptr;
   float* att_lo = lo_global ? m->att_lo : nullptr;
   float* gu_lo = lo_global ? m->gu_lo : nullptr;
+  // split-fp16 operands (B's exact fp16 form; A's exponent from its row
+  // scale or a static bound) where the product is split and A's parts are
+  // made in shared memory
+  auto h16 = [&](GemmArgs& g, const DevMat& W, bool from_rs, bool ok, int aexp) {
+    if (!split || lo_global || !W.h16 || !ok) return;
+    g.B16 = W.h16;
+    g.b_exp = W.h16_exp;
+    g.a_exp_rs = from_rs ? 1 : 0;
+    g.a_exp = aexp;
+  };
 
   const double act_bytes = double(M) * H * 4.0;
   {
@@ -1118,6 +1218,7 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
     // q|k|v = rowscale ⊙ (x · Wqkv'ᵀ)   (embed.go:193-197)
     GemmArgs g = make_gemm(int(M), m->x, x_lo, H, Wqkv, split);
     g.epi.rowscale = m->rowscale;
+    h16(g, Wqkv, true, true, 0);
     if (tc) {
       // + QK-norm and RoPE (embed.go:198-207) in the epilogue
       g.epi.qkv_attn = 1;
@@ -1163,6 +1264,7 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
     g = make_gemm(int(M), m->att, att_lo, attw, Wo, split);
     g.epi.out = m->tmp;
     g.epi.ldo = H;
+    h16(g, Wo, false, L.att_ok, L.att_exp);
     {
       PhaseScope ps(m, FG_PHASE_GEMM_O, s, gemm_flops(g));
       FG_TRY(gemm_tn(g, m->err, s));
@@ -1181,6 +1283,7 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
     g.epi.ldo_lo = F;
     g.epi.rowscale = m->rowscale;
     g.epi.geglu = 1;
+    h16(g, Wgu, true, true, 0);
     {
       PhaseScope ps(m, FG_PHASE_GEMM_GATE_UP, s, gemm_flops(g));
       FG_TRY(gemm_tn(g, m->err, s));
@@ -1189,6 +1292,7 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
     g = make_gemm(int(M), m->gu, gu_lo, F, Wd, split);
     g.epi.out = m->tmp;
     g.epi.ldo = H;
+    h16(g, Wd, false, L.gu_ok, L.gu_exp);
     {
       PhaseScope ps(m, FG_PHASE_GEMM_DOWN, s, gemm_flops(g));
       FG_TRY(gemm_tn(g, m->err, s));
@@ -1295,6 +1399,8 @@ int fg_model_create(const fg_config* cfg, int device, fg_model** out) {
   m->attn_simt = att && std::string(att) == "simt";
   const char* alo = std::getenv("FG_GEMM_ALO");
   m->alo_global = alo && std::string(alo) == "global";
+  const char* h16 = std::getenv("FG_GEMM_H16");
+  m->h16 = !(h16 && h16[0] == '0');
   const char* wm = std::getenv("FG_WEIGHTS");
   if (wm && std::string(wm) == "bf16") m->weight_mode = FG_WEIGHTS_BF16;
   *out = m;

@@ -273,6 +273,60 @@ __device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
+// Pair MMA, M = 256 (128 rows per CTA), FP16 inputs, FP32 accumulate.
+__device__ __forceinline__ void mma_f16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Instruction descriptor: kind::f16 with FP16 A and B, FP32 accumulator, K-major.
+__host__ __device__ constexpr uint32_t idesc_f16(int m, int n) {
+  return (1u << 4)                                 // D format: F32
+         | (0u << 7)                               // A format: F16
+         | (0u << 10)                              // B format: F16
+         | (static_cast<uint32_t>(n >> 3) << 17)   // N / 8
+         | (static_cast<uint32_t>(m >> 4) << 24);  // M / 16
+}
+
+// fp16x2 packing: `lo_elem` in bits 0-15, `hi_elem` in bits 16-31, round to nearest.
+__device__ __forceinline__ uint32_t pack_f16x2(float lo_elem, float hi_elem) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi_elem), "f"(lo_elem));
+  return r;
+}
+// Named barrier over `nthreads` threads (whole warps) with an AND of `v`:
+// every participant gets true only if all passed true. Shared-memory
+// accesses before it are ordered before those after it for all of them.
+__device__ __forceinline__ bool named_bar_and(int id, int nthreads, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 q, %1, 0;\n\t"
+      "bar.red.and.pred p, %2, %3, q;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"(v ? 1 : 0), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
+
+// 2^k as a float for k in [-126, 127] (exact).
+__host__ __device__ __forceinline__ float pow2f(int k) {
+#ifdef __CUDA_ARCH__
+  return __int_as_float((127 + k) << 23);
+#else
+  uint32_t u = static_cast<uint32_t>(127 + k) << 23;
+  float f;
+  __builtin_memcpy(&f, &u, 4);
+  return f;
+#endif
+}
+
 // Instruction descriptor: kind::f16 with BF16 A and B, FP32 accumulator, K-major.
 __host__ __device__ constexpr uint32_t idesc_bf16(int m, int n) {
   return (1u << 4)                                 // D format: F32

@@ -171,7 +171,7 @@ def test_embedding_table_bf16_residency(small, monkeypatch):
 
 
 @pytest.mark.parametrize("norm_std", [0.0, 0.1])
-def test_bf16_resident_projections_are_bitwise_identical(norm_std):
+def test_bf16_resident_projections_are_bitwise_identical(norm_std, monkeypatch):
     """gemma.WeightsBF16(): projections resident as bf16, widened, gain-folded
     and split per layer on the device, give the same embeddings bit for bit
     as the fp32-resident weights, in split-TF32 and plain TF32, with zero
@@ -180,6 +180,7 @@ def test_bf16_resident_projections_are_bitwise_identical(norm_std):
     from ai_b200 import _lib, gemma
     from ai_b200 import synthetic as S
 
+    monkeypatch.setenv("FG_GEMM_H16", "0")  # both on the split-TF32 GEMM
     cfg = S.small_config(layers=3, vocab=2048)
     w = S.make_weights(cfg, seed=31, norm_std=norm_std)
     ids = S.make_ids(4, 96, 6, cfg["vocab_size"])
@@ -206,6 +207,7 @@ def test_stored_low_parts_equal_shared_memory_low_parts(monkeypatch):
     from ai_b200 import gemma
     from ai_b200 import synthetic as S
 
+    monkeypatch.setenv("FG_GEMM_H16", "0")  # both on the split-TF32 GEMM
     cfg = S.small_config(layers=3, vocab=2048)
     w = S.make_weights(cfg, seed=41, norm_std=0.0)
     ids = S.make_ids(6, 128, 12, cfg["vocab_size"])
@@ -217,6 +219,36 @@ def test_stored_low_parts_equal_shared_memory_low_parts(monkeypatch):
         a, b = m1.embed_padded(ids, lengths), m2.embed_padded(ids, lengths)
         print(f"stored vs shared-memory low parts: max |diff| {np.abs(a - b).max():.3e}")
         assert np.array_equal(a, b)
+    finally:
+        m1.close()
+        m2.close()
+
+
+@pytest.mark.parametrize("norm_std", [0.0, 0.1])
+def test_split_fp16_matches_split_tf32(norm_std, monkeypatch):
+    """The split-fp16 encoder GEMMs (bf16-exact weights as exact fp16, A as
+    two fp16 parts under a power-of-two row scale) agree with split-TF32 to
+    the size of split-TF32's own error, are in use (not bitwise equal) and
+    repeatable. With non-zero norm gains the folded Q/K/V and gate/up
+    weights have no exact fp16 form and stay split-TF32; O and down (not
+    folded) still run split-fp16."""
+    from ai_b200 import gemma
+    from ai_b200 import synthetic as S
+
+    cfg = S.small_config(layers=3, vocab=2048)
+    w = S.make_weights(cfg, seed=43, norm_std=norm_std)
+    ids = S.make_ids(6, 128, 14, cfg["vocab_size"])
+    lengths = np.array([128, 100, 1, 77, 128, 64], np.int32)
+    m1 = gemma.from_synthetic(cfg, w, device=0, max_batch_tokens=4096)
+    monkeypatch.setenv("FG_GEMM_H16", "0")
+    m2 = gemma.from_synthetic(cfg, w, device=0, max_batch_tokens=4096)
+    try:
+        a, b = m1.embed_padded(ids, lengths), m2.embed_padded(ids, lengths)
+        d = np.abs(a.astype(np.float64) - b).max()
+        print(f"norm_std {norm_std}: split-fp16 vs split-TF32 max |diff| {d:.3e}")
+        assert d <= 5e-6
+        assert not np.array_equal(a, b)
+        assert np.array_equal(a, m1.embed_padded(ids, lengths))  # repeatable
     finally:
         m1.close()
         m2.close()
