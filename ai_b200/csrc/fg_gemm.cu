@@ -50,7 +50,8 @@ struct KParams {
   // the epilogue multiplies each row by 2^-(e_r + b_exp), which is exact.
   int h16;
   int a_exp, a_exp_rs, b_exp;
-  float a_norm_k;  // sqrt(K): max|a_r| <= sqrt(K) / rowscale[r]
+  float a_norm_k;      // sqrt(K): max|a_r| <= sqrt(K) / a_rs[r]
+  const float* a_rs;   // A's row scales 1/sqrt(mean(a²) + eps) (a_exp_rs)
 };
 
 // Exponent e_r of A row r in the split-fp16 product: |a_r|·2^e_r < 2^14, so
@@ -60,7 +61,7 @@ struct KParams {
 // eps): max|a_r| <= sqrt(K·ms) < sqrt(K)/rs.
 __device__ __forceinline__ int a_row_exp(const KParams& p, int row) {
   if (!p.a_exp_rs) return p.a_exp;
-  const float rs = row < p.M ? p.e.rowscale[row] : 1.f;
+  const float rs = row < p.M ? p.a_rs[row] : 1.f;
   const int e = 13 - ilogbf(p.a_norm_k / rs);
   return max(-60, min(60, e));
 }
@@ -1321,6 +1322,10 @@ int launch_b_mode(const GemmArgs& g, const KParams& kp, int* dev_err, cudaStream
 
 int dispatch(const GemmArgs& g, KParams& kp, int* dev_err, cudaStream_t stream) {
   kp.nk = (g.K + 31) / 32;
+  // split-fp16 where B has an exact fp16 form and A's parts are made here
+  const bool h16 = g.B16 && g.a_lo_smem && !g.A_lo && (g.ldb % 8) == 0 && (!g.a_exp_rs || kp.a_rs) &&
+                   use_pair(g) && (g.epi.geglu || g.Nb > 128);
+  if (!h16 && !g.B) return set_error(FG_EINVAL, "gemm: B has only an fp16 form and the split-fp16 kernel does not apply");
   if (g.epi.geglu) {
     kp.Nout = g.Nb / 2;
     kp.ntn = g.Nb / 256;
@@ -1333,9 +1338,7 @@ int dispatch(const GemmArgs& g, KParams& kp, int* dev_err, cudaStream_t stream) 
     kp.ntn = (g.Nb + 255) / 256;
   }
   if (use_pair(g)) {
-    // split-fp16 where B has an exact fp16 form and A's parts are made here
-    if (g.B16 && g.a_lo_smem && !g.A_lo && (g.ldb % 8) == 0 && (!g.a_exp_rs || g.epi.rowscale))
-      return launch_pair<true, false, false, true>(g, kp, dev_err, stream);
+    if (h16) return launch_pair<true, false, false, true>(g, kp, dev_err, stream);
     if (g.B_lo) {
       if (g.A_lo) return launch_pair<false, true, true>(g, kp, dev_err, stream);
       if (g.a_lo_smem) return launch_pair<true, false, true>(g, kp, dev_err, stream);
@@ -1349,6 +1352,12 @@ int dispatch(const GemmArgs& g, KParams& kp, int* dev_err, cudaStream_t stream) 
 }
 
 }  // namespace
+
+bool gemm_h16_applies(int M) {
+  GemmArgs g;
+  g.M = M;
+  return use_pair(g);
+}
 
 int gemm_tn(const GemmArgs& g, int* dev_err, cudaStream_t stream) {
   if (g.M <= 0 || g.Nb <= 0 || g.K <= 0) {
@@ -1372,6 +1381,7 @@ int gemm_tn(const GemmArgs& g, int* dev_err, cudaStream_t stream) {
   kp.a_exp_rs = g.a_exp_rs;
   kp.b_exp = g.b_exp;
   kp.a_norm_k = sqrtf(float(g.K));
+  kp.a_rs = g.a_rs ? g.a_rs : g.epi.rowscale;
   return dispatch(g, kp, dev_err, stream);
 }
 

@@ -108,16 +108,21 @@ struct GemmArgs {
   bool a_lo_smem = false;
   // Split-fp16 (with a_lo_smem, M >= 256): B16 = the fp16 bits of B·2^b_exp,
   // exact; A's rows are scaled by 2^e_r (a_exp, or from the epilogue's
-  // rowscale when a_exp_rs) so that |A|·2^e_r < 2^14. The products are
+  // row scales a_rs / epi.rowscale, 1/sqrt(mean(a²) + eps), when a_exp_rs)
+  // so that |A|·2^e_r < 2^14. The products are
   // A_hi·B + A_lo·B in kind::f16; the epilogue undoes the scales exactly.
   const uint16_t* B16 = nullptr;
   int b_exp = 0;
   int a_exp = 0;
   int a_exp_rs = 0;
+  const float* a_rs = nullptr;  // row scales behind a_exp_rs (null: epi.rowscale)
   GemmEpilogue epi;
 };
 
 int gemm_tn(const GemmArgs& g, int* dev_err, cudaStream_t stream);
+// Whether an M-row product can take the split-fp16 pair kernel (CTA pairs
+// enabled, M >= 256), the only kernel that reads B16 without B.
+bool gemm_h16_applies(int M);
 
 // Elementwise split of n floats into TF32 high and exact low parts.
 // *any_lo_nonzero (device int, optional) is set to 1 when some low part is non-zero.

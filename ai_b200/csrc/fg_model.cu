@@ -25,6 +25,8 @@
 #include <string>
 #include <vector>
 
+#include <cuda_fp16.h>
+
 #include "fg_internal.h"
 #include "fg_kernels.cuh"
 #include "fg_ptx.cuh"
@@ -94,6 +96,10 @@ struct Bf16Mat {
   uint16_t* w = nullptr;
   const float* gain = nullptr;
   bool lo = false;  // the folded values have non-zero split-TF32 low parts
+  // with split-fp16: w holds the folded values as fp16 bits of v·2^exp
+  // (exact), the split-fp16 GEMM's B operand as it is (gain null, no lo)
+  bool f16 = false;
+  int exp = 0;
 };
 
 struct Layer {
@@ -291,6 +297,8 @@ struct WidenJob {
   float* lo;
   int64_t n4;  // groups of 4 values
   int cols;    // a multiple of 4
+  int f16;     // w holds fp16 bits of the folded values times 2^f16_exp
+  int f16_exp;
 };
 struct WidenJobs {
   WidenJob j[4];
@@ -307,6 +315,14 @@ __global__ void __launch_bounds__(256) widen_fold_kernel(WidenJobs jobs) {
     const uint2 h = __ldg(reinterpret_cast<const uint2*>(J.w) + i);
     float v[4] = {__uint_as_float(h.x << 16), __uint_as_float(h.x & 0xffff0000u),
                   __uint_as_float(h.y << 16), __uint_as_float(h.y & 0xffff0000u)};
+    if (J.f16) {
+      // exact: an fp16 value times a power of two in fp32's normal range
+      const float sc = pow2f(-J.f16_exp);
+      v[0] = __half2float(__ushort_as_half(uint16_t(h.x & 0xffffu))) * sc;
+      v[1] = __half2float(__ushort_as_half(uint16_t(h.x >> 16))) * sc;
+      v[2] = __half2float(__ushort_as_half(uint16_t(h.y & 0xffffu))) * sc;
+      v[3] = __half2float(__ushort_as_half(uint16_t(h.y >> 16))) * sc;
+    }
     if (J.gain) {
       const int c = int((i * 4) % J.cols);
       const float4 g = __ldg(reinterpret_cast<const float4*>(J.gain + c));
@@ -360,15 +376,21 @@ bool h16_exponent(double bound, int* e) {
   return *e > -100 && *e < 100;
 }
 
-// hi·2^e as fp16 bits, e from the largest |value|, when exact for all.
-int upload_h16(fg_model* m, const std::vector<float>& h, DevMat* out) {
+// h·2^e as fp16 bits, e from the largest |value|, when exact for all.
+bool f16_form(const std::vector<float>& h, std::vector<uint16_t>& b, int* e) {
   double mx = 0;
   for (float v : h) mx = std::max(mx, double(std::fabs(v)));
-  int e = 0;
-  if (!h16_exponent(mx, &e)) return FG_OK;
-  std::vector<uint16_t> b(h.size());
+  if (!h16_exponent(mx, e)) return false;
+  b.resize(h.size());
   for (size_t i = 0; i < h.size(); ++i)
-    if (!f16_exact(std::ldexp(h[i], e), &b[i])) return FG_OK;
+    if (!f16_exact(std::ldexp(h[i], *e), &b[i])) return false;
+  return true;
+}
+
+int upload_h16(fg_model* m, const std::vector<float>& h, DevMat* out) {
+  std::vector<uint16_t> b;
+  int e = 0;
+  if (!f16_form(h, b, &e)) return FG_OK;
   FG_TRY(dev_alloc_t(m, &out->h16, b.size()));
   FG_CUDA_TRY(cudaMemcpy(out->h16, b.data(), b.size() * 2, cudaMemcpyHostToDevice));
   out->h16_exp = e;
@@ -612,6 +634,20 @@ int finalize_v2(fg_model* m, int64_t max_tokens) {
     FG_TRY(upload_mat(m, wd->data, int(H), int(F), &Ly.wd));
     FG_TRY(upload_mat(m, pg->data, int(P), int(H), &Ly.wpg));
     FG_TRY(upload_mat(m, pp->data, int(H), int(P), &Ly.wpp));
+    if (m->h16) {
+      // split-fp16 bounds of the O and down inputs: v is RMS-normalised
+      // without a weight, so |v| < sqrt(D) and so is the attention output;
+      // the gated activations as in EmbeddingGemma (‖rs·x‖ < sqrt(H))
+      const double sh = std::sqrt(double(H));
+      double bgu = 0;
+      for (int64_t k = 0; k < F; ++k) {
+        const double bg = sh * folded_row_norm(wg->data.data(), g_pf, k, H);
+        const double bu = sh * folded_row_norm(wu->data.data(), g_pf, k, H);
+        bgu = std::max(bgu, std::max(bg, 0.2) * bu);
+      }
+      Ly.att_ok = h16_exponent(std::sqrt(double(D)) * 1.01, &Ly.att_exp);
+      Ly.gu_ok = h16_exponent(bgu * 1.01, &Ly.gu_exp);
+    }
     FG_TRY(gain(p + "self_attn.q_norm.weight", D, &Ly.qgain));
     FG_TRY(gain(p + "self_attn.k_norm.weight", D, &Ly.kgain));
     FG_TRY(upload(m, std::vector<float>(size_t(D), 1.0f), &Ly.vgain));  // v_norm has no weight
@@ -739,12 +775,30 @@ int finalize(fg_model* m, int64_t max_tokens) {
         out->lo = lo;
         return FG_OK;
       };
+      // with split-fp16, a projection whose folded values have an exact
+      // fp16 form stays resident in that form instead (same bytes): the
+      // GEMM reads it directly, and plain TF32 widens it
+      auto put16 = [&](const std::vector<float>& folded, Bf16Mat* out, bool* done) -> int {
+        std::vector<uint16_t> b;
+        int e = 0;
+        *done = m->h16 && f16_form(folded, b, &e);
+        if (!*done) return FG_OK;
+        FG_TRY(put(b, nullptr, false, out));
+        out->f16 = true;
+        out->exp = e;
+        return FG_OK;
+      };
       FG_TRY(upload(m, g_in, &L.g_in));
       FG_TRY(upload(m, g_pf, &L.g_pf));
-      FG_TRY(put(bqkv, L.g_in, fold_has_lo(rqkv.data(), &g_in, qkv_rows, H), &L.bqkv));
-      FG_TRY(put(bo, nullptr, false, &L.bo));
-      FG_TRY(put(bgu, L.g_pf, fold_has_lo(rgu.data(), &g_pf, 2 * F, H), &L.bgu));
-      FG_TRY(put(bd, nullptr, false, &L.bd));
+      bool done = false;
+      FG_TRY(put16(fold(rqkv, g_in, H), &L.bqkv, &done));
+      if (!done) FG_TRY(put(bqkv, L.g_in, fold_has_lo(rqkv.data(), &g_in, qkv_rows, H), &L.bqkv));
+      FG_TRY(put16(wo->data, &L.bo, &done));
+      if (!done) FG_TRY(put(bo, nullptr, false, &L.bo));
+      FG_TRY(put16(fold(rgu, g_pf, H), &L.bgu, &done));
+      if (!done) FG_TRY(put(bgu, L.g_pf, fold_has_lo(rgu.data(), &g_pf, 2 * F, H), &L.bgu));
+      FG_TRY(put16(wd->data, &L.bd, &done));
+      if (!done) FG_TRY(put(bd, nullptr, false, &L.bd));
       L.wqkv = DevMat{nullptr, nullptr, int(qkv_rows), int(H)};
       L.wo = DevMat{nullptr, nullptr, int(H), int(Hq * D)};
       L.wgu = DevMat{nullptr, nullptr, int(2 * F), int(H)};
@@ -754,24 +808,24 @@ int finalize(fg_model* m, int64_t max_tokens) {
       FG_TRY(upload_mat(m, wo->data, int(H), int(Hq * D), &L.wo));
       FG_TRY(upload_mat(m, fold(rgu, g_pf, H), int(2 * F), int(H), &L.wgu));
       FG_TRY(upload_mat(m, wd->data, int(H), int(F), &L.wd));
-      if (m->h16) {
-        // Bounds for the split-fp16 scales of the O and down inputs. With
-        // rs = 1/sqrt(mean(x²) + eps), ‖rs·x‖ < sqrt(H), so each projection
-        // output is below sqrt(H)·‖W'_row‖ (Cauchy-Schwarz): v, hence the
-        // attention output (convex combinations of v rows); gate and up,
-        // hence GELU(g)·u (|GELU(g)| <= max(|g|, 0.17)).
-        const double sh = std::sqrt(double(H));
-        double bv = 0, bgu = 0;
-        for (int64_t r = (Hq + Hkv) * D; r < qkv_rows; ++r)
-          bv = std::max(bv, sh * folded_row_norm(rqkv.data(), g_in, r, H));
-        for (int64_t k = 0; k < F; ++k) {
-          const double bg = sh * folded_row_norm(wg->data.data(), g_pf, k, H);
-          const double bu = sh * folded_row_norm(wu->data.data(), g_pf, k, H);
-          bgu = std::max(bgu, std::max(bg, 0.2) * bu);
-        }
-        L.att_ok = h16_exponent(bv * 1.01, &L.att_exp);
-        L.gu_ok = h16_exponent(bgu * 1.01, &L.gu_exp);
+    }
+    if (m->h16) {
+      // Bounds for the split-fp16 scales of the O and down inputs. With
+      // rs = 1/sqrt(mean(x²) + eps), ‖rs·x‖ < sqrt(H), so each projection
+      // output is below sqrt(H)·‖W'_row‖ (Cauchy-Schwarz): v, hence the
+      // attention output (convex combinations of v rows); gate and up,
+      // hence GELU(g)·u (|GELU(g)| <= max(|g|, 0.17)).
+      const double sh = std::sqrt(double(H));
+      double bv = 0, bgu = 0;
+      for (int64_t r = (Hq + Hkv) * D; r < qkv_rows; ++r)
+        bv = std::max(bv, sh * folded_row_norm(rqkv.data(), g_in, r, H));
+      for (int64_t k = 0; k < F; ++k) {
+        const double bg = sh * folded_row_norm(wg->data.data(), g_pf, k, H);
+        const double bu = sh * folded_row_norm(wu->data.data(), g_pf, k, H);
+        bgu = std::max(bgu, std::max(bg, 0.2) * bu);
       }
+      L.att_ok = h16_exponent(bv * 1.01, &L.att_exp);
+      L.gu_ok = h16_exponent(bgu * 1.01, &L.gu_exp);
     }
 
     FG_TRY(upload(m, plus_one(*qn), &L.qgain));
@@ -888,6 +942,19 @@ GemmArgs make_gemm(int M, const float* A, const float* A_lo, int64_t lda, const 
   return g;
 }
 
+// Split-fp16 operands for a split product whose A parts are made in shared
+// memory: B's exact fp16 form, and A's exponent from its row scales a_rs
+// (1/sqrt(mean(a²) + eps)) or, without them, the static aexp (ok: the bound
+// behind it is finite).
+void use_h16(const fg_model* m, GemmArgs& g, const DevMat& W, const float* a_rs, bool ok, int aexp) {
+  if (!m->h16 || !g.a_lo_smem || !W.h16 || !ok) return;
+  g.B16 = W.h16;
+  g.b_exp = W.h16_exp;
+  g.a_rs = a_rs;
+  g.a_exp_rs = a_rs ? 1 : 0;
+  g.a_exp = aexp;
+}
+
 struct Batch {
   int start, count, T;  // positions [start, start+count) of the order; padded length T ≥ 1
 };
@@ -999,6 +1066,7 @@ int forward_v2(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, i
     if (tc) FG_TRY(grow_attn_ws(m, attn_tc_workspace_bytes(B, T, T, Hq, Hkv, D), s));
     GemmArgs g = make_gemm(int(M), m->x, nullptr, H, Ly.wqkv, split);
     g.epi.rowscale = m->rowscale;
+    use_h16(m, g, Ly.wqkv, m->rowscale, true, 0);
     if (fused) {
       FG_TRY(attn_tc_carve(m->attn_ws, B, T, T, Hq, Hkv, &ops));
       g.epi.qkv_attn = 1;
@@ -1047,6 +1115,7 @@ int forward_v2(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, i
     g = make_gemm(int(M), m->att, nullptr, attw, Ly.wo, split);
     g.epi.out = m->tmp;
     g.epi.ldo = H;
+    use_h16(m, g, Ly.wo, nullptr, Ly.att_ok, Ly.att_exp);
     {
       PhaseScope ps(m, FG_PHASE_GEMM_O, s, gemm_flops(g));
       FG_TRY(gemm_tn(g, m->err, s));
@@ -1061,6 +1130,7 @@ int forward_v2(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, i
     g.epi.ldo = F;
     g.epi.rowscale = m->rowscale;
     g.epi.geglu = 1;
+    use_h16(m, g, Ly.wgu, m->rowscale, true, 0);
     {
       PhaseScope ps(m, FG_PHASE_GEMM_GATE_UP, s, gemm_flops(g));
       FG_TRY(gemm_tn(g, m->err, s));
@@ -1068,6 +1138,7 @@ int forward_v2(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, i
     g = make_gemm(int(M), m->gu, nullptr, F, Ly.wd, split);
     g.epi.out = m->tmp;
     g.epi.ldo = H;
+    use_h16(m, g, Ly.wd, nullptr, Ly.gu_ok, Ly.gu_exp);
     {
       PhaseScope ps(m, FG_PHASE_GEMM_DOWN, s, gemm_flops(g));
       FG_TRY(gemm_tn(g, m->err, s));
@@ -1084,6 +1155,7 @@ int forward_v2(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, i
     g.epi.act = FG_ACT_GELU;
     g.epi.mul = m->ple_buf + int64_t(l) * P;
     g.epi.ldm = int64_t(L) * P;
+    use_h16(m, g, Ly.wpg, m->rowscale, true, 0);  // rowscale: this x's RMS scale
     {
       PhaseScope ps(m, FG_PHASE_GEMM_GATE_UP, s, gemm_flops(g));
       FG_TRY(gemm_tn(g, m->err, s));
@@ -1143,16 +1215,6 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
   float* x_lo = lo_global ? m->x_lo : nullptr;
   float* att_lo = lo_global ? m->att_lo : nullptr;
   float* gu_lo = lo_global ? m->gu_lo : nullptr;
-  // split-fp16 operands (B's exact fp16 form; A's exponent from its row
-  // scale or a static bound) where the product is split and A's parts are
-  // made in shared memory
-  auto h16 = [&](GemmArgs& g, const DevMat& W, bool from_rs, bool ok, int aexp) {
-    if (!split || lo_global || !W.h16 || !ok) return;
-    g.B16 = W.h16;
-    g.b_exp = W.h16_exp;
-    g.a_exp_rs = from_rs ? 1 : 0;
-    g.a_exp = aexp;
-  };
 
   const double act_bytes = double(M) * H * 4.0;
   {
@@ -1174,22 +1236,33 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
     // stream, have finished reading it).
     DevMat Wqkv = L.wqkv, Wo = L.wo, Wgu = L.wgu, Wd = L.wd;
     if (L.resident_bf16) {
-      Wqkv = DevMat{m->ws_qkv.hi, L.bqkv.lo ? m->ws_qkv.lo : nullptr, L.wqkv.rows, L.wqkv.cols};
-      Wo = DevMat{m->ws_o.hi, nullptr, L.wo.rows, L.wo.cols};
-      Wgu = DevMat{m->ws_gu.hi, L.bgu.lo ? m->ws_gu.lo : nullptr, L.wgu.rows, L.wgu.cols};
-      Wd = DevMat{m->ws_d.hi, nullptr, L.wd.rows, L.wd.cols};
-      WidenJobs jobs{};
+      // A projection resident in its fp16 form is read as it is by the
+      // split-fp16 GEMM; the others are widened into the workspace.
+      const bool h16ok = split && m->h16 && !lo_global && gemm_h16_applies(int(M));
       const Bf16Mat* src[4] = {&L.bqkv, &L.bo, &L.bgu, &L.bd};
-      const DevMat* dst[4] = {&Wqkv, &Wo, &Wgu, &Wd};
+      DevMat* dst[4] = {&Wqkv, &Wo, &Wgu, &Wd};
+      const DevMat* ws[4] = {&m->ws_qkv, &m->ws_o, &m->ws_gu, &m->ws_d};
+      const bool a_ok[4] = {true, L.att_ok, true, L.gu_ok};
+      WidenJobs jobs{};
+      int nj = 0;
       double bytes = 0;
       for (int i = 0; i < 4; ++i) {
-        const int64_t n = int64_t(dst[i]->rows) * dst[i]->cols;
-        jobs.j[i] = WidenJob{src[i]->w, src[i]->gain, dst[i]->hi, dst[i]->lo, n / 4, dst[i]->cols};
-        bytes += double(n) * (2 + 4 + (dst[i]->lo ? 4 : 0)) + (src[i]->gain ? dst[i]->cols * 4.0 : 0.0);
+        const int rows = dst[i]->rows, cols = dst[i]->cols;
+        if (h16ok && src[i]->f16 && a_ok[i]) {
+          *dst[i] = DevMat{nullptr, nullptr, rows, cols, src[i]->w, src[i]->exp};
+          continue;
+        }
+        *dst[i] = DevMat{ws[i]->hi, src[i]->lo ? ws[i]->lo : nullptr, rows, cols};
+        const int64_t n = int64_t(rows) * cols;
+        jobs.j[nj++] = WidenJob{src[i]->w, src[i]->gain, dst[i]->hi, dst[i]->lo, n / 4, cols,
+                                src[i]->f16 ? 1 : 0, src[i]->exp};
+        bytes += double(n) * (2 + 4 + (dst[i]->lo ? 4 : 0)) + (src[i]->gain ? cols * 4.0 : 0.0);
       }
-      PhaseScope ps(m, FG_PHASE_WIDEN, s, bytes);
-      widen_fold_kernel<<<dim3(4 * 148, 4), 256, 0, s>>>(jobs);
-      FG_CUDA_TRY(cudaGetLastError());
+      if (nj > 0) {
+        PhaseScope ps(m, FG_PHASE_WIDEN, s, bytes);
+        widen_fold_kernel<<<dim3(4 * 148, nj), 256, 0, s>>>(jobs);
+        FG_CUDA_TRY(cudaGetLastError());
+      }
     }
     // attention arguments (embed.go:209, attention.go:130)
     AttnArgs a{};
@@ -1218,7 +1291,7 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
     // q|k|v = rowscale ⊙ (x · Wqkv'ᵀ)   (embed.go:193-197)
     GemmArgs g = make_gemm(int(M), m->x, x_lo, H, Wqkv, split);
     g.epi.rowscale = m->rowscale;
-    h16(g, Wqkv, true, true, 0);
+    use_h16(m, g, Wqkv, m->rowscale, true, 0);
     if (tc) {
       // + QK-norm and RoPE (embed.go:198-207) in the epilogue
       g.epi.qkv_attn = 1;
@@ -1264,7 +1337,7 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
     g = make_gemm(int(M), m->att, att_lo, attw, Wo, split);
     g.epi.out = m->tmp;
     g.epi.ldo = H;
-    h16(g, Wo, false, L.att_ok, L.att_exp);
+    use_h16(m, g, Wo, nullptr, L.att_ok, L.att_exp);
     {
       PhaseScope ps(m, FG_PHASE_GEMM_O, s, gemm_flops(g));
       FG_TRY(gemm_tn(g, m->err, s));
@@ -1283,7 +1356,7 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
     g.epi.ldo_lo = F;
     g.epi.rowscale = m->rowscale;
     g.epi.geglu = 1;
-    h16(g, Wgu, true, true, 0);
+    use_h16(m, g, Wgu, m->rowscale, true, 0);
     {
       PhaseScope ps(m, FG_PHASE_GEMM_GATE_UP, s, gemm_flops(g));
       FG_TRY(gemm_tn(g, m->err, s));
@@ -1292,7 +1365,7 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
     g = make_gemm(int(M), m->gu, gu_lo, F, Wd, split);
     g.epi.out = m->tmp;
     g.epi.ldo = H;
-    h16(g, Wd, false, L.gu_ok, L.gu_exp);
+    use_h16(m, g, Wd, nullptr, L.gu_ok, L.gu_exp);
     {
       PhaseScope ps(m, FG_PHASE_GEMM_DOWN, s, gemm_flops(g));
       FG_TRY(gemm_tn(g, m->err, s));

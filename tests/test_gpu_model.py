@@ -170,17 +170,21 @@ def test_embedding_table_bf16_residency(small, monkeypatch):
     assert not np.array_equal(got, base)
 
 
+@pytest.mark.parametrize("h16", ["0", "1"])
 @pytest.mark.parametrize("norm_std", [0.0, 0.1])
-def test_bf16_resident_projections_are_bitwise_identical(norm_std, monkeypatch):
+def test_bf16_resident_projections_are_bitwise_identical(norm_std, h16, monkeypatch):
     """gemma.WeightsBF16(): projections resident as bf16, widened, gain-folded
     and split per layer on the device, give the same embeddings bit for bit
-    as the fp32-resident weights, in split-TF32 and plain TF32, with zero
-    norm weights (folded weights bf16-exact, no low parts) and non-zero ones
-    (folded weights with low parts); the weights take fewer device bytes."""
+    as the fp32-resident weights, in split precision and plain TF32, with
+    zero norm weights (folded weights bf16-exact, no low parts) and non-zero
+    ones (folded weights with low parts); the weights take fewer device
+    bytes. With split-fp16 (FG_GEMM_H16 on) the projections that have an
+    exact fp16 form stay resident in it and are read by the GEMM as they
+    are (plain TF32 widens them); with it off, all are bf16 and widened."""
     from ai_b200 import _lib, gemma
     from ai_b200 import synthetic as S
 
-    monkeypatch.setenv("FG_GEMM_H16", "0")  # both on the split-TF32 GEMM
+    monkeypatch.setenv("FG_GEMM_H16", h16)
     cfg = S.small_config(layers=3, vocab=2048)
     w = S.make_weights(cfg, seed=31, norm_std=norm_std)
     ids = S.make_ids(4, 96, 6, cfg["vocab_size"])
