@@ -801,15 +801,12 @@ __global__ void __launch_bounds__(Cfg<BN, SA, SB, BK, CV>::kThreads, 1)
 //
 // H16 (split-fp16, with CV): the converters write A·2^e_r as two fp16 parts
 // (hi = a's top 11 significant bits, lo = fp16(a − hi): 22 significant
-// bits, as split-TF32 keeps) over the fp32 A tile they came from: rows
-// 8g..8g+7 fill the 1 KB 128-byte-swizzle atom g of the fp32 tile, and
-// their hi and lo rows become the two 512-byte 64-byte-swizzle atoms of the
-// same 1 KB (hi, then lo), so each warp overwrites only what it read itself
-// and the hi and lo operands are [128 × 32] fp16 tiles with 8-row atoms
-// 1024 bytes apart. B arrives as fp16 (B·2^b exactly: bf16-exact weights),
-// and each stage is 2 × 2 pair MMAs of kind::f16 (K = 16) instead of 2 × 4
-// of kind::tf32 (K = 8) — half the tensor-pipe time for the same products.
-// Stage: A (then A_hi/A_lo) | B, 24 KB, so 8 stages are in flight.
+// bits, as split-TF32 keeps) as two 64-byte-swizzled [128 × 32] tiles over
+// the fp32 A tile they came from (same 16 KB), B arrives as fp16 (B·2^b
+// exactly: bf16-exact weights), and each stage is 2 × 2 pair MMAs of
+// kind::f16 (K = 16) instead of 2 × 4 of kind::tf32 (K = 8) — half the
+// tensor-pipe time for the same products. Stage: A (then A_hi | A_lo) | B,
+// 24 KB, so 8 stages are in flight.
 template <bool CV, bool SA = false, bool SB = false, bool H16 = false>
 struct PairCfg {
   static_assert(!H16 || (CV && !SA && !SB), "split-fp16 takes A's parts from the converters");
@@ -818,6 +815,7 @@ struct PairCfg {
   static constexpr bool kLo = CV || SA;
   static constexpr uint32_t kABytes = 128 * BK * 4;  // this CTA's A rows
   static constexpr uint32_t kBBytes = 128 * BK * (H16 ? 2 : 4);  // this CTA's half of the B rows
+  static constexpr uint32_t kPartBytes = 128 * BK * 2;  // one fp16 part of A (H16), in A's place
   static constexpr uint32_t kStageBytes =
       H16 ? kABytes + kBBytes : kABytes * (kLo ? 2 : 1) + kBBytes * (SB ? 2 : 1);
   static constexpr uint32_t kBOffset = H16 ? kABytes : kABytes * (kLo ? 2 : 1);
@@ -960,15 +958,14 @@ __global__ void __launch_bounds__(320, 1)
           const uint32_t blo_addr = b_addr + C::kBBytes;
           if constexpr (H16) {
             // hi·B then lo·B, K = 16 fp16 (32 bytes of the 64-byte rows) per MMA
-            const uint32_t hi_addr = a_addr, lo_addr = a_addr + 512;
+            const uint32_t hi_addr = a_addr, lo_addr = a_addr + C::kPartBytes;
 #pragma unroll
             for (int k = 0; k < BK / 16; ++k)
-              mma_f16_pair(d_tmem, sw64_kmajor_desc_sbo(hi_addr + k * 32, 1024), kmajor_desc<64>(b_addr + k * 32),
-                           kIdesc, (kb | k) != 0 ? 1u : 0u);
+              mma_f16_pair(d_tmem, kmajor_desc<64>(hi_addr + k * 32), kmajor_desc<64>(b_addr + k * 32), kIdesc,
+                           (kb | k) != 0 ? 1u : 0u);
 #pragma unroll
             for (int k = 0; k < BK / 16; ++k)
-              mma_f16_pair(d_tmem, sw64_kmajor_desc_sbo(lo_addr + k * 32, 1024), kmajor_desc<64>(b_addr + k * 32),
-                           kIdesc, 1u);
+              mma_f16_pair(d_tmem, kmajor_desc<64>(lo_addr + k * 32), kmajor_desc<64>(b_addr + k * 32), kIdesc, 1u);
           } else {
 #pragma unroll
           for (int k = 0; k < BK / kUmmaK; ++k) {
@@ -1016,56 +1013,55 @@ __global__ void __launch_bounds__(320, 1)
     uint32_t phase = 0;
     if constexpr (H16) {
       // Row ct of the CTA's 128 A rows: the fp32 row (128-byte swizzled:
-      // 16-byte chunk c at c ^ (ct & 7)) is read whole; its hi and lo rows
-      // (64-byte swizzled: chunk j at j ^ ((ct >> 1) & 3)) go to the hi and
-      // lo atoms of its 8-row group. The next stage's rows are read before
-      // this stage's parts are written, so the shared-memory latency of one
-      // overlaps the other. Exits are warp-uniform (__all_sync).
-      const int rr = ct & 7;
-      const uint32_t src_off = uint32_t(ct) * 128, hi_off = uint32_t(ct >> 3) * 1024 + uint32_t(rr) * 64;
-      auto load_row = [&](int st, float4 (&v)[8]) {
-        const float4* src = reinterpret_cast<const float4*>(smem + size_t(st) * C::kStageBytes + src_off);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) v[c] = src[c ^ rr];
-      };
+      // 16-byte chunk c at c ^ (ct & 7)) is read whole, all 128 threads
+      // meet, then its fp16 hi and lo rows (64-byte swizzled: chunk j at
+      // j ^ ((ct >> 1) & 3)) go over the tile. Every exit is decided
+      // together (the AND of the named barrier), so no thread is left
+      // waiting at it.
       for (int tile = pair; tile < ntiles; tile += npairs) {
+        bool ok = true;
         const float sc = pow2f(a_row_exp(p, (tile / p.ntn) * 256 + int(rank) * 128 + ct));
-        float4 v[8];
-        bool ok = __all_sync(0xffffffffu, mbar_wait(full_bar(stage), phase, abort_flag, p.err, kDevTimeoutFull));
-        if (ok) load_row(stage, v);
-        for (int kb = 0; kb < p.nk && ok; ++kb) {
-          uint32_t h[16], l[16];
+        for (int kb = 0; kb < p.nk; ++kb) {
+          const bool got = mbar_wait(full_bar(stage), phase, abort_flag, p.err, kDevTimeoutFull);
+          uint8_t* base = smem + size_t(stage) * C::kStageBytes;
+          float4 v[8];
+          if (got) {
+            const float4* src = reinterpret_cast<const float4*>(base) + ct * 8;
 #pragma unroll
-          for (int q = 0; q < 16; ++q) {
-            const float4 w = v[q >> 1];
-            const float a0 = ((q & 1) ? w.z : w.x) * sc, a1 = ((q & 1) ? w.w : w.y) * sc;
+            for (int c = 0; c < 8; ++c) v[c] = src[c ^ (ct & 7)];
+          }
+          if (!named_bar_and(1, 128, got)) {
+            ok = false;
+            break;
+          }
+          uint4* dhi = reinterpret_cast<uint4*>(base) + ct * 4;
+          uint4* dlo = reinterpret_cast<uint4*>(base + C::kPartBytes) + ct * 4;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float4 v0 = v[2 * j], v1 = v[2 * j + 1];
+            const float a[8] = {v0.x * sc, v0.y * sc, v0.z * sc, v0.w * sc,
+                                v1.x * sc, v1.y * sc, v1.z * sc, v1.w * sc};
             // hi: a's top 11 significant bits (exact in fp16 above 2^-14,
             // rounded on the subnormal grid below: 2^-25 at most, 2^-39 of
             // the row bound); lo = a − hi (exact), rounded to fp16
-            const float h0 = tf32_hi(a0), h1 = tf32_hi(a1);
-            h[q] = pack_f16x2(h0, h1);
-            l[q] = pack_f16x2(a0 - h0, a1 - h1);
-          }
-          const int ns = stage + 1 == S ? 0 : stage + 1;
-          const uint32_t nph = ns == 0 ? phase ^ 1u : phase;
-          if (kb + 1 < p.nk) {
-            ok = __all_sync(0xffffffffu, mbar_wait(full_bar(ns), nph, abort_flag, p.err, kDevTimeoutFull));
-            if (ok) load_row(ns, v);
-          }
-          __syncwarp();  // every lane's reads of this stage before any lane's writes
-          uint8_t* dst = smem + size_t(stage) * C::kStageBytes + hi_off;
+            uint32_t h[4], l[4];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int pj = (j ^ ((rr >> 1) & 3)) * 16;
-            *reinterpret_cast<uint4*>(dst + pj) = make_uint4(h[4 * j], h[4 * j + 1], h[4 * j + 2], h[4 * j + 3]);
-            *reinterpret_cast<uint4*>(dst + 512 + pj) =
-                make_uint4(l[4 * j], l[4 * j + 1], l[4 * j + 2], l[4 * j + 3]);
+            for (int q = 0; q < 4; ++q) {
+              const float h0 = tf32_hi(a[2 * q]), h1 = tf32_hi(a[2 * q + 1]);
+              h[q] = pack_f16x2(h0, h1);
+              l[q] = pack_f16x2(a[2 * q] - h0, a[2 * q + 1] - h1);
+            }
+            const int pj = j ^ ((ct >> 1) & 3);
+            dhi[pj] = make_uint4(h[0], h[1], h[2], h[3]);
+            dlo[pj] = make_uint4(l[0], l[1], l[2], l[3]);
           }
           fence_proxy_async_smem();  // generic-proxy writes → visible to the tensor core
           __syncwarp();
           if (lane == 0) mbar_arrive_remote(mapa_shared(ready_bar(stage), 0));
-          stage = ns;
-          phase = nph;
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1;
+          }
         }
         if (!ok) break;
       }

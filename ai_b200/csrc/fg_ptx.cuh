@@ -299,6 +299,22 @@ __device__ __forceinline__ uint32_t pack_f16x2(float lo_elem, float hi_elem) {
   asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi_elem), "f"(lo_elem));
   return r;
 }
+// Named barrier over `nthreads` threads (whole warps) with an AND of `v`:
+// every participant gets true only if all passed true. Shared-memory
+// accesses before it are ordered before those after it for all of them.
+__device__ __forceinline__ bool named_bar_and(int id, int nthreads, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 q, %1, 0;\n\t"
+      "bar.red.and.pred p, %2, %3, q;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(r)
+      : "r"(v ? 1 : 0), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
+
 // 2^k as a float for k in [-126, 127] (exact).
 __host__ __device__ __forceinline__ float pow2f(int k) {
 #ifdef __CUDA_ARCH__
@@ -414,18 +430,6 @@ __device__ __forceinline__ uint64_t kmajor_desc(uint32_t saddr) {
   d |= static_cast<uint64_t>((8u * SW) >> 4) << 32;
   d |= static_cast<uint64_t>(1u) << 46;
   d |= static_cast<uint64_t>(SW == 128 ? 2u : 4u) << 61;
-  return d;
-}
-
-// A 64-byte-swizzled K-major operand whose 8-row atoms (512 bytes each,
-// 512-byte aligned) lie `sbo` bytes apart instead of back to back.
-__device__ __forceinline__ uint64_t sw64_kmajor_desc_sbo(uint32_t saddr, uint32_t sbo) {
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
-  d |= static_cast<uint64_t>(1u) << 16;
-  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
-  d |= static_cast<uint64_t>(1u) << 46;
-  d |= static_cast<uint64_t>(4u) << 61;  // SWIZZLE_64B
   return d;
 }
 
