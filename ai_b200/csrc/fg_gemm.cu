@@ -826,6 +826,7 @@ struct PairCfg {
   static constexpr uint32_t kTmemCols = 512;  // two 256-column accumulators
   static constexpr size_t kSmemBytes = 1024 + size_t(kStages) * kStageBytes + kEpiStageBytes + 256;
   static_assert(kStages >= 3, "stage ring too shallow");
+  static_assert(!H16 || kStages % 2 == 0, "the two converter groups take alternate stages");
 };
 
 template <bool CV, bool SA = false, bool SB = false, bool H16 = false>
@@ -864,7 +865,7 @@ __global__ void __launch_bounds__(320, 1)
     for (int s = 0; s < S; ++s) {
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
-      mbar_init(ready_bar(s), 8);  // 4 converter warps in each CTA
+      mbar_init(ready_bar(s), H16 ? 4 : 8);  // converter warps per stage in each CTA: 2 (H16) or 4
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(accf_bar(a), 1);
@@ -1012,52 +1013,67 @@ __global__ void __launch_bounds__(320, 1)
     int stage = 0;
     uint32_t phase = 0;
     if constexpr (H16) {
-      // Row ct of the CTA's 128 A rows: the fp32 row (128-byte swizzled:
-      // 16-byte chunk c at c ^ (ct & 7)) is read whole, all 128 threads
-      // meet, then its fp16 hi and lo rows (64-byte swizzled: chunk j at
-      // j ^ ((ct >> 1) & 3)) go over the tile. Every exit is decided
-      // together (the AND of the named barrier), so no thread is left
-      // waiting at it.
+      // Two groups of two warps take alternate stages (even / odd), so two
+      // stages are converted at once. In a group, thread gt converts rows
+      // gt and gt + 64 of the CTA's 128 A rows: each fp32 row (128-byte
+      // swizzled: 16-byte chunk c at c ^ (row & 7)) is read whole, the
+      // group's 64 threads meet, then the fp16 hi and lo rows (64-byte
+      // swizzled: chunk j at j ^ ((row >> 1) & 3)) go over the tile. Every
+      // exit is decided together (the AND of the group's named barrier), so
+      // no thread is left waiting at it.
+      const int grp = (warp - 6) >> 1;
+      const int gt = ct - grp * 64;
       for (int tile = pair; tile < ntiles; tile += npairs) {
         bool ok = true;
-        const float sc = pow2f(a_row_exp(p, (tile / p.ntn) * 256 + int(rank) * 128 + ct));
+        const int row0 = (tile / p.ntn) * 256 + int(rank) * 128;
+        const float sc[2] = {pow2f(a_row_exp(p, row0 + gt)), pow2f(a_row_exp(p, row0 + gt + 64))};
         for (int kb = 0; kb < p.nk; ++kb) {
-          const bool got = mbar_wait(full_bar(stage), phase, abort_flag, p.err, kDevTimeoutFull);
-          uint8_t* base = smem + size_t(stage) * C::kStageBytes;
-          float4 v[8];
-          if (got) {
-            const float4* src = reinterpret_cast<const float4*>(base) + ct * 8;
+          if ((stage & 1) == grp) {
+            const bool got = mbar_wait(full_bar(stage), phase, abort_flag, p.err, kDevTimeoutFull);
+            uint8_t* base = smem + size_t(stage) * C::kStageBytes;
+            float4 v[2][8];
+            if (got) {
 #pragma unroll
-            for (int c = 0; c < 8; ++c) v[c] = src[c ^ (ct & 7)];
-          }
-          if (!named_bar_and(1, 128, got)) {
-            ok = false;
-            break;
-          }
-          uint4* dhi = reinterpret_cast<uint4*>(base) + ct * 4;
-          uint4* dlo = reinterpret_cast<uint4*>(base + C::kPartBytes) + ct * 4;
+              for (int h = 0; h < 2; ++h) {
+                const int r = gt + 64 * h;
+                const float4* src = reinterpret_cast<const float4*>(base) + r * 8;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float4 v0 = v[2 * j], v1 = v[2 * j + 1];
-            const float a[8] = {v0.x * sc, v0.y * sc, v0.z * sc, v0.w * sc,
-                                v1.x * sc, v1.y * sc, v1.z * sc, v1.w * sc};
-            // hi: a's top 11 significant bits (exact in fp16 above 2^-14,
-            // rounded on the subnormal grid below: 2^-25 at most, 2^-39 of
-            // the row bound); lo = a − hi (exact), rounded to fp16
-            uint32_t h[4], l[4];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const float h0 = tf32_hi(a[2 * q]), h1 = tf32_hi(a[2 * q + 1]);
-              h[q] = pack_f16x2(h0, h1);
-              l[q] = pack_f16x2(a[2 * q] - h0, a[2 * q + 1] - h1);
+                for (int c = 0; c < 8; ++c) v[h][c] = src[c ^ (r & 7)];
+              }
             }
-            const int pj = j ^ ((ct >> 1) & 3);
-            dhi[pj] = make_uint4(h[0], h[1], h[2], h[3]);
-            dlo[pj] = make_uint4(l[0], l[1], l[2], l[3]);
+            if (!named_bar_and(1 + grp, 64, got)) {
+              ok = false;
+              break;
+            }
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int r = gt + 64 * h;
+              uint4* dhi = reinterpret_cast<uint4*>(base) + r * 4;
+              uint4* dlo = reinterpret_cast<uint4*>(base + C::kPartBytes) + r * 4;
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float4 v0 = v[h][2 * j], v1 = v[h][2 * j + 1];
+                const float a[8] = {v0.x * sc[h], v0.y * sc[h], v0.z * sc[h], v0.w * sc[h],
+                                    v1.x * sc[h], v1.y * sc[h], v1.z * sc[h], v1.w * sc[h]};
+                // hi: a's top 11 significant bits (exact in fp16 above 2^-14,
+                // rounded on the subnormal grid below: 2^-25 at most, 2^-39
+                // of the row bound); lo = a − hi (exact), rounded to fp16
+                uint32_t hw[4], lw[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  const float h0 = tf32_hi(a[2 * q]), h1 = tf32_hi(a[2 * q + 1]);
+                  hw[q] = pack_f16x2(h0, h1);
+                  lw[q] = pack_f16x2(a[2 * q] - h0, a[2 * q + 1] - h1);
+                }
+                const int pj = j ^ ((r >> 1) & 3);
+                dhi[pj] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                dlo[pj] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+              }
+            }
+            fence_proxy_async_smem();  // generic-proxy writes → visible to the tensor core
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(mapa_shared(ready_bar(stage), 0));
           }
-          fence_proxy_async_smem();  // generic-proxy writes → visible to the tensor core
-          __syncwarp();
-          if (lane == 0) mbar_arrive_remote(mapa_shared(ready_bar(stage), 0));
           if (++stage == S) {
             stage = 0;
             phase ^= 1;
