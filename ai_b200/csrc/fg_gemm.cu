@@ -52,6 +52,7 @@ struct KParams {
   int a_exp, a_exp_rs, b_exp;
   float a_norm_k;      // sqrt(K): max|a_r| <= sqrt(K) / a_rs[r]
   const float* a_rs;   // A's row scales 1/sqrt(mean(a²) + eps) (a_exp_rs)
+  const float* a_gain;  // per-column gain on A (split-fp16 with an unfolded B), or null
 };
 
 // Exponent e_r of A row r in the split-fp16 product: |a_r|·2^e_r < 2^14, so
@@ -1045,6 +1046,14 @@ __global__ void __launch_bounds__(320, 1)
               ok = false;
               break;
             }
+            // the columns' gains (a fold moved to A's side), times 2^e_r below:
+            // a·(g·2^e) = fl(a·g)·2^e exactly
+            const bool gained = p.a_gain != nullptr;
+            float4 gq[8];
+            if (gained) {
+#pragma unroll
+              for (int c = 0; c < 8; ++c) gq[c] = __ldg(reinterpret_cast<const float4*>(p.a_gain + kb * BK) + c);
+            }
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
               const int r = gt + 64 * h;
@@ -1053,8 +1062,16 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
                 const float4 v0 = v[h][2 * j], v1 = v[h][2 * j + 1];
-                const float a[8] = {v0.x * sc[h], v0.y * sc[h], v0.z * sc[h], v0.w * sc[h],
-                                    v1.x * sc[h], v1.y * sc[h], v1.z * sc[h], v1.w * sc[h]};
+                const float s = sc[h];
+                float a[8];
+                if (gained) {
+                  const float4 g0 = gq[2 * j], g1 = gq[2 * j + 1];
+                  a[0] = v0.x * (g0.x * s); a[1] = v0.y * (g0.y * s); a[2] = v0.z * (g0.z * s); a[3] = v0.w * (g0.w * s);
+                  a[4] = v1.x * (g1.x * s); a[5] = v1.y * (g1.y * s); a[6] = v1.z * (g1.z * s); a[7] = v1.w * (g1.w * s);
+                } else {
+                  a[0] = v0.x * s; a[1] = v0.y * s; a[2] = v0.z * s; a[3] = v0.w * s;
+                  a[4] = v1.x * s; a[5] = v1.y * s; a[6] = v1.z * s; a[7] = v1.w * s;
+                }
                 // hi: a's top 11 significant bits (exact in fp16 above 2^-14,
                 // rounded on the subnormal grid below: 2^-25 at most, 2^-39
                 // of the row bound); lo = a − hi (exact), rounded to fp16
@@ -1336,6 +1353,7 @@ int dispatch(const GemmArgs& g, KParams& kp, int* dev_err, cudaStream_t stream) 
   kp.nk = (g.K + 31) / 32;
   // split-fp16 where B has an exact fp16 form and A's parts are made here
   const bool h16 = g.B16 && g.a_lo_smem && !g.A_lo && (g.ldb % 8) == 0 && (!g.a_exp_rs || kp.a_rs) &&
+                   (!g.a_gain || (g.K % 32 == 0 && (reinterpret_cast<uintptr_t>(g.a_gain) & 15) == 0)) &&
                    use_pair(g) && (g.epi.geglu || g.Nb > 128);
   if (!h16 && !g.B) return set_error(FG_EINVAL, "gemm: B has only an fp16 form and the split-fp16 kernel does not apply");
   if (g.epi.geglu) {
@@ -1392,8 +1410,9 @@ int gemm_tn(const GemmArgs& g, int* dev_err, cudaStream_t stream) {
   kp.a_exp = g.a_exp;
   kp.a_exp_rs = g.a_exp_rs;
   kp.b_exp = g.b_exp;
-  kp.a_norm_k = sqrtf(float(g.K));
+  kp.a_norm_k = sqrtf(float(g.K)) * (g.a_gain ? g.a_gain_max : 1.f);
   kp.a_rs = g.a_rs ? g.a_rs : g.epi.rowscale;
+  kp.a_gain = g.a_gain;
   return dispatch(g, kp, dev_err, stream);
 }
 

@@ -116,6 +116,11 @@ struct GemmArgs {
   int a_exp = 0;
   int a_exp_rs = 0;
   const float* a_rs = nullptr;  // row scales behind a_exp_rs (null: epi.rowscale)
+  // Split-fp16 with the pre-norm gain on A: B16 holds the unfolded weight and
+  // the converters multiply A's column k by a_gain[k] (|a_gain| <= a_gain_max;
+  // K a multiple of 32), the product of a fold W·diag(g) moved to A's side.
+  const float* a_gain = nullptr;
+  float a_gain_max = 1.f;
   GemmEpilogue epi;
 };
 

@@ -88,6 +88,10 @@ struct DevMat {
   // split-fp16 GEMM's B operand), else null
   uint16_t* h16 = nullptr;
   int h16_exp = 0;
+  // when not null: h16 is the weight before its fold with this column gain
+  // (|gain| <= h16_gmax), which the split-fp16 GEMM applies to A instead
+  const float* h16_gain = nullptr;
+  float h16_gmax = 1.f;
 };
 
 // A projection resident as bf16 (FG_WEIGHTS_BF16): [rows, cols] bits and
@@ -100,6 +104,9 @@ struct Bf16Mat {
   // (exact), the split-fp16 GEMM's B operand as it is (gain null, no lo)
   bool f16 = false;
   int exp = 0;
+  // f16 with a gain: w is the weight before the fold (the GEMM applies the
+  // gain to A; widening folds it), |gain| <= gmax
+  float gmax = 1.f;
 };
 
 struct Layer {
@@ -424,6 +431,21 @@ int upload_mat(fg_model* m, const std::vector<float>& h, int rows, int cols, Dev
   return FG_OK;
 }
 
+// The split-fp16 form of a folded projection whose folded values have no
+// exact fp16 form: the unfolded weight (bf16 values are), with the fold's
+// column gain left for the GEMM to apply to A.
+int upload_h16_unfolded(fg_model* m, const std::vector<float>& raw, const float* gain_dev,
+                        const std::vector<float>& gain, DevMat* out) {
+  if (!m->h16 || out->h16) return FG_OK;
+  FG_TRY(upload_h16(m, raw, out));
+  if (!out->h16) return FG_OK;
+  double gm = 0;
+  for (float v : gain) gm = std::max(gm, double(std::fabs(v)));
+  out->h16_gain = gain_dev;
+  out->h16_gmax = float(gm);
+  return FG_OK;
+}
+
 // sqrt(Σ_c (w[r][c]·g[c])²) of row r of a [rows, cols] matrix folded with
 // the column gain g (fp32 products, as the fold stores them).
 double folded_row_norm(const float* w, const std::vector<float>& g, int64_t r, int64_t cols) {
@@ -631,6 +653,12 @@ int finalize_v2(fg_model* m, int64_t max_tokens) {
     FG_TRY(upload_mat(m, fold(rqkv, g_in, H), int((Hq + 2 * Hkv) * D), int(H), &Ly.wqkv));
     FG_TRY(upload_mat(m, wo->data, int(H), int(Hq * D), &Ly.wo));
     FG_TRY(upload_mat(m, fold(rgu, g_pf, H), int(2 * F), int(H), &Ly.wgu));
+    if (m->h16) {
+      FG_TRY(upload(m, g_in, &Ly.g_in));
+      FG_TRY(upload(m, g_pf, &Ly.g_pf));
+      FG_TRY(upload_h16_unfolded(m, rqkv, Ly.g_in, g_in, &Ly.wqkv));
+      FG_TRY(upload_h16_unfolded(m, rgu, Ly.g_pf, g_pf, &Ly.wgu));
+    }
     FG_TRY(upload_mat(m, wd->data, int(H), int(F), &Ly.wd));
     FG_TRY(upload_mat(m, pg->data, int(P), int(H), &Ly.wpg));
     FG_TRY(upload_mat(m, pp->data, int(H), int(P), &Ly.wpp));
@@ -767,6 +795,8 @@ int finalize(fg_model* m, int64_t max_tokens) {
     L.resident_bf16 = m->weight_mode == FG_WEIGHTS_BF16 && pack_bf16(rqkv.data(), rqkv.size(), bqkv) &&
                       pack_bf16(wo->data.data(), wo->data.size(), bo) &&
                       pack_bf16(rgu.data(), rgu.size(), bgu) && pack_bf16(wd->data.data(), wd->data.size(), bd);
+    FG_TRY(upload(m, g_in, &L.g_in));
+    FG_TRY(upload(m, g_pf, &L.g_pf));
     if (L.resident_bf16) {
       auto put = [&](const std::vector<uint16_t>& b, const float* gain, bool lo, Bf16Mat* out) -> int {
         FG_TRY(dev_alloc_t(m, &out->w, b.size()));
@@ -788,15 +818,33 @@ int finalize(fg_model* m, int64_t max_tokens) {
         out->exp = e;
         return FG_OK;
       };
-      FG_TRY(upload(m, g_in, &L.g_in));
-      FG_TRY(upload(m, g_pf, &L.g_pf));
       bool done = false;
+      // else the unfolded weight's fp16 form with the gain (the GEMM puts
+      // it on A; widening folds it as the host fold does)
+      auto put16g = [&](const std::vector<float>& raw, const float* gain_dev, const std::vector<float>& gain,
+                        bool lo, Bf16Mat* out, bool* done) -> int {
+        std::vector<uint16_t> b;
+        int e = 0;
+        *done = m->h16 && f16_form(raw, b, &e);
+        if (!*done) return FG_OK;
+        FG_TRY(put(b, gain_dev, lo, out));
+        out->f16 = true;
+        out->exp = e;
+        double gm = 0;
+        for (float v : gain) gm = std::max(gm, double(std::fabs(v)));
+        out->gmax = float(gm);
+        return FG_OK;
+      };
       FG_TRY(put16(fold(rqkv, g_in, H), &L.bqkv, &done));
-      if (!done) FG_TRY(put(bqkv, L.g_in, fold_has_lo(rqkv.data(), &g_in, qkv_rows, H), &L.bqkv));
+      const bool lo_qkv = fold_has_lo(rqkv.data(), &g_in, qkv_rows, H);
+      if (!done) FG_TRY(put16g(rqkv, L.g_in, g_in, lo_qkv, &L.bqkv, &done));
+      if (!done) FG_TRY(put(bqkv, L.g_in, lo_qkv, &L.bqkv));
       FG_TRY(put16(wo->data, &L.bo, &done));
       if (!done) FG_TRY(put(bo, nullptr, false, &L.bo));
       FG_TRY(put16(fold(rgu, g_pf, H), &L.bgu, &done));
-      if (!done) FG_TRY(put(bgu, L.g_pf, fold_has_lo(rgu.data(), &g_pf, 2 * F, H), &L.bgu));
+      const bool lo_gu = fold_has_lo(rgu.data(), &g_pf, 2 * F, H);
+      if (!done) FG_TRY(put16g(rgu, L.g_pf, g_pf, lo_gu, &L.bgu, &done));
+      if (!done) FG_TRY(put(bgu, L.g_pf, lo_gu, &L.bgu));
       FG_TRY(put16(wd->data, &L.bd, &done));
       if (!done) FG_TRY(put(bd, nullptr, false, &L.bd));
       L.wqkv = DevMat{nullptr, nullptr, int(qkv_rows), int(H)};
@@ -808,6 +856,8 @@ int finalize(fg_model* m, int64_t max_tokens) {
       FG_TRY(upload_mat(m, wo->data, int(H), int(Hq * D), &L.wo));
       FG_TRY(upload_mat(m, fold(rgu, g_pf, H), int(2 * F), int(H), &L.wgu));
       FG_TRY(upload_mat(m, wd->data, int(H), int(F), &L.wd));
+      FG_TRY(upload_h16_unfolded(m, rqkv, L.g_in, g_in, &L.wqkv));
+      FG_TRY(upload_h16_unfolded(m, rgu, L.g_pf, g_pf, &L.wgu));
     }
     if (m->h16) {
       // Bounds for the split-fp16 scales of the O and down inputs. With
@@ -953,6 +1003,8 @@ void use_h16(const fg_model* m, GemmArgs& g, const DevMat& W, const float* a_rs,
   g.a_rs = a_rs;
   g.a_exp_rs = a_rs ? 1 : 0;
   g.a_exp = aexp;
+  g.a_gain = W.h16_gain;
+  g.a_gain_max = W.h16_gmax;
 }
 
 struct Batch {
@@ -1249,7 +1301,7 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
       for (int i = 0; i < 4; ++i) {
         const int rows = dst[i]->rows, cols = dst[i]->cols;
         if (h16ok && src[i]->f16 && a_ok[i]) {
-          *dst[i] = DevMat{nullptr, nullptr, rows, cols, src[i]->w, src[i]->exp};
+          *dst[i] = DevMat{nullptr, nullptr, rows, cols, src[i]->w, src[i]->exp, src[i]->gain, src[i]->gmax};
           continue;
         }
         *dst[i] = DevMat{ws[i]->hi, src[i]->lo ? ws[i]->lo : nullptr, rows, cols};
