@@ -278,10 +278,9 @@ def run_ours(args, rank, local_rank, world, cfg):
     tf32_peak = pk["bf16_sustained"] / 2.0
     achieved = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else None
     passes = 1 if prec == gemma.PREC_TF32 else 2
-    # split-fp16 on all four encoder GEMMs: bf16-exact weights (zero norm
-    # gains, so the folds keep them exact), fp32 residency, not switched off
-    h16 = (prec == gemma.PREC_SPLIT_TF32 and args.weights == "f32" and args.norm_std == 0.0
-           and os.environ.get("FG_GEMM_H16", "1") != "0")
+    # split-fp16 on all four encoder GEMMs (bf16 weights; non-zero norm
+    # gains go on A), unless switched off
+    h16 = prec == gemma.PREC_SPLIT_TF32 and os.environ.get("FG_GEMM_H16", "1") != "0"
     traffic = None
     tp = ROOT / "profiles" / "gemm_traffic.json"
     if tp.exists():
