@@ -148,6 +148,16 @@ __device__ __forceinline__ float gelu_tanh(float x) {
   return t * 0.5f;
 }
 
+// The same tanh-GELU for the gated FFN epilogue, in the form
+// 0.5·x·(1 + tanh(u)) = x·σ(2u) = x / (1 + 2^(−2u·log2 e)) with the hardware
+// exp2 and reciprocal: ~10 instructions instead of ~40 (the rational tanh and
+// an IEEE division), about 1e-7 relative from the form above. +∞ and −∞
+// arguments of the exponential give x and −0.
+__device__ __forceinline__ float gelu_sigmoid(float x) {
+  const float u = x * fmaf(0.7978845608028654f * 0.044715f, x * x, 0.7978845608028654f);
+  return x * rcp_approx(1.f + ex2_approx(u * -2.8853900817779268f));
+}
+
 __device__ __forceinline__ float apply_act(float v, int act) {
   if (act == FG_ACT_RELU) return fmaxf(v, 0.f);
   if (act == FG_ACT_GELU) return gelu_tanh(v);
@@ -482,7 +492,7 @@ __device__ __forceinline__ void epilogue_tile(const KParams& p, const OutMaps& o
       for (int j = 0; j < 32; ++j) {
         const float g = __uint_as_float(rg[j]) * rs;
         const float u = __uint_as_float(ru[j]) * rs;
-        v[j] = gelu_tanh(g) * u;
+        v[j] = gelu_sigmoid(g) * u;
       }
       if (tma) store_box_tma(&om.m[0], es, v, col0, row0, ncols > 0 && rows > 0);
       else if (row_ok && ncols > 0) store_row32(out + int64_t(row) * ldo + col0, v, ncols, vec_out);
