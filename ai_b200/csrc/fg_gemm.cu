@@ -290,8 +290,9 @@ __device__ __forceinline__ void qkv_attn_epilogue(const GemmEpilogue& e, const O
     __nv_bfloat16* const lo = static_cast<__nv_bfloat16*>(is_q ? e.q_lo : e.k_lo);
     const int width = (is_q ? Hq : Hkv) * D;
     const int head = is_q ? tn : tn - Hq;
-    // pass 1: Σ y² over the head, columns in order
-    float ss = 0.f;
+    // pass 1: Σ y² over the head in four interleaved partial sums (columns
+    // ≡ q mod 4 ... in order), so the dependent chain is 64 adds, not 256
+    float ss4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
     for (int h0 = 0; h0 < D; h0 += 128) {
       uint32_t r[4][32];
@@ -301,9 +302,10 @@ __device__ __forceinline__ void qkv_attn_epilogue(const GemmEpilogue& e, const O
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const float y = __fmul_rn(__uint_as_float(r[q][j]), rs);
-          ss = __fadd_rn(ss, __fmul_rn(y, y));
+          ss4[j & 3] = __fmaf_rn(y, y, ss4[j & 3]);
         }
     }
+    const float ss = (ss4[0] + ss4[1]) + (ss4[2] + ss4[3]);
     const float m = __fadd_rn(__fdiv_rn(ss, float(D)), eps);
     const float inv = float(1.0 / sqrt(double(m)));
     const int lane = threadIdx.x & 31;
