@@ -1085,8 +1085,9 @@ __global__ void __launch_bounds__(320, 1)
                   a[4] = v1.x * s; a[5] = v1.y * s; a[6] = v1.z * s; a[7] = v1.w * s;
                 }
                 // hi: a's top 11 significant bits (exact in fp16 above 2^-14,
-                // rounded on the subnormal grid below: 2^-25 at most, 2^-39
-                // of the row bound); lo = a − hi (exact), rounded to fp16
+                // rounded on the subnormal grid below, as lo is: 2^-24 at
+                // most for the two, 2^-38 of the row bound); lo = a − hi
+                // (exact), rounded to fp16
                 uint32_t hw[4], lw[4];
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
