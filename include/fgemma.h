@@ -42,7 +42,11 @@ extern "C" {
 #define FG_ENODEV (-6)   /* no usable sm_100 device */
 
 /* ---- arithmetic modes -------------------------------------------------- */
-#define FG_PREC_SPLIT_TF32 0 /* 3-pass split TF32: fp32-level products (default) */
+/* FG_PREC_SPLIT_TF32: fp32-level products (default). The model's encoder
+ * GEMMs run it as split-fp16 (A as two fp16 parts under a power-of-two row
+ * scale, bf16 weights as exact fp16, 2 fp16 passes) on SM pairs; other
+ * products as split TF32 (up to 3 TF32 passes). */
+#define FG_PREC_SPLIT_TF32 0
 #define FG_PREC_TF32 1       /* one TF32 pass per product */
 
 /* ---- activations: blas.Activation, internal/blas/gemm.go:270-274 -------- */
@@ -149,13 +153,15 @@ int fg_model_finalize(fg_model* m, int64_t max_batch_tokens);
  * fg_model_finalize (no counterpart in the reference, whose TODO.md lists
  * "bf16 weight storage expanded during GEMM packing (halves the 1.2 GB)";
  * its bf16 widening is safetensors/convert.go:31-38).
- * FG_WEIGHTS_F32 (default): the gain-folded fp32 projections and their
- * split-TF32 low parts stay resident. FG_WEIGHTS_BF16: every bf16-exact
- * projection stays resident as bf16 beside its fp32 pre-norm gain, and each
- * layer's are widened, folded and split into one layer's fp32 workspace on
- * the stream just before that layer's GEMMs — the same operands bit for
- * bit, so the embeddings are identical. A layer with a projection that is
- * not bf16-exact stays fp32. Returns FG_ESTATE after finalize. */
+ * FG_WEIGHTS_F32 (default): the gain-folded fp32 projections, their
+ * split-TF32 low parts and their fp16 forms for split-fp16 stay resident.
+ * FG_WEIGHTS_BF16: every bf16-exact projection stays resident in 2 bytes per
+ * value — its fp16 form, read by the split-fp16 GEMM as it is, or bf16 —
+ * beside its fp32 pre-norm gain; what a product needs in fp32 is widened,
+ * folded and split into one layer's fp32 workspace on the stream just
+ * before that layer's GEMMs — the same operands bit for bit, so the
+ * embeddings are identical. A layer with a projection that is not
+ * bf16-exact stays fp32. Returns FG_ESTATE after finalize. */
 #define FG_WEIGHTS_F32 0
 #define FG_WEIGHTS_BF16 1
 int fg_model_set_weight_residency(fg_model* m, int mode);
