@@ -1423,7 +1423,8 @@ int gemm_tn(const GemmArgs& g, int* dev_err, cudaStream_t stream) {
   kp.a_exp = g.a_exp;
   kp.a_exp_rs = g.a_exp_rs;
   kp.b_exp = g.b_exp;
-  kp.a_norm_k = sqrtf(float(g.K)) * (g.a_gain ? g.a_gain_max : 1.f);
+  // all-zero gains make A zero: any exponent serves, keep the bound positive
+  kp.a_norm_k = sqrtf(float(g.K)) * (g.a_gain && g.a_gain_max > 0.f ? g.a_gain_max : 1.f);
   kp.a_rs = g.a_rs ? g.a_rs : g.epi.rowscale;
   kp.a_gain = g.a_gain;
   return dispatch(g, kp, dev_err, stream);
