@@ -816,7 +816,9 @@ __global__ void __launch_bounds__(Cfg<BN, SA, SB, BK, CV>::kThreads, 1)
 // (hi = a's top 11 significant bits, lo = fp16(a − hi): 22 significant
 // bits, as split-TF32 keeps) as two 64-byte-swizzled [128 × 32] tiles over
 // the fp32 A tile they came from (same 16 KB), B arrives as fp16 (B·2^b
-// exactly: bf16-exact weights), and each stage is 2 × 2 pair MMAs of
+// exactly: bf16 weights; unfolded, with the fold's column gain applied to
+// A by the converters, when the folded values have no fp16 form), and each
+// stage is 2 × 2 pair MMAs of
 // kind::f16 (K = 16) instead of 2 × 4 of kind::tf32 (K = 8) — half the
 // tensor-pipe time for the same products. Stage: A (then A_hi | A_lo) | B,
 // 24 KB, so 8 stages are in flight.
