@@ -101,3 +101,34 @@ def test_gelu_sigmoid_form_equals_tanh_form():
     # the tanh form flushes the far negative tail to -0 (1 + tanh = 0 in
     # float64); the sigmoid form keeps it, below 1e-15 there
     assert np.allclose(sig_form, tanh_form, rtol=1e-12, atol=1e-15)
+
+
+def test_static_bounds_of_attention_output_and_gated_activations():
+    """The model's split-fp16 exponents for the O and down inputs come from
+    bounds on the weights alone (fg_model.cu, finalize): with rs =
+    1/sqrt(mean(x²) + eps), ‖rs·x‖ < sqrt(H), so |v| < sqrt(H)·max‖W'_v row‖
+    and any convex combination of v rows (the attention output) too; and
+    |GELU(g)·u| < max(sqrt(H)‖W'_g row‖, 0.2)·sqrt(H)‖W'_u row‖."""
+    rng = np.random.default_rng(7)
+    h, f, d, eps = 768, 1152, 256, 1e-6
+    gain = (1.0 + 0.3 * rng.standard_normal(h)).astype(np.float32)
+    wv = (rng.standard_normal((d, h)) * 0.05).astype(np.float32) * gain
+    wg = (rng.standard_normal((f, h)) * 0.05).astype(np.float32) * gain
+    wu = (rng.standard_normal((f, h)) * 0.05).astype(np.float32) * gain
+    x = (rng.standard_normal((512, h)) * np.exp2(rng.uniform(-6, 8, (512, 1)))).astype(np.float64)
+    x[:8] = wv[:8] / np.linalg.norm(wv[:8], axis=1, keepdims=True) * 1e3  # aligned with W'_v rows
+    rs = 1.0 / np.sqrt((x ** 2).mean(1) + eps)
+    xs = x * rs[:, None]
+    sh = np.sqrt(h)
+    bv = sh * np.linalg.norm(wv.astype(np.float64), axis=1).max()
+    v = xs @ wv.T.astype(np.float64)
+    assert np.abs(v).max() < bv
+    p = rng.dirichlet(np.ones(512), size=64)  # softmax rows: convex weights
+    assert np.abs(p @ v).max() < bv
+    g = xs @ wg.T.astype(np.float64)
+    u = xs @ wu.T.astype(np.float64)
+    c = np.sqrt(2.0 / np.pi)
+    gelu = g / (1.0 + np.exp(-2.0 * c * (g + 0.044715 * g ** 3)))
+    bg = sh * np.linalg.norm(wg.astype(np.float64), axis=1)
+    bu = sh * np.linalg.norm(wu.astype(np.float64), axis=1)
+    assert np.abs(gelu * u).max() < (np.maximum(bg, 0.2) * bu).max()
