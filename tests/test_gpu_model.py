@@ -234,8 +234,8 @@ def test_split_fp16_matches_split_tf32(norm_std, monkeypatch):
     two fp16 parts under a power-of-two row scale) agree with split-TF32 to
     the size of split-TF32's own error, are in use (not bitwise equal) and
     repeatable. With non-zero norm gains the folded Q/K/V and gate/up
-    weights have no exact fp16 form and stay split-TF32; O and down (not
-    folded) still run split-fp16."""
+    weights have no exact fp16 form: those GEMMs take the unfolded weights
+    and apply the gains to A."""
     from ai_b200 import gemma
     from ai_b200 import synthetic as S
 
