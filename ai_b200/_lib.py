@@ -19,8 +19,9 @@ FG_ETIMEOUT = -4
 FG_ESTATE = -5
 FG_ENODEV = -6
 
-PREC_SPLIT_TF32 = 0
+PREC_SPLIT = 0  # fp32-level: split-fp16 where the weights allow, else split-TF32
 PREC_TF32 = 1
+PREC_SPLIT_TF32 = 2  # fp32-level, every product split-TF32
 
 ACT_NONE = 0
 ACT_RELU = 1
@@ -98,6 +99,7 @@ SIGNATURES = {
     "fg_memcpy_h2d": (C.c_int, [C.c_int, _vp, _vp, _i64]),
     "fg_memcpy_d2h": (C.c_int, [C.c_int, _vp, _vp, _i64]),
     "fg_synchronize": (C.c_int, [C.c_int]),
+    "fg_set_wait_limit": (C.c_int, [C.c_int, _i64]),
     "fg_model_create": (C.c_int, [C.POINTER(Config), C.c_int, C.POINTER(_vp)]),
     "fg_model_set_weight": (C.c_int, [_vp, C.c_char_p, C.c_int, C.POINTER(_i64), C.c_int, _vp]),
     "fg_model_finalize": (C.c_int, [_vp, _i64]),

@@ -22,7 +22,7 @@ import numpy as np
 import torch
 
 from . import _lib
-from ._lib import PREC_SPLIT_TF32, PREC_TF32  # noqa: F401
+from ._lib import PREC_SPLIT, PREC_SPLIT_TF32, PREC_TF32  # noqa: F401
 
 
 class ClusterError(ValueError):
@@ -49,7 +49,7 @@ def Normalize(x: torch.Tensor) -> torch.Tensor:
     return out
 
 
-def Similarities(queries: torch.Tensor, docs: torch.Tensor, precision: int = PREC_SPLIT_TF32) -> torch.Tensor:
+def Similarities(queries: torch.Tensor, docs: torch.Tensor, precision: int = PREC_SPLIT) -> torch.Tensor:
     """The [q, n] cosine similarities of unit-length rows: queries · docsᵀ."""
     _rows("Similarities", queries)
     _rows("Similarities", docs)
@@ -65,7 +65,7 @@ def Similarities(queries: torch.Tensor, docs: torch.Tensor, precision: int = PRE
 
 
 def Nearest(x: torch.Tensor, centres: torch.Tensor,
-            precision: int = PREC_SPLIT_TF32) -> Tuple[List[int], List[float]]:
+            precision: int = PREC_SPLIT) -> Tuple[List[int], List[float]]:
     """For every row of x, the index of the most similar centre (first on
     ties) and that similarity."""
     _rows("Nearest", x)
@@ -100,7 +100,7 @@ class Result:
         return float(np.sum(1.0 - s) / len(s))
 
 
-def KMeans(x: torch.Tensor, k: int, iters: int, seed: int, precision: int = PREC_SPLIT_TF32) -> Result:
+def KMeans(x: torch.Tensor, k: int, iters: int, seed: int, precision: int = PREC_SPLIT) -> Result:
     """k-means of the unit-length rows of x by cosine similarity:
     k-means++ seeding, then up to iters rounds, stopping early when no row
     changes centre."""

@@ -213,7 +213,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (j >= 1) load_v(j - 1);
       }
       if (ok) load_v(ntiles - 1);
-      if (*abort_flag) {
+      {
+        // Every load issued above lands before the CTA retires, also when
+        // another role gave up and left it unconsumed (after a normal run
+        // these phases have completed and the waits return at once).
         for (int s = 0; s < kStages; ++s) {
           if (!armed[s]) continue;
           const uint64_t t0 = globaltimer_ns();

@@ -304,7 +304,7 @@ int similarities(const float* x, int64_t ldx, int64_t n, int64_t d, const float*
   int* err = nullptr;
   FG_TRY(device_error_word(&err));
   const int64_t dp = round_up4(d);
-  const bool lo_pass = precision == FG_PREC_SPLIT_TF32;
+  const bool lo_pass = precision != FG_PREC_TF32;
   float *bhi = cbuf, *blo = cbuf ? cbuf + k * dp : nullptr;
   if (!bhi) {
     FG_TRY(ds.alloc(&bhi, size_t(k * dp)));
@@ -350,7 +350,7 @@ int fg_similarities(int64_t q, int64_t n, int64_t d, const float* queries, int64
                     int64_t ldd, float* out, int64_t ldo, int precision, void* stream) {
   clear_error();
   if (q < 0 || n < 0 || d <= 0) return set_error(FG_EINVAL, "fg_similarities: shapes [%lld x %lld] and [%lld x %lld]", (long long)q, (long long)d, (long long)n, (long long)d);
-  if (precision != FG_PREC_SPLIT_TF32 && precision != FG_PREC_TF32)
+  if (precision != FG_PREC_SPLIT && precision != FG_PREC_TF32 && precision != FG_PREC_SPLIT_TF32)
     return set_error(FG_EINVAL, "fg_similarities: unknown precision %d", precision);
   if (q == 0 || n == 0) return FG_OK;
   if (!queries || !docs || !out || ldq < d || ldd < d || ldo < n)
@@ -363,7 +363,7 @@ int fg_nearest(int64_t n, int64_t k, int64_t d, const float* x, int64_t ldx, con
                int32_t* index, float* similarity, int precision, void* stream) {
   clear_error();
   if (n < 0 || k <= 0 || d <= 0 || k > INT32_MAX) return set_error(FG_EINVAL, "fg_nearest: bad shape");
-  if (precision != FG_PREC_SPLIT_TF32 && precision != FG_PREC_TF32)
+  if (precision != FG_PREC_SPLIT && precision != FG_PREC_TF32 && precision != FG_PREC_SPLIT_TF32)
     return set_error(FG_EINVAL, "fg_nearest: unknown precision %d", precision);
   if (n == 0) return FG_OK;
   if (!x || !centres || !index || !similarity || ldx < d || ldc < d)
@@ -383,7 +383,7 @@ int fg_kmeans(int64_t n, int64_t d, const float* x, int64_t ldx, int k, int iter
   clear_error();
   if (k <= 0 || int64_t(k) > n) return set_error(FG_EINVAL, "cluster: k must be between 1 and the number of rows");
   if (d <= 0 || d > INT32_MAX || iters < 0) return set_error(FG_EINVAL, "fg_kmeans: bad shape");
-  if (precision != FG_PREC_SPLIT_TF32 && precision != FG_PREC_TF32)
+  if (precision != FG_PREC_SPLIT && precision != FG_PREC_TF32 && precision != FG_PREC_SPLIT_TF32)
     return set_error(FG_EINVAL, "fg_kmeans: unknown precision %d", precision);
   if (!x || !centres || !assignment || !similarity || !sizes || !iterations || ldx < d)
     return set_error(FG_EINVAL, "fg_kmeans: bad operand");

@@ -638,8 +638,10 @@ __global__ void __launch_bounds__(Cfg<BN, SA, SB, BK, CV>::kThreads, 1)
           }
         }
       }
-      if (*abort_flag) {
-        // Let every load this thread issued land before the CTA retires.
+      {
+        // Let every load this thread issued land before the CTA retires,
+        // also when another role gave up and left stages unconsumed (after
+        // a normal run every phase has completed and these return at once).
         for (int s = 0; s < S; ++s) {
           if (armed[s] == 0) continue;
           const uint32_t par = uint32_t(armed[s] - 1) & 1u;
@@ -933,8 +935,10 @@ __global__ void __launch_bounds__(320, 1)
           }
         }
       }
-      if (*abort_flag) {
-        // Let every load this thread issued land before the CTA retires.
+      {
+        // Let every load this thread issued land before the CTA retires,
+        // also when another role gave up and left stages unconsumed (after
+        // a normal run every phase has completed and these return at once).
         for (int s = 0; s < S; ++s) {
           if (armed[s] == 0) continue;
           const uint32_t par = uint32_t(armed[s] - 1) & 1u;
@@ -1196,10 +1200,6 @@ int make_map(CUtensorMap* m, const float* ptr, int64_t rows, int64_t cols, int64
   return FG_OK;
 }
 
-// TMA-store maps for the epilogue's outputs ([32 × 32] fp32 boxes) where the
-// output allows them (16-byte aligned, row stride a multiple of 4 floats);
-// the attention-operand epilogue writes its bf16 parts itself.
-// FG_GEMM_TMA_STORE=0 selects direct row stores everywhere.
 // Row-major [rows, cols] bf16 matrix, [32 × 32] boxes with 64-byte swizzling.
 int make_map_bf16(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, int64_t ld) {
   cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
@@ -1229,18 +1229,17 @@ int make_map_f16(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, in
   return FG_OK;
 }
 
+// TMA-store maps for the epilogue's outputs ([32 × 32] fp32 boxes, or the
+// attention operands' bf16 parts) where the output allows them (16-byte
+// aligned, row stride a multiple of 4 floats); other outputs are written by
+// direct row stores.
 int prepare_out_maps(const GemmArgs& g, KParams& kp, OutMaps* om) {
-  static const bool enabled = [] {
-    const char* v = std::getenv("FG_GEMM_TMA_STORE");
-    return !(v && v[0] == '0');
-  }();
   auto ok = [](const float* ptr, int64_t ld) {
     return ptr != nullptr && (reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && ld % 4 == 0;
   };
   kp.tma_out = 0;
   kp.tma_out_lo = 0;
   kp.tma_qk = 0;
-  if (!enabled) return FG_OK;
   if (g.epi.qkv_attn) {
     const GemmEpilogue& e = g.epi;
     const void* ps[4] = {e.q_hi, e.q_lo, e.k_hi, e.k_lo};
@@ -1339,15 +1338,8 @@ int launch_pair(const GemmArgs& g, KParams kp, int* dev_err, cudaStream_t stream
   return FG_OK;
 }
 
-// Pair kernel for 256-wide N tiles (M of at least one pair tile);
-// FG_GEMM_PAIR=0 selects the single-CTA kernel instead.
-bool use_pair(const GemmArgs& g) {
-  static const bool enabled = [] {
-    const char* v = std::getenv("FG_GEMM_PAIR");
-    return !(v && v[0] == '0');
-  }();
-  return enabled && g.M >= 256;
-}
+// Pair kernel for 256-wide N tiles (M of at least one pair tile).
+bool use_pair(const GemmArgs& g) { return g.M >= 256; }
 
 // A's low part: none (plain TF32), loaded (SA), or computed in shared memory (CV).
 template <int BN, bool SB>

@@ -38,11 +38,17 @@ const char* last_error();
 // Number of SMs of the current device (cached per device).
 int sm_count();
 
-// Device error word of the current device; kernels record bounded-wait
-// timeouts there. check_device_error_word() synchronises the device and
-// turns a recorded timeout into FG_ETIMEOUT, resetting the word.
+// Status block of the current device (error word, then the pipeline-wait
+// limit; fg_ptx.cuh DeviceStatus); kernels record bounded-wait timeouts
+// there. check_device_error_word() synchronises the device and turns a
+// recorded timeout into FG_ETIMEOUT, resetting the word.
 int device_error_word(int** out);
 int check_device_error_word();
+// Registers another status block of device `dev` (the no-allocation entry
+// point's static one) for check_device_error_word and the wait limit.
+int register_status_block(int dev, int* block);
+// Sets device `dev`'s pipeline-wait limit in every status block it has.
+int set_wait_limit(int dev, unsigned long long ns);
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no
 // libcuda link dependency); resolved once.

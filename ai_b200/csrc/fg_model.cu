@@ -14,8 +14,9 @@
 //                   yields 128 finished GeGLU columns; pre-norm folded
 //              Wd   [hidden, ffn]
 //              each with its TF32 low part when it is non-zero
-//   activations, token-major [B·T, ·]: x (residual stream) + x_lo, qkv,
-//   att + att_lo, gu + gu_lo, tmp; rowscale [B·T].
+//   activations, token-major [B·T, ·]: x (residual stream), qkv, att, gu,
+//   tmp; rowscale [B·T]. The split products make their A operand's low part
+//   (or fp16 parts) in shared memory from the A tile.
 #include <algorithm>
 #include <cmath>
 #include <cstdlib>
@@ -166,21 +167,18 @@ struct fg_model {
   // workspace
   int64_t cap_tokens = 0;
   int cap_batch = 0;
-  float *x = nullptr, *x_lo = nullptr, *rowscale = nullptr, *qkv = nullptr, *att = nullptr,
-        *att_lo = nullptr, *gu = nullptr, *gu_lo = nullptr, *tmp = nullptr;
-  float *pooled = nullptr, *pooled_lo = nullptr, *head_a = nullptr, *head_a_lo = nullptr,
-        *head_b = nullptr, *head_b_lo = nullptr;
+  float *x = nullptr, *rowscale = nullptr, *qkv = nullptr, *att = nullptr, *gu = nullptr,
+        *tmp = nullptr;
+  float *pooled = nullptr, *head_a = nullptr, *head_b = nullptr;
   int32_t* eff_len = nullptr;
   int* err = nullptr;
   void* attn_ws = nullptr;  // split-bf16 operands of the tensor-core attention
   size_t attn_ws_bytes = 0;
-  bool attn_simt = false;   // FG_ATTENTION=simt selects the SIMT kernel
-  // FG_GEMM_ALO=global: producers write the split-TF32 low parts of the
-  // GEMM inputs to memory instead of the GEMM computing them in shared memory
-  bool alo_global = false;
-  // split-fp16 encoder GEMMs where the weights have an exact fp16 form
-  // (FG_GEMM_H16=0: split-TF32 everywhere)
+  // The fp16 forms the split-fp16 encoder GEMMs read are prepared at
+  // finalize wherever the weights have one; use16 is the current forward's
+  // choice (FG_PREC_SPLIT: yes; FG_PREC_SPLIT_TF32 / FG_PREC_TF32: no).
   bool h16 = true;
+  bool use16 = true;
   int weight_mode = FG_WEIGHTS_F32;
   size_t weight_bytes = 0;  // device bytes allocated by finalize before the activation workspace
   size_t alloc_bytes = 0;
@@ -524,13 +522,10 @@ int ensure_workspace(fg_model* m, int64_t tokens, int batch) {
     }
     const int64_t F = c.intermediate_size;
     FG_TRY(dev_alloc_t(m, &m->x, tokens * H));
-    FG_TRY(dev_alloc_t(m, &m->x_lo, tokens * H));
     FG_TRY(dev_alloc_t(m, &m->rowscale, tokens));
     FG_TRY(dev_alloc_t(m, &m->qkv, tokens * qkvw));
     FG_TRY(dev_alloc_t(m, &m->att, tokens * attw));
-    FG_TRY(dev_alloc_t(m, &m->att_lo, tokens * attw));
     FG_TRY(dev_alloc_t(m, &m->gu, tokens * F));
-    FG_TRY(dev_alloc_t(m, &m->gu_lo, tokens * F));
     FG_TRY(dev_alloc_t(m, &m->tmp, tokens * std::max(H, attw)));
     if (c.variant == 2) {
       const int64_t P = c.ple_dim, L = c.num_layers;
@@ -549,11 +544,8 @@ int ensure_workspace(fg_model* m, int64_t tokens, int batch) {
     for (auto& d : m->dense) widest = std::max(widest, std::max(d.in, d.out));
     const int64_t nb = std::max(batch, 1);
     FG_TRY(dev_alloc_t(m, &m->pooled, nb * c.hidden_size));
-    FG_TRY(dev_alloc_t(m, &m->pooled_lo, nb * c.hidden_size));
     FG_TRY(dev_alloc_t(m, &m->head_a, nb * widest));
-    FG_TRY(dev_alloc_t(m, &m->head_a_lo, nb * widest));
     FG_TRY(dev_alloc_t(m, &m->head_b, nb * widest));
-    FG_TRY(dev_alloc_t(m, &m->head_b_lo, nb * widest));
     FG_TRY(dev_alloc_t(m, &m->eff_len, nb));
     m->cap_batch = int(nb);
   }
@@ -997,7 +989,7 @@ GemmArgs make_gemm(int M, const float* A, const float* A_lo, int64_t lda, const 
 // (1/sqrt(mean(a²) + eps)) or, without them, the static aexp (ok: the bound
 // behind it is finite).
 void use_h16(const fg_model* m, GemmArgs& g, const DevMat& W, const float* a_rs, bool ok, int aexp) {
-  if (!m->h16 || !g.a_lo_smem || !W.h16 || !ok) return;
+  if (!m->h16 || !m->use16 || !g.a_lo_smem || !W.h16 || !ok) return;
   g.B16 = W.h16;
   g.b_exp = W.h16_exp;
   g.a_rs = a_rs;
@@ -1063,7 +1055,8 @@ int grow_attn_ws(fg_model* m, size_t need, cudaStream_t s) {
 int forward_v2(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int T, int dim,
                int precision, float* out, cudaStream_t s) {
   const fg_config& c = m->cfg;
-  const bool split = precision == FG_PREC_SPLIT_TF32;
+  const bool split = precision != FG_PREC_TF32;
+  m->use16 = precision == FG_PREC_SPLIT;
   const int H = c.hidden_size, Hq = c.num_heads, F = c.intermediate_size;
   const int L = c.num_layers, P = c.ple_dim, E = c.embedding_dim;
   const int64_t M = int64_t(B) * T;
@@ -1112,7 +1105,7 @@ int forward_v2(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, i
     // q|k|v = rowscale ⊙ (x · Wqkv'ᵀ)   (embed.go:285-288); on the
     // 256-wide layers the epilogue also applies the q/k norms, RoPE and the
     // v_norm and writes the tensor-core attention's operands
-    const bool tc = !m->attn_simt && attn_tc_supported(a);
+    const bool tc = attn_tc_supported(a);
     const bool fused = tc && D == 256 && m->rope_cosT[size_t(Ly.rope)] != nullptr;
     AttnOperands ops{};
     if (tc) FG_TRY(grow_attn_ws(m, attn_tc_workspace_bytes(B, T, T, Hq, Hkv, D), s));
@@ -1254,25 +1247,25 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
             int precision, float* out, cudaStream_t s) {
   if (m->cfg.variant == 2) return forward_v2(m, ids, lengths, B, T, dim, precision, out, s);
   const fg_config& c = m->cfg;
-  const bool split = precision == FG_PREC_SPLIT_TF32;
+  const bool split = precision != FG_PREC_TF32;
+  m->use16 = precision == FG_PREC_SPLIT;
   const int H = c.hidden_size, D = c.head_dim, Hq = c.num_heads, Hkv = c.num_kv_heads;
   const int F = c.intermediate_size;
   const int64_t M = int64_t(B) * T;
   if (M > INT32_MAX) return set_error(FG_EINVAL, "batch too large");
   FG_TRY(ensure_workspace(m, M, B));
   const int qkvw = (Hq + 2 * Hkv) * D, attw = Hq * D;
-  // Split-TF32 low parts of GEMM inputs: made in shared memory by the GEMM
-  // (default), or written to memory by their producers (FG_GEMM_ALO=global).
-  const bool lo_global = split && m->alo_global;
-  float* x_lo = lo_global ? m->x_lo : nullptr;
-  float* att_lo = lo_global ? m->att_lo : nullptr;
-  float* gu_lo = lo_global ? m->gu_lo : nullptr;
+  // The split products' A low parts are made in shared memory by the GEMM
+  // from the A tile, so no producer writes one.
+  float* const x_lo = nullptr;
+  float* const att_lo = nullptr;
+  float* const gu_lo = nullptr;
 
   const double act_bytes = double(M) * H * 4.0;
   {
     // table rows read (2 or 4 B per value) + x (+ x_lo) written + ids and rowscale
     const double row_read = double(M) * H * (m->embed_bf16 ? 2.0 : 4.0);
-    PhaseScope ps(m, FG_PHASE_EMBED, s, row_read + act_bytes * (lo_global ? 2 : 1) + double(M) * 8, 2);
+    PhaseScope ps(m, FG_PHASE_EMBED, s, row_read + act_bytes + double(M) * 8, 2);
     eff_len_kernel<<<(B + 127) / 128, 128, 0, s>>>(lengths, B, T, m->eff_len);
     FG_CUDA_TRY(cudaGetLastError());
     const float emb_scale = float(std::sqrt(double(H)));
@@ -1290,7 +1283,7 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
     if (L.resident_bf16) {
       // A projection resident in its fp16 form is read as it is by the
       // split-fp16 GEMM; the others are widened into the workspace.
-      const bool h16ok = split && m->h16 && !lo_global && gemm_h16_applies(int(M));
+      const bool h16ok = split && m->h16 && m->use16 && gemm_h16_applies(int(M));
       const Bf16Mat* src[4] = {&L.bqkv, &L.bo, &L.bgu, &L.bd};
       DevMat* dst[4] = {&Wqkv, &Wo, &Wgu, &Wd};
       const DevMat* ws[4] = {&m->ws_qkv, &m->ws_o, &m->ws_gu, &m->ws_d};
@@ -1334,7 +1327,7 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
     a.scale = c.attn_scale;
     // Tensor-core attention: the QKV GEMM's epilogue applies QK-norm and
     // RoPE and writes the split-bf16 operands straight into its workspace.
-    const bool tc = !m->attn_simt && attn_tc_supported(a);
+    const bool tc = attn_tc_supported(a);
     AttnOperands ops{};
     if (tc) {
       FG_TRY(grow_attn_ws(m, attn_tc_workspace_bytes(B, T, T, Hq, Hkv), s));
@@ -1396,7 +1389,7 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
     }
     // x += RMSNorm(o0)   (embed.go:216-220), and the FFN pre-norm factor
     {
-      PhaseScope ps(m, FG_PHASE_RESIDUAL, s, act_bytes * (lo_global ? 4 : 3) + double(M) * 4);
+      PhaseScope ps(m, FG_PHASE_RESIDUAL, s, act_bytes * 3 + double(M) * 4);
       FG_TRY(residual_postnorm(m->x, x_lo, m->tmp, L.post_attn, c.rms_norm_eps, m->rowscale,
                                nullptr, M, H, s));
     }
@@ -1424,7 +1417,7 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
     }
     // x += RMSNorm(mlp0)   (embed.go:231-235); final norm on the last layer (embed.go:237)
     {
-      PhaseScope ps(m, FG_PHASE_RESIDUAL, s, act_bytes * ((lo_global && !last) ? 4 : 3) + double(M) * 4);
+      PhaseScope ps(m, FG_PHASE_RESIDUAL, s, act_bytes * 3 + double(M) * 4);
       FG_TRY(residual_postnorm(m->x, x_lo, m->tmp, L.post_ffn, c.rms_norm_eps, m->rowscale,
                                last ? m->final_gain : nullptr, M, H, s));
     }
@@ -1433,23 +1426,18 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
 
   // pool (embed.go:381-404), head (embed.go:408-429), L2 (embed.go:472-475)
   PhaseScope ps(m, FG_PHASE_POOL_HEAD, s, act_bytes, 2 + int(m->dense.size()));
-  FG_TRY(mean_pool(m->x, m->eff_len, B, T, H, m->pooled, lo_global ? m->pooled_lo : nullptr, s));
+  FG_TRY(mean_pool(m->x, m->eff_len, B, T, H, m->pooled, nullptr, s));
   const float* cur = m->pooled;
-  const float* cur_lo = lo_global ? m->pooled_lo : nullptr;
   int width = H;
   float* bufs[2] = {m->head_a, m->head_b};
-  float* bufs_lo[2] = {m->head_a_lo, m->head_b_lo};
   for (size_t j = 0; j < m->dense.size(); ++j) {
     const Dense& d = m->dense[j];
-    GemmArgs g = make_gemm(B, cur, cur_lo, width, d.w, split);
+    GemmArgs g = make_gemm(B, cur, nullptr, width, d.w, split);
     g.epi.out = bufs[j & 1];
     g.epi.ldo = d.out;
-    g.epi.out_lo = lo_global ? bufs_lo[j & 1] : nullptr;
-    g.epi.ldo_lo = d.out;
     g.epi.act = d.tanh ? kActTanh : FG_ACT_NONE;
     FG_TRY(gemm_tn(g, m->err, s));
     cur = bufs[j & 1];
-    cur_lo = lo_global ? bufs_lo[j & 1] : nullptr;
     width = d.out;
   }
   if (dim > width) return set_error(FG_EINVAL, "gemma: Dim(%d) outside 1..%d", dim, width);
@@ -1520,12 +1508,6 @@ int fg_model_create(const fg_config* cfg, int device, fg_model** out) {
   }
   m->cfg.layer_head_dim = m->head_dim_l.data();
   m->cfg.layer_kv_heads = m->kv_l.data();
-  const char* att = std::getenv("FG_ATTENTION");
-  m->attn_simt = att && std::string(att) == "simt";
-  const char* alo = std::getenv("FG_GEMM_ALO");
-  m->alo_global = alo && std::string(alo) == "global";
-  const char* h16 = std::getenv("FG_GEMM_H16");
-  m->h16 = !(h16 && h16[0] == '0');
   const char* wm = std::getenv("FG_WEIGHTS");
   if (wm && std::string(wm) == "bf16") m->weight_mode = FG_WEIGHTS_BF16;
   *out = m;
@@ -1602,7 +1584,7 @@ int fg_embed_ids_device(fg_model* m, const int32_t* d_ids, const int32_t* d_leng
   if (B == 0) return FG_OK;
   if (T == 0) return set_error(FG_EINVAL, "T must be at least 1");
   if (T > m->cfg.max_tokens) return set_error(FG_EINVAL, "T=%d exceeds max_tokens %d", T, m->cfg.max_tokens);
-  if (precision != FG_PREC_SPLIT_TF32 && precision != FG_PREC_TF32)
+  if (precision != FG_PREC_SPLIT && precision != FG_PREC_TF32 && precision != FG_PREC_SPLIT_TF32)
     return set_error(FG_EINVAL, "unknown precision %d", precision);
   const int full = model_dim(m);
   if (dim < 1 || dim > full) return set_error(FG_EINVAL, "gemma: Dim(%d) outside 1..%d", dim, full);
@@ -1678,7 +1660,7 @@ int fg_embed_many(fg_model* m, const int32_t* ids, const int64_t* offsets, int n
   if (nseq == 0) return FG_OK;
   if (!offsets || !out) return set_error(FG_EINVAL, "null buffer");
   if (batch_tokens < 1) return set_error(FG_EINVAL, "batch_tokens %lld < 1", (long long)batch_tokens);
-  if (precision != FG_PREC_SPLIT_TF32 && precision != FG_PREC_TF32)
+  if (precision != FG_PREC_SPLIT && precision != FG_PREC_TF32 && precision != FG_PREC_SPLIT_TF32)
     return set_error(FG_EINVAL, "unknown precision %d", precision);
   const int full = model_dim(m);
   if (dim < 1 || dim > full) return set_error(FG_EINVAL, "gemma: Dim(%d) outside 1..%d", dim, full);
@@ -1707,7 +1689,7 @@ int fg_embed_many(fg_model* m, const int32_t* ids, const int64_t* offsets, int n
   for (const Batch& b : batches) {
     max_bt = std::max<int64_t>(max_bt, int64_t(b.count) * b.T);
     max_b = std::max(max_b, b.count);
-    if (!m->attn_simt && m->cfg.head_dim == 256)
+    if (m->cfg.head_dim == 256)
       attn_need = std::max(attn_need, attn_tc_workspace_bytes(b.count, b.T, b.T, m->cfg.num_heads, m->cfg.num_kv_heads));
   }
   FG_CUDA_TRY(cudaSetDevice(m->device));

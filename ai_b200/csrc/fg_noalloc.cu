@@ -9,17 +9,25 @@
 // cudaMalloc, cudaFree or other allocating routine.
 //
 // The scratch is the file-scope array below (kScratchBytes, 32 MiB), which
-// every GPU that loads the library holds until the process exits. In host
-// code the array's name is only a host-side stand-in, so the device
-// address is obtained with cudaGetSymbolAddress, once per device, with that
-// device current, on the first call made on it; that first call should
-// therefore come before any stream capture. All calls share the one array:
-// calls that overlap on the GPU (different streams, or concurrent host
-// threads) race on it and must be serialised by the caller.
+// every GPU that loads the library holds until the process exits. The CUDA
+// driver reserves it when it loads this file's module on a device: at the
+// first call on that device under lazy module loading (the CUDA 12
+// default), or when the context is created under CUDA_MODULE_LOADING=EAGER.
+// A caller whose allocator reserves the GPU's memory up front should make
+// one call (or set eager loading) before that reservation. In host code the
+// array's name is only a host-side stand-in, so the device address is
+// obtained with cudaGetSymbolAddress, once per device, with that device
+// current, on the first call made on it; that first call should therefore
+// come before any stream capture. All calls share the one array: calls
+// that overlap on the GPU (different streams, or concurrent host threads)
+// race on it and must be serialised by the caller. A bounded wait that
+// gives up in one of its kernels is recorded in the entry point's own
+// status block, which fg_synchronize reads and clears (FG_ETIMEOUT).
 #include <mutex>
 
 #include "fg_internal.h"
 #include "fg_kernels.cuh"
+#include "fg_ptx.cuh"
 
 namespace fg {
 namespace {
@@ -31,9 +39,11 @@ constexpr int kMaxDevices = 64;
 // (the split / pack kernels fill exactly the rows and columns the GEMM's
 // tensor maps cover), so nothing needs clearing between calls.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
-// Bounded-wait timeouts of kernels launched by this entry point are
-// recorded here (the call itself never blocks to read it back).
-static __device__ int g_noalloc_err;
+// Status block of the kernels this entry point launches: their
+// bounded-wait timeouts are recorded in its first word, and their wait
+// limit is read from it (DeviceStatus). It is registered with the runtime
+// at set-up, so fg_synchronize reads and clears it like the library's own.
+static __device__ __align__(16) DeviceStatus g_noalloc_status = {0, 0, kWaitTimeoutNs};
 
 struct DevicePointers {
   unsigned char* scratch = nullptr;
@@ -57,11 +67,12 @@ int device_pointers(DevicePointers* out) {
       return set_error(FG_ECUDA, "cudaGetSymbolAddress(scratch) failed: %s", cudaGetErrorString(e));
     }
     void* q = nullptr;
-    e = cudaGetSymbolAddress(&q, g_noalloc_err);
+    e = cudaGetSymbolAddress(&q, g_noalloc_status);
     if (e != cudaSuccess) {
       cudaGetLastError();
-      return set_error(FG_ECUDA, "cudaGetSymbolAddress(error word) failed: %s", cudaGetErrorString(e));
+      return set_error(FG_ECUDA, "cudaGetSymbolAddress(status block) failed: %s", cudaGetErrorString(e));
     }
+    FG_TRY(register_status_block(dev, static_cast<int*>(q)));
     d.scratch = static_cast<unsigned char*>(p);
     d.err = static_cast<int*>(q);
     d.ready = true;
@@ -85,7 +96,7 @@ extern "C" int fg_matmul_noalloc(int64_t m, int64_t n, int64_t k, const float* x
   if (m < 0 || n < 0 || k <= 0 || m > INT32_MAX || n > INT32_MAX || k > INT32_MAX)
     return set_error(FG_EINVAL, "fg_matmul_noalloc: bad shape m=%lld n=%lld k=%lld",
                      (long long)m, (long long)n, (long long)k);
-  if (precision != FG_PREC_SPLIT_TF32 && precision != FG_PREC_TF32)
+  if (precision != FG_PREC_SPLIT && precision != FG_PREC_TF32 && precision != FG_PREC_SPLIT_TF32)
     return set_error(FG_EINVAL, "fg_matmul_noalloc: unknown precision %d", precision);
   if (m == 0 || n == 0) return FG_OK;
   if (!x || !w || !out) return set_error(FG_EINVAL, "fg_matmul_noalloc: null operand");
@@ -98,7 +109,7 @@ extern "C" int fg_matmul_noalloc(int64_t m, int64_t n, int64_t k, const float* x
 
   // Scratch plan: x split (or re-strided) into [m, kp] parts, w transposed
   // to [n, kp] when given as [k, n], and w split into [n, kp] parts.
-  const bool split = precision == FG_PREC_SPLIT_TF32;
+  const bool split = precision != FG_PREC_TF32;
   const int64_t kp = (k + 3) / 4 * 4;
   const bool a_direct = !split && (reinterpret_cast<uintptr_t>(x) & 15) == 0 && ldx % 4 == 0;
   const bool b_direct = !split && w_transposed && (reinterpret_cast<uintptr_t>(w) & 15) == 0 &&

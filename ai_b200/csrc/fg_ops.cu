@@ -64,7 +64,7 @@ int fg_matmul(int64_t m, int64_t n, int64_t k, const float* x, int64_t ldx, cons
   clear_error();
   if (m < 0 || n < 0 || k < 0 || m > INT32_MAX || n > INT32_MAX || k > INT32_MAX)
     return set_error(FG_EINVAL, "fg_matmul: bad shape m=%lld n=%lld k=%lld", (long long)m, (long long)n, (long long)k);
-  if (precision != FG_PREC_SPLIT_TF32 && precision != FG_PREC_TF32)
+  if (precision != FG_PREC_SPLIT && precision != FG_PREC_TF32 && precision != FG_PREC_SPLIT_TF32)
     return set_error(FG_EINVAL, "fg_matmul: unknown precision %d", precision);
   if (m == 0 || n == 0) return FG_OK;
   if (!x || !w || !out) return set_error(FG_EINVAL, "fg_matmul: null operand");
@@ -95,7 +95,7 @@ int fg_matmul(int64_t m, int64_t n, int64_t k, const float* x, int64_t ldx, cons
     return set_error(FG_EINVAL, "fg_matmul: k = 0 is not supported");
   }
 
-  const bool split = precision == FG_PREC_SPLIT_TF32;
+  const bool split = precision != FG_PREC_TF32;
   const int64_t kp = round4(k);
   const bool a_direct = !split && aligned16(x) && ldx % 4 == 0;
   const bool b_direct = !split && w_transposed && aligned16(w) && ldw % 4 == 0;
@@ -195,7 +195,7 @@ int fg_attention(const float* q, const float* k, const float* v, int B, int Hq, 
   clear_error();
   if (B < 0 || Hq <= 0 || Hkv <= 0 || T < 0 || S < 0 || D <= 0)
     return set_error(FG_EINVAL, "fg_attention: bad shape");
-  if (precision != FG_PREC_SPLIT_TF32 && precision != FG_PREC_TF32)
+  if (precision != FG_PREC_SPLIT && precision != FG_PREC_TF32 && precision != FG_PREC_SPLIT_TF32)
     return set_error(FG_EINVAL, "fg_attention: unknown precision %d", precision);
   AttnArgs a{};
   a.q = q;
@@ -213,8 +213,7 @@ int fg_attention(const float* q, const float* k, const float* v, int B, int Hq, 
   a.window = window;
   a.scale = scale;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const char* att = std::getenv("FG_ATTENTION");
-  if (!(att && std::string(att) == "simt") && attn_tc_supported(a)) {
+  if (attn_tc_supported(a)) {
     int* err = nullptr;
     FG_TRY(device_error_word(&err));
     const size_t need = attn_tc_workspace_bytes(B, T, S, Hq, Hkv, D);

@@ -2,10 +2,12 @@
 // TMA tile loads, tcgen05 (TMEM allocation, MMA issue, commit, loads) and
 // the shared-memory matrix descriptor for 128-byte-swizzled K-major tiles.
 //
-// Every wait in this library is bounded: a wait that does not complete
-// within kWaitTimeoutNs sets the CTA's abort flag and a device error word,
-// and returns false, so a kernel that meets a broken pipeline ends with an
-// error status the host reads instead of hanging the GPU.
+// Every wait in this library is bounded: a pipeline wait that does not
+// complete within the device's wait limit (DeviceStatus, 2 s by default)
+// sets the CTA's abort flag and the device error word, and returns false,
+// so a kernel that meets a broken pipeline ends with an error status the
+// host reads instead of hanging the GPU. The teardown waits for a CTA's own
+// copies and MMAs in flight always use the fixed kWaitTimeoutNs.
 #pragma once
 
 #include <cstdint>
@@ -26,7 +28,24 @@ enum DeviceError : int {
   kDevBadArgs = 6,          // a kernel saw arguments it cannot handle
 };
 
+// Default limit of a pipeline wait, and the fixed limit of the teardown
+// waits that let a CTA's own copies and MMAs finish before it retires.
 constexpr uint64_t kWaitTimeoutNs = 2000ull * 1000ull * 1000ull;  // 2 s
+
+// The per-device status block kernels receive as `int* gerr`: the error
+// word first, then the pipeline-wait limit in nanoseconds (set from the
+// host, fg_set_wait_limit). 16 bytes, zero error and kWaitTimeoutNs when
+// created.
+struct DeviceStatus {
+  int err;
+  int reserved;
+  unsigned long long wait_limit_ns;
+};
+static_assert(sizeof(DeviceStatus) == 16, "status block layout");
+
+__device__ __forceinline__ uint64_t wait_limit_ns(const int* gerr) {
+  return reinterpret_cast<const volatile DeviceStatus*>(gerr)->wait_limit_ns;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -68,16 +87,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Waits for the phase with the given parity to complete. Gives up after
-// kWaitTimeoutNs, or as soon as another role of the CTA has aborted
+// the device's wait limit (gerr's status block), or as soon as another role of the CTA has aborted
 // (*abort != 0); on a timeout it raises the abort flag and records `code`.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
                                           int* gerr, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
+  const uint64_t limit = wait_limit_ns(gerr);
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+    if (globaltimer_ns() - t0 > limit) {
       *abort = 1;
       atomicCAS(gerr, 0, code);
       return false;
@@ -207,10 +227,11 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity,
                                                   int* gerr, int code) {
   if (mbar_try_wait_cluster(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
+  const uint64_t limit = wait_limit_ns(gerr);
   while (true) {
     if (mbar_try_wait_cluster(bar, parity)) return true;
     if (*abort) return false;
-    if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+    if (globaltimer_ns() - t0 > limit) {
       *abort = 1;
       atomicCAS(gerr, 0, code);
       return false;

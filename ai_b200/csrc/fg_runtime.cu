@@ -1,6 +1,6 @@
 // Library runtime: thread-local error messages, device queries, the
-// per-device error word kernels report bounded-wait timeouts into, and the
-// device-memory helpers of the C ABI.
+// per-device status block kernels report bounded-wait timeouts into (and
+// read their wait limit from), and the device-memory helpers of the C ABI.
 #include <mutex>
 #include <vector>
 
@@ -11,8 +11,18 @@ namespace fg {
 namespace {
 thread_local std::string t_last_error;
 std::mutex g_mu;
-std::vector<int*> g_dev_err;  // per device, lazily allocated
+std::vector<int*> g_dev_err;    // per device status block, lazily allocated
+std::vector<int*> g_extra_err;  // per device: the no-allocation entry point's block
+std::vector<unsigned long long> g_wait_limit;  // per device, 0 = default
 std::vector<int> g_sms;
+
+// Host image of the device status block (fg_ptx.cuh DeviceStatus).
+struct DeviceStatusHost {
+  int err;
+  int reserved;
+  unsigned long long wait_limit_ns;
+};
+constexpr unsigned long long kDefaultWaitLimitNs = 2000ull * 1000ull * 1000ull;
 }  // namespace
 
 int set_error(int code, const char* fmt, ...) {
@@ -41,34 +51,76 @@ int sm_count() {
   return g_sms[dev];
 }
 
-// Device error word of the current device (zeroed at allocation).
+// Status block of the current device: the error word (zeroed at
+// allocation) followed by the pipeline-wait limit. Allocated on first use.
 int device_error_word(int** out) {
   int dev = 0;
   FG_CUDA_TRY(cudaGetDevice(&dev));
   std::lock_guard<std::mutex> lk(g_mu);
   if (int(g_dev_err.size()) <= dev) g_dev_err.resize(dev + 1, nullptr);
   if (g_dev_err[dev] == nullptr) {
+    DeviceStatusHost init{0, 0, kDefaultWaitLimitNs};
+    if (int(g_wait_limit.size()) > dev && g_wait_limit[dev] != 0) init.wait_limit_ns = g_wait_limit[dev];
     int* p = nullptr;
-    FG_CUDA_TRY(cudaMalloc(&p, sizeof(int)));
-    FG_CUDA_TRY(cudaMemset(p, 0, sizeof(int)));
+    FG_CUDA_TRY(cudaMalloc(&p, sizeof(DeviceStatusHost)));
+    FG_CUDA_TRY(cudaMemcpy(p, &init, sizeof(init), cudaMemcpyHostToDevice));
     g_dev_err[dev] = p;
   }
   *out = g_dev_err[dev];
   return FG_OK;
 }
 
+int register_status_block(int dev, int* block) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (int(g_extra_err.size()) <= dev) g_extra_err.resize(dev + 1, nullptr);
+  g_extra_err[dev] = block;
+  if (int(g_wait_limit.size()) > dev && g_wait_limit[dev] != 0) {
+    const unsigned long long v = g_wait_limit[dev];
+    FG_CUDA_TRY(cudaMemcpy(reinterpret_cast<char*>(block) + 8, &v, sizeof(v), cudaMemcpyHostToDevice));
+  }
+  return FG_OK;
+}
+
 // Synchronises the current device and converts a recorded kernel timeout
-// into FG_ETIMEOUT (resetting the word).
+// into FG_ETIMEOUT, resetting the error words. Reads the library's status
+// block and the one registered by the no-allocation entry point; allocates
+// nothing (a block not yet created holds no record).
 int check_device_error_word() {
   FG_CUDA_TRY(cudaDeviceSynchronize());
-  int* w = nullptr;
-  FG_TRY(device_error_word(&w));
-  int v = 0;
-  FG_CUDA_TRY(cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost));
-  if (v != 0) {
-    FG_CUDA_TRY(cudaMemset(w, 0, sizeof(int)));
-    return set_error(FG_ETIMEOUT, "a device wait gave up (kernel status %d)", v);
+  int dev = 0;
+  FG_CUDA_TRY(cudaGetDevice(&dev));
+  int* words[2] = {nullptr, nullptr};
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (int(g_dev_err.size()) > dev) words[0] = g_dev_err[dev];
+    if (int(g_extra_err.size()) > dev) words[1] = g_extra_err[dev];
   }
+  int first = 0;
+  for (int* w : words) {
+    if (!w) continue;
+    int v = 0;
+    FG_CUDA_TRY(cudaMemcpy(&v, w, sizeof(int), cudaMemcpyDeviceToHost));
+    if (v != 0) {
+      const int zero = 0;
+      FG_CUDA_TRY(cudaMemcpy(w, &zero, sizeof(int), cudaMemcpyHostToDevice));
+      if (!first) first = v;
+    }
+  }
+  if (first) return set_error(FG_ETIMEOUT, "a device wait gave up (kernel status %d)", first);
+  return FG_OK;
+}
+
+int set_wait_limit(int dev, unsigned long long ns) {
+  int* blocks[2] = {nullptr, nullptr};
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (int(g_wait_limit.size()) <= dev) g_wait_limit.resize(dev + 1, 0);
+    g_wait_limit[dev] = ns;
+    if (int(g_dev_err.size()) > dev) blocks[0] = g_dev_err[dev];
+    if (int(g_extra_err.size()) > dev) blocks[1] = g_extra_err[dev];
+  }
+  for (int* b : blocks)
+    if (b) FG_CUDA_TRY(cudaMemcpy(reinterpret_cast<char*>(b) + 8, &ns, sizeof(ns), cudaMemcpyHostToDevice));
   return FG_OK;
 }
 
@@ -142,6 +194,16 @@ int fg_memcpy_d2h(int device, void* dst, const void* src, int64_t bytes) {
 int fg_synchronize(int device) {
   FG_CUDA_TRY(cudaSetDevice(device));
   return fg::check_device_error_word();
+}
+
+int fg_set_wait_limit(int device, int64_t nanoseconds) {
+  fg::clear_error();
+  if (nanoseconds < 0) return fg::set_error(FG_EINVAL, "fg_set_wait_limit: negative limit");
+  FG_CUDA_TRY(cudaSetDevice(device));
+  FG_CUDA_TRY(cudaDeviceSynchronize());
+  const unsigned long long ns =
+      nanoseconds == 0 ? fg::kDefaultWaitLimitNs : static_cast<unsigned long long>(nanoseconds);
+  return fg::set_wait_limit(device, ns);
 }
 
 }  // extern "C"

@@ -36,7 +36,7 @@ from typing import Callable, Dict, List, Optional, Sequence, Tuple
 import numpy as np
 
 from . import _lib
-from ._lib import PREC_SPLIT_TF32, PREC_TF32  # noqa: F401
+from ._lib import PREC_SPLIT, PREC_SPLIT_TF32, PREC_TF32  # noqa: F401
 from .synthetic import read_safetensors
 
 
@@ -375,7 +375,7 @@ class Model:
 
     # -- embedBatch / Embed
     def embed_padded(self, ids: np.ndarray, lengths: np.ndarray, dim: Optional[int] = None,
-                     precision: int = PREC_SPLIT_TF32, out: Optional[np.ndarray] = None) -> np.ndarray:
+                     precision: int = PREC_SPLIT, out: Optional[np.ndarray] = None) -> np.ndarray:
         """One forward over an already padded [B, T] batch (host buffers;
         pinned ones are copied without staging)."""
         ids = np.ascontiguousarray(ids, dtype=np.int32)
@@ -394,7 +394,7 @@ class Model:
         return out
 
     def embed_batch(self, seqs: Sequence[Sequence[int]], dim: Optional[int] = None,
-                    precision: int = PREC_SPLIT_TF32) -> np.ndarray:
+                    precision: int = PREC_SPLIT) -> np.ndarray:
         """embedBatch (embed.go:118-157): right-pad with id 0, encode, pool, head."""
         B = len(seqs)
         T = max((len(s) for s in seqs), default=0)
@@ -406,7 +406,7 @@ class Model:
         return self.embed_padded(ids, lengths, dim, precision)
 
     def embed_device(self, d_ids, d_lengths, B: int, T: int, dim: int, d_out, stream=None,
-                     precision: int = PREC_SPLIT_TF32) -> None:
+                     precision: int = PREC_SPLIT) -> None:
         """Device-resident forward: ids/lengths/out are device pointers (ints)
         or CUDA tensors; asynchronous on `stream` (a torch stream or handle)."""
         p = lambda t: t if isinstance(t, int) else t.data_ptr()
@@ -434,7 +434,7 @@ class Model:
                 for i, p in enumerate(_lib.PHASES)}
 
     def embed_ids(self, seqs: Sequence[Sequence[int]], Dim: Optional[int] = None,
-                  precision: int = PREC_SPLIT_TF32) -> List[np.ndarray]:
+                  precision: int = PREC_SPLIT) -> List[np.ndarray]:
         """(*Model).Embed (embed.go:15-80) from token ids: truncation, the
         stable length sort, greedy batches under BatchTokens and the
         overlapped host/GPU pipeline all run in fg_embed_many."""
@@ -503,14 +503,20 @@ def Load(d, *options: Option, device: int = 0, max_batch_tokens: int = 8192) -> 
 
 def from_synthetic(cfg_dict: dict, weights_bf16: Dict[str, np.ndarray], device: int = 0,
                    max_batch_tokens: int = 8192, options: Sequence[Option] = ()) -> Model:
-    """A model from in-memory bf16 weights (ai_b200.synthetic.make_weights),
-    the same path Load takes after reading the files."""
+    """A model from in-memory weights — bf16 bits as uint16 arrays
+    (ai_b200.synthetic.make_weights) or float32 arrays (make_weights_f32, an
+    fp32 checkpoint) — the same path Load takes after reading the files."""
     cfg = config_from_dict(cfg_dict)
-    body = {k: (_lib.DT_BF16, v) for k, v in weights_bf16.items() if not k.startswith("dense.")}
+
+    def dt(v):
+        return _lib.DT_F32 if np.asarray(v).dtype == np.float32 else _lib.DT_BF16
+
+    body = {k: (dt(v), v) for k, v in weights_bf16.items() if not k.startswith("dense.")}
     dense = []
     j = 0
     while f"dense.{j}.linear.weight" in weights_bf16:
-        dense.append(DenseSpec(weights_bf16[f"dense.{j}.linear.weight"], _lib.DT_BF16))
+        v = weights_bf16[f"dense.{j}.linear.weight"]
+        dense.append(DenseSpec(v, dt(v)))
         j += 1
     return Model(cfg, body, dense, True, device=device, max_batch_tokens=max_batch_tokens,
                  options=options)

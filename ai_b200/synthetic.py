@@ -118,6 +118,26 @@ def make_weights(cfg: dict = EMBEDDINGGEMMA_300M, seed: int = 0, norm_std: float
     return out
 
 
+def make_weights_f32(cfg: dict = EMBEDDINGGEMMA_300M, seed: int = 0, norm_std: float = 0.0,
+                     head=HEAD_DIMS) -> Dict[str, np.ndarray]:
+    """The same draws as ``make_weights`` kept in float32, not rounded to
+    bfloat16: a checkpoint stored in fp32 (a fine-tuned or re-saved model),
+    whose projections have no exact fp16 form and carry TF32 low parts."""
+    rng = np.random.default_rng(seed)
+    nrng = np.random.default_rng(seed + 1000)
+    out = {}
+    for name, shape, kind in weight_specs(cfg, head):
+        if kind == "w":
+            x = rng.standard_normal(shape, dtype=np.float32)
+            x *= np.float32(0.02)
+        elif norm_std > 0:
+            x = nrng.standard_normal(shape, dtype=np.float32) * np.float32(norm_std)
+        else:
+            x = np.zeros(shape, dtype=np.float32)
+        out[name] = x
+    return out
+
+
 # EmbeddingGemma 2's text tower, shaped as the reference's config test
 # (models/gemma/gemma2_test.go TestConfig2): 12 layers of width 512, layers 5
 # and 11 global with 512-wide heads and one KV head, per-layer inputs of 512,

@@ -25,7 +25,7 @@ from typing import Optional, Sequence
 import torch
 
 from . import _lib
-from ._lib import ACT_GELU, ACT_NONE, ACT_RELU, PREC_SPLIT_TF32, PREC_TF32  # noqa: F401
+from ._lib import ACT_GELU, ACT_NONE, ACT_RELU, PREC_SPLIT, PREC_SPLIT_TF32, PREC_TF32  # noqa: F401
 
 NoAct = ACT_NONE
 ReLUAct = ACT_RELU
@@ -69,7 +69,7 @@ class Fused:
 
 
 def MatMulFused(x: torch.Tensor, w: torch.Tensor, f: Fused = Fused(),
-                precision: int = PREC_SPLIT_TF32) -> torch.Tensor:
+                precision: int = PREC_SPLIT) -> torch.Tensor:
     """epilogue(x · w) for 2-D x [m×k] and w [k×n] (matmul_fused.go:40-96).
 
     ``w`` may be a transposed view of an [n×k] row-major matrix (``W.t()``),
@@ -120,7 +120,7 @@ def MatMulFused(x: torch.Tensor, w: torch.Tensor, f: Fused = Fused(),
     return out
 
 
-def MatMul(x: torch.Tensor, w: torch.Tensor, precision: int = PREC_SPLIT_TF32) -> torch.Tensor:
+def MatMul(x: torch.Tensor, w: torch.Tensor, precision: int = PREC_SPLIT) -> torch.Tensor:
     """x · w for 2-D operands (tensor/matmul.go:19)."""
     return MatMulFused(x, w, Fused(), precision)
 
@@ -180,7 +180,7 @@ def RoPE(x: torch.Tensor, base: float, positions: Sequence[int]) -> torch.Tensor
 def AttentionScaled(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                     key_lengths: Optional[torch.Tensor] = None, window: int = 0,
                     scale: Optional[float] = None,
-                    precision: int = PREC_SPLIT_TF32) -> torch.Tensor:
+                    precision: int = PREC_SPLIT) -> torch.Tensor:
     """softmax(scale·q·kᵀ + mask)·v (attention.go:67) for q [B,Hq,T,D] and
     k, v [B,Hkv,S,D] (grouped-query heads share a KV head, the reference's
     Expand view). The mask is PaddingMask(key_lengths) + WindowMask(window).

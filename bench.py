@@ -6,11 +6,16 @@ Workload: benchmark config 2 — the EmbeddingGemma-300m-shaped encoder with
 random-init weights (seed 0, bf16 widened to fp32) on a batch of 256
 sequences × 512 tokens, all full length, ids from seed 1. A step is one
 forward of that batch (ids → L2-normalised 768-d embeddings) on every GPU,
-plus the NCCL gather of the embeddings onto rank 0 when N > 1. Each GPU is
-an independent replica with its own 256×512 batch (weak scaling, no
-collective on the data path besides that gather).
+plus the NCCL gather of the embeddings onto rank 0 when N > 1. By default
+each GPU is an independent replica with its own 256×512 batch (weak
+scaling, no collective on the data path besides that gather);
+--global-batch G splits one G-sequence batch into contiguous per-GPU
+slices instead (strong scaling: G = 256 is the 8-GPU target point, and
+--batch 32 --seq 2048 --global-batch 32 is config 5).
 
 Usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+       [--precision split|split_tf32|tf32] [--checkpoint bf16|f32] [--global-batch G]
+       [--workload encoder|ragged|eg2|cluster|matmul]
 (N > 1 under torchrun). Rank 0 prints one JSON line.
 
 --impl reference times the reference's CPU path on this host: the Go
@@ -22,6 +27,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -62,6 +68,23 @@ def peaks():
         return {"hbm_gbs": d["hbm_gbs"], "bf16": d["bf16_tflops"],
                 "bf16_sustained": d["bf16_tflops_sustained"], "source": "measured"}
     return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
+
+
+def host_cpu() -> dict:
+    """Host CPU model name and core counts (lscpu), for the CPU baseline."""
+    info = {"model_name": None, "cpus": os.cpu_count()}
+    try:
+        out = subprocess.run(["lscpu"], capture_output=True, text=True, timeout=10).stdout
+        for line in out.splitlines():
+            k, _, v = line.partition(":")
+            k, v = k.strip(), v.strip()
+            if k == "Model name":
+                info["model_name"] = v
+            elif k in ("Core(s) per socket", "Socket(s)", "Thread(s) per core"):
+                info[k.lower().replace("(s)", "s").replace(" ", "_")] = int(v)
+    except (OSError, ValueError, subprocess.SubprocessError):
+        pass
+    return info
 
 
 class ClockSampler:
@@ -161,12 +184,26 @@ def run_reference(args, rank, world, cfg):
         "config": {"workload": "config 2: 256 x 512 tokens, all full length (CPU: bounded sample)",
                    "seq_len": SEQ, "parallelism": "host threads"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": sample},
+                         "host_cpu": host_cpu(), "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "Go reference unbuildable here (no Go toolchain on this box or the GPU box); "
                 "timed CPU restatement of its float32 path",
     }
     print(json.dumps(line), flush=True)
+
+
+PREC_NAMES = {"split": "split_fp16", "split_tf32": "split_tf32", "tf32": "tf32"}
+
+
+def prec_code(gemma, name: str) -> int:
+    return {"split": gemma.PREC_SPLIT, "split_tf32": gemma.PREC_SPLIT_TF32, "tf32": gemma.PREC_TF32}[name]
+
+
+def rank_slice(total: int, world: int, rank: int):
+    """Contiguous [start, stop) of `total` sequences for `rank`, sizes within one."""
+    base, extra = divmod(total, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
 
 
 def run_ours(args, rank, local_rank, world, cfg):
@@ -183,25 +220,47 @@ def run_ours(args, rank, local_rank, world, cfg):
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
-    prec = gemma.PREC_TF32 if args.precision == "tf32" else gemma.PREC_SPLIT_TF32
-    w = S.make_weights(cfg, seed=0, norm_std=args.norm_std)
+    prec = prec_code(gemma, args.precision)
+    if args.checkpoint == "f32":
+        w = S.make_weights_f32(cfg, seed=0, norm_std=args.norm_std)
+    else:
+        w = S.make_weights(cfg, seed=0, norm_std=args.norm_std)
     opts = [gemma.WeightsBF16()] if args.weights == "bf16" else []
-    model = gemma.from_synthetic(cfg, w, device=local_rank, max_batch_tokens=BATCH * SEQ, options=opts)
+    strong = args.global_batch is not None
+    if strong:
+        # the fixed global batch (ids seed 1) cut into contiguous per-rank slices
+        lo, hi = rank_slice(args.global_batch, world, rank)
+        ids_np = S.make_ids(args.global_batch, SEQ, 1)[lo:hi]
+        if world > 1 and args.global_batch % world != 0:
+            raise SystemExit("--global-batch must be a multiple of the number of GPUs")
+    else:
+        # replicas: each rank embeds its own batch
+        ids_np = S.make_ids(BATCH, SEQ, 1 if rank == 0 else 1000 + rank)
+    nb = ids_np.shape[0]
+    model = gemma.from_synthetic(cfg, w, device=local_rank, max_batch_tokens=nb * SEQ, options=opts)
     dim = model.Dim()
-    ids_np = S.make_ids(BATCH, SEQ, 1 if rank == 0 else 1000 + rank)
-    len_np = np.full(BATCH, SEQ, np.int32)
+    len_np = np.full(nb, SEQ, np.int32)
     d_ids = torch.from_numpy(ids_np).to(dev)
     d_len = torch.from_numpy(len_np).to(dev)
-    out = torch.empty((BATCH, dim), dtype=torch.float32, device=dev)
-    # replicas: each rank embeds its own batch; the embeddings meet on rank 0
-    # in one NCCL gather per step (the collective the multi-GPU path has)
+    out = torch.empty((nb, dim), dtype=torch.float32, device=dev)
+    # the embeddings meet on rank 0 in one NCCL gather per step (the only
+    # collective of the multi-GPU path)
     gathered = [torch.empty_like(out) for _ in range(world)] if (world > 1 and rank == 0) else None
     stream = torch.cuda.current_stream(dev)
+    ev = []  # per timed step: (forward start, forward end, gather end)
 
-    def step():
-        model.embed_device(d_ids, d_len, BATCH, SEQ, dim, out, stream, prec)
+    def step(record=False):
+        if record:
+            e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            e[0].record(stream)
+        model.embed_device(d_ids, d_len, nb, SEQ, dim, out, stream, prec)
+        if record:
+            e[1].record(stream)
         if world > 1:
             dist.gather(out, gathered, dst=0)
+        if record:
+            e[2].record(stream)
+            ev.append(e)
 
     def sync_all():
         torch.cuda.synchronize(dev)
@@ -214,7 +273,7 @@ def run_ours(args, rank, local_rank, world, cfg):
     model.check()
     model.read_profile()  # discard warm-up counts
 
-    # ---- device-timed value (inputs resident in HBM)
+    # ---- device-timed value (inputs resident in HBM): exactly K steps
     sampler = ClockSampler(list(range(world)) if rank == 0 else [])
     sync_all()
     if rank == 0:
@@ -226,26 +285,52 @@ def run_ours(args, rank, local_rank, world, cfg):
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
-        step()
+        step(record=True)
     e1.record(stream)
     sync_all()
     ms = e0.elapsed_time(e1)
     model.set_profiling(False)
     prof = model.read_profile()
-    clocks = sampler.stop() if rank == 0 else None
-    model.check()
+    fwd_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / len(ev)
+    gather_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / len(ev)
     t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    per_rank = torch.tensor([fwd_ms, gather_ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        parts = [torch.zeros_like(per_rank) for _ in range(world)]
+        dist.all_gather(parts, per_rank)
+        per_rank_all = [[round(float(x), 3) for x in q.tolist()] for q in parts]
+    else:
+        per_rank_all = [[round(fwd_ms, 3), round(gather_ms, 3)]]
     ms_max = float(t.item())
     per_step_s = ms_max / 1e3 / args.steps
-    value = world * BATCH / per_step_s
+    total_seqs = args.global_batch if strong else world * BATCH
+    value = total_seqs / per_step_s
+
+    # ---- five windows of at least 1 s each (3 warm-ups above), median
+    win_steps = max(args.steps, int(math.ceil(1.0 / per_step_s)))
+    windows = []
+    for _ in range(args.windows):
+        sync_all()
+        a0 = torch.cuda.Event(enable_timing=True)
+        a1 = torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        for _ in range(win_steps):
+            step()
+        a1.record(stream)
+        sync_all()
+        tw = torch.tensor([a0.elapsed_time(a1)], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(tw, op=dist.ReduceOp.MAX)
+        windows.append(total_seqs * win_steps / (float(tw.item()) / 1e3))
+    clocks = sampler.stop() if rank == 0 else None
+    model.check()
 
     # ---- end to end through the public host API (pinned host buffers)
     ids_pin = torch.from_numpy(ids_np).pin_memory().numpy()
     len_pin = torch.from_numpy(len_np).pin_memory().numpy()
-    out_pin = torch.empty((BATCH, dim), dtype=torch.float32).pin_memory().numpy()
-    host_res = torch.empty((BATCH, dim), dtype=torch.float32, device=dev)
+    out_pin = torch.empty((nb, dim), dtype=torch.float32).pin_memory().numpy()
+    host_res = torch.empty((nb, dim), dtype=torch.float32, device=dev)
     g2 = [torch.empty_like(host_res) for _ in range(world)] if (world > 1 and rank == 0) else None
 
     def e2e_step():
@@ -266,7 +351,7 @@ def run_ours(args, rank, local_rank, world, cfg):
     te = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_value = world * BATCH * args.steps / float(te.item())
+    e2e_value = total_seqs * args.steps / float(te.item())
 
     # ---- roofline of the dominant kernel family (the tcgen05 GEMM)
     pk = peaks()
@@ -274,42 +359,39 @@ def run_ours(args, rank, local_rank, world, cfg):
     gemm_phases = ["gemm_qkv", "gemm_o", "gemm_gate_up", "gemm_down"]
     gemm_ms = sum(prof[p]["ms"] for p in gemm_phases)
     gemm_launches = sum(prof[p]["launches"] for p in gemm_phases)
-    gemm_flops = linear * BATCH * args.steps
+    gemm_flops = linear * nb * args.steps
     tf32_peak = pk["bf16_sustained"] / 2.0
     achieved = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else None
-    passes = 1 if prec == gemma.PREC_TF32 else 2
-    # split-fp16 on all four encoder GEMMs (bf16 weights; non-zero norm
-    # gains go on A), unless switched off
-    h16 = prec == gemma.PREC_SPLIT_TF32 and os.environ.get("FG_GEMM_H16", "1") != "0"
+    # split-fp16 runs where the projections have an exact fp16 form (a bf16
+    # checkpoint; non-zero norm gains go on A); an fp32 checkpoint has none
+    h16 = prec == gemma.PREC_SPLIT and args.checkpoint == "bf16"
+    if h16:
+        arith, passes = "split_fp16", 2
+    elif prec == gemma.PREC_TF32:
+        arith, passes = "tf32", 1
+    else:
+        lo_b = args.checkpoint == "f32" or args.norm_std > 0
+        arith, passes = "split_tf32", (3 if lo_b else 2)
     traffic = None
     tp = ROOT / "profiles" / "gemm_traffic.json"
-    if tp.exists():
+    if tp.exists() and h16:
         traffic = json.loads(tp.read_text()).get("bytes_per_launch")
-    if h16:
-        peak = pk["bf16_sustained"]
-        roofline = {
-            "bound": "tensor",
-            "kernel": "gemm_pair_kernel (tcgen05 cta_group::2 kind::f16 split-fp16, all encoder projections)",
-            "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-            "frac": achieved / peak if achieved else None, "traffic": traffic,
-            "peak_source": f"{pk['source']} bf16 sustained {pk['bf16_sustained']} TFLOP/s "
-                           "(dense fp16 runs at the bf16 rate)",
-            "issued_mma_passes": passes,
-            "issued_frac": (achieved * passes / peak) if achieved else None,
-            "frac_of_tf32_peak": achieved / tf32_peak if achieved else None,
-            "launches": gemm_launches,
-        }
-    else:
-        roofline = {
-            "bound": "tensor", "kernel": "gemm_pair_kernel (tcgen05 cta_group::2 split-TF32, all encoder projections)",
-            "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s",
-            "frac": achieved / tf32_peak if achieved else None, "traffic": traffic,
-            "peak_source": f"{pk['source']} bf16 sustained {pk['bf16_sustained']} TFLOP/s / 2 "
-                           "(dense TF32 runs at half the bf16 rate)",
-            "issued_mma_passes": passes,
-            "issued_frac": (achieved * passes / tf32_peak) if achieved else None,
-            "launches": gemm_launches,
-        }
+    peak = pk["bf16_sustained"] if h16 else tf32_peak
+    roofline = {
+        "bound": "tensor",
+        "kernel": ("gemm_pair_kernel (tcgen05 cta_group::2 kind::f16 split-fp16, all encoder projections)" if h16 else
+                   f"gemm_pair_kernel (tcgen05 cta_group::2 kind::tf32 {arith}, all encoder projections)"),
+        "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+        "frac": achieved / peak if achieved else None, "traffic": traffic,
+        "traffic_source": ("profiles/gemm_traffic.json: ncu dram bytes of the four encoder GEMMs at batch 64, "
+                           "scaled x4 to a 256-sequence launch (traffic grows with M)") if traffic else None,
+        "peak_source": (f"{pk['source']} bf16 sustained {pk['bf16_sustained']} TFLOP/s "
+                        + ("(dense fp16 runs at the bf16 rate)" if h16 else "/ 2 (dense TF32 runs at half the bf16 rate)")),
+        "issued_mma_passes": passes,
+        "issued_frac": (achieved * passes / peak) if achieved else None,
+        "frac_of_tf32_peak": achieved / tf32_peak if achieved else None,
+        "launches": gemm_launches,
+    }
     phases = {p: round(v["ms"] / args.steps, 3) for p, v in prof.items()}
     attn_ms = prof["attention"]["ms"]
     launches_total = sum(v["launches"] for v in prof.values())
@@ -318,35 +400,51 @@ def run_ours(args, rank, local_rank, world, cfg):
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             threads = os.cpu_count() or 1
-            w32 = f32_weights(w)
+            w32 = w if args.checkpoint == "f32" else f32_weights(w)
             ids_s = ids_np[:CPU_SAMPLE_SEQS]
             secs = cpu_time_sample(cfg, w32, ids_s, len_np[:CPU_SAMPLE_SEQS], threads)
             cpu = {"value": CPU_SAMPLE_SEQS / secs, "unit": UNIT, "cores": threads, "kind": "port",
-                   "sample": f"{CPU_SAMPLE_SEQS} sequences x {SEQ} tokens of config 2, oracle "
-                             "float32 mode (the reference's arithmetic), one pass"}
+                   "host_cpu": host_cpu(),
+                   "sample": f"{CPU_SAMPLE_SEQS} sequences x {SEQ} tokens of the same workload, oracle "
+                             "float32 mode (the reference's arithmetic, packed AVX-512 GEMM), one pass; "
+                             "CPU restatement, not the reference binary"}
+        if strong:
+            workload = (f"global batch {args.global_batch} sequences x {SEQ} tokens, all full length, "
+                        f"split over {world} GPU(s): {nb} per GPU")
+        else:
+            workload = f"config 2: {BATCH} sequences x {SEQ} tokens per GPU, all full length"
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic: random-init EmbeddingGemma-300m-shaped weights (seed 0, bf16 "
-                    "widened to fp32), ids uniform in [3, 262144) seed 1, BOS first",
-            "config": {"workload": "config 2: 256 sequences x 512 tokens per GPU, all full length",
-                       "global_batch": BATCH * world, "seq_len": SEQ,
-                       "parallelism": f"replicas x{world} + NCCL gather of embeddings onto rank 0" if world > 1 else "single GPU",
-                       "precision": args.precision,
-                       "gemm_arithmetic": ("split-fp16: A as two fp16 parts under a power-of-two row scale, "
-                                           "bf16-exact weights as exact fp16" if h16 else
-                                           "split-TF32" if prec == gemma.PREC_SPLIT_TF32 else "TF32"),
+            "higher_is_better": True, "scaling": "strong" if strong else "weak", "vs_baseline": None,
+            "dtype": "f32",
+            "data": ("synthetic: random-init EmbeddingGemma-300m-shaped weights (seed 0, "
+                     + ("fp32, not bf16-exact" if args.checkpoint == "f32" else "bf16 widened to fp32")
+                     + "), ids uniform in [3, 262144) seed 1, BOS first"),
+            "config": {"workload": workload,
+                       "global_batch": total_seqs, "seq_len": SEQ,
+                       "parallelism": (f"{world} GPUs, contiguous slices of the batch + NCCL gather of "
+                                       "embeddings onto rank 0" if strong else
+                                       f"replicas x{world} + NCCL gather of embeddings onto rank 0")
+                       if world > 1 else "single GPU",
+                       "precision": arith,
+                       "precision_requested": args.precision,
+                       "checkpoint": args.checkpoint,
                        "weights_resident": args.weights,
                        "norm_std": args.norm_std,
                        "weight_bytes": model.weight_bytes(),
-                       "l2_flush": "none: inputs larger than L2 (weights 1.2 GB, activations > 4 GB per step)"},
+                       "l2_flush": "none: inputs larger than L2 (weights 0.7-1.2 GB, activations > 1 GB per step)"},
             "tokens_per_s": value * SEQ,
-            "attention_tflops": (attn * BATCH * args.steps / (attn_ms / 1e3) / 1e12) if attn_ms else None,
+            "windows": {"steps_per_window": win_steps, "values": [round(v, 1) for v in windows],
+                        "median": statistics.median(windows) if windows else None,
+                        "rule": "3+ warm-ups, windows of >= 1 s, median of 5 (device time, max over ranks)"},
+            "per_rank_ms": {"forward_and_gather": per_rank_all,
+                            "note": "per GPU: [forward ms, gather ms] per step, CUDA events on the step's stream"},
+            "attention_tflops": (attn * nb * args.steps / (attn_ms / 1e3) / 1e12) if attn_ms else None,
             "clocks": clocks,
             "e2e": {"value": e2e_value, "unit": UNIT,
                     "h2d_bytes_per_step": int(ids_np.nbytes + len_np.nbytes),
-                    "d2h_bytes_per_step": int(BATCH * dim * 4)},
+                    "d2h_bytes_per_step": int(nb * dim * 4)},
             "gpu_launches": int(launches_total),
             "roofline": roofline,
             "phases_ms_per_step": phases,
@@ -380,7 +478,7 @@ def run_ragged(args, rank, local_rank, world, cfg):
         import datetime
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-    prec = gemma.PREC_TF32 if args.precision == "tf32" else gemma.PREC_SPLIT_TF32
+    prec = prec_code(gemma, args.precision)
     budget = 131072
     w = S.make_weights(cfg, seed=0)
     model = gemma.from_synthetic(cfg, w, device=local_rank, max_batch_tokens=budget,
@@ -601,13 +699,99 @@ def run_cluster(args):
     print(json.dumps(line))
 
 
+MATMUL_MS = [128, 1024, 8192, 65536]
+MATMUL_KN = [(768, 768), (768, 1152), (768, 2304), (768, 3072), (1152, 768)]
+
+
+def run_matmul(args):
+    """--workload matmul: benchmark config 4, the standalone tensor.MatMul
+    sweep (tensor/matmul.go:19-72) through fg_matmul on one GPU: M ∈ {128,
+    1024, 8192, 65536} × (K, N) ∈ {768} × {768, 1152, 2304, 3072} plus
+    (1152, 768), as A·B and as A·Wᵀ (transposed view, no copy), in split
+    precision (fp32-level) and plain TF32. N(0, 1) entries from seed 3.
+    Each call (operand split / packing included) is timed with CUDA events
+    on its stream, L2 flushed (a 256 MB write) before every timed call."""
+    import torch
+
+    from ai_b200 import tensor as T
+
+    dev = torch.device("cuda:0")
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(64 << 20, dtype=torch.float32, device=dev)  # 256 MB > L2
+    pk = peaks()
+    tf32_peak = pk["bf16_sustained"] / 2.0
+    reps = max(args.steps, 3)
+    rows = []
+    tot = {"split": [0.0, 0.0], "tf32": [0.0, 0.0]}
+    clocks = ClockSampler([0])
+    clocks.start()
+    g = torch.Generator(device=dev).manual_seed(3)
+    for m in MATMUL_MS:
+        for k, n in MATMUL_KN:
+            a = torch.randn(m, k, generator=g, device=dev)
+            w_kn = torch.randn(k, n, generator=g, device=dev)
+            w_nk = torch.randn(n, k, generator=g, device=dev)
+            for form, w in (("A.B", w_kn), ("A.Wt", w_nk.t())):
+                for prec_name, prec in (("split", T.PREC_SPLIT), ("tf32", T.PREC_TF32)):
+                    for _ in range(max(args.warmup, 2)):
+                        T.MatMul(a, w, precision=prec)
+                    ms = 0.0
+                    for _ in range(reps):
+                        flush.zero_()
+                        e0 = torch.cuda.Event(enable_timing=True)
+                        e1 = torch.cuda.Event(enable_timing=True)
+                        e0.record(stream)
+                        T.MatMul(a, w, precision=prec)
+                        e1.record(stream)
+                        torch.cuda.synchronize()
+                        ms += e0.elapsed_time(e1)
+                    ms /= reps
+                    flops = 2.0 * m * n * k
+                    tf = flops / (ms / 1e3) / 1e12
+                    tot[prec_name][0] += flops * reps
+                    tot[prec_name][1] += ms * reps / 1e3
+                    rows.append({"m": m, "k": k, "n": n, "form": form, "precision": prec_name,
+                                 "ms": round(ms, 4), "tflops": round(tf, 2),
+                                 "frac_of_tf32_peak": round(tf / tf32_peak, 4)})
+    clk = clocks.stop()
+    agg = {p: (f / t / 1e12 if t else None) for p, (f, t) in tot.items()}
+    big = [r for r in rows if r["m"] == 65536 and r["n"] == 3072 and r["precision"] == "split"]
+    top = max(big, key=lambda r: r["tflops"])
+    line = {
+        "metric": "tensor.MatMul fp32 sweep TFLOP/s (config 4), 1 B200", "value": agg["split"],
+        "unit": "TFLOP/s", "n_gpus": 1, "steps": reps, "warmup": max(args.warmup, 2),
+        "ms_per_step": None, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic: N(0, 1) entries, torch generator seed 3",
+        "config": {"workload": "config 4: M in {128,1024,8192,65536} x (K,N) in {768}x{768,1152,2304,3072} "
+                               "+ (1152,768), A.B and A.Wt, split and plain TF32",
+                   "l2_flush": "256 MB write before every timed call"},
+        "aggregate_tflops": agg,
+        "roofline": {"bound": "tensor", "kernel": "fg_matmul split (operand split + gemm_pair_kernel), "
+                     f"M=65536 K=768 N=3072 {top['form']}", "achieved": top["tflops"], "peak": tf32_peak,
+                     "unit": "TFLOP/s", "frac": top["tflops"] / tf32_peak, "traffic": None,
+                     "peak_source": f"{pk['source']} bf16 sustained / 2 (dense TF32)"},
+        "shapes": rows,
+        "clocks": clk,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--precision", choices=["split_tf32", "tf32"], default="split_tf32")
+    ap.add_argument("--precision", choices=["split", "split_tf32", "tf32"], default="split",
+                    help="split (default): fp32-level, split-fp16 products where the weights have an exact "
+                         "fp16 form, else split-TF32; split_tf32: every product split-TF32; tf32: one pass")
+    ap.add_argument("--checkpoint", choices=["bf16", "f32"], default="bf16",
+                    help="bf16 (the spec: random-init weights rounded to bf16) or f32 (the same draws kept "
+                         "in fp32: no exact fp16 form, TF32 low parts on every projection)")
+    ap.add_argument("--global-batch", type=int, default=None,
+                    help="strong scaling: this many sequences in total, split over the GPUs (default: "
+                         "weak scaling, --batch sequences per GPU)")
+    ap.add_argument("--windows", type=int, default=5, help="timing windows of >= 1 s after the K steps")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--norm-std", type=float, default=0.0,
                     help="RMSNorm weights ~N(0, s^2) instead of the spec's zeros (checkpoint-like: the "
@@ -617,12 +801,16 @@ def main():
     ap.add_argument("--batch", type=int, default=BATCH,
                     help="sequences per GPU (default 256; smaller only for profiling runs)")
     ap.add_argument("--seq", type=int, default=SEQ, help="tokens per sequence (default 512)")
-    ap.add_argument("--workload", choices=["encoder", "ragged", "cluster", "eg2"], default="encoder",
+    ap.add_argument("--workload", choices=["encoder", "ragged", "cluster", "eg2", "matmul"], default="encoder",
                     help="encoder (config 2, the headline, default), ragged (config 3 end to end), "
-                         "cluster (Nearest / KMeans on one GPU) or eg2 (EmbeddingGemma 2 text tower)")
+                         "cluster (Nearest / KMeans on one GPU), eg2 (EmbeddingGemma 2 text tower) or "
+                         "matmul (config 4, the tensor.MatMul sweep)")
     args = ap.parse_args()
     if args.workload == "cluster":
         run_cluster(args)
+        return
+    if args.workload == "matmul":
+        run_matmul(args)
         return
     if args.workload == "eg2":
         globals().update(BATCH=args.batch, SEQ=args.seq)

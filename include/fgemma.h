@@ -42,12 +42,17 @@ extern "C" {
 #define FG_ENODEV (-6)   /* no usable sm_100 device */
 
 /* ---- arithmetic modes -------------------------------------------------- */
-/* FG_PREC_SPLIT_TF32: fp32-level products (default). The model's encoder
- * GEMMs run it as split-fp16 (A as two fp16 parts under a power-of-two row
- * scale, bf16 weights as exact fp16, 2 fp16 passes) on SM pairs; other
- * products as split TF32 (up to 3 TF32 passes). */
-#define FG_PREC_SPLIT_TF32 0
-#define FG_PREC_TF32 1       /* one TF32 pass per product */
+/* FG_PREC_SPLIT (default): fp32-level products, the arithmetic chosen per
+ * product. The model's encoder GEMMs run split-fp16 (A as two fp16 parts
+ * under a power-of-two row scale, bf16-exact weights as exact fp16 under a
+ * power-of-two scale, 2 fp16 passes on SM pairs) where the weights have an
+ * exact fp16 form, else split TF32; other products run split TF32.
+ * FG_PREC_SPLIT_TF32: every product as split TF32 (A·B + A·B_lo + A_lo·B,
+ * up to 3 TF32 passes), the fp32-level mode without fp16 parts.
+ * FG_PREC_TF32: one TF32 pass per product (about 1e-4 relative). */
+#define FG_PREC_SPLIT 0
+#define FG_PREC_TF32 1
+#define FG_PREC_SPLIT_TF32 2
 
 /* ---- activations: blas.Activation, internal/blas/gemm.go:270-274 -------- */
 #define FG_ACT_NONE 0
@@ -127,6 +132,13 @@ int fg_memcpy_d2h(int device, void* dst, const void* src, int64_t bytes);
 /* Waits for all work on `device`; returns FG_ETIMEOUT (and clears the
  * record) when a kernel's bounded wait gave up since the last check. */
 int fg_synchronize(int device);
+/* Limit, in nanoseconds, of every pipeline wait (mbarrier) inside the
+ * library's kernels on `device`; 0 restores the default of 2 s. A wait that
+ * runs out makes its kernel drain its own copies and MMAs, free its tensor
+ * memory and return, and the next fg_synchronize / fg_model_check reports
+ * FG_ETIMEOUT. Synchronises the device. No counterpart in the reference
+ * (its CPU kernels never wait on hardware). */
+int fg_set_wait_limit(int device, int64_t nanoseconds);
 
 /* ---- model: gemma.Load + (*Model).embedBatch ---------------------------- */
 /* Creates an empty model on `device` for the given configuration.
@@ -251,12 +263,18 @@ int fg_matmul(int64_t m, int64_t n, int64_t k, const float* x, int64_t ldx, cons
  * the splitting/packing scratch lives in a fixed 32 MiB device array owned
  * by the library (held by every GPU that loads it, until exit), so calls
  * whose scratch would exceed 32 MiB — 4·(2·m·k' + 3·n·k') bytes in the worst
- * case, k' = k rounded up to 4 — are refused with FG_EINVAL. The first call
- * on a device looks up the array's device address (cudaGetSymbolAddress)
- * and should come before any stream capture. All calls share the array:
- * calls that overlap on the GPU race on it and must be serialised by the
- * caller. Allocates nothing: no cudaMalloc, cudaFree or allocating library
- * routine. */
+ * case, k' = k rounded up to 4 — are refused with FG_EINVAL. The call itself
+ * allocates nothing (no cudaMalloc, cudaFree or allocating library routine),
+ * but the CUDA driver reserves the array when it loads the module holding
+ * it: at the first call on a device under lazy module loading (the CUDA 12
+ * default), or at context creation with CUDA_MODULE_LOADING=EAGER. A caller
+ * whose allocator reserves the GPU's memory up front should make one call
+ * (or set eager loading) before reserving. The first call on a device also
+ * looks up the array's device address (cudaGetSymbolAddress) and should
+ * come before any stream capture. All calls share the array: calls that
+ * overlap on the GPU race on it and must be serialised by the caller. A
+ * bounded wait that gave up inside its kernels is reported by the next
+ * fg_synchronize on that device (FG_ETIMEOUT), as for fg_matmul. */
 int fg_matmul_noalloc(int64_t m, int64_t n, int64_t k, const float* x, int64_t ldx,
                       const float* w, int64_t ldw, int w_transposed, float* out, int64_t ldo,
                       const fg_epilogue* epi, int precision, void* stream);

@@ -7,6 +7,9 @@ depend on size, plus the float64 oracle on sampled sequences:
 - config 3 (8192 ragged sequences, lengths 16..2048, through the batching
   of Model.embed_ids): unit norms, and the shortest, a middle and the
   longest sequence match the oracle.
+- config 2 in the other modes: split-TF32 everywhere meets the bar, plain
+  TF32 is reported; an fp32 checkpoint (no exact fp16 forms, split-TF32
+  with stored weight low parts) meets the bar.
 - config 5 (32 x 2048): a 2048-token sequence matches the oracle; two runs
   are bitwise equal.
 - config 4 (MatMul sweep, M = 65536): split-TF32 against a float64 product
@@ -69,6 +72,59 @@ def test_config2_full_batch_properties(full):
         c, m = _cmp(e1[k], _oracle(orc, ids[k]))
         print(f"config 2 seq {k}: cos {c:.9f} maxabs {m:.2e}")
         assert c >= COS_MIN and m <= MAXABS
+
+
+def test_config2_precision_modes(full):
+    """The north star's named modes on config-2 sequences: split-TF32 for
+    every product (PREC_SPLIT_TF32) meets the bar against the float64
+    oracle; plain TF32 is reported (cosine and max-abs printed) and held
+    only to a TF32-sized bound."""
+    from ai_b200 import gemma
+    from ai_b200 import synthetic as S
+
+    model, orc = full
+    ids = S.make_ids(256, 512, 1)[:4]
+    lengths = np.full(4, 512, np.int32)
+    want = np.stack([_oracle(orc, ids[k]) for k in (0, 3)])
+    st = model.embed_padded(ids, lengths, precision=gemma.PREC_SPLIT_TF32)[[0, 3]]
+    c, m = _cmp(st, want)
+    print(f"config 2 split-TF32: cos {c:.9f} maxabs {m:.2e}")
+    assert c >= COS_MIN and m <= MAXABS
+    pt = model.embed_padded(ids, lengths, precision=gemma.PREC_TF32)[[0, 3]]
+    c, m = _cmp(pt, want)
+    print(f"config 2 plain TF32: cos {c:.9f} maxabs {m:.2e}")
+    assert c >= 0.9999 and m <= 2e-3
+
+
+def test_config2_fp32_checkpoint():
+    """A checkpoint stored in fp32 (weights not bf16-exact, norm gains
+    non-zero): no projection has an exact fp16 form, so every encoder GEMM
+    takes split-TF32 with the weights' stored low parts (the general path
+    of safetensors/convert.go:31-38 → models/gemma/model.go:206-222). The
+    full config-2 batch: bitwise repeatable, unit norms; sampled sequences
+    match the float64 oracle on the same fp32 weights."""
+    from ai_b200 import gemma
+    from ai_b200 import synthetic as S
+    from oracle import oracle as O
+
+    cfg = dict(S.EMBEDDINGGEMMA_300M)
+    w = S.make_weights_f32(cfg, seed=0, norm_std=0.1)
+    model = gemma.from_synthetic(cfg, w, device=0, max_batch_tokens=256 * 512)
+    try:
+        ids = S.make_ids(256, 512, 1)
+        lengths = np.full(256, 512, np.int32)
+        e1 = model.embed_padded(ids, lengths)
+        e2 = model.embed_padded(ids, lengths)
+        assert np.array_equal(e1, e2)
+        assert np.allclose(np.linalg.norm(e1.astype(np.float64), axis=1), 1.0, atol=1e-5)
+        orc = O.OracleModel(cfg, w)
+        for k in (0, 200):
+            want = orc.embed_padded(ids[k:k + 1], lengths[k:k + 1], mode=O.F64)[0]
+            c, m = _cmp(e1[k], want)
+            print(f"fp32 checkpoint seq {k}: cos {c:.9f} maxabs {m:.2e}")
+            assert c >= COS_MIN and m <= MAXABS
+    finally:
+        model.close()
 
 
 def test_config3_ragged_full_set(full):

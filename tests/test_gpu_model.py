@@ -170,21 +170,19 @@ def test_embedding_table_bf16_residency(small, monkeypatch):
     assert not np.array_equal(got, base)
 
 
-@pytest.mark.parametrize("h16", ["0", "1"])
 @pytest.mark.parametrize("norm_std", [0.0, 0.1])
-def test_bf16_resident_projections_are_bitwise_identical(norm_std, h16, monkeypatch):
-    """gemma.WeightsBF16(): projections resident as bf16, widened, gain-folded
-    and split per layer on the device, give the same embeddings bit for bit
-    as the fp32-resident weights, in split precision and plain TF32, with
-    zero norm weights (folded weights bf16-exact, no low parts) and non-zero
-    ones (folded weights with low parts); the weights take fewer device
-    bytes. With split-fp16 (FG_GEMM_H16 on) the projections that have an
-    exact fp16 form stay resident in it and are read by the GEMM as they
-    are (plain TF32 widens them); with it off, all are bf16 and widened."""
+def test_bf16_resident_projections_are_bitwise_identical(norm_std):
+    """gemma.WeightsBF16(): projections resident in 2 bytes per value,
+    widened, gain-folded and split per layer on the device where a product
+    needs fp32, give the same embeddings bit for bit as the fp32-resident
+    weights, in all three precisions, with zero norm weights (folded weights
+    bf16-exact, no low parts) and non-zero ones (folded weights with low
+    parts); the weights take fewer device bytes. Projections with an exact
+    fp16 form stay resident in it: the split-fp16 products (PREC_SPLIT) read
+    it as it is, split-TF32 and plain TF32 widen it."""
     from ai_b200 import _lib, gemma
     from ai_b200 import synthetic as S
 
-    monkeypatch.setenv("FG_GEMM_H16", h16)
     cfg = S.small_config(layers=3, vocab=2048)
     w = S.make_weights(cfg, seed=31, norm_std=norm_std)
     ids = S.make_ids(4, 96, 6, cfg["vocab_size"])
@@ -192,7 +190,7 @@ def test_bf16_resident_projections_are_bitwise_identical(norm_std, h16, monkeypa
     m32 = gemma.from_synthetic(cfg, w, device=0, max_batch_tokens=4096)
     m16 = gemma.from_synthetic(cfg, w, device=0, max_batch_tokens=4096, options=[gemma.WeightsBF16()])
     try:
-        for prec in (_lib.PREC_SPLIT_TF32, _lib.PREC_TF32):
+        for prec in (_lib.PREC_SPLIT, _lib.PREC_SPLIT_TF32, _lib.PREC_TF32):
             a = m32.embed_padded(ids, lengths, precision=prec)
             b = m16.embed_padded(ids, lengths, precision=prec)
             assert np.array_equal(a, b), prec
@@ -204,32 +202,8 @@ def test_bf16_resident_projections_are_bitwise_identical(norm_std, h16, monkeypa
         m16.close()
 
 
-def test_stored_low_parts_equal_shared_memory_low_parts(monkeypatch):
-    """FG_GEMM_ALO=global (the producers write A's split-TF32 low parts and
-    the SM-pair GEMM loads them by TMA) computes the same products as the
-    default (the GEMM makes them in shared memory): bitwise equal."""
-    from ai_b200 import gemma
-    from ai_b200 import synthetic as S
-
-    monkeypatch.setenv("FG_GEMM_H16", "0")  # both on the split-TF32 GEMM
-    cfg = S.small_config(layers=3, vocab=2048)
-    w = S.make_weights(cfg, seed=41, norm_std=0.0)
-    ids = S.make_ids(6, 128, 12, cfg["vocab_size"])
-    lengths = np.array([128, 100, 1, 77, 128, 64], np.int32)
-    m1 = gemma.from_synthetic(cfg, w, device=0, max_batch_tokens=4096)
-    monkeypatch.setenv("FG_GEMM_ALO", "global")
-    m2 = gemma.from_synthetic(cfg, w, device=0, max_batch_tokens=4096)
-    try:
-        a, b = m1.embed_padded(ids, lengths), m2.embed_padded(ids, lengths)
-        print(f"stored vs shared-memory low parts: max |diff| {np.abs(a - b).max():.3e}")
-        assert np.array_equal(a, b)
-    finally:
-        m1.close()
-        m2.close()
-
-
 @pytest.mark.parametrize("norm_std", [0.0, 0.1])
-def test_split_fp16_matches_split_tf32(norm_std, monkeypatch):
+def test_split_fp16_matches_split_tf32(norm_std):
     """The split-fp16 encoder GEMMs (bf16-exact weights as exact fp16, A as
     two fp16 parts under a power-of-two row scale) agree with split-TF32 to
     the size of split-TF32's own error, are in use (not bitwise equal) and
@@ -244,10 +218,9 @@ def test_split_fp16_matches_split_tf32(norm_std, monkeypatch):
     ids = S.make_ids(6, 128, 14, cfg["vocab_size"])
     lengths = np.array([128, 100, 1, 77, 128, 64], np.int32)
     m1 = gemma.from_synthetic(cfg, w, device=0, max_batch_tokens=4096)
-    monkeypatch.setenv("FG_GEMM_H16", "0")
-    m2 = gemma.from_synthetic(cfg, w, device=0, max_batch_tokens=4096)
     try:
-        a, b = m1.embed_padded(ids, lengths), m2.embed_padded(ids, lengths)
+        a = m1.embed_padded(ids, lengths)
+        b = m1.embed_padded(ids, lengths, precision=gemma.PREC_SPLIT_TF32)
         d = np.abs(a.astype(np.float64) - b).max()
         print(f"norm_std {norm_std}: split-fp16 vs split-TF32 max |diff| {d:.3e}")
         assert d <= 5e-6
@@ -255,7 +228,6 @@ def test_split_fp16_matches_split_tf32(norm_std, monkeypatch):
         assert np.array_equal(a, m1.embed_padded(ids, lengths))  # repeatable
     finally:
         m1.close()
-        m2.close()
 
 
 def test_batch_invariance(small):

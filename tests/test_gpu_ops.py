@@ -292,33 +292,3 @@ def test_attention_running_max_rescale(cuda):
     want = _naive_attention(q, k, v, None, 0, 1 / 16)
     got = TT.AttentionScaled(_t(q, cuda), _t(k, cuda), _t(v, cuda), None, 0, 1 / 16).cpu().numpy()
     assert np.abs(got - want).max() <= 1e-4, np.abs(got - want).max()
-
-
-def test_attention_tensor_core_matches_simt_head_dim_512(cuda, monkeypatch):
-    from ai_b200 import tensor as TT
-    import torch
-
-    rng = np.random.default_rng(10)
-    q = rng.standard_normal((2, 4, 260, 512), dtype=np.float32)
-    k = rng.standard_normal((2, 2, 260, 512), dtype=np.float32)
-    v = rng.standard_normal((2, 2, 260, 512), dtype=np.float32)
-    lens = torch.tensor([260, 131], dtype=torch.int32)
-    tc = TT.AttentionScaled(_t(q, cuda), _t(k, cuda), _t(v, cuda), lens, 100, 1 / 32).cpu().numpy()
-    monkeypatch.setenv("FG_ATTENTION", "simt")
-    simt = TT.AttentionScaled(_t(q, cuda), _t(k, cuda), _t(v, cuda), lens, 100, 1 / 32).cpu().numpy()
-    assert np.abs(tc - simt).max() <= 1e-4
-
-
-def test_attention_tensor_core_matches_simt(cuda, monkeypatch):
-    from ai_b200 import tensor as TT
-    import torch
-
-    rng = np.random.default_rng(9)
-    q = rng.standard_normal((2, 3, 300, 256), dtype=np.float32)
-    k = rng.standard_normal((2, 1, 300, 256), dtype=np.float32)
-    v = rng.standard_normal((2, 1, 300, 256), dtype=np.float32)
-    lens = torch.tensor([300, 123], dtype=torch.int32)
-    tc = TT.AttentionScaled(_t(q, cuda), _t(k, cuda), _t(v, cuda), lens, 257, 1 / 16).cpu().numpy()
-    monkeypatch.setenv("FG_ATTENTION", "simt")
-    simt = TT.AttentionScaled(_t(q, cuda), _t(k, cuda), _t(v, cuda), lens, 257, 1 / 16).cpu().numpy()
-    assert np.abs(tc - simt).max() <= 1e-4
