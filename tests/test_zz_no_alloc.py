@@ -86,8 +86,11 @@ def test_noalloc_takes_no_device_memory(cuda):
         a, w, rs, epi = _operands(cuda, rng, m, k, n, transposed)
         out = torch.empty((m, n), dtype=torch.float32, device=cuda)
         cases.append((a, w, rs, epi, out, transposed))
-    for a, w, rs, epi, out, transposed in cases:
-        _call(lib.fg_matmul_noalloc, a, w, out, epi, transposed, 0)
+    # first calls: the module holding the array and every kernel these
+    # calls launch are loaded (lazy loading may take device memory for them)
+    for precision in (0, 1):
+        for a, w, rs, epi, out, transposed in cases:
+            _call(lib.fg_matmul_noalloc, a, w, out, epi, transposed, precision)
     torch.cuda.synchronize()
     free0, _ = torch.cuda.mem_get_info()
     for _ in range(3):
