@@ -109,6 +109,10 @@ SIGNATURES = {
     "fg_embed_ids_device": (C.c_int, [_vp, _vp, _vp, C.c_int, C.c_int, C.c_int, C.c_int, _vp, _vp]),
     "fg_embed_many": (C.c_int, [_vp, _vp, _vp, C.c_int, C.c_int, _i64, C.c_int, C.c_int, _vp]),
     "fg_plan_batches": (C.c_int, [_vp, C.c_int, _i64, _vp, _vp]),
+    "fg_embed_many_multi": (C.c_int, [C.POINTER(_vp), C.c_int, _vp, _vp, C.c_int, C.c_int, _i64, C.c_int,
+                                      C.c_int, _vp]),
+    "fg_plan_split": (C.c_int, [_vp, C.c_int, C.c_int, _vp, _vp]),
+    "fg_sequence_cost": (C.c_double, [C.c_int]),
     "fg_model_check": (C.c_int, [_vp]),
     "fg_model_destroy": (None, [_vp]),
     "fg_model_set_profiling": (C.c_int, [_vp, C.c_int]),

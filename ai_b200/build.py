@@ -28,6 +28,7 @@ SOURCES = [
     "fg_ops.cu",
     "fg_model.cu",
     "fg_noalloc.cu",
+    "fg_multi.cu",
     "fg_cluster.cu",
 ]
 

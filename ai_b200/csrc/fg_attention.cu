@@ -12,6 +12,7 @@
 // One CTA: 64 query rows of one head, 256 threads. K/V tiles of 32 keys are
 // staged in shared memory; scores and the P·V update are register-blocked.
 #include <algorithm>
+#include <atomic>
 #include <cfloat>
 
 #include "fg_kernels.cuh"
@@ -258,7 +259,7 @@ template <int DP>
 int launch_attn(const AttnArgs& a, cudaStream_t s) {
   auto kern = attn_simt_kernel<DP>;
   const size_t smem = AttnSmem<DP>::kBytes;
-  static bool set[64] = {false};
+  static std::atomic<bool> set[64];  // per device
   int dev = 0;
   cudaGetDevice(&dev);
   if (!set[dev & 63]) {

@@ -32,6 +32,7 @@
 // never loaded. Masked keys get weight exactly 0, as the reference's
 // flushing exp gives them (internal/kernel/generic.go:283-291).
 #include <algorithm>
+#include <atomic>
 #include <cfloat>
 #include <cudaTypedefs.h>
 
@@ -761,7 +762,7 @@ int attention_tc_operands(const AttnArgs& a, const AttnOperands& o, int* err, cu
     prm.tma_out = 1;
     prm.tma_out_lo = a.out_lo ? 1 : 0;
   }
-  static bool attr[64][2] = {};
+  static std::atomic<bool> attr[64][2];  // per device and head width
   int dev = 0;
   cudaGetDevice(&dev);
   const int wide = Dh == 512 ? 1 : 0;

@@ -24,6 +24,7 @@
 // A_hi·B + A_lo·B in kind::f16 — the same 22 bits of A as split-TF32, exact
 // products, at the fp16 rate (twice TF32's).
 #include <algorithm>
+#include <atomic>
 #include <cstdlib>
 #include <cudaTypedefs.h>
 
@@ -1276,7 +1277,7 @@ int launch_variant(const GemmArgs& g, KParams kp, int* dev_err, cudaStream_t str
   for (CUtensorMap& m : om.m) m = mA;
   FG_TRY(prepare_out_maps(g, kp, &om));
   auto kern = gemm_tf32_kernel<BN, SA, SB, BK, CV>;
-  static bool attr_set[64] = {false};
+  static std::atomic<bool> attr_set[64];  // per device; concurrent host threads may launch
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev & 63]) {
@@ -1307,8 +1308,8 @@ int launch_pair(const GemmArgs& g, KParams kp, int* dev_err, cudaStream_t stream
   kp.ntm = (g.M + 255) / 256;
   kp.h16 = H16 ? 1 : 0;
   auto kern = gemm_pair_kernel<CV, SA, SB, H16>;
-  static bool attr_set[64] = {false};
-  static int max_pairs[64] = {0};
+  static std::atomic<bool> attr_set[64];  // per device; max_pairs is stored before attr_set
+  static std::atomic<int> max_pairs[64];
   int dev = 0;
   cudaGetDevice(&dev);
   cudaLaunchConfig_t cfg = {};
@@ -1332,7 +1333,7 @@ int launch_pair(const GemmArgs& g, KParams kp, int* dev_err, cudaStream_t stream
     attr_set[dev & 63] = true;
   }
   const int ntiles = kp.ntm * kp.ntn;
-  cfg.gridDim = dim3(2 * std::max(1, std::min(ntiles, max_pairs[dev & 63])));
+  cfg.gridDim = dim3(2 * std::max(1, std::min(ntiles, max_pairs[dev & 63].load())));
   FG_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, mA, mAlo, mB, mBlo, om, kp));
   (void)dev_err;
   return FG_OK;

@@ -50,6 +50,10 @@ int register_status_block(int dev, int* block);
 // Sets device `dev`'s pipeline-wait limit in every status block it has.
 int set_wait_limit(int dev, unsigned long long ns);
 
+// The model's sequence cap (fg_config.max_tokens), for callers that split a
+// batch before handing it to fg_embed_many.
+int model_max_tokens(const fg_model* m);
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no
 // libcuda link dependency); resolved once.
 int tensor_map_encoder(PFN_cuTensorMapEncodeTiled_v12000* fn);

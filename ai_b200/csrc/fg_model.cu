@@ -1453,6 +1453,9 @@ int model_dim(const fg_model* m) {
 }
 
 }  // namespace
+
+int model_max_tokens(const fg_model* m) { return m->cfg.max_tokens; }
+
 }  // namespace fg
 
 using namespace fg;

@@ -4,6 +4,8 @@
 #include <mutex>
 #include <vector>
 
+#include <atomic>
+
 #include "fg_internal.h"
 
 namespace fg {
@@ -125,8 +127,8 @@ int set_wait_limit(int dev, unsigned long long ns) {
 }
 
 int tensor_map_encoder(PFN_cuTensorMapEncodeTiled_v12000* fn) {
-  static PFN_cuTensorMapEncodeTiled_v12000 cached = nullptr;
-  if (!cached) {
+  static std::atomic<PFN_cuTensorMapEncodeTiled_v12000> cached{nullptr};
+  if (!cached.load()) {
     void* f = nullptr;
     cudaDriverEntryPointQueryResult q;
     cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q);
@@ -134,9 +136,9 @@ int tensor_map_encoder(PFN_cuTensorMapEncodeTiled_v12000* fn) {
       cudaGetLastError();
       return set_error(FG_ECUDA, "cuTensorMapEncodeTiled entry point unavailable");
     }
-    cached = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    cached.store(reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f));
   }
-  *fn = cached;
+  *fn = cached.load();
   return FG_OK;
 }
 

@@ -446,19 +446,73 @@ class Model:
         n = len(seqs)
         if n == 0:
             return []
-        lens = np.fromiter((len(s) for s in seqs), dtype=np.int64, count=n)
-        offsets = np.zeros(n + 1, dtype=np.int64)
-        np.cumsum(lens, out=offsets[1:])
-        flat = np.zeros(max(int(offsets[-1]), 1), dtype=np.int32)
-        for i, s in enumerate(seqs):
-            if lens[i]:
-                flat[offsets[i]:offsets[i + 1]] = s
+        flat, offsets = _pack(seqs)
         out = np.empty((n, dim), dtype=np.float32)
         _lib.check(_lib.lib().fg_embed_many(self._h, flat.ctypes.data_as(C.c_void_p),
                                             offsets.ctypes.data_as(C.c_void_p), n, int(self.max_tokens),
                                             int(self.batch_tokens), dim, precision,
                                             out.ctypes.data_as(C.c_void_p)))
         return list(out)
+
+
+def _pack(seqs: Sequence[Sequence[int]]):
+    n = len(seqs)
+    lens = np.fromiter((len(s) for s in seqs), dtype=np.int64, count=n)
+    offsets = np.zeros(n + 1, dtype=np.int64)
+    np.cumsum(lens, out=offsets[1:])
+    flat = np.zeros(max(int(offsets[-1]), 1), dtype=np.int32)
+    for i, s in enumerate(seqs):
+        if lens[i]:
+            flat[offsets[i]:offsets[i + 1]] = s
+    return flat, offsets
+
+
+def embed_ids_multi(models: Sequence[Model], seqs: Sequence[Sequence[int]], Dim: Optional[int] = None,
+                    precision: int = PREC_SPLIT) -> np.ndarray:
+    """(*Model).Embed (embed.go:15-80) over several GPUs in one process
+    (fg_embed_many_multi): the length-sorted sequences cut into one
+    cost-balanced contiguous slice per model (one model per GPU, the same
+    weights), each slice embedded on its own host thread, the embeddings
+    returned as [len(seqs), dim] in the caller's order. BatchTokens and the
+    truncation come from models[0]."""
+    if not models:
+        raise GemmaError("gemma: no models")
+    m0 = models[0]
+    dim = m0.Dim()
+    if Dim is not None and Dim != 0:
+        if Dim < 1 or Dim > dim:
+            raise GemmaError(f"gemma: Dim({Dim}) outside 1..{dim}")
+        dim = Dim
+    n = len(seqs)
+    out = np.empty((n, dim), dtype=np.float32)
+    if n == 0:
+        return out
+    flat, offsets = _pack(seqs)
+    hs = (C.c_void_p * len(models))(*[m._h for m in models])
+    _lib.check(_lib.lib().fg_embed_many_multi(hs, len(models), flat.ctypes.data_as(C.c_void_p),
+                                              offsets.ctypes.data_as(C.c_void_p), n, int(m0.max_tokens),
+                                              int(m0.batch_tokens), dim, precision,
+                                              out.ctypes.data_as(C.c_void_p)))
+    return out
+
+
+def plan_split(lengths: Sequence[int], parts: int) -> List[np.ndarray]:
+    """fg_plan_split: each part's sequence indices, contiguous runs of the
+    stable length order cut at equal estimated cost."""
+    n = len(lengths)
+    ln = np.ascontiguousarray(lengths, dtype=np.int32)
+    order = np.zeros(max(n, 1), np.int32)
+    bounds = np.zeros(parts + 1, np.int32)
+    _lib.check(_lib.lib().fg_plan_split(ln.ctypes.data_as(C.c_void_p), n, int(parts),
+                                        order.ctypes.data_as(C.c_void_p), bounds.ctypes.data_as(C.c_void_p)))
+    o = order[:n].astype(np.int64)
+    return [o[bounds[r]:bounds[r + 1]] for r in range(parts)]
+
+
+def sequence_cost(lengths) -> np.ndarray:
+    """fg_sequence_cost of each length (units: one token of a 512-token sequence)."""
+    f = _lib.lib().fg_sequence_cost
+    return np.array([f(int(x)) for x in np.asarray(lengths).ravel()], dtype=np.float64)
 
 
 def plan_batches(lengths: Sequence[int], batch_tokens: int) -> Tuple[List[int], List[List[int]]]:

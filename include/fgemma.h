@@ -205,6 +205,33 @@ int fg_embed_ids(fg_model* m, const int32_t* ids, const int32_t* lengths, int B,
 int fg_embed_many(fg_model* m, const int32_t* ids, const int64_t* offsets, int nseq, int max_tokens,
                   int64_t batch_tokens, int dim, int precision, float* out);
 
+/* (*Model).Embed (models/gemma/embed.go:15-80) over several GPUs of one
+ * process: models[r] (r < nmodels) are models holding the same weights,
+ * normally one per GPU (fg_model_create on device r, the same
+ * fg_model_set_weight calls, fg_model_finalize). The sequences (as for
+ * fg_embed_many, truncated to max_tokens) are stably sorted by length and
+ * cut into nmodels contiguous slices of about equal estimated GPU time
+ * (fg_plan_split); slice r is embedded by fg_embed_many on models[r] on its
+ * own host thread (the calling thread takes slice 0), and every embedding
+ * lands in out [nseq, dim] in the caller's order. No collective is needed:
+ * sequences never interact. Each slice's result is bitwise what
+ * fg_embed_many gives for that slice alone. Synchronous; the first error of
+ * any slice is returned, with the slice's model named in the message. */
+int fg_embed_many_multi(fg_model* const* models, int nmodels, const int32_t* ids, const int64_t* offsets,
+                        int nseq, int max_tokens, int64_t batch_tokens, int dim, int precision, float* out);
+
+/* fg_embed_many_multi's split alone, on the host: lengths [nseq] → order
+ * [nseq] (indices stably sorted by increasing length, as sortIndex,
+ * models/gemma/model.go:412) and bounds [nparts + 1] (slice r is
+ * order[bounds[r] .. bounds[r+1])), cut where the running cost reaches
+ * r/nparts of the total. No counterpart in the reference (it embeds on one
+ * process). */
+int fg_plan_split(const int32_t* lengths, int nseq, int nparts, int32_t* order, int32_t* bounds);
+
+/* The split's estimated GPU time of one sequence of `length` tokens, in
+ * units of one token of a 512-token sequence (length 0 counts as 1). */
+double fg_sequence_cost(int length);
+
 /* fg_embed_many's batching alone, on the host (no device work): lengths
  * [nseq] → order [nseq] (indices stably sorted by length) and batch_end
  * [number of batches ≤ nseq] (each batch's end position in order). Returns

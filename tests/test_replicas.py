@@ -57,7 +57,7 @@ def test_plan_slices_cover_each_sequence_once_in_sorted_runs():
             assert len(sl) == world
             allidx = np.concatenate(sl) if n else np.zeros(0, np.int64)
             assert sorted(allidx.tolist()) == list(range(n))
-            order = np.argsort(-lengths, kind="stable")
+            order = np.argsort(lengths, kind="stable")
             assert np.array_equal(allidx, order)  # contiguous runs of the sorted batch
 
 
