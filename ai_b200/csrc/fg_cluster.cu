@@ -267,8 +267,9 @@ struct GoRand {
   double float64() { return double((uint64() << 11) >> 11) / 9007199254740992.0; }
 };
 
-// Stream-ordered scratch (the stream's memory pool): released after the
-// work queued on the stream before the release.
+// Stream-ordered scratch from the library's per-device pool: released
+// after the work queued on the stream before the release, and kept
+// reserved by the pool for the next call.
 struct DevScratch {
   cudaStream_t s;
   std::vector<void*> ptrs;
@@ -276,16 +277,13 @@ struct DevScratch {
   template <class T>
   int alloc(T** p, size_t count) {
     void* v = nullptr;
-    if (cudaMallocAsync(&v, std::max<size_t>(count, 1) * sizeof(T), s) != cudaSuccess) {
-      cudaGetLastError();
-      return set_error(FG_ENOMEM, "cluster scratch of %zu bytes failed", count * sizeof(T));
-    }
+    FG_TRY(scratch_alloc(&v, std::max<size_t>(count, 1) * sizeof(T), s));
     ptrs.push_back(v);
     *p = static_cast<T*>(v);
     return FG_OK;
   }
   ~DevScratch() {
-    for (void* v : ptrs) cudaFreeAsync(v, s);
+    for (void* v : ptrs) scratch_free(v, s);
   }
 };
 

@@ -54,6 +54,11 @@ int set_wait_limit(int dev, unsigned long long ns);
 // batch before handing it to fg_embed_many.
 int model_max_tokens(const fg_model* m);
 
+// Stream-ordered scratch from the library's per-device pool (kept
+// reserved between calls); freed back to the pool on the same stream.
+int scratch_alloc(void** p, size_t bytes, cudaStream_t s);
+void scratch_free(void* p, cudaStream_t s);
+
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no
 // libcuda link dependency); resolved once.
 int tensor_map_encoder(PFN_cuTensorMapEncodeTiled_v12000* fn);
@@ -138,6 +143,20 @@ int gemm_tn(const GemmArgs& g, int* dev_err, cudaStream_t stream);
 // Whether an M-row product can take the split-fp16 pair kernel (CTA pairs
 // enabled, M >= 256), the only kernel that reads B16 without B.
 bool gemm_h16_applies(int M);
+
+// The op-level product (fg_matmul, fg_matmul_noalloc): its scratch plan
+// and its run on a given scratch pointer of plan.total() bytes (fg_ops.cu).
+struct MatmulPlan {
+  bool a_direct, b_direct, split;
+  int64_t kp, ldb;
+  size_t a_bytes, bt_bytes, blo_bytes;
+  size_t total() const { return a_bytes + bt_bytes + blo_bytes; }
+};
+MatmulPlan plan_matmul(int64_t m, int64_t n, int64_t k, const float* x, int64_t ldx, const float* w,
+                       int64_t ldw, int w_transposed, int precision);
+int matmul_run(const MatmulPlan& p, int64_t m, int64_t n, int64_t k, const float* x, int64_t ldx,
+               const float* w, int64_t ldw, int w_transposed, float* out, int64_t ldo,
+               const fg_epilogue* epi, void* scratch, int* err, cudaStream_t s);
 
 // Elementwise split of n floats into TF32 high and exact low parts.
 // *any_lo_nonzero (device int, optional) is set to 1 when some low part is non-zero.

@@ -81,8 +81,6 @@ int device_pointers(DevicePointers* out) {
   return FG_OK;
 }
 
-size_t round256(size_t v) { return (v + 255) / 256 * 256; }
-
 }  // namespace
 }  // namespace fg
 
@@ -107,80 +105,14 @@ extern "C" int fg_matmul_noalloc(int64_t m, int64_t n, int64_t k, const float* x
   if (epi && ((epi->mul && epi->ldm < n) || (epi->residual && epi->ldr < n)))
     return set_error(FG_EINVAL, "fg_matmul_noalloc: Mul/Residual leading dimension smaller than n");
 
-  // Scratch plan: x split (or re-strided) into [m, kp] parts, w transposed
-  // to [n, kp] when given as [k, n], and w split into [n, kp] parts.
-  const bool split = precision != FG_PREC_TF32;
-  const int64_t kp = (k + 3) / 4 * 4;
-  const bool a_direct = !split && (reinterpret_cast<uintptr_t>(x) & 15) == 0 && ldx % 4 == 0;
-  const bool b_direct = !split && w_transposed && (reinterpret_cast<uintptr_t>(w) & 15) == 0 &&
-                        ldw % 4 == 0;
-  const size_t a_bytes = round256(size_t(m) * kp * 4), b_bytes = round256(size_t(n) * kp * 4);
-  size_t need = 0;
-  if (!a_direct) need += a_bytes * (split ? 2 : 1);
-  if (!w_transposed) need += b_bytes;
-  if (!b_direct) need += b_bytes * (split ? 2 : 1);
-  if (need > kScratchBytes)
+  const MatmulPlan plan = plan_matmul(m, n, k, x, ldx, w, ldw, w_transposed, precision);
+  if (plan.total() > kScratchBytes)
     return set_error(FG_EINVAL,
                      "fg_matmul_noalloc: needs %zu bytes of scratch for m=%lld n=%lld k=%lld, "
                      "more than its fixed %zu-byte array; use fg_matmul",
-                     need, (long long)m, (long long)n, (long long)k, kScratchBytes);
-
+                     plan.total(), (long long)m, (long long)n, (long long)k, kScratchBytes);
   DevicePointers dp;
   FG_TRY(device_pointers(&dp));
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  unsigned char* cur = dp.scratch;
-  auto take = [&](size_t bytes) {
-    float* r = reinterpret_cast<float*>(cur);
-    cur += bytes;
-    return r;
-  };
-
-  GemmEpilogue e;
-  e.out = out;
-  e.ldo = ldo;
-  if (epi) {
-    e.bias = epi->bias;
-    e.rowscale = epi->row_scale;
-    e.act = epi->act;
-    e.mul = epi->mul;
-    e.ldm = epi->ldm;
-    e.residual = epi->residual;
-    e.ldr = epi->ldr;
-  }
-  GemmArgs g;
-  g.M = int(m);
-  g.Nb = int(n);
-  g.K = int(k);
-  if (a_direct) {
-    g.A = x;
-    g.lda = ldx;
-  } else {
-    float* ahi = take(a_bytes);
-    float* alo = split ? take(a_bytes) : nullptr;
-    FG_TRY(split_copy_2d(x, ldx, m, k, ahi, alo, kp, split ? 1 : 0, s));
-    g.A = ahi;
-    g.A_lo = alo;
-    g.lda = kp;
-  }
-  const float* bsrc = w;
-  int64_t ldb_src = ldw;
-  if (!w_transposed) {
-    float* bt = take(b_bytes);
-    FG_TRY(transpose_f32(w, ldw, k, n, bt, kp, s));
-    bsrc = bt;
-    ldb_src = kp;
-  }
-  if (b_direct) {
-    g.B = w;
-    g.ldb = ldw;
-  } else {
-    float* bhi = take(b_bytes);
-    float* blo = split ? take(b_bytes) : nullptr;
-    FG_TRY(split_copy_2d(bsrc, ldb_src, n, k, bhi, blo, kp, split ? 1 : 0, s));
-    g.B = bhi;
-    g.B_lo = blo;
-    g.ldb = kp;
-  }
-  g.epi = e;
-  return gemm_tn(g, dp.err, s);
+  return matmul_run(plan, m, n, k, x, ldx, w, ldw, w_transposed, out, ldo, epi, dp.scratch, dp.err,
+                    static_cast<cudaStream_t>(stream));
 }

@@ -1,6 +1,7 @@
 // Op-level C ABI: the tensor operations the encoder calls, on device
 // pointers. Scratch space for operand splitting and packing is
-// stream-ordered (cudaMallocAsync / cudaFreeAsync on the caller's stream).
+// stream-ordered on the caller's stream, from the library's per-device
+// pool, which keeps it reserved between calls.
 #include <cmath>
 #include <cstdlib>
 #include <string>
@@ -19,18 +20,8 @@ struct StreamScratch {
   cudaStream_t s;
   void* p = nullptr;
   explicit StreamScratch(cudaStream_t st) : s(st) {}
-  int alloc(size_t bytes) {
-    if (bytes == 0) return FG_OK;
-    if (cudaMallocAsync(&p, bytes, s) != cudaSuccess) {
-      cudaGetLastError();
-      p = nullptr;
-      return set_error(FG_ENOMEM, "scratch allocation of %zu bytes failed", bytes);
-    }
-    return FG_OK;
-  }
-  ~StreamScratch() {
-    if (p) cudaFreeAsync(p, s);
-  }
+  int alloc(size_t bytes) { return scratch_alloc(&p, bytes, s); }
+  ~StreamScratch() { scratch_free(p, s); }
 };
 
 // cos/sin tables [T, D/2] in float64, stored as float32 (tensor/rope.go:36-50).
@@ -56,6 +47,98 @@ void rope_tables(double base, const int32_t* positions, int T, int D, std::vecto
 
 using namespace fg;
 
+namespace fg {
+
+// Scratch of a product as fg_matmul runs it, and the run itself on a
+// given scratch pointer (shared with fg_matmul_noalloc, so both take the
+// same path bit for bit).
+//   A: read in place when 16-byte aligned with a row stride of whole 16-byte
+//      units (a split product then makes A's low part in shared memory);
+//      else re-strided into scratch [m, kp] (with its low part when split).
+//   B: w given as the transposed view of an [n, k] matrix (K-major, the
+//      layout the tensor core reads) is read in place when aligned; [k, n]
+//      is transposed into scratch [n, kp]. A split product adds B's low part
+//      [n, ldb] (the high part is B itself: the tensor core reads its top
+//      19 bits).
+namespace {
+size_t round256(size_t v) { return (v + 255) / 256 * 256; }
+}  // namespace
+
+MatmulPlan plan_matmul(int64_t m, int64_t n, int64_t k, const float* x, int64_t ldx, const float* w,
+                       int64_t ldw, int w_transposed, int precision) {
+  MatmulPlan p{};
+  p.split = precision != FG_PREC_TF32;
+  p.kp = round4(k);
+  p.a_direct = aligned16(x) && ldx % 4 == 0;
+  p.b_direct = w_transposed && aligned16(w) && ldw % 4 == 0;
+  p.ldb = p.b_direct ? ldw : p.kp;
+  p.a_bytes = p.a_direct ? 0 : round256(size_t(m) * p.kp * 4) * (p.split ? 2 : 1);
+  p.bt_bytes = p.b_direct ? 0 : round256(size_t(n) * p.kp * 4);
+  p.blo_bytes = p.split ? round256(size_t(n) * p.ldb * 4) : 0;
+  return p;
+}
+
+int matmul_run(const MatmulPlan& p, int64_t m, int64_t n, int64_t k, const float* x, int64_t ldx,
+               const float* w, int64_t ldw, int w_transposed, float* out, int64_t ldo, const fg_epilogue* epi,
+               void* scratch, int* err, cudaStream_t s) {
+  unsigned char* cur = static_cast<unsigned char*>(scratch);
+  auto take = [&](size_t bytes) {
+    float* r = reinterpret_cast<float*>(cur);
+    cur += bytes;
+    return r;
+  };
+  GemmEpilogue e;
+  e.out = out;
+  e.ldo = ldo;
+  if (epi) {
+    e.bias = epi->bias;
+    e.rowscale = epi->row_scale;
+    e.act = epi->act;
+    e.mul = epi->mul;
+    e.ldm = epi->ldm;
+    e.residual = epi->residual;
+    e.ldr = epi->ldr;
+  }
+  GemmArgs g;
+  g.M = int(m);
+  g.Nb = int(n);
+  g.K = int(k);
+  if (p.a_direct) {
+    g.A = x;
+    g.lda = ldx;
+    g.a_lo_smem = p.split;
+  } else {
+    const size_t part = p.a_bytes / (p.split ? 2 : 1);
+    float* ahi = take(part);
+    float* alo = p.split ? take(part) : nullptr;
+    FG_TRY(split_copy_2d(x, ldx, m, k, ahi, alo, p.kp, p.split ? 1 : 0, s));
+    g.A = ahi;
+    g.A_lo = alo;
+    g.lda = p.kp;
+  }
+  if (p.b_direct) {
+    g.B = w;
+  } else {
+    float* bt = take(p.bt_bytes);
+    if (w_transposed) {
+      FG_TRY(split_copy_2d(w, ldw, n, k, bt, nullptr, p.kp, 0, s));  // re-strided, aligned copy
+    } else {
+      FG_TRY(transpose_f32(w, ldw, k, n, bt, p.kp, s));
+    }
+    g.B = bt;
+  }
+  g.ldb = p.ldb;
+  if (p.split) {
+    float* blo = take(p.blo_bytes);
+    FG_TRY(split_copy_2d(g.B, p.ldb, n, k, nullptr, blo, p.ldb, 0, s));
+    g.B_lo = blo;
+  }
+  g.epi = e;
+  return gemm_tn(g, err, s);
+}
+
+}  // namespace fg
+
 extern "C" {
 
 int fg_matmul(int64_t m, int64_t n, int64_t k, const float* x, int64_t ldx, const float* w,
@@ -74,82 +157,14 @@ int fg_matmul(int64_t m, int64_t n, int64_t k, const float* x, int64_t ldx, cons
     return set_error(FG_EINVAL, "fg_matmul: unknown activation %d", epi->act);
   if (epi && ((epi->mul && epi->ldm < n) || (epi->residual && epi->ldr < n)))
     return set_error(FG_EINVAL, "fg_matmul: Mul/Residual leading dimension smaller than n");
+  if (k == 0) return set_error(FG_EINVAL, "fg_matmul: k = 0 is not supported");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int* err = nullptr;
   FG_TRY(device_error_word(&err));
-
-  GemmEpilogue e;
-  e.out = out;
-  e.ldo = ldo;
-  if (epi) {
-    e.bias = epi->bias;
-    e.rowscale = epi->row_scale;
-    e.act = epi->act;
-    e.mul = epi->mul;
-    e.ldm = epi->ldm;
-    e.residual = epi->residual;
-    e.ldr = epi->ldr;
-  }
-  if (k == 0) {
-    // Empty inner dimension: the product is zero; the epilogue still applies.
-    return set_error(FG_EINVAL, "fg_matmul: k = 0 is not supported");
-  }
-
-  const bool split = precision != FG_PREC_TF32;
-  const int64_t kp = round4(k);
-  const bool a_direct = !split && aligned16(x) && ldx % 4 == 0;
-  const bool b_direct = !split && w_transposed && aligned16(w) && ldw % 4 == 0;
-  // scratch: A hi/lo [m, kp], B (packed [n, kp]) hi/lo
-  size_t need = 0;
-  const size_t a_elems = size_t(m) * kp, b_elems = size_t(n) * kp;
-  if (!a_direct) need += a_elems * (split ? 2 : 1);
-  if (!w_transposed) need += b_elems;  // transposed copy of w
-  if (!b_direct) need += b_elems * (split ? 2 : 1);
+  const MatmulPlan p = plan_matmul(m, n, k, x, ldx, w, ldw, w_transposed, precision);
   StreamScratch scratch(s);
-  FG_TRY(scratch.alloc(need * sizeof(float)));
-  float* cur = static_cast<float*>(scratch.p);
-  auto take = [&](size_t elems) {
-    float* r = cur;
-    cur += elems;
-    return r;
-  };
-
-  GemmArgs g;
-  g.M = int(m);
-  g.Nb = int(n);
-  g.K = int(k);
-  if (a_direct) {
-    g.A = x;
-    g.lda = ldx;
-  } else {
-    float* ahi = take(a_elems);
-    float* alo = split ? take(a_elems) : nullptr;
-    FG_TRY(split_copy_2d(x, ldx, m, k, ahi, alo, kp, split ? 1 : 0, s));
-    g.A = ahi;
-    g.A_lo = alo;
-    g.lda = kp;
-  }
-  const float* bsrc = w;
-  int64_t ldb_src = ldw;
-  if (!w_transposed) {
-    float* bt = take(b_elems);
-    FG_TRY(transpose_f32(w, ldw, k, n, bt, kp, s));
-    bsrc = bt;
-    ldb_src = kp;
-  }
-  if (b_direct) {
-    g.B = w;
-    g.ldb = ldw;
-  } else {
-    float* bhi = take(b_elems);
-    float* blo = split ? take(b_elems) : nullptr;
-    FG_TRY(split_copy_2d(bsrc, ldb_src, n, k, bhi, blo, kp, split ? 1 : 0, s));
-    g.B = bhi;
-    g.B_lo = blo;
-    g.ldb = kp;
-  }
-  g.epi = e;
-  return gemm_tn(g, err, s);
+  FG_TRY(scratch.alloc(p.total()));
+  return matmul_run(p, m, n, k, x, ldx, w, ldw, w_transposed, out, ldo, epi, scratch.p, err, s);
 }
 
 int fg_row_sum_squares(const float* x, int64_t rows, int64_t n, int64_t ldx, float* out,

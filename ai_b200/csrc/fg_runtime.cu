@@ -17,6 +17,7 @@ std::vector<int*> g_dev_err;    // per device status block, lazily allocated
 std::vector<int*> g_extra_err;  // per device: the no-allocation entry point's block
 std::vector<unsigned long long> g_wait_limit;  // per device, 0 = default
 std::vector<int> g_sms;
+std::vector<cudaMemPool_t> g_pools;  // per device: op-level scratch
 
 // Host image of the device status block (fg_ptx.cuh DeviceStatus).
 struct DeviceStatusHost {
@@ -124,6 +125,46 @@ int set_wait_limit(int dev, unsigned long long ns) {
   for (int* b : blocks)
     if (b) FG_CUDA_TRY(cudaMemcpy(reinterpret_cast<char*>(b) + 8, &ns, sizeof(ns), cudaMemcpyHostToDevice));
   return FG_OK;
+}
+
+// Library-owned stream-ordered pool per device for the op-level calls'
+// scratch (operand splits, transposes, attention operands). Its release
+// threshold is unlimited, so memory freed at the end of one call stays
+// reserved and the next call reuses it without mapping new pages (with the
+// device's default pool, whose threshold is 0, every synchronisation
+// returned the memory and every call paid for mapping it again).
+int scratch_alloc(void** p, size_t bytes, cudaStream_t s) {
+  *p = nullptr;
+  if (bytes == 0) return FG_OK;
+  int dev = 0;
+  FG_CUDA_TRY(cudaGetDevice(&dev));
+  cudaMemPool_t pool = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (int(g_pools.size()) <= dev) g_pools.resize(dev + 1, nullptr);
+    if (!g_pools[dev]) {
+      cudaMemPoolProps props = {};
+      props.allocType = cudaMemAllocationTypePinned;
+      props.location.type = cudaMemLocationTypeDevice;
+      props.location.id = dev;
+      cudaMemPool_t mp = nullptr;
+      FG_CUDA_TRY(cudaMemPoolCreate(&mp, &props));
+      cuuint64_t keep = ~cuuint64_t(0);
+      FG_CUDA_TRY(cudaMemPoolSetAttribute(mp, cudaMemPoolAttrReleaseThreshold, &keep));
+      g_pools[dev] = mp;
+    }
+    pool = g_pools[dev];
+  }
+  if (cudaMallocFromPoolAsync(p, bytes, pool, s) != cudaSuccess) {
+    cudaGetLastError();
+    *p = nullptr;
+    return set_error(FG_ENOMEM, "scratch allocation of %zu bytes failed", bytes);
+  }
+  return FG_OK;
+}
+
+void scratch_free(void* p, cudaStream_t s) {
+  if (p) cudaFreeAsync(p, s);
 }
 
 int tensor_map_encoder(PFN_cuTensorMapEncodeTiled_v12000* fn) {

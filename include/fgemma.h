@@ -275,8 +275,12 @@ int fg_model_read_profile(fg_model* m, double* ms, int64_t* launches, double* wo
  * and tensor.MatMulFused (tensor/matmul_fused.go:40). w is [k, n] row-major
  * with leading dimension ldw, or, when w_transposed != 0, the transposed
  * view of an [n, k] row-major matrix (x · Wᵀ, the `w.T()` case). epi may be
- * NULL. Row strides must be multiples of 4 floats and pointers 16-byte
- * aligned. */
+ * NULL. x, and w as a transposed view, are read in place when 16-byte
+ * aligned with row strides of whole 16-byte units; other layouts are copied
+ * into stream-ordered scratch from a pool the library keeps per device
+ * (memory it keeps reserved between calls). In split precision the
+ * product is A·B + A·B_lo + A_lo·B in TF32 with B_lo computed per call and
+ * A's low part made in shared memory. */
 int fg_matmul(int64_t m, int64_t n, int64_t k, const float* x, int64_t ldx, const float* w,
               int64_t ldw, int w_transposed, float* out, int64_t ldo, const fg_epilogue* epi,
               int precision, void* stream);
@@ -289,8 +293,12 @@ int fg_matmul(int64_t m, int64_t n, int64_t k, const float* x, int64_t ldx, cons
  * allocates host memory freely). Same arguments and results as fg_matmul;
  * the splitting/packing scratch lives in a fixed 32 MiB device array owned
  * by the library (held by every GPU that loads it, until exit), so calls
- * whose scratch would exceed 32 MiB — 4·(2·m·k' + 3·n·k') bytes in the worst
- * case, k' = k rounded up to 4 — are refused with FG_EINVAL. The call itself
+ * whose scratch would exceed 32 MiB are refused with FG_EINVAL. The scratch
+ * is 4·(2·m + 2·n)·k' bytes at most (k' = k rounded up to 4): none for x
+ * when x is 16-byte aligned with a row stride of whole 16-byte units (else
+ * 4·2·m·k' in split precision, 4·m·k' in TF32); none for w in TF32 when it
+ * is such an aligned transposed view (else 4·n·k' for its K-major copy);
+ * plus 4·n·k' for w's low part in split precision. The call itself
  * allocates nothing (no cudaMalloc, cudaFree or allocating library routine),
  * but the CUDA driver reserves the array when it loads the module holding
  * it: at the first call on a device under lazy module loading (the CUDA 12

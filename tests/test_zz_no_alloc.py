@@ -108,7 +108,7 @@ def test_noalloc_refuses_more_than_its_scratch(cuda):
 
     from ai_b200 import _lib
 
-    m, k, n = 4096, 1024, 1024  # needs 4·(2·m·k + 3·n·k) ≈ 46 MB > 32 MiB
+    m, k, n = 256, 1024, 8192  # w as [k, n]: transposed copy + low part = 4·2·n·k = 64 MiB > 32 MiB
     x = torch.zeros((m, k), device=cuda)
     w = torch.zeros((k, n), device=cuda)
     out = torch.zeros((m, n), device=cuda)
