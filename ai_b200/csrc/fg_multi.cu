@@ -26,14 +26,14 @@ namespace fg {
 namespace {
 
 // Time per token (ns) of full-length 131 072-token batches of
-// EmbeddingGemma-300m on one B200 with the default split precision, by
-// sequence length: short sequences pay per-sequence attention tiles and
-// pooling, long ones the quadratic global layers. Only the ratios matter
-// for the split.
+// EmbeddingGemma-300m on one B200 with the default split precision
+// (split-fp16 products), by sequence length, measured with CUDA events:
+// short sequences pay per-sequence attention tiles and pooling, long ones
+// the quadratic global layers. Only the ratios matter for the split.
 constexpr double kNsPerToken[][2] = {
-    {16, 959.4},   {32, 805.2},   {64, 730.1},   {128, 688.3},  {192, 730.0},
-    {256, 704.1},  {384, 732.0},  {512, 751.2},  {768, 771.9},  {1024, 784.0},
-    {1280, 788.0}, {1536, 809.8}, {1792, 811.1}, {2048, 822.0}};
+    {16, 827.9},   {32, 669.3},   {64, 592.9},   {128, 557.9},  {192, 594.4},
+    {256, 577.5},  {384, 602.2},  {512, 615.6},  {768, 635.4},  {1024, 651.1},
+    {1280, 658.6}, {1536, 667.8}, {1792, 674.7}, {2048, 686.4}};
 constexpr int kTable = int(sizeof(kNsPerToken) / sizeof(kNsPerToken[0]));
 
 double ns_per_token(double L) {

@@ -185,6 +185,115 @@ static void unfold(folded* f, int ndense) {
 }
 
 /* ------------------------------------------------------------------ */
+/* ------------------------------------------------------------------ */
+/* Packed AVX-512 kernels of the float32 mode, shaped like the reference's
+ * SGEMM (internal/blas/gemm.go:562-702 driving the 14×32 micro-kernel of
+ * internal/kernel/kernel_avx512_amd64.s): W packed once per call into
+ * 32-column panels [k][32], A packed per 14-row block as [k][14], and a
+ * 14×32 register tile of 28 accumulators. Every C element is still one
+ * sequential chain of fused multiply-adds over k starting from 0, so the
+ * results are bit for bit those of the simple loops (orc_set_fast_kernels(0)
+ * selects those; tests compare the two). The attention scores go 16 keys
+ * at a time over a transposed K, each lane one key's sequential chain over
+ * the head dimension. */
+#include <immintrin.h>
+
+static int g_fast = 1;
+void orc_set_fast_kernels(int on) { g_fast = on != 0; }
+
+#define ORC_MR 14
+#define ORC_NR 32
+
+static void gemm_f32_packed(const float* A, const float* W, int m, int k, int n, float* C) {
+  const int np = (n + ORC_NR - 1) / ORC_NR, mb = (m + ORC_MR - 1) / ORC_MR;
+  float* Wp = (float*)aligned_alloc(64, (size_t)np * k * ORC_NR * sizeof(float) + 64);
+  float* Ap = (float*)aligned_alloc(64, (size_t)mb * k * ORC_MR * sizeof(float) + 64);
+  if (!Wp || !Ap) {
+    free(Wp);
+    free(Ap);
+    return;
+  }
+#pragma omp parallel for schedule(static)
+  for (int p = 0; p < np; ++p) {
+    const int n0 = p * ORC_NR, cols = (n - n0) < ORC_NR ? (n - n0) : ORC_NR;
+    float* dst = Wp + (size_t)p * k * ORC_NR;
+    for (int kk = 0; kk < k; ++kk) {
+      const float* src = W + (size_t)kk * n + n0;
+      for (int j = 0; j < ORC_NR; ++j) dst[(size_t)kk * ORC_NR + j] = j < cols ? src[j] : 0.0f;
+    }
+  }
+#pragma omp parallel for schedule(static)
+  for (int b = 0; b < mb; ++b) {
+    const int i0 = b * ORC_MR, rows = (m - i0) < ORC_MR ? (m - i0) : ORC_MR;
+    float* dst = Ap + (size_t)b * k * ORC_MR;
+    for (int kk = 0; kk < k; ++kk)
+      for (int r = 0; r < ORC_MR; ++r) dst[(size_t)kk * ORC_MR + r] = r < rows ? A[(size_t)(i0 + r) * k + kk] : 0.0f;
+  }
+  /* tasks of 8 row blocks × 4 panels: both operands' packed slices stay in L2 */
+  const int rb = 8, pb = 4;
+  const int tr = (mb + rb - 1) / rb, tp = (np + pb - 1) / pb;
+#pragma omp parallel for schedule(dynamic, 1)
+  for (int task = 0; task < tr * tp; ++task) {
+    const int b0 = (task / tp) * rb, p0 = (task % tp) * pb;
+    for (int p = p0; p < p0 + pb && p < np; ++p) {
+      const float* wp = Wp + (size_t)p * k * ORC_NR;
+      const int n0 = p * ORC_NR, cols = (n - n0) < ORC_NR ? (n - n0) : ORC_NR;
+      for (int b = b0; b < b0 + rb && b < mb; ++b) {
+        const float* ap = Ap + (size_t)b * k * ORC_MR;
+        __m512 c0[ORC_MR], c1[ORC_MR];
+        for (int r = 0; r < ORC_MR; ++r) {
+          c0[r] = _mm512_setzero_ps();
+          c1[r] = _mm512_setzero_ps();
+        }
+        for (int kk = 0; kk < k; ++kk) {
+          const __m512 w0 = _mm512_load_ps(wp + (size_t)kk * ORC_NR);
+          const __m512 w1 = _mm512_load_ps(wp + (size_t)kk * ORC_NR + 16);
+          const float* a = ap + (size_t)kk * ORC_MR;
+#pragma GCC unroll 14
+          for (int r = 0; r < ORC_MR; ++r) {
+            const __m512 av = _mm512_set1_ps(a[r]);
+            c0[r] = _mm512_fmadd_ps(av, w0, c0[r]);
+            c1[r] = _mm512_fmadd_ps(av, w1, c1[r]);
+          }
+        }
+        const int i0 = b * ORC_MR, rows = (m - i0) < ORC_MR ? (m - i0) : ORC_MR;
+        for (int r = 0; r < rows; ++r) {
+          float* crow = C + (size_t)(i0 + r) * n + n0;
+          if (cols == ORC_NR) {
+            _mm512_storeu_ps(crow, c0[r]);
+            _mm512_storeu_ps(crow + 16, c1[r]);
+          } else {
+            float t[ORC_NR];
+            _mm512_storeu_ps(t, c0[r]);
+            _mm512_storeu_ps(t + 16, c1[r]);
+            for (int j = 0; j < cols; ++j) crow[j] = t[j];
+          }
+        }
+      }
+    }
+  }
+  free(Wp);
+  free(Ap);
+}
+
+/* s[j] = Σ_d q[d]·K[j][d], j < S, from KT [D][ldt] (K transposed), each
+ * score a sequential chain of fused multiply-adds over d from 0. */
+static void scores_f32_packed(const float* q, const float* KT, int S, int D, int ldt, float* s) {
+  int j0 = 0;
+  for (; j0 + 16 <= S; j0 += 16) {
+    __m512 acc = _mm512_setzero_ps();
+    for (int d = 0; d < D; ++d) acc = _mm512_fmadd_ps(_mm512_set1_ps(q[d]), _mm512_loadu_ps(KT + (size_t)d * ldt + j0), acc);
+    _mm512_storeu_ps(s + j0, acc);
+  }
+  if (j0 < S) {
+    const __mmask16 mk = (__mmask16)((1u << (S - j0)) - 1u);
+    __m512 acc = _mm512_setzero_ps();
+    for (int d = 0; d < D; ++d)
+      acc = _mm512_fmadd_ps(_mm512_set1_ps(q[d]), _mm512_maskz_loadu_ps(mk, KT + (size_t)d * ldt + j0), acc);
+    _mm512_mask_storeu_ps(s + j0, mk, acc);
+  }
+}
+
 #define R double
 #define SFX(name) name##_f64
 #define MADD(a, b, c) fma((a), (b), (c))
@@ -267,7 +376,7 @@ void orc_attention_head(const float* q, const float* k, const float* v, const fl
     float* s = (float*)malloc((size_t)(S > 0 ? S : 1) * sizeof(float));
     for (int i = 0; i < T; ++i)
       attn_row_f32(q + (size_t)i * D, k, v, S, D, D, NULL, mask ? mask + (size_t)i * S : NULL,
-                   scale, s, out + (size_t)i * D);
+                   scale, s, out + (size_t)i * D, NULL, 0);
     free(s);
     return;
   }
@@ -280,7 +389,7 @@ void orc_attention_head(const float* q, const float* k, const float* v, const fl
   for (size_t e = 0; e < (size_t)S * D; ++e) kd[e] = k[e], vd[e] = v[e];
   for (int i = 0; i < T; ++i) {
     attn_row_f64(qd + (size_t)i * D, kd, vd, S, D, D, NULL, mask ? mask + (size_t)i * S : NULL,
-                 scale, s, o);
+                 scale, s, o, NULL, 0);
     for (int d = 0; d < D; ++d) out[(size_t)i * D + d] = (float)o[d];
   }
   free(qd); free(kd); free(vd); free(s); free(o);

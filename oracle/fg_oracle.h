@@ -93,6 +93,12 @@ void orc_exp_ref(const float* x, int n, float* out);   /* reference float32 exp 
 void orc_tanh_ref(const float* x, int n, float* out);  /* reference float32 tanh */
 void orc_gelu_ref(const float* x, int n, float* out);  /* reference float32 GELU */
 
+/* Float32-mode kernels: 1 (default) = the packed AVX-512 GEMM and the
+ * 16-keys-at-a-time attention scores; 0 = the simple loops. Both give the
+ * same results bit for bit (same fused multiply-add chains in the same
+ * order); the switch exists for the test that checks it. */
+void orc_set_fast_kernels(int on);
+
 #ifdef __cplusplus
 }
 #endif

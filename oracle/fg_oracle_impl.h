@@ -11,6 +11,10 @@
  * layout; each C element accumulates sequentially over k (the order of the
  * reference's micro-kernel, internal/kernel/kernel_avx512_amd64.s), in R. */
 static void SFX(gemm)(const R* A, const float* W, int m, int k, int n, R* C) {
+  if (sizeof(R) == sizeof(float) && g_fast) {
+    gemm_f32_packed((const float*)A, W, m, k, n, (float*)C);
+    return;
+  }
 #pragma omp parallel for schedule(dynamic, 1)
   for (int i0 = 0; i0 < m; i0 += 4) {
     const int rows = (m - i0) < 4 ? (m - i0) : 4;
@@ -81,11 +85,15 @@ static R SFX(tanh_mode)(R x) {
  * hiding key j (padding, window), so the mask value is −1e9·maskcnt[j]. */
 static void SFX(attn_row)(const R* q, const R* K, const R* V, int S, int D, int ld,
                           const unsigned char* maskcnt, const float* fmask, float scale, R* s,
-                          R* out) {
-  for (int j = 0; j < S; ++j) {
-    R acc = 0;
-    for (int d = 0; d < D; ++d) acc = MADD(q[d], K[(size_t)j * ld + d], acc);
-    s[j] = acc;
+                          R* out, const R* KT, int ldt) {
+  if (sizeof(R) == sizeof(float) && KT) {
+    scores_f32_packed((const float*)q, (const float*)KT, S, D, ldt, (float*)s);
+  } else {
+    for (int j = 0; j < S; ++j) {
+      R acc = 0;
+      for (int d = 0; d < D; ++d) acc = MADD(q[d], K[(size_t)j * ld + d], acc);
+      s[j] = acc;
+    }
   }
   const R inv_scale = (R)(1.0f / scale);
   if (sizeof(R) == sizeof(float)) {
@@ -229,7 +237,22 @@ static int SFX(embed)(const orc_config* c, const folded* fw, const int32_t* ids,
       for (int h = 0; h < Hq; ++h) SFX(rope_vec)(q + r * qw + (size_t)h * D, D, L->cos_t, L->sin_t, t);
       for (int h = 0; h < Hkv; ++h) SFX(rope_vec)(kk + r * kw + (size_t)h * D, D, L->cos_t, L->sin_t, t);
     }
-    /* attention with PaddingMask (+ WindowMask on sliding layers) (embed.go:168-186, 209) */
+    /* attention with PaddingMask (+ WindowMask on sliding layers) (embed.go:168-186, 209);
+     * float32 with the fast kernels: K transposed per (sequence, KV head) to
+     * [D][T] so the scores go 16 keys at a time */
+    R* kt = NULL;
+    if (sizeof(R) == sizeof(float) && g_fast) {
+      kt = (R*)malloc(M * kw * sizeof(R));
+      if (kt) {
+#pragma omp parallel for schedule(static) collapse(2)
+        for (int b = 0; b < B; ++b)
+          for (int hk = 0; hk < Hkv; ++hk) {
+            R* dst = kt + ((size_t)b * Hkv + hk) * D * T;
+            for (int t = 0; t < T; ++t)
+              for (int d = 0; d < D; ++d) dst[(size_t)d * T + t] = kk[((size_t)b * T + t) * kw + (size_t)hk * D + d];
+          }
+      }
+    }
 #pragma omp parallel
     {
       R* s = (R*)malloc((size_t)T * sizeof(R));
@@ -248,12 +271,14 @@ static int SFX(embed)(const orc_config* c, const folded* fw, const int32_t* ids,
             const R* Kb = kk + (size_t)b * T * kw + (size_t)hk * D;
             const R* Vb = vv + (size_t)b * T * kw + (size_t)hk * D;
             R* o = att + ((size_t)b * T + i) * qw + (size_t)h * D;
-            SFX(attn_row)(qr, Kb, Vb, T, D, kw, mc, NULL, c->attn_scale, s, o);
+            const R* KTb = kt ? kt + ((size_t)b * Hkv + hk) * D * T : NULL;
+            SFX(attn_row)(qr, Kb, Vb, T, D, kw, mc, NULL, c->attn_scale, s, o, KTb, T);
           }
         }
       free(s);
       free(mc);
     }
+    free(kt);
     /* o = RMSNorm(att·Wo, 1+postAttn); x += o (embed.go:212-220) */
     SFX(gemm)(att, L->wo, (int)M, qw, H, t1);
     SFX(rmsnorm_rows)(t1, M, H, L->post_attn, c->eps, t1);

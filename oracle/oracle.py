@@ -49,6 +49,12 @@ class OrcWeights(C.Structure):
 _lib = None
 
 
+def set_fast_kernels(on: bool) -> None:
+    """Float32 mode: packed AVX-512 kernels (default) or the simple loops;
+    bit for bit the same results."""
+    lib().orc_set_fast_kernels(1 if on else 0)
+
+
 def build() -> Path:
     """Builds libfgoracle.so with the committed Makefile (idempotent)."""
     subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
@@ -77,6 +83,8 @@ def lib() -> C.CDLL:
         h.orc_padding_mask.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p]
         for n in ("orc_exp_ref", "orc_tanh_ref", "orc_gelu_ref"):
             getattr(h, n).argtypes = [C.c_void_p, C.c_int, C.c_void_p]
+        h.orc_set_fast_kernels.argtypes = [C.c_int]
+        h.orc_set_fast_kernels.restype = None
         _lib = h
     return _lib
 

@@ -190,3 +190,42 @@ def test_bf16_widening_exact():
     x = np.random.default_rng(0).standard_normal(10000).astype(np.float32)
     r = S.bf16_to_f32(S.bf16_round(x))
     assert np.all(np.abs(r - x) <= np.abs(x) * 2.0 ** -8)
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 7, 5), (13, 768, 33), (14, 64, 32), (29, 1152, 768),
+                                   (130, 768, 3072), (300, 96, 97)])
+def test_fast_f32_gemm_is_bitwise_the_simple_loops(m, k, n):
+    """The packed AVX-512 float32 GEMM (14×32 register tiles over packed
+    panels) computes every element as the same sequential chain of fused
+    multiply-adds over k as the simple loops: bit for bit equal, ragged
+    edges included."""
+    rng = np.random.default_rng(m * 1000 + n)
+    a = rng.standard_normal((m, k), dtype=np.float32)
+    w = rng.standard_normal((k, n), dtype=np.float32)
+    try:
+        O.set_fast_kernels(False)
+        slow = O.matmul_fused(a, w, mode=O.F32)
+        O.set_fast_kernels(True)
+        fast = O.matmul_fused(a, w, mode=O.F32)
+    finally:
+        O.set_fast_kernels(True)
+    assert np.array_equal(fast, slow)
+
+
+def test_fast_f32_encoder_is_bitwise_the_simple_loops():
+    """The whole float32-mode encoder (packed GEMMs, attention scores 16 keys
+    at a time over a transposed K) equals the simple loops bit for bit, with
+    padding and the sliding window active."""
+    cfg = S.small_config(layers=2, vocab=512, sliding_window=64)
+    w = S.make_weights(cfg, seed=5, norm_std=0.1)
+    ids = S.make_ids(3, 150, 2, cfg["vocab_size"])
+    lengths = np.array([150, 77, 1], np.int32)
+    om = O.from_bf16(cfg, w)
+    try:
+        O.set_fast_kernels(False)
+        slow = om.embed_padded(ids, lengths, mode=O.F32)
+        O.set_fast_kernels(True)
+        fast = om.embed_padded(ids, lengths, mode=O.F32)
+    finally:
+        O.set_fast_kernels(True)
+    assert np.array_equal(fast, slow)
