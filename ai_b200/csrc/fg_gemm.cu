@@ -1126,7 +1126,6 @@ __global__ void __launch_bounds__(320, 1)
           *reinterpret_cast<uint2*>(base + C::kPartBytes + off) = lw;
         }
         fence_proxy_async_smem();  // generic-proxy writes → visible to the tensor core
-        __syncwarp();              // every lane's parts are written before lane 0 signals
         // B's half of the stage has landed (TMA) before the stage is declared ready
         const bool landed = mbar_wait(full_bar(stage), phase, abort_flag, p.err, kDevTimeoutFull);
         if (!__all_sync(0xffffffffu, landed)) break;
