@@ -54,8 +54,6 @@ struct KParams {
   float a_norm_k;      // sqrt(K): max|a_r| <= sqrt(K) / a_rs[r]
   const float* a_rs;   // A's row scales 1/sqrt(mean(a²) + eps) (a_exp_rs)
   const float* a_gain;  // per-column gain on A (split-fp16 with an unfolded B), or null
-  const float* A;       // A itself, for converters that read its rows from global memory
-  int64_t lda;
 };
 
 // Exponent e_r of A row r in the split-fp16 product: |a_r|·2^e_r < 2^14, so
@@ -827,17 +825,9 @@ __global__ void __launch_bounds__(Cfg<BN, SA, SB, BK, CV>::kThreads, 1)
 // kind::f16 (K = 16) instead of 2 × 4 of kind::tf32 (K = 8) — half the
 // tensor-pipe time for the same products. Stage: A (then A_hi | A_lo) | B,
 // 24 KB, so 8 stages are in flight.
-//
-// LA (with H16): the converter warps read A's fp32 rows straight from
-// global memory instead of from a TMA-loaded tile, and only B is loaded by
-// TMA. Per stage that takes the TMA write of the 16 KB fp32 tile and the
-// converters' 16 KB read of it out of shared memory, whose bandwidth the
-// stage otherwise exceeds (TMA 24 KB + converter 32 KB + MMA 32 KB of
-// shared-memory traffic per 512 tensor cycles, against 128 B per cycle).
-template <bool CV, bool SA = false, bool SB = false, bool H16 = false, bool LA = false>
+template <bool CV, bool SA = false, bool SB = false, bool H16 = false>
 struct PairCfg {
   static_assert(!H16 || (CV && !SA && !SB), "split-fp16 takes A's parts from the converters");
-  static_assert(!LA || H16, "global-memory A rows are a split-fp16 form");
   static constexpr int BN = 256, BK = 32;
   static constexpr int kThreads = 320;
   static constexpr bool kLo = CV || SA;
@@ -847,26 +837,22 @@ struct PairCfg {
   static constexpr uint32_t kStageBytes =
       H16 ? kABytes + kBBytes : kABytes * (kLo ? 2 : 1) + kBBytes * (SB ? 2 : 1);
   static constexpr uint32_t kBOffset = H16 ? kABytes : kABytes * (kLo ? 2 : 1);
-  static constexpr uint32_t kTmaBytes = LA ? kBBytes : kABytes * (SA ? 2 : 1) + kBBytes * (SB ? 2 : 1);
+  static constexpr uint32_t kTmaBytes = kABytes * (SA ? 2 : 1) + kBBytes * (SB ? 2 : 1);
   static constexpr uint32_t kEpiStageBytes = kEpiStageBytesAll;
   static constexpr int kStagesRaw = (kSmemLimit - 2048 - int(kEpiStageBytes)) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
   static constexpr uint32_t kTmemCols = 512;  // two 256-column accumulators
-  // stage-ready arrivals per stage: converter warps of both CTAs (each of
-  // the four writes a quarter of the rows under LA; two groups of two take
-  // alternate stages otherwise), or 4 per CTA without split-fp16
-  static constexpr uint32_t kReadyCount = H16 ? (LA ? 8 : 4) : 8;
   static constexpr size_t kSmemBytes = 1024 + size_t(kStages) * kStageBytes + kEpiStageBytes + 256;
   static_assert(kStages >= 3, "stage ring too shallow");
   static_assert(!H16 || kStages % 2 == 0, "the two converter groups take alternate stages");
 };
 
-template <bool CV, bool SA = false, bool SB = false, bool H16 = false, bool LA = false>
+template <bool CV, bool SA = false, bool SB = false, bool H16 = false>
 __global__ void __launch_bounds__(320, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap mA, const __grid_constant__ CUtensorMap mAlo,
                      const __grid_constant__ CUtensorMap mB, const __grid_constant__ CUtensorMap mBlo,
                      const __grid_constant__ OutMaps om, const __grid_constant__ KParams p) {
-  using C = PairCfg<CV, SA, SB, H16, LA>;
+  using C = PairCfg<CV, SA, SB, H16>;
   constexpr int S = C::kStages;
   constexpr int BN = C::BN, BK = C::BK;
   constexpr uint32_t kIdesc = H16 ? idesc_f16(256, BN) : idesc_tf32(256, BN);
@@ -897,7 +883,7 @@ __global__ void __launch_bounds__(320, 1)
     for (int s = 0; s < S; ++s) {
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
-      mbar_init(ready_bar(s), C::kReadyCount);
+      mbar_init(ready_bar(s), H16 ? 4 : 8);  // converter warps per stage in each CTA: 2 (H16) or 4
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(accf_bar(a), 1);
@@ -940,7 +926,7 @@ __global__ void __launch_bounds__(320, 1)
           mbar_arrive_expect_tx(fb, C::kTmaBytes);
           armed[stage]++;
           const uint32_t dst = smem_u32(smem + size_t(stage) * C::kStageBytes);
-          if (!LA) tma_load_2d(dst, &mA, fb, kb * BK, arow);
+          tma_load_2d(dst, &mA, fb, kb * BK, arow);
           if (SA) tma_load_2d(dst + C::kABytes, &mAlo, fb, kb * BK, arow);
           tma_load_2d(dst + C::kBOffset, &mB, fb, kb * BK, brow);
           if (SB) tma_load_2d(dst + C::kBOffset + C::kBBytes, &mBlo, fb, kb * BK, brow);
@@ -1046,102 +1032,7 @@ __global__ void __launch_bounds__(320, 1)
     const int ct = threadIdx.x - 192;  // 0..127
     int stage = 0;
     uint32_t phase = 0;
-    if constexpr (H16 && LA) {
-      // Each converter warp cw writes rows 32·cw .. 32·cw + 31 of the CTA's
-      // 128 A rows of every stage, read straight from global memory: lane l
-      // holds 16-byte chunk l & 7 of rows 4i + (l >> 3), i < 8, so every
-      // load instruction reads four whole 128-byte row segments. The next
-      // (tile, k-block) is loaded into registers while the current one is
-      // converted, and the segments PD blocks ahead are prefetched into L2.
-      // The arithmetic is the TMA-tile converters' below (same parts, same
-      // 64-byte-swizzled layout), so both give the same operands.
-      constexpr int PD = 4;
-      const int cw = warp - 6;
-      const int rsub = lane >> 3, chunk = lane & 7;
-      const float* const Ag = p.A;
-      const int64_t lda = p.lda;
-      const bool gained = p.a_gain != nullptr;
-      auto tile_row0 = [&](int t) { return (t / p.ntn) * 256 + int(rank) * 128 + cw * 32; };
-      auto load = [&](int t, int k, float4 (&d)[8]) {
-        const int r0 = tile_row0(t);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int r = r0 + 4 * i + rsub;
-          d[i] = r < p.M ? __ldg(reinterpret_cast<const float4*>(Ag + int64_t(r) * lda + k * BK) + chunk)
-                         : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-      };
-      auto prefetch_l2 = [&](int t, int k) {
-        const int r = tile_row0(t) + lane;
-        if (r < p.M)
-          asm volatile("prefetch.global.L2 [%0];" ::"l"(Ag + int64_t(r) * lda + k * BK) : "memory");
-      };
-      float sc[8];
-      auto scales = [&](int t) {
-        const int r0 = tile_row0(t);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) sc[i] = pow2f(a_row_exp(p, r0 + 4 * i + rsub));
-      };
-      int tile = pair, kb = 0;
-      float4 cur[8];
-      if (tile < ntiles) {
-        load(tile, 0, cur);
-        scales(tile);
-        for (int k = 1; k < PD && k < p.nk; ++k) prefetch_l2(tile, k);
-      }
-      while (tile < ntiles) {
-        int ntile = tile, nkb = kb + 1;
-        if (nkb == p.nk) {
-          nkb = 0;
-          ntile = tile + npairs;
-        }
-        float4 nxt[8];
-        if (ntile < ntiles) load(ntile, nkb, nxt);
-        if (kb + PD < p.nk) prefetch_l2(tile, kb + PD);
-        else if (ntile < ntiles && kb + PD - p.nk < p.nk) prefetch_l2(ntile, kb + PD - p.nk);
-        // the stage is free once the MMAs that read it have completed
-        const bool freed = mbar_wait_cluster(empty_bar(stage), phase ^ 1, abort_flag, p.err, kDevTimeoutEmpty);
-        if (!__all_sync(0xffffffffu, freed)) break;
-        float4 g4 = make_float4(1.f, 1.f, 1.f, 1.f);
-        if (gained) g4 = __ldg(reinterpret_cast<const float4*>(p.a_gain + kb * BK) + chunk);
-        uint8_t* base = smem + size_t(stage) * C::kStageBytes;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int r = cw * 32 + 4 * i + rsub;  // row of the CTA's 128
-          const float s = sc[i];
-          const float4 v = cur[i];
-          float a[4];
-          if (gained) {
-            a[0] = v.x * (g4.x * s); a[1] = v.y * (g4.y * s); a[2] = v.z * (g4.z * s); a[3] = v.w * (g4.w * s);
-          } else {
-            a[0] = v.x * s; a[1] = v.y * s; a[2] = v.z * s; a[3] = v.w * s;
-          }
-          const float h0 = tf32_hi(a[0]), h1 = tf32_hi(a[1]), h2 = tf32_hi(a[2]), h3 = tf32_hi(a[3]);
-          const uint2 hw = make_uint2(pack_f16x2(h0, h1), pack_f16x2(h2, h3));
-          const uint2 lw = make_uint2(pack_f16x2(a[0] - h0, a[1] - h1), pack_f16x2(a[2] - h2, a[3] - h3));
-          // 64-byte-swizzled row r: 16-byte chunk j at j ^ ((r >> 1) & 3); this
-          // lane's four columns are the (chunk & 1) half of chunk chunk >> 1
-          const uint32_t off = uint32_t(r) * 64u + uint32_t(((chunk >> 1) ^ ((r >> 1) & 3)) * 16 + (chunk & 1) * 8);
-          *reinterpret_cast<uint2*>(base + off) = hw;
-          *reinterpret_cast<uint2*>(base + C::kPartBytes + off) = lw;
-        }
-        fence_proxy_async_smem();  // generic-proxy writes → visible to the tensor core
-        // B's half of the stage has landed (TMA) before the stage is declared ready
-        const bool landed = mbar_wait(full_bar(stage), phase, abort_flag, p.err, kDevTimeoutFull);
-        if (!__all_sync(0xffffffffu, landed)) break;
-        if (lane == 0) mbar_arrive_remote(mapa_shared(ready_bar(stage), 0));
-        if (++stage == S) {
-          stage = 0;
-          phase ^= 1;
-        }
-        const bool new_tile = ntile != tile;
-        tile = ntile;
-        kb = nkb;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) cur[i] = nxt[i];
-        if (new_tile && tile < ntiles) scales(tile);
-      }
-    } else if constexpr (H16) {
+    if constexpr (H16) {
       // Two groups of two warps take alternate stages (even / odd), so two
       // stages are converted at once. In a group, thread gt converts rows
       // gt and gt + 64 of the CTA's 128 A rows: each fp32 row (128-byte
@@ -1402,9 +1293,9 @@ int launch_variant(const GemmArgs& g, KParams kp, int* dev_err, cudaStream_t str
 }
 
 // CTA-pair kernel: 256-row M tiles, 256-column N tiles.
-template <bool CV, bool SA = false, bool SB = false, bool H16 = false, bool LA = false>
+template <bool CV, bool SA = false, bool SB = false, bool H16 = false>
 int launch_pair(const GemmArgs& g, KParams kp, int* dev_err, cudaStream_t stream) {
-  using C = PairCfg<CV, SA, SB, H16, LA>;
+  using C = PairCfg<CV, SA, SB, H16>;
   CUtensorMap mA, mAlo, mB, mBlo;
   FG_TRY(make_map(&mA, g.A, g.M, g.K, g.lda, 128, 32));
   if (SA) FG_TRY(make_map(&mAlo, g.A_lo, g.M, g.K, g.lda, 128, 32)); else mAlo = mA;
@@ -1416,7 +1307,7 @@ int launch_pair(const GemmArgs& g, KParams kp, int* dev_err, cudaStream_t stream
   FG_TRY(prepare_out_maps(g, kp, &om));
   kp.ntm = (g.M + 255) / 256;
   kp.h16 = H16 ? 1 : 0;
-  auto kern = gemm_pair_kernel<CV, SA, SB, H16, LA>;
+  auto kern = gemm_pair_kernel<CV, SA, SB, H16>;
   static std::atomic<bool> attr_set[64];  // per device; max_pairs is stored before attr_set
   static std::atomic<int> max_pairs[64];
   int dev = 0;
@@ -1485,13 +1376,7 @@ int dispatch(const GemmArgs& g, KParams& kp, int* dev_err, cudaStream_t stream) 
     kp.ntn = (g.Nb + 255) / 256;
   }
   if (use_pair(g)) {
-    if (h16) {
-      // A's rows read by the converters from global memory (whole 32-column
-      // blocks, 16-byte aligned rows), else through TMA tiles
-      const bool la = g.K % 32 == 0 && g.lda % 4 == 0 && (reinterpret_cast<uintptr_t>(g.A) & 15) == 0;
-      if (la) return launch_pair<true, false, false, true, true>(g, kp, dev_err, stream);
-      return launch_pair<true, false, false, true>(g, kp, dev_err, stream);
-    }
+    if (h16) return launch_pair<true, false, false, true>(g, kp, dev_err, stream);
     if (g.B_lo) {
       if (g.A_lo) return launch_pair<false, true, true>(g, kp, dev_err, stream);
       if (g.a_lo_smem) return launch_pair<true, false, true>(g, kp, dev_err, stream);
@@ -1537,8 +1422,6 @@ int gemm_tn(const GemmArgs& g, int* dev_err, cudaStream_t stream) {
   kp.a_norm_k = sqrtf(float(g.K)) * (g.a_gain && g.a_gain_max > 0.f ? g.a_gain_max : 1.f);
   kp.a_rs = g.a_rs ? g.a_rs : g.epi.rowscale;
   kp.a_gain = g.a_gain;
-  kp.A = g.A;
-  kp.lda = g.lda;
   return dispatch(g, kp, dev_err, stream);
 }
 
