@@ -141,8 +141,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sRing + kStages * kStageBytes);
   // bars: 0 Q d-chunk 0 | 1..3 kv_full | 4..6 kv_empty | 7,8 s_full | 9,10 p_full |
   //       11,12 s_free | 13 o_prog | 14 o_final | 15 drain | 16..18 Q d-chunks 1..3 |
-  //       19 row-sum halves written | 20 Q buffer free | 21 row-sum halves read
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 22);
+  //       19 row-sum halves written | 20 Q buffer free | 21 row-sum halves read |
+  //       22..29 S read by both warps of a quadrant (quad · 2 + S buffer)
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 30);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   float* red = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);  // [8 warps][32 rows]
 
@@ -175,6 +176,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(red_full, 8);  // one arrive per softmax warp
     mbar_init(q_free, 1);
     mbar_init(red_free, 8);
+    for (int k = 0; k < 8; ++k) mbar_init(bar(22 + k), 2);  // one arrive per warp of the pair
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -489,6 +491,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const float mt = fmaxf(fmaxf(fmaxf(mt8[0], mt8[1]), fmaxf(mt8[2], mt8[3])),
                                fmaxf(fmaxf(mt8[4], mt8[5]), fmaxf(mt8[6], mt8[7])));
+        // Both warps of the quadrant have read all 128 columns of S before
+        // either writes its P over its own 64 (the other warp may still be
+        // in an earlier phase: the previous item's stores, say).
+        {
+          const uint32_t sr_bar = bar(22 + quad * 2 + sb);
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(sr_bar);
+          const bool both = waitb(sr_bar, uint32_t(jg >> 1) & 1u, abort_flag, p.err, kDevTimeoutAccFull);
+          if (!__all_sync(0xffffffffu, both)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
         const bool any = lo_c < hi_c && lo_c < kKT && hi_c > 0;
         float factor = 1.f;
         if (any) {
