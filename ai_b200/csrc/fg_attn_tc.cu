@@ -10,12 +10,7 @@
 // part: a TF32 hi/lo pair does not fit shared memory beside the K/V ring,
 // the bf16 pair does.)
 //
-// Persistent: one CTA per SM (10 warps, 512 TMEM columns, Q + a 3-stage
-// ring in shared memory) loops over work items (query tile of 128 rows,
-// head slot, sequence). The roles keep their pipelines running across
-// items: the next item's Q loads once the current item's score MMAs have
-// completed, its first score MMAs run while the softmax warps store the
-// current item's output.
+// One CTA per (query tile of 128 rows, query head, sequence), 6 warps:
 //   warp 0      TMA producer: Q (hi/lo, resident), then per key tile the K
 //               d-chunks and the Vᵀ (d-half × key-half) chunks through a
 //               3-stage ring of 32 KB, in the order the MMA warp uses them.
@@ -23,17 +18,16 @@
 //               S_j = Q·K_jᵀ into one of two 128-column S buffers while the
 //               softmax warps work on S_{j−1}; then O += P_{j−1}·V_{j−1}
 //               with P read from TMEM (A operand), O in columns 256..511.
-//   warps 2..9  softmax, two warps per query row quadrant: visibility by
-//               index arithmetic (padding: j < len; sliding layers:
-//               |i−j| < window), running max with lazy rescaling (O is
-//               rescaled in TMEM only when the max grows by more than 2^8),
-//               P = exp2 written back over S as packed bf16 hi/lo; the
-//               final 1/Σ and the row stores of the item's output.
+//   warps 2..5  softmax, one query row per thread: visibility by index
+//               arithmetic (padding: j < len; sliding layers: |i−j| < window),
+//               running max with lazy rescaling (O is rescaled in TMEM only
+//               when the max grows by more than 2^8), P = exp2 written back
+//               over S as packed bf16 hi/lo; the final 1/Σ and the store.
 // Head_dim 512 (EmbeddingGemma 2's global layers): Q (256 KB as split
 // bf16) does not fit beside the ring, so its d-chunks are streamed through
-// the ring with the K chunks they meet, and each item produces one 256-wide
+// the ring with the K chunks they meet, and each CTA produces one 256-wide
 // half of the output (O in TMEM stays 256 columns), the two halves of a
-// head being two items (head slot 2·head + half) that both compute S.
+// head being two CTAs (blockIdx.y = 2·head + half) that both compute S.
 // Key tiles outside a query tile's window or past the sequence length are
 // never loaded. Masked keys get weight exactly 0, as the reference's
 // flushing exp gives them (internal/kernel/generic.go:283-291).
@@ -59,8 +53,7 @@ constexpr int kStages = 3;
 constexpr uint32_t kChunk = 128 * 64 * 2;           // [128 rows × 64 bf16] = 16 KB
 constexpr uint32_t kQBytes = 2 * 4 * kChunk;        // Q hi/lo × 4 d-chunks = 128 KB
 constexpr uint32_t kStageBytes = 2 * kChunk;        // hi + lo chunk = 32 KB
-// Q, the K/V ring, 256 bytes of barriers, the row-sum exchange [8 warps × 32]
-constexpr size_t kSmem = 1024 + kQBytes + kStages * kStageBytes + 256 + 1024;
+constexpr size_t kSmem = 1024 + kQBytes + kStages * kStageBytes + 256;
 constexpr int kThreads = 320;  // producer, MMA issuer, 8 softmax warps
 constexpr uint32_t kIdesc = idesc_bf16(128, 128);
 constexpr float kRescaleLog2 = 8.f;  // rescale O when the max grows by more than 2^8
@@ -75,6 +68,7 @@ struct Params {
   float* out_lo;
   int64_t osb, osh, ost;
   int* err;
+  int tma_out, tma_out_lo;  // out / out_lo written by TMA stores (maps mO / mOlo)
 };
 
 // NC 64-column d-chunks per head (4: head_dim 256, Q resident; 8: head_dim
@@ -84,55 +78,12 @@ __device__ __forceinline__ bool waitb(uint32_t bar, uint32_t par, volatile int* 
   return mbar_wait(bar, par, ab, err, code);
 }
 
-// One work item of the persistent kernel: a query tile of one head slot
-// (the head, or 2·head + output half for 512-wide heads) of one sequence,
-// with the key tiles it sees. Items are numbered query tile fastest, then
-// head slot, then sequence, so the CTAs running at one time work on few
-// sequences and share their K/V in L2.
-struct Item {
-  int b, h, oh, hk, i0, qlen, klen, kt0, ntiles;
-};
-
-template <bool QS>
-__device__ __forceinline__ Item item_of(const Params& p, int w, int nqt) {
-  const int hslots = QS ? 2 * p.Hq : p.Hq;
-  Item it;
-  const int qt = w % nqt;
-  const int r = w / nqt;
-  const int hs = r % hslots;
-  it.b = r / hslots;
-  it.h = QS ? hs >> 1 : hs;
-  it.oh = QS ? hs & 1 : 0;
-  it.hk = it.h / (p.Hq / p.Hkv);
-  it.i0 = qt * kQ;
-  it.qlen = p.qlen ? min(p.qlen[it.b], p.T) : p.T;
-  it.klen = p.klen ? max(0, min(p.klen[it.b], p.S)) : p.S;
-  int kbeg = 0, kend = it.klen;
-  if (p.window > 0) {
-    kbeg = max(0, it.i0 - p.window + 1);
-    kend = min(it.klen, it.i0 + kQ - 1 + p.window);
-  }
-  if (it.i0 >= it.qlen || kend <= kbeg) {  // no row to compute or no visible key: zeros
-    it.kt0 = 0;
-    it.ntiles = 0;
-  } else {
-    it.kt0 = kbeg / kKT;
-    it.ntiles = (kend + kKT - 1) / kKT - it.kt0;
-  }
-  return it;
-}
-
-// Persistent: one CTA per SM runs items w = blockIdx.x, + gridDim.x, ...
-// The roles keep running counters across items, so the next item's Q load
-// (once every score MMA of the current item has completed), its first
-// score MMAs and the current item's output stores overlap. Barrier phases
-// of per-tile barriers follow the global tile count g; those of per-item
-// barriers the count of items with work (act).
 template <int NC, bool QS>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap mQ0, const __grid_constant__ CUtensorMap mQ1,
                    const __grid_constant__ CUtensorMap mK0, const __grid_constant__ CUtensorMap mK1,
                    const __grid_constant__ CUtensorMap mV0, const __grid_constant__ CUtensorMap mV1,
+                   const __grid_constant__ CUtensorMap mO, const __grid_constant__ CUtensorMap mOlo,
                    const __grid_constant__ Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -141,23 +92,50 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sRing + kStages * kStageBytes);
   // bars: 0 Q d-chunk 0 | 1..3 kv_full | 4..6 kv_empty | 7,8 s_full | 9,10 p_full |
   //       11,12 s_free | 13 o_prog | 14 o_final | 15 drain | 16..18 Q d-chunks 1..3 |
-  //       19 row-sum halves written | 20 Q buffer free | 21 row-sum halves read |
-  //       22..29 S read by both warps of a quadrant (quad · 2 + S buffer)
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 30);
+  //       19 row-sum halves exchanged | 20..27 S read by both warps of a
+  //       quadrant (quad · 2 + S buffer)
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 28);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  float* red = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);  // [8 warps][32 rows]
 
   constexpr int Dh = NC * 64;  // head dimension
+  const int qt = blockIdx.x, b = blockIdx.z;
+  const int h = QS ? int(blockIdx.y >> 1) : int(blockIdx.y);
+  const int oh = QS ? int(blockIdx.y & 1) : 0;  // output half of a 512-wide head
+  const int hk = h / (p.Hq / p.Hkv);
+  const int i0 = qt * kQ;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nqt = (p.T + kQ - 1) / kQ;
-  const int nitems = nqt * (QS ? 2 * p.Hq : p.Hq) * p.B;
+  const int qlen = p.qlen ? min(p.qlen[b], p.T) : p.T;
+  const int klen = p.klen ? max(0, min(p.klen[b], p.S)) : p.S;
+  float* obase = p.out + b * p.osb + h * p.osh + oh * kD;
+  float* olbase = p.out_lo ? p.out_lo + b * p.osb + h * p.osh + oh * kD : nullptr;
+  int kbeg = 0, kend = klen;
+  if (p.window > 0) {
+    kbeg = max(0, i0 - p.window + 1);
+    kend = min(klen, i0 + kQ - 1 + p.window);
+  }
+
+  if (i0 >= qlen || kend <= kbeg) {  // no row to compute or no visible key: zeros
+    for (int r = warp; r < kQ; r += kThreads / 32) {
+      const int i = i0 + r;
+      if (i >= p.T) break;
+      float* o = obase + i * p.ost;
+      float* ol = olbase ? olbase + i * p.ost : nullptr;
+      for (int c = lane; c < kD; c += 32) {
+        o[c] = 0.f;
+        if (ol) ol[c] = 0.f;
+      }
+    }
+    return;
+  }
+  const int kt0 = kbeg / kKT;
+  const int ntiles = (kend + kKT - 1) / kKT - kt0;
 
   auto bar = [&](int k) { return smem_u32(&bars[k]); };
   // Q arrives per 64-column d-chunk (hi and lo), so the first score MMAs
   // start when their chunk has landed rather than after all 128 KB.
   auto q_bar = [&](int c) { return c == 0 ? bar(0) : bar(15 + c); };
+  const uint32_t s_full0 = bar(7), p_full0 = bar(9), s_free0 = bar(11);
   const uint32_t o_prog = bar(13), o_final = bar(14), drain = bar(15);
-  const uint32_t red_full = bar(19), q_free = bar(20), red_free = bar(21);
 
   if (threadIdx.x == 0) {
     for (int c = 0; c < 4; ++c) mbar_init(q_bar(c), 1);
@@ -173,10 +151,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(o_prog, 1);
     mbar_init(o_final, 1);
     mbar_init(drain, 1);
-    mbar_init(red_full, 8);  // one arrive per softmax warp
-    mbar_init(q_free, 1);
-    mbar_init(red_free, 8);
-    for (int k = 0; k < 8; ++k) mbar_init(bar(22 + k), 2);  // one arrive per warp of the pair
+    mbar_init(bar(19), 8);  // row-sum halves written, one arrive per softmax warp
+    for (int k = 0; k < 8; ++k) mbar_init(bar(20 + k), 2);  // one arrive per warp of the pair
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -196,60 +172,50 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&mQ0);
       tma_prefetch_desc(&mK0);
       tma_prefetch_desc(&mV0);
+      const int qrow = b * p.T + i0;
+      if (!QS) {
+        for (int c = 0; c < 4; ++c) {
+          mbar_arrive_expect_tx(q_bar(c), 2 * kChunk);
+          tma_load_2d(smem_u32(sQ + (0 * 4 + c) * kChunk), &mQ0, q_bar(c), h * Dh + c * 64, qrow);
+          tma_load_2d(smem_u32(sQ + (1 * 4 + c) * kChunk), &mQ1, q_bar(c), h * Dh + c * 64, qrow);
+        }
+      }
       int armed[kStages] = {0, 0, 0};
-      int q_armed = 0;
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      int act = 0;
-      for (int w = blockIdx.x; w < nitems && ok; w += gridDim.x) {
-        const Item it = item_of<QS>(p, w, nqt);
-        if (it.ntiles == 0) continue;
-        const int qrow = it.b * p.T + it.i0;
-        if (!QS) {
-          // the Q buffer is free once every score MMA of the previous item has completed
-          if (act > 0 && !waitb(q_free, uint32_t(act - 1) & 1u, abort_flag, p.err, kDevTimeoutEmpty)) break;
-          for (int c = 0; c < 4; ++c) {
-            mbar_arrive_expect_tx(q_bar(c), 2 * kChunk);
-            tma_load_2d(smem_u32(sQ + (0 * 4 + c) * kChunk), &mQ0, q_bar(c), it.h * Dh + c * 64, qrow);
-            tma_load_2d(smem_u32(sQ + (1 * 4 + c) * kChunk), &mQ1, q_bar(c), it.h * Dh + c * 64, qrow);
-          }
-          ++q_armed;
+      auto next = [&](const CUtensorMap* m0, const CUtensorMap* m1, int x, int y) {
+        if (!waitb(bar(4 + stage), phase ^ 1, abort_flag, p.err, kDevTimeoutEmpty)) return false;
+        const uint32_t fb = bar(1 + stage);
+        mbar_arrive_expect_tx(fb, kStageBytes);
+        armed[stage]++;
+        uint8_t* dst = sRing + stage * kStageBytes;
+        tma_load_2d(smem_u32(dst), m0, fb, x, y);
+        tma_load_2d(smem_u32(dst + kChunk), m1, fb, x, y);
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1;
         }
-        auto next = [&](const CUtensorMap* m0, const CUtensorMap* m1, int x, int y) {
-          if (!waitb(bar(4 + stage), phase ^ 1, abort_flag, p.err, kDevTimeoutEmpty)) return false;
-          const uint32_t fb = bar(1 + stage);
-          mbar_arrive_expect_tx(fb, kStageBytes);
-          armed[stage]++;
-          uint8_t* dst = sRing + stage * kStageBytes;
-          tma_load_2d(smem_u32(dst), m0, fb, x, y);
-          tma_load_2d(smem_u32(dst + kChunk), m1, fb, x, y);
-          if (++stage == kStages) {
-            stage = 0;
-            phase ^= 1;
-          }
-          return true;
-        };
-        auto load_k = [&](int j) {
-          const int key0 = (it.kt0 + j) * kKT;
-          for (int c = 0; c < NC && ok; ++c) {
-            if (QS) ok = next(&mQ0, &mQ1, it.h * Dh + c * 64, qrow);  // Q chunk c, then the K chunk it meets
-            if (ok) ok = next(&mK0, &mK1, it.hk * Dh + c * 64, it.b * p.S + key0);
-          }
-        };
-        auto load_v = [&](int j) {
-          const int key0 = (it.kt0 + j) * kKT;
-          const int vrow = (it.b * p.Hkv + it.hk) * Dh + it.oh * kD;
-          for (int dh = 0; dh < 2 && ok; ++dh)
-            for (int kh = 0; kh < 2 && ok; ++kh) ok = next(&mV0, &mV1, key0 + kh * 64, vrow + dh * 128);
-        };
-        for (int j = 0; j < it.ntiles && ok; ++j) {
-          load_k(j);
-          if (j >= 1) load_v(j - 1);
+        return true;
+      };
+      auto load_k = [&](int j) {
+        const int key0 = (kt0 + j) * kKT;
+        for (int c = 0; c < NC && ok; ++c) {
+          if (QS) ok = next(&mQ0, &mQ1, h * Dh + c * 64, qrow);  // Q chunk c, then the K chunk it meets
+          if (ok) ok = next(&mK0, &mK1, hk * Dh + c * 64, b * p.S + key0);
         }
-        if (ok) load_v(it.ntiles - 1);
-        ++act;
+      };
+      auto load_v = [&](int j) {
+        const int key0 = (kt0 + j) * kKT;
+        const int vrow = (b * p.Hkv + hk) * Dh + oh * kD;
+        for (int dh = 0; dh < 2 && ok; ++dh)
+          for (int kh = 0; kh < 2 && ok; ++kh) ok = next(&mV0, &mV1, key0 + kh * 64, vrow + dh * 128);
+      };
+      for (int j = 0; j < ntiles && ok; ++j) {
+        load_k(j);
+        if (j >= 1) load_v(j - 1);
       }
+      if (ok) load_v(ntiles - 1);
       {
         // Every load issued above lands before the CTA retires, also when
         // another role gave up and left it unconsumed (after a normal run
@@ -260,9 +226,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           while (!mbar_try_wait(bar(1 + s), uint32_t(armed[s] - 1) & 1u))
             if (globaltimer_ns() - t0 > kWaitTimeoutNs) break;
         }
-        for (int c = 0; c < (q_armed > 0 ? 4 : 0); ++c) {
+        for (int c = 0; c < (QS ? 0 : 4); ++c) {
           const uint64_t t0 = globaltimer_ns();
-          while (!mbar_try_wait(q_bar(c), uint32_t(q_armed - 1) & 1u))
+          while (!mbar_try_wait(q_bar(c), 0))
             if (globaltimer_ns() - t0 > kWaitTimeoutNs) break;
         }
       }
@@ -274,12 +240,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       bool issued = false;
-      int g = 0;    // key tiles of the previous items (S buffer and per-tile barrier phases)
-      int act = 0;  // items with work before this one (per-item barrier phases)
-      // O += P_jj · V_jj for the global tile jg (local index jl of its item)
-      auto pv = [&](int jg, int jl) {
-        const int sb = jg & 1;
-        if (!waitb(bar(9 + sb), uint32_t(jg >> 1) & 1u, abort_flag, p.err, kDevTimeoutAccFull)) return false;
+      auto pv = [&](int jj) {
+        const int sb = jj & 1;
+        if (!waitb(bar(9 + sb), uint32_t(jj >> 1) & 1u, abort_flag, p.err, kDevTimeoutAccFull)) return false;
         tc_fence_after();
         const uint32_t tP = tmem + uint32_t(sb * 128);
         for (int dh = 0; dh < 2; ++dh) {
@@ -297,7 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const uint64_t b0 = sw128_kmajor_desc(v0 + kk * 32);
               const uint64_t b1 = sw128_kmajor_desc(v1 + kk * 32);
               const uint32_t d = tO + uint32_t(dh * 128);
-              const uint32_t first = (jl == 0 && kh == 0 && kk == 0) ? 0u : 1u;
+              const uint32_t first = (jj == 0 && kh == 0 && kk == 0) ? 0u : 1u;
               mma_bf16_ts(d, tP + hcol, b0, kIdesc, first);       // p_hi · v_hi
               mma_bf16_ts(d, tP + hcol, b1, kIdesc, 1u);          // p_hi · v_lo
               mma_bf16_ts(d, tP + hcol + 16, b0, kIdesc, 1u);     // p_lo · v_hi
@@ -313,87 +276,73 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_commit(o_prog);
         return true;
       };
-      for (int w = blockIdx.x; w < nitems && ok; w += gridDim.x) {
-        const Item it = item_of<QS>(p, w, nqt);
-        if (it.ntiles == 0) continue;
-        for (int j = 0; j < it.ntiles && ok; ++j) {
-          const int jg = g + j;
-          const int sb = jg & 1;
-          if (jg >= 2) {
-            if (!waitb(bar(11 + sb), uint32_t((jg - 2) >> 1) & 1u, abort_flag, p.err, kDevTimeoutAccEmpty)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
+      for (int j = 0; j < ntiles && ok; ++j) {
+        const int sb = j & 1;
+        if (j >= 2) {
+          if (!waitb(bar(11 + sb), uint32_t((j - 2) >> 1) & 1u, abort_flag, p.err, kDevTimeoutAccEmpty)) {
+            ok = false;
+            break;
           }
-          const uint32_t tS = tmem + uint32_t(sb * 128);
-          for (int c = 0; c < NC && ok; ++c) {
-            uint32_t q0, q1;
-            int qstage = 0;
-            if (QS) {
-              // the Q chunk occupies the ring stage before its K chunk
-              if (!waitb(bar(1 + stage), phase, abort_flag, p.err, kDevTimeoutFull)) {
-                ok = false;
-                break;
-              }
-              qstage = stage;
-              q0 = smem_u32(sRing + stage * kStageBytes);
-              q1 = q0 + kChunk;
-              if (++stage == kStages) {
-                stage = 0;
-                phase ^= 1;
-              }
-            } else {
-              if (j == 0 && !waitb(q_bar(c), uint32_t(act) & 1u, abort_flag, p.err, kDevTimeoutFull)) {
-                ok = false;
-                break;
-              }
-              q0 = smem_u32(sQ + c * kChunk);
-              q1 = smem_u32(sQ + (4 + c) * kChunk);
-            }
+          tc_fence_after();
+        }
+        const uint32_t tS = tmem + uint32_t(sb * 128);
+        for (int c = 0; c < NC && ok; ++c) {
+          uint32_t q0, q1;
+          int qstage = 0;
+          if (QS) {
+            // the Q chunk occupies the ring stage before its K chunk
             if (!waitb(bar(1 + stage), phase, abort_flag, p.err, kDevTimeoutFull)) {
               ok = false;
               break;
             }
-            tc_fence_after();
-            const uint32_t k0 = smem_u32(sRing + stage * kStageBytes);
-            const uint32_t k1 = k0 + kChunk;
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t a0 = sw128_kmajor_desc(q0 + kk * 32);
-              const uint64_t a1 = sw128_kmajor_desc(q1 + kk * 32);
-              const uint64_t b0 = sw128_kmajor_desc(k0 + kk * 32);
-              const uint64_t b1 = sw128_kmajor_desc(k1 + kk * 32);
-              mma_bf16_ss(tS, a0, b0, kIdesc, (c | kk) != 0 ? 1u : 0u);  // q_hi · k_hi
-              mma_bf16_ss(tS, a0, b1, kIdesc, 1u);                       // q_hi · k_lo
-              mma_bf16_ss(tS, a1, b0, kIdesc, 1u);                       // q_lo · k_hi
-            }
-            issued = true;
-            if (QS) mma_commit(bar(4 + qstage));
-            mma_commit(bar(4 + stage));
+            qstage = stage;
+            q0 = smem_u32(sRing + stage * kStageBytes);
+            q1 = q0 + kChunk;
             if (++stage == kStages) {
               stage = 0;
               phase ^= 1;
             }
+          } else {
+            if (j == 0 && !waitb(q_bar(c), 0, abort_flag, p.err, kDevTimeoutFull)) {
+              ok = false;
+              break;
+            }
+            q0 = smem_u32(sQ + c * kChunk);
+            q1 = smem_u32(sQ + (4 + c) * kChunk);
           }
-          if (!ok) break;
-          mma_commit(bar(7 + sb));
-          // every score MMA of the item is issued: the Q buffer is free when they complete
-          if (!QS && j == it.ntiles - 1) mma_commit(q_free);
-          if (j >= 1 && !pv(jg - 1, j - 1)) {
+          if (!waitb(bar(1 + stage), phase, abort_flag, p.err, kDevTimeoutFull)) {
             ok = false;
             break;
           }
+          tc_fence_after();
+          const uint32_t k0 = smem_u32(sRing + stage * kStageBytes);
+          const uint32_t k1 = k0 + kChunk;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t a0 = sw128_kmajor_desc(q0 + kk * 32);
+            const uint64_t a1 = sw128_kmajor_desc(q1 + kk * 32);
+            const uint64_t b0 = sw128_kmajor_desc(k0 + kk * 32);
+            const uint64_t b1 = sw128_kmajor_desc(k1 + kk * 32);
+            mma_bf16_ss(tS, a0, b0, kIdesc, (c | kk) != 0 ? 1u : 0u);  // q_hi · k_hi
+            mma_bf16_ss(tS, a0, b1, kIdesc, 1u);                       // q_hi · k_lo
+            mma_bf16_ss(tS, a1, b0, kIdesc, 1u);                       // q_lo · k_hi
+          }
+          issued = true;
+          if (QS) mma_commit(bar(4 + qstage));
+          mma_commit(bar(4 + stage));
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
         }
         if (!ok) break;
-        if (!pv(g + it.ntiles - 1, it.ntiles - 1)) {
+        mma_commit(bar(7 + sb));
+        if (j >= 1 && !pv(j - 1)) {
           ok = false;
           break;
         }
-        mma_commit(o_final);
-        g += it.ntiles;
-        ++act;
       }
+      if (ok && pv(ntiles - 1)) mma_commit(o_final);
       if (issued) {
         mma_commit(drain);
         const uint64_t t0 = globaltimer_ns();
@@ -414,229 +363,241 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quad = warp & 3;
     const int half = (warp - 2) >> 2;
     const int r = quad * 32 + lane;
+    const int i = i0 + r;
     const uint32_t lane_off = uint32_t(quad * 32) << 16;
+    // visible keys of row i: [vlo, vhi)
+    int vlo = 0, vhi = klen;
+    if (p.window > 0) {
+      vlo = max(0, i - p.window + 1);
+      vhi = min(klen, i + p.window);
+    }
     const float c = p.scale_log2;
-    const int col_base = half * 128;  // this warp's output columns
-    int g = 0, act = 0;
-    for (int w = blockIdx.x; w < nitems; w += gridDim.x) {
-      const Item it = item_of<QS>(p, w, nqt);
-      float* obase = p.out + it.b * p.osb + it.h * p.osh + it.oh * kD;
-      float* olbase = p.out_lo ? p.out_lo + it.b * p.osb + it.h * p.osh + it.oh * kD : nullptr;
-      if (it.ntiles == 0) {
-        // no row to compute or no visible key: zeros, spread over the 8 warps
-        for (int rr = warp - 2; rr < kQ; rr += 8) {
-          const int i = it.i0 + rr;
-          if (i >= p.T) break;
-          float* o = obase + i * p.ost;
-          float* ol = olbase ? olbase + i * p.ost : nullptr;
-          for (int cc = lane; cc < kD; cc += 32) {
-            o[cc] = 0.f;
-            if (ol) ol[cc] = 0.f;
-          }
+    float m = -FLT_MAX;
+    bool have = false;
+    float l = 0.f;  // this warp's columns only; the halves are added at the end
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      const int sb = j & 1;
+      const int key0 = (kt0 + j) * kKT;
+      const bool got = waitb(bar(7 + sb), uint32_t(j >> 1) & 1u, abort_flag, p.err, kDevTimeoutAccFull);
+      if (!__all_sync(0xffffffffu, got)) {  // warp-uniform before the collective tcgen05.ld
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t tS = tmem + lane_off + uint32_t(sb * 128);
+      const int lo_c = vlo - key0, hi_c = vhi - key0;  // visible columns [lo_c, hi_c)
+      const bool full_row = lo_c <= 0 && hi_c >= kKT;
+      const int span = max(0, hi_c - lo_c);  // col is visible iff unsigned(col - lo_c) < span
+      // pass 1: row maximum over the visible columns, two 64-column halves,
+      // eight independent chains (few live registers leave room for the
+      // long-latency exponentials and conversions of pass 2 to overlap)
+      float mt8[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) mt8[u] = -FLT_MAX;
+#pragma unroll 1
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t sr[2][32];
+        tmem_ld_32x32b_x32(tS + uint32_t(hh * 64), sr[0]);
+        tmem_ld_32x32b_x32(tS + uint32_t(hh * 64 + 32), sr[1]);
+        tmem_ld_wait();
+        if (full_row) {
+#pragma unroll
+          for (int q = 0; q < 2; ++q)
+#pragma unroll
+            for (int e = 0; e < 32; ++e) mt8[e & 7] = fmaxf(mt8[e & 7], __uint_as_float(sr[q][e]));
+        } else {
+#pragma unroll
+          for (int q = 0; q < 2; ++q)
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const int col = hh * 64 + q * 32 + e;
+              const bool in = unsigned(col - lo_c) < unsigned(span);
+              mt8[e & 7] = fmaxf(mt8[e & 7], in ? __uint_as_float(sr[q][e]) : -FLT_MAX);
+            }
         }
-        continue;
       }
-      const int i = it.i0 + r;
-      // visible keys of row i: [vlo, vhi)
-      int vlo = 0, vhi = it.klen;
-      if (p.window > 0) {
-        vlo = max(0, i - p.window + 1);
-        vhi = min(it.klen, i + p.window);
-      }
-      float m = -FLT_MAX;
-      bool have = false;
-      float l = 0.f;  // this warp's columns only; the halves are added at the end
-      bool ok = true;
-      for (int j = 0; j < it.ntiles; ++j) {
-        const int jg = g + j;
-        const int sb = jg & 1;
-        const int key0 = (it.kt0 + j) * kKT;
-        const bool got = waitb(bar(7 + sb), uint32_t(jg >> 1) & 1u, abort_flag, p.err, kDevTimeoutAccFull);
-        if (!__all_sync(0xffffffffu, got)) {  // warp-uniform before the collective tcgen05.ld
+      const float mt = fmaxf(fmaxf(fmaxf(mt8[0], mt8[1]), fmaxf(mt8[2], mt8[3])),
+                             fmaxf(fmaxf(mt8[4], mt8[5]), fmaxf(mt8[6], mt8[7])));
+      // Both warps of the quadrant have read all 128 columns of S before
+      // either writes its P over its own 64 columns.
+      {
+        const uint32_t sr_bar = bar(20 + quad * 2 + sb);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(sr_bar);
+        const bool both = waitb(sr_bar, uint32_t(j >> 1) & 1u, abort_flag, p.err, kDevTimeoutAccFull);
+        if (!__all_sync(0xffffffffu, both)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t tS = tmem + lane_off + uint32_t(sb * 128);
-        const int lo_c = vlo - key0, hi_c = vhi - key0;  // visible columns [lo_c, hi_c)
-        const bool full_row = lo_c <= 0 && hi_c >= kKT;
-        const int span = max(0, hi_c - lo_c);  // col is visible iff unsigned(col - lo_c) < span
-        // pass 1: row maximum over the visible columns, two 64-column halves,
-        // eight independent chains (few live registers leave room for the
-        // long-latency exponentials and conversions of pass 2 to overlap)
-        float mt8[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) mt8[u] = -FLT_MAX;
+      }
+      const bool any = lo_c < hi_c && lo_c < kKT && hi_c > 0;
+      float factor = 1.f;
+      if (any) {
+        if (!have) {
+          m = mt;
+          have = true;
+        } else if ((mt - m) * c > kRescaleLog2) {
+          factor = ex2_approx((m - mt) * c);
+          m = mt;
+        }
+      }
+      // O rows rescale (this warp's 128 columns): the whole warp takes part
+      // if any lane needs it
+      const bool need = factor != 1.f;
+      if (__any_sync(0xffffffffu, need) && j > 0) {
+        const bool done = waitb(o_prog, uint32_t(j - 1) & 1u, abort_flag, p.err, kDevTimeoutAccFull);
+        if (!__all_sync(0xffffffffu, done)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
 #pragma unroll 1
-        for (int hh = 0; hh < 2; ++hh) {
-          uint32_t sr[2][32];
-          tmem_ld_32x32b_x32(tS + uint32_t(hh * 64), sr[0]);
-          tmem_ld_32x32b_x32(tS + uint32_t(hh * 64 + 32), sr[1]);
-          tmem_ld_wait();
-          if (full_row) {
-#pragma unroll
-            for (int q = 0; q < 2; ++q)
-#pragma unroll
-              for (int e = 0; e < 32; ++e) mt8[e & 7] = fmaxf(mt8[e & 7], __uint_as_float(sr[q][e]));
-          } else {
-#pragma unroll
-            for (int q = 0; q < 2; ++q)
-#pragma unroll
-              for (int e = 0; e < 32; ++e) {
-                const int col = hh * 64 + q * 32 + e;
-                const bool in = unsigned(col - lo_c) < unsigned(span);
-                mt8[e & 7] = fmaxf(mt8[e & 7], in ? __uint_as_float(sr[q][e]) : -FLT_MAX);
-              }
-          }
-        }
-        const float mt = fmaxf(fmaxf(fmaxf(mt8[0], mt8[1]), fmaxf(mt8[2], mt8[3])),
-                               fmaxf(fmaxf(mt8[4], mt8[5]), fmaxf(mt8[6], mt8[7])));
-        // Both warps of the quadrant have read all 128 columns of S before
-        // either writes its P over its own 64 (the other warp may still be
-        // in an earlier phase: the previous item's stores, say).
-        {
-          const uint32_t sr_bar = bar(22 + quad * 2 + sb);
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(sr_bar);
-          const bool both = waitb(sr_bar, uint32_t(jg >> 1) & 1u, abort_flag, p.err, kDevTimeoutAccFull);
-          if (!__all_sync(0xffffffffu, both)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-        }
-        const bool any = lo_c < hi_c && lo_c < kKT && hi_c > 0;
-        float factor = 1.f;
-        if (any) {
-          if (!have) {
-            m = mt;
-            have = true;
-          } else if ((mt - m) * c > kRescaleLog2) {
-            factor = ex2_approx((m - mt) * c);
-            m = mt;
-          }
-        }
-        // O rows rescale (this warp's 128 columns): the whole warp takes part
-        // if any lane needs it, once the previous tile's P·V has completed
-        const bool need = factor != 1.f;
-        if (__any_sync(0xffffffffu, need) && j > 0) {
-          const bool done = waitb(o_prog, uint32_t(jg - 1) & 1u, abort_flag, p.err, kDevTimeoutAccFull);
-          if (!__all_sync(0xffffffffu, done)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-#pragma unroll 1
-          for (int ch = 0; ch < 4; ++ch) {
-            uint32_t ov[32];
-            const uint32_t ta = tO + lane_off + uint32_t(half * 128 + ch * 32);
-            tmem_ld_32x32b_x32(ta, ov);
-            tmem_ld_wait();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * factor);
-            tmem_st_32x32b_x32(ta, ov);
-          }
-          tmem_st_wait();
-        }
-        l *= factor;
-        const float mc = m * c;
-        // pass 2: probabilities of this warp's 64 columns, split into packed
-        // bf16 hi / lo. The 32-column chunk q of S is overwritten by its own
-        // P: hi (16 columns of bf16 pairs) at columns 32q.., lo at 32q+16..
-        float ps8[8];  // eight independent partial sums
-#pragma unroll
-        for (int u = 0; u < 8; ++u) ps8[u] = 0.f;
-        const bool all_vis = have && full_row;
-        {
-          const int hh = half;
-          uint32_t sr[2][32];
-          tmem_ld_32x32b_x32(tS + uint32_t(hh * 64), sr[0]);
-          tmem_ld_32x32b_x32(tS + uint32_t(hh * 64 + 32), sr[1]);
+        for (int ch = 0; ch < 4; ++ch) {
+          uint32_t ov[32];
+          const uint32_t ta = tO + lane_off + uint32_t(half * 128 + ch * 32);
+          tmem_ld_32x32b_x32(ta, ov);
           tmem_ld_wait();
 #pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            uint32_t hw[16], lw[16];
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-              const int col = hh * 64 + q * 32 + 2 * e;
-              float a, bb;
-              if (all_vis) {
-                a = ex2_approx(fmaf(__uint_as_float(sr[q][2 * e]), c, -mc));
-                bb = ex2_approx(fmaf(__uint_as_float(sr[q][2 * e + 1]), c, -mc));
-              } else {
-                // masked scores become -inf, whose exponential is exactly 0
-                const float s0 = unsigned(col - lo_c) < unsigned(span) ? __uint_as_float(sr[q][2 * e]) : -INFINITY;
-                const float s1 = unsigned(col + 1 - lo_c) < unsigned(span) ? __uint_as_float(sr[q][2 * e + 1]) : -INFINITY;
-                a = have ? ex2_approx(fmaf(s0, c, -mc)) : 0.f;
-                bb = have ? ex2_approx(fmaf(s1, c, -mc)) : 0.f;
-              }
-              ps8[e & 7] += a + bb;
-              const uint32_t h2 = pack_bf16x2(a, bb);  // RN bf16 of both, a in the low half
-              const float ah = __uint_as_float(h2 << 16), bh = __uint_as_float(h2 & 0xffff0000u);
-              hw[e] = h2;
-              lw[e] = pack_bf16x2(a - ah, bb - bh);
-            }
-            const uint32_t cq = uint32_t((hh * 2 + q) * 32);
-            tmem_st_32x32b_x16(tS + cq, hw);
-            tmem_st_32x32b_x16(tS + cq + 16, lw);
-          }
+          for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * factor);
+          tmem_st_32x32b_x32(ta, ov);
         }
-        l += ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
         tmem_st_wait();
-        tc_fence_before();
-        mbar_arrive(bar(9 + sb));
       }
-      if (!ok) break;
-      // -------------------------------------------------------- item epilogue
-      const bool fin = waitb(o_final, uint32_t(act) & 1u, abort_flag, p.err, kDevTimeoutAccFull);
-      if (!__all_sync(0xffffffffu, fin)) break;
+      l *= factor;
+      const float mc = m * c;
+      // pass 2: probabilities of this warp's 64 columns, split into packed
+      // bf16 hi / lo. The 32-column chunk q of S is overwritten by its own
+      // P: hi (16 columns of bf16 pairs) at columns 32q.., lo at 32q+16..
+      float ps8[8];  // eight independent partial sums
+#pragma unroll
+      for (int u = 0; u < 8; ++u) ps8[u] = 0.f;
+      const bool all_vis = have && full_row;
+      {
+        const int hh = half;
+        uint32_t sr[2][32];
+        tmem_ld_32x32b_x32(tS + uint32_t(hh * 64), sr[0]);
+        tmem_ld_32x32b_x32(tS + uint32_t(hh * 64 + 32), sr[1]);
+        tmem_ld_wait();
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          uint32_t hw[16], lw[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            const int col = hh * 64 + q * 32 + 2 * e;
+            float a, bb;
+            if (all_vis) {
+              a = ex2_approx(fmaf(__uint_as_float(sr[q][2 * e]), c, -mc));
+              bb = ex2_approx(fmaf(__uint_as_float(sr[q][2 * e + 1]), c, -mc));
+            } else {
+              // masked scores become -inf, whose exponential is exactly 0
+              const float s0 = unsigned(col - lo_c) < unsigned(span) ? __uint_as_float(sr[q][2 * e]) : -INFINITY;
+              const float s1 = unsigned(col + 1 - lo_c) < unsigned(span) ? __uint_as_float(sr[q][2 * e + 1]) : -INFINITY;
+              a = have ? ex2_approx(fmaf(s0, c, -mc)) : 0.f;
+              bb = have ? ex2_approx(fmaf(s1, c, -mc)) : 0.f;
+            }
+            ps8[e & 7] += a + bb;
+            const uint32_t h2 = pack_bf16x2(a, bb);  // RN bf16 of both, a in the low half
+            const float ah = __uint_as_float(h2 << 16), bh = __uint_as_float(h2 & 0xffff0000u);
+            hw[e] = h2;
+            lw[e] = pack_bf16x2(a - ah, bb - bh);
+          }
+          const uint32_t cq = uint32_t((hh * 2 + q) * 32);
+          tmem_st_32x32b_x16(tS + cq, hw);
+          tmem_st_32x32b_x16(tS + cq + 16, lw);
+        }
+      }
+      l += ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(bar(9 + sb));
+    }
+    // ---------------------------------------------------------- epilogue
+    const bool fin = ok && waitb(o_final, 0, abort_flag, p.err, kDevTimeoutAccFull);
+    if (__all_sync(0xffffffffu, fin)) {
       tc_fence_after();
-      // row sum = both halves' sums: each warp's l through shared memory
-      // (written once the previous item's values have been read by all)
-      if (act > 0) {
-        const bool freed = waitb(red_free, uint32_t(act - 1) & 1u, abort_flag, p.err, kDevTimeoutAccFull);
-        if (!__all_sync(0xffffffffu, freed)) break;
-      }
+      // row sum = both halves' sums (l of the other warp of the quadrant,
+      // through the K/V ring, free now that every MMA has completed)
+      float* red = reinterpret_cast<float*>(sRing);
       red[(half * 4 + quad) * 32 + lane] = l;
       __syncwarp();
-      if (lane == 0) mbar_arrive(red_full);
-      const bool both = waitb(red_full, uint32_t(act) & 1u, abort_flag, p.err, kDevTimeoutAccFull);
-      if (!__all_sync(0xffffffffu, both)) break;
+      if (lane == 0) mbar_arrive(bar(19));  // a bounded wait, unlike a named barrier, cannot hang
+      waitb(bar(19), 0, abort_flag, p.err, kDevTimeoutAccFull);
       const float l_lo = red[quad * 32 + lane], l_hi = red[(4 + quad) * 32 + lane];
-      __syncwarp();
-      if (lane == 0) mbar_arrive(red_free);
       const float lsum = l_lo + l_hi;  // same order in both warps
       const bool row_ok = i < p.T;
-      const float inv = (i < it.qlen && lsum > 0.f) ? 1.f / lsum : 0.f;
-      // O of this warp's 32 rows × 128 columns, read out of TMEM (before the
-      // next item's first P·V, which waits for this warp's next arrive) and
-      // stored row by row
-      float* o = obase + int64_t(i) * p.ost + col_base;
-      float* ol = olbase ? olbase + int64_t(i) * p.ost + col_base : nullptr;
+      const float inv = (i < qlen && lsum > 0.f) ? 1.f / lsum : 0.f;
+      const int col_base = half * 128;  // this warp's output columns
+      if (p.tma_out) {
+        // The warp's 32 rows × 128 columns as four [32 × 32] boxes in its
+        // 16 KB of the Q region (every MMA that read Q has completed), then
+        // TMA stores; rows past the sequence end fall outside the map.
+        uint8_t* stg = sQ + size_t(warp - 2) * 16384;
+        const int tw = i0 + quad * 32;
+        const int parts = olbase ? 2 : 1;
 #pragma unroll 1
-      for (int ch = 0; ch < 4; ++ch) {
-        uint32_t ov[32];
-        tmem_ld_32x32b_x32(tO + lane_off + uint32_t(col_base + ch * 32), ov);
-        tmem_ld_wait();
-        if (row_ok) {
-          float4* o4 = reinterpret_cast<float4*>(o + ch * 32);
-          float4* l4 = ol ? reinterpret_cast<float4*>(ol + ch * 32) : nullptr;
+        for (int part = 0; part < parts; ++part) {
+          if (part == 1) {
+            if (lane == 0) tma_store_wait_read<0>();  // the hi boxes have been read
+            __syncwarp();
+          }
+#pragma unroll 1
+          for (int ch = 0; ch < 4; ch += 2) {
+            uint32_t ov[2][32];
+            tmem_ld_32x32b_x32(tO + lane_off + uint32_t(col_base + ch * 32), ov[0]);
+            tmem_ld_32x32b_x32(tO + lane_off + uint32_t(col_base + ch * 32 + 32), ov[1]);
+            tmem_ld_wait();
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            float4 v;
-            v.x = __uint_as_float(ov[4 * e]) * inv;
-            v.y = __uint_as_float(ov[4 * e + 1]) * inv;
-            v.z = __uint_as_float(ov[4 * e + 2]) * inv;
-            v.w = __uint_as_float(ov[4 * e + 3]) * inv;
-            o4[e] = v;
-            if (l4) l4[e] = make_float4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
+            for (int u = 0; u < 2; ++u) {
+              float4* rowp = reinterpret_cast<float4*>(stg + (ch + u) * 4096 + lane * 128);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                float4 v;
+                v.x = __uint_as_float(ov[u][4 * e]) * inv;
+                v.y = __uint_as_float(ov[u][4 * e + 1]) * inv;
+                v.z = __uint_as_float(ov[u][4 * e + 2]) * inv;
+                v.w = __uint_as_float(ov[u][4 * e + 3]) * inv;
+                if (part == 1) v = make_float4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
+                rowp[e ^ (lane & 7)] = v;  // 128-byte swizzle: chunk e of row r at e ^ (r % 8)
+              }
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && tw < p.T) {
+            for (int ch = 0; ch < 4; ++ch)
+              tma_store_3d(part ? &mOlo : &mO, smem_u32(stg + ch * 4096), h * Dh + oh * kD + col_base + ch * 32, tw, b);
+            tma_store_commit();
+          }
+        }
+        if (lane == 0) tma_store_wait_read<0>();  // the boxes are read; the writes complete on their own
+        __syncwarp();
+      } else {
+        float* o = obase + int64_t(i) * p.ost + col_base;
+        float* ol = olbase ? olbase + int64_t(i) * p.ost + col_base : nullptr;
+#pragma unroll 1
+        for (int ch = 0; ch < 4; ++ch) {
+          uint32_t ov[32];
+          tmem_ld_32x32b_x32(tO + lane_off + uint32_t(col_base + ch * 32), ov);
+          tmem_ld_wait();
+          if (row_ok) {
+            float4* o4 = reinterpret_cast<float4*>(o + ch * 32);
+            float4* l4 = ol ? reinterpret_cast<float4*>(ol + ch * 32) : nullptr;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              float4 v;
+              v.x = __uint_as_float(ov[4 * e]) * inv;
+              v.y = __uint_as_float(ov[4 * e + 1]) * inv;
+              v.z = __uint_as_float(ov[4 * e + 2]) * inv;
+              v.w = __uint_as_float(ov[4 * e + 3]) * inv;
+              o4[e] = v;
+              if (l4) l4[e] = make_float4(tf32_lo(v.x), tf32_lo(v.y), tf32_lo(v.z), tf32_lo(v.w));
+            }
           }
         }
       }
-      tc_fence_before();
-      g += it.ntiles;
-      ++act;
     }
   }
 
@@ -717,6 +678,20 @@ int make_map_bf16(CUtensorMap* m, const void* ptr, int64_t rows, int64_t cols, i
   return FG_OK;
 }
 
+// fp32 output viewed as [B][T][cols] (row stride ost, sequence stride osb,
+// in elements), [1 × 32 × 32] boxes with 128-byte swizzling.
+int make_map_out3d(CUtensorMap* m, const float* ptr, int B, int T, int64_t cols, int64_t ost, int64_t osb) {
+  cuuint64_t dims[3] = {cuuint64_t(cols), cuuint64_t(T), cuuint64_t(B)};
+  cuuint64_t strides[2] = {cuuint64_t(ost) * 4, cuuint64_t(osb) * 4};
+  cuuint32_t box[3] = {32u, 32u, 1u};
+  cuuint32_t es[3] = {1u, 1u, 1u};
+  CUresult r = g_encode_bf16(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(ptr), dims, strides, box,
+                             es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(FG_ECUDA, "cuTensorMapEncodeTiled (attention output) failed (%d)", int(r));
+  return FG_OK;
+}
+
 }  // namespace
 
 size_t attn_tc_workspace_bytes(int B, int T, int S, int Hq, int Hkv, int D) {
@@ -788,6 +763,21 @@ int attention_tc_operands(const AttnArgs& a, const AttnOperands& o, int* err, cu
   prm.osh = a.osh;
   prm.ost = a.ost;
   prm.err = err;
+  // Output as a [B][T][cols] tensor with row stride ost: TMA stores when
+  // the heads are contiguous 256-column blocks and the strides allow it.
+  CUtensorMap mo = mq0, mol = mq0;
+  auto tma_ok = [&](const float* ptr) {
+    return ptr && (reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && a.osh == Dh && a.ost % 4 == 0 &&
+           a.osb % 4 == 0 && a.ost >= int64_t(Hq) * Dh && a.osb >= int64_t(T) * a.ost;
+  };
+  prm.tma_out = 0;
+  prm.tma_out_lo = 0;
+  if (tma_ok(a.out) && (a.out_lo == nullptr || tma_ok(a.out_lo))) {
+    FG_TRY(make_map_out3d(&mo, a.out, B, T, Hq * Dh, a.ost, a.osb));
+    if (a.out_lo) FG_TRY(make_map_out3d(&mol, a.out_lo, B, T, Hq * Dh, a.ost, a.osb));
+    prm.tma_out = 1;
+    prm.tma_out_lo = a.out_lo ? 1 : 0;
+  }
   static std::atomic<bool> attr[64][2];  // per device and head width
   int dev = 0;
   cudaGetDevice(&dev);
@@ -799,14 +789,13 @@ int attention_tc_operands(const AttnArgs& a, const AttnOperands& o, int* err, cu
       FG_CUDA_TRY(cudaFuncSetAttribute(attn_tc_kernel<4, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(kSmem)));
     attr[dev & 63][wide] = true;
   }
-  // persistent: one CTA per SM over every (query tile, head slot, sequence)
-  const int64_t items = int64_t((T + kQ - 1) / kQ) * Hq * (wide + 1) * B;
-  if (items > INT32_MAX) return set_error(FG_EINVAL, "attention has too many work items");
-  const int grid = int(std::min<int64_t>(items, sm_count()));
+  if ((T + kQ - 1) / kQ > 65535 || B > 65535 || Hq * (wide + 1) > 65535)
+    return set_error(FG_EINVAL, "attention grid too large");
+  dim3 grid(unsigned((T + kQ - 1) / kQ), unsigned(Hq * (wide + 1)), unsigned(B));
   if (wide)
-    attn_tc_kernel<8, true><<<grid, kThreads, kSmem, s>>>(mq0, mq1, mk0, mk1, mv0, mv1, prm);
+    attn_tc_kernel<8, true><<<grid, kThreads, kSmem, s>>>(mq0, mq1, mk0, mk1, mv0, mv1, mo, mol, prm);
   else
-    attn_tc_kernel<4, false><<<grid, kThreads, kSmem, s>>>(mq0, mq1, mk0, mk1, mv0, mv1, prm);
+    attn_tc_kernel<4, false><<<grid, kThreads, kSmem, s>>>(mq0, mq1, mk0, mk1, mv0, mv1, mo, mol, prm);
   FG_CUDA_TRY(cudaGetLastError());
   return FG_OK;
 }
