@@ -28,6 +28,8 @@
 #include <cstdlib>
 #include <cudaTypedefs.h>
 
+#include <cuda_fp16.h>
+
 #include "fg_internal.h"
 #include "fg_ptx.cuh"
 
@@ -51,6 +53,7 @@ struct KParams {
   // the epilogue multiplies each row by 2^-(e_r + b_exp), which is exact.
   int h16;
   int a_exp, a_exp_rs, b_exp;
+  const int* b_exp_dev;  // when set, B's exponent as the device computed it (overrides b_exp)
   float a_norm_k;      // sqrt(K): max|a_r| <= sqrt(K) / a_rs[r]
   const float* a_rs;   // A's row scales 1/sqrt(mean(a²) + eps) (a_exp_rs)
   const float* a_gain;  // per-column gain on A (split-fp16 with an unfolded B), or null
@@ -476,7 +479,8 @@ __device__ __forceinline__ void epilogue_tile(const KParams& p, const OutMaps& o
   float rs = (rowscale && row_ok) ? rowscale[row] : 1.f;
   // split-fp16: undo the operands' power-of-two scales (exact); applied to
   // the accumulator first where a bias is added before the row scale
-  const float fac = p.h16 ? pow2f(-(a_row_exp(p, row) + p.b_exp)) : 1.f;
+  const int bexp = p.b_exp_dev ? *p.b_exp_dev : p.b_exp;
+  const float fac = p.h16 ? pow2f(-(a_row_exp(p, row) + bexp)) : 1.f;
   if (!bias) rs *= fac;
   if (qkv) {
     qkv_attn_epilogue(e, om, p.tma_qk != 0, taddr, tn, row, row_ok, rs, es, rows);
@@ -825,9 +829,17 @@ __global__ void __launch_bounds__(Cfg<BN, SA, SB, BK, CV>::kThreads, 1)
 // kind::f16 (K = 16) instead of 2 × 4 of kind::tf32 (K = 8) — half the
 // tensor-pipe time for the same products. Stage: A (then A_hi | A_lo) | B,
 // 24 KB, so 8 stages are in flight.
+//
+// H16 with SB: B has no exact fp16 form (an fp32 checkpoint, or the
+// op-level product's arbitrary operand), so it comes as two fp16 parts under
+// one power-of-two scale, B_hi (its top 11 significant bits) and B_lo =
+// fp16(B − B_hi), and each stage adds the A_hi·B_lo pass: A_hi·B_hi +
+// A_hi·B_lo + A_lo·B_hi (A_lo·B_lo, 2^-22 of the product, is dropped, as in
+// split-TF32) — three fp16 passes, the tensor-pipe time of 1.5 TF32 passes.
+// Stage: A (then its parts) | B_hi | B_lo = 32 KB, 6 stages.
 template <bool CV, bool SA = false, bool SB = false, bool H16 = false>
 struct PairCfg {
-  static_assert(!H16 || (CV && !SA && !SB), "split-fp16 takes A's parts from the converters");
+  static_assert(!H16 || (CV && !SA), "split-fp16 takes A's parts from the converters");
   static constexpr int BN = 256, BK = 32;
   static constexpr int kThreads = 320;
   static constexpr bool kLo = CV || SA;
@@ -835,7 +847,7 @@ struct PairCfg {
   static constexpr uint32_t kBBytes = 128 * BK * (H16 ? 2 : 4);  // this CTA's half of the B rows
   static constexpr uint32_t kPartBytes = 128 * BK * 2;  // one fp16 part of A (H16), in A's place
   static constexpr uint32_t kStageBytes =
-      H16 ? kABytes + kBBytes : kABytes * (kLo ? 2 : 1) + kBBytes * (SB ? 2 : 1);
+      H16 ? kABytes + kBBytes * (SB ? 2 : 1) : kABytes * (kLo ? 2 : 1) + kBBytes * (SB ? 2 : 1);
   static constexpr uint32_t kBOffset = H16 ? kABytes : kABytes * (kLo ? 2 : 1);
   static constexpr uint32_t kTmaBytes = kABytes * (SA ? 2 : 1) + kBBytes * (SB ? 2 : 1);
   static constexpr uint32_t kEpiStageBytes = kEpiStageBytesAll;
@@ -978,12 +990,15 @@ __global__ void __launch_bounds__(320, 1)
           const uint32_t b_addr = a_addr + C::kBOffset;
           const uint32_t blo_addr = b_addr + C::kBBytes;
           if constexpr (H16) {
-            // hi·B then lo·B, K = 16 fp16 (32 bytes of the 64-byte rows) per MMA
+            // hi·B (and hi·B_lo) then lo·B, K = 16 fp16 (32 bytes of the
+            // 64-byte rows) per MMA
             const uint32_t hi_addr = a_addr, lo_addr = a_addr + C::kPartBytes;
 #pragma unroll
-            for (int k = 0; k < BK / 16; ++k)
-              mma_f16_pair(d_tmem, kmajor_desc<64>(hi_addr + k * 32), kmajor_desc<64>(b_addr + k * 32), kIdesc,
-                           (kb | k) != 0 ? 1u : 0u);
+            for (int k = 0; k < BK / 16; ++k) {
+              const uint64_t da = kmajor_desc<64>(hi_addr + k * 32);
+              mma_f16_pair(d_tmem, da, kmajor_desc<64>(b_addr + k * 32), kIdesc, (kb | k) != 0 ? 1u : 0u);
+              if (SB) mma_f16_pair(d_tmem, da, kmajor_desc<64>(blo_addr + k * 32), kIdesc, 1u);
+            }
 #pragma unroll
             for (int k = 0; k < BK / 16; ++k)
               mma_f16_pair(d_tmem, kmajor_desc<64>(lo_addr + k * 32), kmajor_desc<64>(b_addr + k * 32), kIdesc, 1u);
@@ -1301,7 +1316,9 @@ int launch_pair(const GemmArgs& g, KParams kp, int* dev_err, cudaStream_t stream
   if (SA) FG_TRY(make_map(&mAlo, g.A_lo, g.M, g.K, g.lda, 128, 32)); else mAlo = mA;
   if (H16) FG_TRY(make_map_f16(&mB, g.B16, g.Nb, g.K, g.ldb, 128));
   else FG_TRY(make_map(&mB, g.B, g.Nb, g.K, g.ldb, 128, 32));
-  if (SB) FG_TRY(make_map(&mBlo, g.B_lo, g.Nb, g.K, g.ldb, 128, 32)); else mBlo = mB;
+  if (SB && H16) FG_TRY(make_map_f16(&mBlo, g.B16_lo, g.Nb, g.K, g.ldb, 128));
+  else if (SB) FG_TRY(make_map(&mBlo, g.B_lo, g.Nb, g.K, g.ldb, 128, 32));
+  else mBlo = mB;
   OutMaps om;
   for (CUtensorMap& m : om.m) m = mA;
   FG_TRY(prepare_out_maps(g, kp, &om));
@@ -1376,7 +1393,10 @@ int dispatch(const GemmArgs& g, KParams& kp, int* dev_err, cudaStream_t stream) 
     kp.ntn = (g.Nb + 255) / 256;
   }
   if (use_pair(g)) {
-    if (h16) return launch_pair<true, false, false, true>(g, kp, dev_err, stream);
+    if (h16) {
+      if (g.B16_lo) return launch_pair<true, false, true, true>(g, kp, dev_err, stream);
+      return launch_pair<true, false, false, true>(g, kp, dev_err, stream);
+    }
     if (g.B_lo) {
       if (g.A_lo) return launch_pair<false, true, true>(g, kp, dev_err, stream);
       if (g.a_lo_smem) return launch_pair<true, false, true>(g, kp, dev_err, stream);
@@ -1418,6 +1438,7 @@ int gemm_tn(const GemmArgs& g, int* dev_err, cudaStream_t stream) {
   kp.a_exp = g.a_exp;
   kp.a_exp_rs = g.a_exp_rs;
   kp.b_exp = g.b_exp;
+  kp.b_exp_dev = g.b_exp_dev;
   // all-zero gains make A zero: any exponent serves, keep the bound positive
   kp.a_norm_k = sqrtf(float(g.K)) * (g.a_gain && g.a_gain_max > 0.f ? g.a_gain_max : 1.f);
   kp.a_rs = g.a_rs ? g.a_rs : g.epi.rowscale;
@@ -1457,6 +1478,76 @@ __global__ void transpose_kernel(const float* __restrict__ src, int64_t lds, int
   }
 }
 }  // namespace
+
+namespace {
+// |x| maximum as float bits (non-negative floats order like their bits)
+__global__ void abs_max_kernel(const float* __restrict__ x, int64_t ld, int64_t rows, int64_t cols,
+                               unsigned* __restrict__ out) {
+  float m = 0.f;
+  const int64_t total = rows * cols;
+  for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < total; e += int64_t(gridDim.x) * blockDim.x)
+    m = fmaxf(m, fabsf(x[(e / cols) * ld + e % cols]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(out, __float_as_uint(m));
+}
+
+__global__ void split_f16_kernel(const float* __restrict__ x, int64_t ld, int64_t rows, int64_t cols,
+                                 const unsigned* __restrict__ maxbits, uint16_t* __restrict__ hi,
+                                 uint16_t* __restrict__ lo, int64_t ldo, int* __restrict__ exp_out) {
+  const float mx = __uint_as_float(*maxbits);
+  // max·2^t < 2^14: both parts finite, every element down to 2^-17 of the
+  // maximum keeps 22 significant bits
+  const int t = mx > 0.f && isfinite(mx) ? max(-60, min(60, 13 - ilogbf(mx))) : 0;
+  if (blockIdx.x == 0 && threadIdx.x == 0) *exp_out = t;
+  const float sc = pow2f(t);
+  const int64_t total = rows * cols;
+  for (int64_t e = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; e < total; e += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = e / cols, c = e % cols;
+    const float v = x[r * ld + c] * sc;
+    const float h = tf32_hi(v);
+    hi[r * ldo + c] = __half_as_ushort(__float2half_rn(h));
+    lo[r * ldo + c] = __half_as_ushort(__float2half_rn(v - h));
+  }
+}
+
+// one warp per row
+__global__ void row_inv_rms_kernel(const float* __restrict__ x, int64_t ld, int64_t rows, int64_t cols,
+                                   float* __restrict__ rs) {
+  const int64_t r = blockIdx.x * int64_t(blockDim.x / 32) + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const int lane = threadIdx.x & 31;
+  float ss = 0.f;
+  for (int64_t c = lane; c < cols; c += 32) {
+    const float v = x[r * ld + c];
+    ss = fmaf(v, v, ss);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if (lane == 0) rs[r] = 1.f / sqrtf(fmaxf(ss / float(cols), 1e-30f));
+}
+}  // namespace
+
+int split_f16_parts(const float* x, int64_t ld, int64_t rows, int64_t cols, uint16_t* hi, uint16_t* lo,
+                    int64_t ldo, unsigned* scratch_max, int* exp_out, cudaStream_t stream) {
+  if (rows <= 0 || cols <= 0) return FG_OK;
+  FG_CUDA_TRY(cudaMemsetAsync(scratch_max, 0, sizeof(unsigned), stream));
+  const int64_t total = rows * cols;
+  const int grid = int(std::min<int64_t>((total + 255) / 256, int64_t(sm_count()) * 8));
+  abs_max_kernel<<<grid, 256, 0, stream>>>(x, ld, rows, cols, scratch_max);
+  FG_CUDA_TRY(cudaGetLastError());
+  split_f16_kernel<<<grid, 256, 0, stream>>>(x, ld, rows, cols, scratch_max, hi, lo, ldo, exp_out);
+  FG_CUDA_TRY(cudaGetLastError());
+  return FG_OK;
+}
+
+int row_inv_rms(const float* x, int64_t ld, int64_t rows, int64_t cols, float* rs, cudaStream_t stream) {
+  if (rows <= 0) return FG_OK;
+  const int64_t blocks = (rows + 7) / 8;
+  row_inv_rms_kernel<<<unsigned(blocks), 256, 0, stream>>>(x, ld, rows, cols, rs);
+  FG_CUDA_TRY(cudaGetLastError());
+  return FG_OK;
+}
 
 int split_tf32(const float* x, float* hi, float* lo, int64_t n, int* any, cudaStream_t stream) {
   if (n <= 0) return FG_OK;

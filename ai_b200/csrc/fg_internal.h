@@ -127,7 +127,11 @@ struct GemmArgs {
   // so that |A|·2^e_r < 2^14. The products are
   // A_hi·B + A_lo·B in kind::f16; the epilogue undoes the scales exactly.
   const uint16_t* B16 = nullptr;
+  // B without an exact fp16 form: B16 its high part, B16_lo = fp16(B·2^b_exp
+  // − B16) its low part (the product adds the A_hi·B_lo pass)
+  const uint16_t* B16_lo = nullptr;
   int b_exp = 0;
+  const int* b_exp_dev = nullptr;  // b_exp in device memory (computed there), overriding b_exp
   int a_exp = 0;
   int a_exp_rs = 0;
   const float* a_rs = nullptr;  // row scales behind a_exp_rs (null: epi.rowscale)
@@ -148,15 +152,27 @@ bool gemm_h16_applies(int M);
 // and its run on a given scratch pointer of plan.total() bytes (fg_ops.cu).
 struct MatmulPlan {
   bool a_direct, b_direct, split;
-  int64_t kp, ldb;
-  size_t a_bytes, bt_bytes, blo_bytes;
-  size_t total() const { return a_bytes + bt_bytes + blo_bytes; }
+  bool h16;  // split-fp16: B as fp16 hi/lo parts, A's parts made by the converters
+  int64_t kp, ldb, kp16;
+  size_t a_bytes, bt_bytes, blo_bytes, b16_bytes, rs_bytes, misc_bytes;
+  size_t total() const { return a_bytes + bt_bytes + blo_bytes + b16_bytes + rs_bytes + misc_bytes; }
 };
 MatmulPlan plan_matmul(int64_t m, int64_t n, int64_t k, const float* x, int64_t ldx, const float* w,
                        int64_t ldw, int w_transposed, int precision);
 int matmul_run(const MatmulPlan& p, int64_t m, int64_t n, int64_t k, const float* x, int64_t ldx,
                const float* w, int64_t ldw, int w_transposed, float* out, int64_t ldo,
                const fg_epilogue* epi, void* scratch, int* err, cudaStream_t s);
+
+// fp16 parts of a row-major [rows, cols] fp32 matrix (leading dimension
+// ld) under one power-of-two scale 2^t chosen on the device from its
+// largest magnitude (max·2^t < 2^14): hi = the top 11 significant bits of
+// x·2^t, lo = fp16(x·2^t − hi), both [rows, ldo]; t goes to *exp_out.
+// scratch_max: one device word this call clears and uses.
+int split_f16_parts(const float* x, int64_t ld, int64_t rows, int64_t cols, uint16_t* hi, uint16_t* lo,
+                    int64_t ldo, unsigned* scratch_max, int* exp_out, cudaStream_t stream);
+// Row scales rs[r] = 1/sqrt(Σ_c x[r, c]² / cols), finite for zero rows: the
+// split-fp16 converters' exponent bound (max|x_r| ≤ sqrt(cols)/rs[r]).
+int row_inv_rms(const float* x, int64_t ld, int64_t rows, int64_t cols, float* rs, cudaStream_t stream);
 
 // Elementwise split of n floats into TF32 high and exact low parts.
 // *any_lo_nonzero (device int, optional) is set to 1 when some low part is non-zero.

@@ -93,6 +93,10 @@ struct DevMat {
   // (|gain| <= h16_gmax), which the split-fp16 GEMM applies to A instead
   const float* h16_gain = nullptr;
   float h16_gmax = 1.f;
+  // a weight with no exact fp16 form (an fp32 checkpoint): h16 holds the
+  // high part (top 11 significant bits of w·2^h16_exp) and h16_lo =
+  // fp16(w·2^h16_exp − high), for the three-pass split-fp16 product
+  uint16_t* h16_lo = nullptr;
 };
 
 // A projection resident as bf16 (FG_WEIGHTS_BF16): [rows, cols] bits and
@@ -379,6 +383,59 @@ bool h16_exponent(double bound, int* e) {
   if (!(bound > 0) || !std::isfinite(bound)) return false;
   *e = 13 - std::ilogb(bound);
   return *e > -100 && *e < 100;
+}
+
+// Round-to-nearest-even fp16 bits of an fp32 value (subnormals included;
+// the split forms' magnitudes stay below 2^15).
+uint16_t f16_rn(float f) {
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  const uint32_t sign = (u >> 16) & 0x8000u, ex = (u >> 23) & 0xffu, mant = u & 0x7fffffu;
+  if (ex == 0xffu) return uint16_t(sign | 0x7c00u | (mant ? 0x200u : 0u));
+  const int e = int(ex) - 127;
+  if (e > 15) return uint16_t(sign | 0x7c00u);
+  if (e >= -14) {
+    uint32_t h = (uint32_t(e + 15) << 10) | (mant >> 13);
+    const uint32_t r = mant & 0x1fffu;
+    if (r > 0x1000u || (r == 0x1000u && (h & 1u))) h += 1;  // a carry moves into the exponent
+    return uint16_t(sign | h);
+  }
+  if (e < -25 || ex == 0) return uint16_t(sign);
+  // subnormal: the value in units of 2^-24 is (2^23 + mant)·2^(e + 1)
+  const uint32_t m = mant | 0x800000u;
+  const int shift = -(e + 1);
+  uint32_t q = m >> shift;
+  const uint32_t rem = m & ((1u << shift) - 1u), half = 1u << (shift - 1);
+  if (rem > half || (rem == half && (q & 1u))) q += 1;
+  return uint16_t(sign | q);
+}
+
+// Two fp16 parts of h·2^e (e from the largest |value|): the high part is
+// the value's top 11 significant bits (its TF32 truncation), the low part
+// the rounded remainder — as the GEMM converters cut A.
+int upload_h16_split(fg_model* m, const std::vector<float>& h, DevMat* out) {
+  if (!m->h16 || out->h16) return FG_OK;
+  double mx = 0;
+  for (float v : h) mx = std::max(mx, double(std::fabs(v)));
+  int e = 0;
+  if (!h16_exponent(mx, &e)) return FG_OK;
+  std::vector<uint16_t> hi(h.size()), lo(h.size());
+  for (size_t i = 0; i < h.size(); ++i) {
+    const float v = std::ldexp(h[i], e);
+    uint32_t u;
+    std::memcpy(&u, &v, 4);
+    u &= 0xFFFFE000u;
+    float t;
+    std::memcpy(&t, &u, 4);
+    hi[i] = f16_rn(t);
+    lo[i] = f16_rn(v - t);
+  }
+  FG_TRY(dev_alloc_t(m, &out->h16, hi.size()));
+  FG_TRY(dev_alloc_t(m, &out->h16_lo, lo.size()));
+  FG_CUDA_TRY(cudaMemcpy(out->h16, hi.data(), hi.size() * 2, cudaMemcpyHostToDevice));
+  FG_CUDA_TRY(cudaMemcpy(out->h16_lo, lo.data(), lo.size() * 2, cudaMemcpyHostToDevice));
+  out->h16_exp = e;
+  return FG_OK;
 }
 
 // h·2^e as fp16 bits, e from the largest |value|, when exact for all.
@@ -844,12 +901,18 @@ int finalize(fg_model* m, int64_t max_tokens) {
       L.wgu = DevMat{nullptr, nullptr, int(2 * F), int(H)};
       L.wd = DevMat{nullptr, nullptr, int(H), int(F)};
     } else {
-      FG_TRY(upload_mat(m, fold(rqkv, g_in, H), int(qkv_rows), int(H), &L.wqkv));
+      const std::vector<float> fqkv = fold(rqkv, g_in, H), fgu = fold(rgu, g_pf, H);
+      FG_TRY(upload_mat(m, fqkv, int(qkv_rows), int(H), &L.wqkv));
       FG_TRY(upload_mat(m, wo->data, int(H), int(Hq * D), &L.wo));
-      FG_TRY(upload_mat(m, fold(rgu, g_pf, H), int(2 * F), int(H), &L.wgu));
+      FG_TRY(upload_mat(m, fgu, int(2 * F), int(H), &L.wgu));
       FG_TRY(upload_mat(m, wd->data, int(H), int(F), &L.wd));
       FG_TRY(upload_h16_unfolded(m, rqkv, L.g_in, g_in, &L.wqkv));
       FG_TRY(upload_h16_unfolded(m, rgu, L.g_pf, g_pf, &L.wgu));
+      // weights with no exact fp16 form at all (an fp32 checkpoint): two parts
+      FG_TRY(upload_h16_split(m, fqkv, &L.wqkv));
+      FG_TRY(upload_h16_split(m, wo->data, &L.wo));
+      FG_TRY(upload_h16_split(m, fgu, &L.wgu));
+      FG_TRY(upload_h16_split(m, wd->data, &L.wd));
     }
     if (m->h16) {
       // Bounds for the split-fp16 scales of the O and down inputs. With
@@ -997,6 +1060,7 @@ void use_h16(const fg_model* m, GemmArgs& g, const DevMat& W, const float* a_rs,
   g.a_exp = aexp;
   g.a_gain = W.h16_gain;
   g.a_gain_max = W.h16_gmax;
+  g.B16_lo = W.h16_lo;
 }
 
 struct Batch {
