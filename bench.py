@@ -362,11 +362,12 @@ def run_ours(args, rank, local_rank, world, cfg):
     gemm_flops = linear * nb * args.steps
     tf32_peak = pk["bf16_sustained"] / 2.0
     achieved = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else None
-    # split-fp16 runs where the projections have an exact fp16 form (a bf16
-    # checkpoint; non-zero norm gains go on A); an fp32 checkpoint has none
-    h16 = prec == gemma.PREC_SPLIT and args.checkpoint == "bf16"
+    # split-fp16: bf16-checkpoint projections have an exact fp16 form (two
+    # passes; non-zero norm gains go on A); an fp32 checkpoint's come in two
+    # fp16 parts (three passes: A_hi·B_hi, A_hi·B_lo, A_lo·B_hi)
+    h16 = prec == gemma.PREC_SPLIT
     if h16:
-        arith, passes = "split_fp16", 2
+        arith, passes = ("split_fp16", 2) if args.checkpoint == "bf16" else ("split_fp16_b2", 3)
     elif prec == gemma.PREC_TF32:
         arith, passes = "tf32", 1
     else:
@@ -374,12 +375,12 @@ def run_ours(args, rank, local_rank, world, cfg):
         arith, passes = "split_tf32", (3 if lo_b else 2)
     traffic = None
     tp = ROOT / "profiles" / "gemm_traffic.json"
-    if tp.exists() and h16:
+    if tp.exists() and h16 and args.checkpoint == "bf16":
         traffic = json.loads(tp.read_text()).get("bytes_per_launch")
     peak = pk["bf16_sustained"] if h16 else tf32_peak
     roofline = {
         "bound": "tensor",
-        "kernel": ("gemm_pair_kernel (tcgen05 cta_group::2 kind::f16 split-fp16, all encoder projections)" if h16 else
+        "kernel": (f"gemm_pair_kernel (tcgen05 cta_group::2 kind::f16 {arith}, all encoder projections)" if h16 else
                    f"gemm_pair_kernel (tcgen05 cta_group::2 kind::tf32 {arith}, all encoder projections)"),
         "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
         "frac": achieved / peak if achieved else None, "traffic": traffic,

@@ -10,7 +10,9 @@ Bounds:
 - split: |C − C64| ≤ 1e-4·(1 + |C64|) (the reference's bound) or
   REL_SPLIT·‖a_i‖·‖w_j‖. The second term is the size of the tensor core's
   fp32 accumulation error, which grows with the operands' norms, not with
-  |C|; at K = 768 it is ≈ 1.5e-6 of ‖a_i‖‖w_j‖ at most.
+  |C|: measured ≤ 1.1e-6 of ‖a_i‖‖w_j‖ for the split-fp16 products (M ≥
+  256: A and B in two fp16 parts each, three passes) and ≤ 1.4e-6 for the
+  split-TF32 ones (M = 128).
 - plain TF32: the same against the float64 product of the operands with
   their low 13 mantissa bits cleared (the bits the tensor core reads).
 - split, first 128 rows: against the reference's own float32 arithmetic
@@ -30,7 +32,7 @@ pytestmark = pytest.mark.gpu
 
 MS = [128, 1024, 8192, 65536]
 KN = [(768, 768), (768, 1152), (768, 2304), (768, 3072), (1152, 768)]
-REL_SPLIT = 3e-6
+REL_SPLIT = 2e-6
 REL_TF32 = 3e-6
 REL_REF32 = 3e-7  # the float32 reference arithmetic's own error, ≤ 2.1e-7 of ‖a‖‖w‖ here
 CHUNK = 8192
