@@ -43,10 +43,11 @@ extern "C" {
 
 /* ---- arithmetic modes -------------------------------------------------- */
 /* FG_PREC_SPLIT (default): fp32-level products, the arithmetic chosen per
- * product. The model's encoder GEMMs run split-fp16 (A as two fp16 parts
- * under a power-of-two row scale, bf16-exact weights as exact fp16 under a
- * power-of-two scale, 2 fp16 passes on SM pairs) where the weights have an
- * exact fp16 form, else split TF32; other products run split TF32.
+ * product. Products on SM pairs run split-fp16: A as two fp16 parts under
+ * a power-of-two row scale; B as exact fp16 under a power-of-two scale
+ * where it has such a form (bf16 checkpoint weights: 2 fp16 passes), else
+ * as two fp16 parts (3 fp16 passes: A_hi·B_hi + A_hi·B_lo + A_lo·B_hi).
+ * Smaller products run split TF32.
  * FG_PREC_SPLIT_TF32: every product as split TF32 (A·B + A·B_lo + A_lo·B,
  * up to 3 TF32 passes), the fp32-level mode without fp16 parts.
  * FG_PREC_TF32: one TF32 pass per product (about 1e-4 relative). */
@@ -278,9 +279,11 @@ int fg_model_read_profile(fg_model* m, double* ms, int64_t* launches, double* wo
  * NULL. x, and w as a transposed view, are read in place when 16-byte
  * aligned with row strides of whole 16-byte units; other layouts are copied
  * into stream-ordered scratch from a pool the library keeps per device
- * (memory it keeps reserved between calls). In split precision the
- * product is A·B + A·B_lo + A_lo·B in TF32 with B_lo computed per call and
- * A's low part made in shared memory. */
+ * (memory it keeps reserved between calls). FG_PREC_SPLIT with m >= 256,
+ * n > 128 and x read in place runs the three-pass split-fp16 product (B's
+ * fp16 parts and A's row scales made per call on the device); other split
+ * products, and FG_PREC_SPLIT_TF32, run A·B + A·B_lo + A_lo·B in TF32 with
+ * B_lo computed per call and A's low part made in shared memory. */
 int fg_matmul(int64_t m, int64_t n, int64_t k, const float* x, int64_t ldx, const float* w,
               int64_t ldw, int w_transposed, float* out, int64_t ldo, const fg_epilogue* epi,
               int precision, void* stream);
