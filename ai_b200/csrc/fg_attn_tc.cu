@@ -53,7 +53,8 @@ constexpr int kStages = 3;
 constexpr uint32_t kChunk = 128 * 64 * 2;           // [128 rows × 64 bf16] = 16 KB
 constexpr uint32_t kQBytes = 2 * 4 * kChunk;        // Q hi/lo × 4 d-chunks = 128 KB
 constexpr uint32_t kStageBytes = 2 * kChunk;        // hi + lo chunk = 32 KB
-constexpr size_t kSmem = 1024 + kQBytes + kStages * kStageBytes + 256;
+// Q, the K/V ring, 256 bytes of barriers, the half-row maxima [8 warps × 32]
+constexpr size_t kSmem = 1024 + kQBytes + kStages * kStageBytes + 256 + 1024;
 constexpr int kThreads = 320;  // producer, MMA issuer, 8 softmax warps
 constexpr uint32_t kIdesc = idesc_bf16(128, 128);
 constexpr float kRescaleLog2 = 8.f;  // rescale O when the max grows by more than 2^8
@@ -92,9 +93,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sRing + kStages * kStageBytes);
   // bars: 0 Q d-chunk 0 | 1..3 kv_full | 4..6 kv_empty | 7,8 s_full | 9,10 p_full |
   //       11,12 s_free | 13 o_prog | 14 o_final | 15 drain | 16..18 Q d-chunks 1..3 |
-  //       19 row-sum halves exchanged | 20..27 S read by both warps of a
-  //       quadrant (quad · 2 + S buffer)
+  //       19 row-sum halves exchanged | 20..27 half-row maxima written by
+  //       both warps of a quadrant (quad · 2 + S buffer)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 28);
+  float* red_max = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);  // [8 warps][32 rows]
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   constexpr int Dh = NC * 64;  // head dimension
@@ -356,10 +358,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // -------------------------------------------------------------- softmax
     // Two warps per TMEM lane quadrant (warps w and w + 4 hold the same 32
-    // query rows): both find the row maximum over all 128 columns of S (the
-    // same value, so the same running max and rescale decisions without an
-    // exchange); each then handles half of the columns — exponentials for
-    // 64 columns of S, rescaling and output for 128 columns of O.
+    // query rows): each reads its 64 columns of S once, the two half-row
+    // maxima meet in shared memory (both warps then hold the same row
+    // maximum, so the same running max and rescale decisions), and each
+    // handles its half of the columns — exponentials for 64 columns of S,
+    // rescaling and output for 128 columns of O.
     const int quad = warp & 3;
     const int half = (warp - 2) >> 2;
     const int r = quad * 32 + lane;
@@ -389,49 +392,56 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int lo_c = vlo - key0, hi_c = vhi - key0;  // visible columns [lo_c, hi_c)
       const bool full_row = lo_c <= 0 && hi_c >= kKT;
       const int span = max(0, hi_c - lo_c);  // col is visible iff unsigned(col - lo_c) < span
-      // pass 1: row maximum over the visible columns, two 64-column halves,
-      // eight independent chains (few live registers leave room for the
-      // long-latency exponentials and conversions of pass 2 to overlap)
+      // pass 1: this warp's 64 columns of S, kept in registers for pass 2,
+      // and their maximum over the visible columns in eight chains; the row
+      // maximum is the larger of the two warps' halves, exchanged through
+      // shared memory (each warp reads and overwrites only its own columns)
+      uint32_t sr[2][32];
+      tmem_ld_32x32b_x32(tS + uint32_t(half * 64), sr[0]);
+      tmem_ld_32x32b_x32(tS + uint32_t(half * 64 + 32), sr[1]);
+      tmem_ld_wait();
       float mt8[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) mt8[u] = -FLT_MAX;
-#pragma unroll 1
-      for (int hh = 0; hh < 2; ++hh) {
-        uint32_t sr[2][32];
-        tmem_ld_32x32b_x32(tS + uint32_t(hh * 64), sr[0]);
-        tmem_ld_32x32b_x32(tS + uint32_t(hh * 64 + 32), sr[1]);
-        tmem_ld_wait();
-        if (full_row) {
+      if (full_row) {
 #pragma unroll
-          for (int q = 0; q < 2; ++q)
+        for (int q = 0; q < 2; ++q)
 #pragma unroll
-            for (int e = 0; e < 32; ++e) mt8[e & 7] = fmaxf(mt8[e & 7], __uint_as_float(sr[q][e]));
-        } else {
+          for (int e = 0; e < 32; ++e) mt8[e & 7] = fmaxf(mt8[e & 7], __uint_as_float(sr[q][e]));
+      } else {
 #pragma unroll
-          for (int q = 0; q < 2; ++q)
+        for (int q = 0; q < 2; ++q)
 #pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const int col = hh * 64 + q * 32 + e;
-              const bool in = unsigned(col - lo_c) < unsigned(span);
-              mt8[e & 7] = fmaxf(mt8[e & 7], in ? __uint_as_float(sr[q][e]) : -FLT_MAX);
-            }
-        }
+          for (int e = 0; e < 32; ++e) {
+            const int col = half * 64 + q * 32 + e;
+            const bool in = unsigned(col - lo_c) < unsigned(span);
+            mt8[e & 7] = fmaxf(mt8[e & 7], in ? __uint_as_float(sr[q][e]) : -FLT_MAX);
+          }
       }
-      const float mt = fmaxf(fmaxf(fmaxf(mt8[0], mt8[1]), fmaxf(mt8[2], mt8[3])),
+      const float mh = fmaxf(fmaxf(fmaxf(mt8[0], mt8[1]), fmaxf(mt8[2], mt8[3])),
                              fmaxf(fmaxf(mt8[4], mt8[5]), fmaxf(mt8[6], mt8[7])));
-      // Both warps of the quadrant have read all 128 columns of S before
-      // either writes its P over its own 64 columns.
+      float mt;
       {
-        const uint32_t sr_bar = bar(20 + quad * 2 + sb);
-        tc_fence_before();
+        // the slot is reused every tile: the partner has read the previous
+        // tile's value before it arrived on that tile's P barrier
+        if (j >= 1) {
+          const bool prev = waitb(bar(9 + ((j - 1) & 1)), uint32_t((j - 1) >> 1) & 1u, abort_flag, p.err,
+                                  kDevTimeoutAccFull);
+          if (!__all_sync(0xffffffffu, prev)) {
+            ok = false;
+            break;
+          }
+        }
+        red_max[(half * 4 + quad) * 32 + lane] = mh;
+        const uint32_t mx_bar = bar(20 + quad * 2 + sb);
         __syncwarp();
-        if (lane == 0) mbar_arrive(sr_bar);
-        const bool both = waitb(sr_bar, uint32_t(j >> 1) & 1u, abort_flag, p.err, kDevTimeoutAccFull);
+        if (lane == 0) mbar_arrive(mx_bar);
+        const bool both = waitb(mx_bar, uint32_t(j >> 1) & 1u, abort_flag, p.err, kDevTimeoutAccFull);
         if (!__all_sync(0xffffffffu, both)) {
           ok = false;
           break;
         }
-        tc_fence_after();
+        mt = fmaxf(mh, red_max[((1 - half) * 4 + quad) * 32 + lane]);
       }
       const bool any = lo_c < hi_c && lo_c < kKT && hi_c > 0;
       float factor = 1.f;
@@ -477,10 +487,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool all_vis = have && full_row;
       {
         const int hh = half;
-        uint32_t sr[2][32];
-        tmem_ld_32x32b_x32(tS + uint32_t(hh * 64), sr[0]);
-        tmem_ld_32x32b_x32(tS + uint32_t(hh * 64 + 32), sr[1]);
-        tmem_ld_wait();
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
           uint32_t hw[16], lw[16];
