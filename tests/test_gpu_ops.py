@@ -34,7 +34,8 @@ def _gemm_tol(got, want, a=None, w=None, rel=1e-5):
 
 @pytest.mark.parametrize("m,k,n", [(128, 768, 768), (1024, 768, 1152), (128, 768, 2304),
                                    (128, 768, 3072), (1024, 1152, 768), (1, 3, 1), (7, 17, 5),
-                                   (130, 33, 200), (257, 768, 129), (300, 1152, 2304)])
+                                   (130, 33, 200), (257, 768, 129), (300, 1152, 2304), (300, 100, 300),
+                                   (1000, 45, 513)])
 @pytest.mark.parametrize("transposed", [False, True])
 def test_matmul_split_tf32_vs_float64(cuda, m, k, n, transposed):
     from ai_b200 import tensor as T
@@ -55,6 +56,31 @@ def test_matmul_split_tf32_vs_float64(cuda, m, k, n, transposed):
     print(f"gemm m={m} k={k} n={n} T={transposed}: max|err| {np.abs(got - want).max():.3e} "
           f"max err/(|a||w|) {(np.abs(got - want) / scale).max():.3e}")
     assert ok.all(), f"max err {np.abs(got - want).max()} at {np.argwhere(~ok)[:3]}"
+
+
+def test_matmul_split_rows_of_any_scale(cuda):
+    """The split-fp16 product scales each row of A by its own power of two
+    (from the row's norm) and B by one: rows of norm 0, 1e-15 and 1e15 and a
+    B of tiny entries keep fp32-level accuracy relative to their own size."""
+    from ai_b200 import tensor as T
+
+    rng = np.random.default_rng(17)
+    m, k, n = 512, 768, 384
+    a = rng.standard_normal((m, k), dtype=np.float32)
+    a[3] = 0.0
+    a[5] *= np.float32(1e-15)
+    a[7] *= np.float32(1e15)
+    a[9, :100] *= np.float32(1e-6)  # small entries beside large ones in one row
+    for bscale in (1.0, 1e-12):
+        w = (rng.standard_normal((n, k), dtype=np.float32) * np.float32(bscale))
+        want = a.astype(np.float64) @ w.T.astype(np.float64)
+        got = T.MatMul(_t(a, cuda), _t(w, cuda).t()).cpu().numpy().astype(np.float64)
+        scale = np.linalg.norm(a.astype(np.float64), axis=1)[:, None] * \
+            np.linalg.norm(w.astype(np.float64), axis=1)[None, :]
+        err = np.abs(got - want)
+        assert np.all(err[3] == 0), err[3].max()
+        ok = err <= 3e-6 * scale
+        assert ok.all(), (bscale, (err / np.maximum(scale, 1e-300)).max(), np.argwhere(~ok)[:3])
 
 
 def test_matmul_plain_tf32_error_is_tf32_sized(cuda):
