@@ -547,6 +547,58 @@ def run_ragged(args, rank, local_rank, world, cfg):
         dist.destroy_process_group()
 
 
+def run_ragged_multi(args, cfg):
+    """--workload ragged --multi: benchmark config 3 (8192 sequences, lengths
+    uniform in [16, 2048], seed 2) through the one-process multi-GPU entry
+    point fg_embed_many_multi — one model per GPU in this process, the
+    length-sorted sequences cut into cost-balanced contiguous slices, one
+    host thread per GPU, every embedding written into the host result in
+    the caller's order (the call a Go host makes; no torchrun, no NCCL). A
+    step is the whole batch; host wall clock around the synchronous call."""
+    import torch
+
+    from ai_b200 import gemma
+    from ai_b200 import synthetic as S
+
+    n = max(1, min(args.gpus, torch.cuda.device_count()))
+    budget = 131072
+    w = S.make_weights(cfg, seed=0)
+    models = [gemma.from_synthetic(cfg, w, device=d, max_batch_tokens=budget, options=[gemma.BatchTokens(budget)])
+              for d in range(n)]
+    seqs, lengths = S.make_ragged(8192, 16, 2048, 2)
+    tokens = int(np.sum(lengths))
+    for _ in range(max(args.warmup, 1)):
+        gemma.embed_ids_multi(models, seqs)
+    clk = ClockSampler(list(range(n)))
+    clk.start()
+    times = []
+    res = None
+    for _ in range(max(args.steps, 1)):
+        t0 = time.perf_counter()
+        res = gemma.embed_ids_multi(models, seqs)
+        times.append(time.perf_counter() - t0)
+    clocks = clk.stop()
+    sec = statistics.median(times)
+    ok = res is not None and res.shape == (8192, models[0].Dim()) and bool(np.all(np.isfinite(res)))
+    line = {
+        "metric": "EmbeddingGemma embeddings/s, config 3 ragged (8192 seqs, lengths 16..2048), one process",
+        "value": 8192 / sec, "unit": "embeddings/s", "n_gpus": n, "steps": len(times),
+        "warmup": max(args.warmup, 1), "ms_per_step": sec * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: random-init weights (seed 0), ragged ids seed 2",
+        "config": {"workload": "config 3: 8192 sequences, lengths uniform in [16, 2048], right-padded",
+                   "batch_tokens": budget, "valid_tokens": tokens,
+                   "parallelism": f"fg_embed_many_multi: {n} model(s), one host thread per GPU, no collective",
+                   "timing": "host wall clock around the synchronous call (ids on the host to embeddings on "
+                             "the host, caller's order), median of steps"},
+        "tokens_per_s": tokens / sec, "all_finite": ok, "clocks": clocks,
+        "step_ms": [round(x * 1e3, 1) for x in times],
+    }
+    print(json.dumps(line), flush=True)
+    for m in models:
+        m.close()
+
+
 def eg2_work(t: dict, T: int):
     """Algorithmic FLOPs of one EmbeddingGemma 2 sequence of T valid tokens:
     the projections (Q/K/V/O, GeGLU, the PLE projection and each layer's PLE
@@ -793,6 +845,8 @@ def main():
                     help="strong scaling: this many sequences in total, split over the GPUs (default: "
                          "weak scaling, --batch sequences per GPU)")
     ap.add_argument("--windows", type=int, default=5, help="timing windows of >= 1 s after the K steps")
+    ap.add_argument("--multi", action="store_true",
+                    help="with --workload ragged: one process drives --gpus GPUs through fg_embed_many_multi")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--norm-std", type=float, default=0.0,
                     help="RMSNorm weights ~N(0, s^2) instead of the spec's zeros (checkpoint-like: the "
@@ -828,6 +882,8 @@ def main():
     cfg = dict(S.EMBEDDINGGEMMA_300M)
     if args.impl == "reference":
         run_reference(args, rank, world, cfg)
+    elif args.workload == "ragged" and args.multi:
+        run_ragged_multi(args, cfg)
     elif args.workload == "ragged":
         run_ragged(args, rank, local_rank, world, cfg)
     else:
