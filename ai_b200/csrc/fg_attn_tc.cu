@@ -34,6 +34,7 @@
 #include <algorithm>
 #include <atomic>
 #include <cfloat>
+#include <cmath>
 #include <cudaTypedefs.h>
 
 #include "fg_internal.h"
@@ -70,6 +71,9 @@ struct Params {
   int64_t osb, osh, ost;
   int* err;
   int tma_out, tma_out_lo;  // out / out_lo written by TMA stores (maps mO / mOlo)
+  int tma_out16;            // the output's fp16 parts written instead (maps mO / mOlo: hi / lo)
+  float out16_scale;        // 2^out16_exp
+  uint16_t *out16, *out16_lo;  // the same parts (zero rows are written directly)
 };
 
 // NC 64-column d-chunks per head (4: head_dim 256, Q resident; 8: head_dim
@@ -120,6 +124,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int r = warp; r < kQ; r += kThreads / 32) {
       const int i = i0 + r;
       if (i >= p.T) break;
+      if (p.tma_out16) {
+        // kD fp16 of hi and of lo per row, 16 bytes a lane
+        const int64_t off = b * p.osb + h * p.osh + oh * kD + int64_t(i) * p.ost;
+        for (int c = lane * 8; c < kD; c += 256) {
+          *reinterpret_cast<uint4*>(p.out16 + off + c) = make_uint4(0u, 0u, 0u, 0u);
+          *reinterpret_cast<uint4*>(p.out16_lo + off + c) = make_uint4(0u, 0u, 0u, 0u);
+        }
+        continue;
+      }
       float* o = obase + i * p.ost;
       float* ol = olbase ? olbase + i * p.ost : nullptr;
       for (int c = lane; c < kD; c += 32) {
@@ -536,7 +549,54 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool row_ok = i < p.T;
       const float inv = (i < qlen && lsum > 0.f) ? 1.f / lsum : 0.f;
       const int col_base = half * 128;  // this warp's output columns
-      if (p.tma_out) {
+      if (p.tma_out16) {
+        // The next product's fp16 parts of the warp's 32 rows × 128 columns:
+        // a = out·2^e cut as the GEMM converters cut A, four 32-column
+        // chunks of [32 × 32] hi and lo boxes (64-byte rows and swizzle) in
+        // the warp's 16 KB of the Q region, then TMA stores.
+        uint8_t* stg = sQ + size_t(warp - 2) * 16384;
+        const int tw = i0 + quad * 32;
+        const float sc = p.out16_scale;
+        const int sw = (lane >> 1) & 3;
+#pragma unroll 1
+        for (int ch = 0; ch < 4; ch += 2) {
+          uint32_t ov[2][32];
+          tmem_ld_32x32b_x32(tO + lane_off + uint32_t(col_base + ch * 32), ov[0]);
+          tmem_ld_32x32b_x32(tO + lane_off + uint32_t(col_base + ch * 32 + 32), ov[1]);
+          tmem_ld_wait();
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            uint32_t hw[16], lw[16];
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {
+              const float a0 = (__uint_as_float(ov[u][2 * q]) * inv) * sc;
+              const float a1 = (__uint_as_float(ov[u][2 * q + 1]) * inv) * sc;
+              const float h0 = tf32_hi(a0), h1 = tf32_hi(a1);
+              hw[q] = pack_f16x2(h0, h1);
+              lw[q] = pack_f16x2(a0 - h0, a1 - h1);
+            }
+            uint4* rh = reinterpret_cast<uint4*>(stg + (ch + u) * 4096 + lane * 64);
+            uint4* rl = reinterpret_cast<uint4*>(stg + (ch + u) * 4096 + 2048 + lane * 64);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              rh[j ^ sw] = make_uint4(hw[4 * j], hw[4 * j + 1], hw[4 * j + 2], hw[4 * j + 3]);
+              rl[j ^ sw] = make_uint4(lw[4 * j], lw[4 * j + 1], lw[4 * j + 2], lw[4 * j + 3]);
+            }
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && tw < p.T) {
+          for (int ch = 0; ch < 4; ++ch) {
+            const int col = h * Dh + oh * kD + col_base + ch * 32;
+            tma_store_3d(&mO, smem_u32(stg + ch * 4096), col, tw, b);
+            tma_store_3d(&mOlo, smem_u32(stg + ch * 4096 + 2048), col, tw, b);
+          }
+          tma_store_commit();
+        }
+        if (lane == 0) tma_store_wait_read<0>();  // the boxes are read; the writes complete on their own
+        __syncwarp();
+      } else if (p.tma_out) {
         // The warp's 32 rows × 128 columns as four [32 × 32] boxes in its
         // 16 KB of the Q region (every MMA that read Q has completed), then
         // TMA stores; rows past the sequence end fall outside the map.
@@ -698,6 +758,20 @@ int make_map_out3d(CUtensorMap* m, const float* ptr, int B, int T, int64_t cols,
   return FG_OK;
 }
 
+// fp16 output parts viewed as [B][T][cols] (row stride ost, sequence stride
+// osb, in elements), [1 × 32 × 32] boxes with 64-byte swizzling.
+int make_map_out16_3d(CUtensorMap* m, const uint16_t* ptr, int B, int T, int64_t cols, int64_t ost, int64_t osb) {
+  cuuint64_t dims[3] = {cuuint64_t(cols), cuuint64_t(T), cuuint64_t(B)};
+  cuuint64_t strides[2] = {cuuint64_t(ost) * 2, cuuint64_t(osb) * 2};
+  cuuint32_t box[3] = {32u, 32u, 1u};
+  cuuint32_t es[3] = {1u, 1u, 1u};
+  CUresult r = g_encode_bf16(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<uint16_t*>(ptr), dims, strides, box,
+                             es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(FG_ECUDA, "cuTensorMapEncodeTiled (attention fp16 output) failed (%d)", int(r));
+  return FG_OK;
+}
+
 }  // namespace
 
 size_t attn_tc_workspace_bytes(int B, int T, int S, int Hq, int Hkv, int D) {
@@ -778,7 +852,25 @@ int attention_tc_operands(const AttnArgs& a, const AttnOperands& o, int* err, cu
   };
   prm.tma_out = 0;
   prm.tma_out_lo = 0;
-  if (tma_ok(a.out) && (a.out_lo == nullptr || tma_ok(a.out_lo))) {
+  prm.tma_out16 = 0;
+  prm.out16_scale = 1.f;
+  prm.out16 = nullptr;
+  prm.out16_lo = nullptr;
+  if (a.out16) {
+    // the next product's fp16 parts, through TMA only
+    auto ok16 = [&](const uint16_t* ptr) {
+      return ptr && (reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && a.osh == Dh && a.ost % 8 == 0 &&
+             a.osb % 8 == 0 && a.ost >= int64_t(Hq) * Dh && a.osb >= int64_t(T) * a.ost;
+    };
+    if (!ok16(a.out16) || !ok16(a.out16_lo) || a.out16_exp < -126 || a.out16_exp > 127)
+      return set_error(FG_EINVAL, "attention: fp16-parts output needs aligned contiguous heads");
+    FG_TRY(make_map_out16_3d(&mo, a.out16, B, T, Hq * Dh, a.ost, a.osb));
+    FG_TRY(make_map_out16_3d(&mol, a.out16_lo, B, T, Hq * Dh, a.ost, a.osb));
+    prm.tma_out16 = 1;
+    prm.out16_scale = std::ldexp(1.0f, a.out16_exp);
+    prm.out16 = a.out16;
+    prm.out16_lo = a.out16_lo;
+  } else if (tma_ok(a.out) && (a.out_lo == nullptr || tma_ok(a.out_lo))) {
     FG_TRY(make_map_out3d(&mo, a.out, B, T, Hq * Dh, a.ost, a.osb));
     if (a.out_lo) FG_TRY(make_map_out3d(&mol, a.out_lo, B, T, Hq * Dh, a.ost, a.osb));
     prm.tma_out = 1;

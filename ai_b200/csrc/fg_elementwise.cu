@@ -180,7 +180,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(
 // ------------------------------------------------- residual + post-norm
 template <int C4>
 __global__ void __launch_bounds__(256) residual_postnorm_kernel(
-    float* __restrict__ x, float* __restrict__ x_lo, const float* __restrict__ o,
+    float* __restrict__ x, Split16Out parts, const float* __restrict__ o,
     const float* __restrict__ gain, float eps, float* __restrict__ rowscale,
     const float* __restrict__ fgain, int64_t rows, int n, float scalar) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -237,13 +237,29 @@ __global__ void __launch_bounds__(256) residual_postnorm_kernel(
     }
     return;
   }
-  float4* l4 = x_lo ? reinterpret_cast<float4*>(x_lo + row * n) : nullptr;
 #pragma unroll
-  for (int c = 0; c < C4; ++c) {
-    x4[lane + 32 * c] = xv[c];
-    if (l4)
-      l4[lane + 32 * c] =
-          make_float4(tf32_lo(xv[c].x), tf32_lo(xv[c].y), tf32_lo(xv[c].z), tf32_lo(xv[c].w));
+  for (int c = 0; c < C4; ++c) x4[lane + 32 * c] = xv[c];
+  if (parts.hi) {
+    // the next product's fp16 parts of this row, as its converters would cut them
+    const int e = max(-60, min(60, 13 - ilogbf(parts.norm_k / inv_x)));
+    const float sc = pow2f(e);
+    uint2* h2 = reinterpret_cast<uint2*>(parts.hi + row * n);
+    uint2* l2 = reinterpret_cast<uint2*>(parts.lo + row * n);
+    const float4* pg4 = reinterpret_cast<const float4*>(parts.gain);
+#pragma unroll
+    for (int c = 0; c < C4; ++c) {
+      const float4 v = xv[c];
+      float a0, a1, a2, a3;
+      if (parts.gain) {
+        const float4 g = __ldg(pg4 + lane + 32 * c);
+        a0 = v.x * (g.x * sc); a1 = v.y * (g.y * sc); a2 = v.z * (g.z * sc); a3 = v.w * (g.w * sc);
+      } else {
+        a0 = v.x * sc; a1 = v.y * sc; a2 = v.z * sc; a3 = v.w * sc;
+      }
+      const float q0 = tf32_hi(a0), q1 = tf32_hi(a1), q2 = tf32_hi(a2), q3 = tf32_hi(a3);
+      h2[lane + 32 * c] = make_uint2(pack_f16x2(q0, q1), pack_f16x2(q2, q3));
+      l2[lane + 32 * c] = make_uint2(pack_f16x2(a0 - q0, a1 - q1), pack_f16x2(a2 - q2, a3 - q3));
+    }
   }
   if (lane == 0) rowscale[row] = inv_x;
 }
@@ -382,14 +398,15 @@ int qk_norm_rope(float* qkv, float* qkv_lo, int64_t rows, int Hq, int Hkv, int D
   return FG_OK;
 }
 
-int residual_postnorm(float* x, float* x_lo, const float* o, const float* gain, float eps,
+int residual_postnorm(float* x, const Split16Out* parts, const float* o, const float* gain, float eps,
                       float* rowscale, const float* final_gain, int64_t rows, int n,
                       cudaStream_t s, float scalar) {
   if (rows == 0) return FG_OK;
+  const Split16Out p16 = parts ? *parts : Split16Out{nullptr, nullptr, nullptr, 0.f};
   const int grid = grid_for(rows, kWarpsPerBlock);
   switch (n / 128) {
 #define FG_RES(C) \
-  case C: residual_postnorm_kernel<C><<<grid, 256, 0, s>>>(x, x_lo, o, gain, eps, rowscale, final_gain, rows, n, scalar); break;
+  case C: residual_postnorm_kernel<C><<<grid, 256, 0, s>>>(x, p16, o, gain, eps, rowscale, final_gain, rows, n, scalar); break;
     FG_RES(1) FG_RES(2) FG_RES(3) FG_RES(4) FG_RES(5) FG_RES(6) FG_RES(7) FG_RES(8)
 #undef FG_RES
     default:

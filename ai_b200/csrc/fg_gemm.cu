@@ -48,6 +48,7 @@ struct KParams {
   GemmEpilogue e;
   int* err;
   int tma_out, tma_out_lo;  // out / out_lo are written by TMA stores (maps m[0] / m[1])
+  int tma_out16;            // out16 / out16_lo (fp16 parts) are written by TMA stores (maps m[0] / m[1])
   int tma_qk;               // q / k attention operands are written by TMA stores (maps m[0..3])
   // Split-fp16 pair kernel: A·2^e_r and B·2^b_exp in fp16 (see a_row_exp);
   // the epilogue multiplies each row by 2^-(e_r + b_exp), which is exact.
@@ -444,6 +445,43 @@ __device__ __forceinline__ void store_box_tma(const CUtensorMap* map, EpiStage& 
   ++es.n;
 }
 
+// The warp's [32 rows × 32 columns] block (row `lane` in v) written as the
+// next product's fp16 parts: a = v·sc cut into hi (a's top 11 significant
+// bits) and lo = fp16(a − hi), exactly as the GEMM converters cut A; two
+// [32 × 32] fp16 boxes (64-byte rows, 64-byte swizzle: 16-byte chunk j of
+// row r at chunk j ^ ((r / 2) % 4)) in the next staging slot, stored by TMA.
+__device__ __forceinline__ void store_box16_tma(const CUtensorMap* mhi, const CUtensorMap* mlo, EpiStage& es,
+                                                const float (&v)[32], float sc, int col0, int row0, bool inside) {
+  const int lane = threadIdx.x & 31;
+  uint8_t* buf = es.base + (es.n & 1) * 4096;  // hi box at +0, lo box at +2048
+  if (lane == 0) tma_store_wait_read<1>();   // the store that last read this slot is done with it
+  __syncwarp();
+  uint32_t hw[16], lw[16];
+#pragma unroll
+  for (int q = 0; q < 16; ++q) {
+    const float a0 = v[2 * q] * sc, a1 = v[2 * q + 1] * sc;
+    const float h0 = tf32_hi(a0), h1 = tf32_hi(a1);
+    hw[q] = pack_f16x2(h0, h1);
+    lw[q] = pack_f16x2(a0 - h0, a1 - h1);
+  }
+  const int sw = (lane >> 1) & 3;
+  uint4* rh = reinterpret_cast<uint4*>(buf + lane * 64);
+  uint4* rl = reinterpret_cast<uint4*>(buf + 2048 + lane * 64);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    rh[j ^ sw] = make_uint4(hw[4 * j], hw[4 * j + 1], hw[4 * j + 2], hw[4 * j + 3]);
+    rl[j ^ sw] = make_uint4(lw[4 * j], lw[4 * j + 1], lw[4 * j + 2], lw[4 * j + 3]);
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0 && inside) {
+    tma_store_2d(mhi, smem_u32(buf), col0, row0);
+    tma_store_2d(mlo, smem_u32(buf + 2048), col0, row0);
+    tma_store_commit();
+  }
+  ++es.n;
+}
+
 // One accumulator tile through the epilogue, by one of the four epilogue
 // warps: its 32 TMEM lanes at `taddr` (BN columns) hold output rows
 // row0 .. row0+31 of N-tile tn. Results go out by TMA stores when the
@@ -500,6 +538,10 @@ __device__ __forceinline__ void epilogue_tile(const KParams& p, const OutMaps& o
         const float g = __uint_as_float(rg[j]) * rs;
         const float u = __uint_as_float(ru[j]) * rs;
         v[j] = gelu_sigmoid(g) * u;
+      }
+      if (p.tma_out16) {
+        store_box16_tma(&om.m[0], &om.m[1], es, v, pow2f(e.out16_exp), col0, row0, ncols > 0 && rows > 0);
+        continue;
       }
       if (tma) store_box_tma(&om.m[0], es, v, col0, row0, ncols > 0 && rows > 0);
       else if (row_ok && ncols > 0) store_row32(out + int64_t(row) * ldo + col0, v, ncols, vec_out);
@@ -837,9 +879,14 @@ __global__ void __launch_bounds__(Cfg<BN, SA, SB, BK, CV>::kThreads, 1)
 // A_hi·B_lo + A_lo·B_hi (A_lo·B_lo, 2^-22 of the product, is dropped, as in
 // split-TF32) — three fp16 passes, the tensor-pipe time of 1.5 TF32 passes.
 // Stage: A (then its parts) | B_hi | B_lo = 32 KB, 6 stages.
+//
+// H16 with SA (not CV): A's two fp16 parts were written by the kernel that
+// produced A (the same parts, under the same power-of-two row scale, that
+// the converters would make) and are loaded by TMA like B, so the stage
+// needs no conversion: A_hi | A_lo | B (| B_lo).
 template <bool CV, bool SA = false, bool SB = false, bool H16 = false>
 struct PairCfg {
-  static_assert(!H16 || (CV && !SA), "split-fp16 takes A's parts from the converters");
+  static_assert(!H16 || (CV != SA), "split-fp16 takes A's parts from the converters or from memory");
   static constexpr int BN = 256, BK = 32;
   static constexpr int kThreads = 320;
   static constexpr bool kLo = CV || SA;
@@ -849,7 +896,14 @@ struct PairCfg {
   static constexpr uint32_t kStageBytes =
       H16 ? kABytes + kBBytes * (SB ? 2 : 1) : kABytes * (kLo ? 2 : 1) + kBBytes * (SB ? 2 : 1);
   static constexpr uint32_t kBOffset = H16 ? kABytes : kABytes * (kLo ? 2 : 1);
-  static constexpr uint32_t kTmaBytes = kABytes * (SA ? 2 : 1) + kBBytes * (SB ? 2 : 1);
+  // TMA bytes per stage: with H16 the A region (the fp32 tile, or its two
+  // fp16 parts loaded as they are) is kABytes either way
+  static constexpr uint32_t kTmaBytes = H16 ? kABytes + kBBytes * (SB ? 2 : 1)
+                                            : kABytes * (SA ? 2 : 1) + kBBytes * (SB ? 2 : 1);
+  static constexpr uint32_t kALoOffset = H16 ? kPartBytes : kABytes;  // where A's low part sits
+  // stage-ready arrivals per stage: 2 converter warps per CTA take a stage
+  // with split-fp16 conversion, all 4 otherwise (both CTAs)
+  static constexpr uint32_t kReadyCount = (H16 && CV) ? 4 : 8;
   static constexpr uint32_t kEpiStageBytes = kEpiStageBytesAll;
   static constexpr int kStagesRaw = (kSmemLimit - 2048 - int(kEpiStageBytes)) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
@@ -895,7 +949,7 @@ __global__ void __launch_bounds__(320, 1)
     for (int s = 0; s < S; ++s) {
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
-      mbar_init(ready_bar(s), H16 ? 4 : 8);  // converter warps per stage in each CTA: 2 (H16) or 4
+      mbar_init(ready_bar(s), C::kReadyCount);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(accf_bar(a), 1);
@@ -939,7 +993,7 @@ __global__ void __launch_bounds__(320, 1)
           armed[stage]++;
           const uint32_t dst = smem_u32(smem + size_t(stage) * C::kStageBytes);
           tma_load_2d(dst, &mA, fb, kb * BK, arow);
-          if (SA) tma_load_2d(dst + C::kABytes, &mAlo, fb, kb * BK, arow);
+          if (SA) tma_load_2d(dst + C::kALoOffset, &mAlo, fb, kb * BK, arow);
           tma_load_2d(dst + C::kBOffset, &mB, fb, kb * BK, brow);
           if (SB) tma_load_2d(dst + C::kBOffset + C::kBBytes, &mBlo, fb, kb * BK, brow);
           if (++stage == S) {
@@ -1047,7 +1101,7 @@ __global__ void __launch_bounds__(320, 1)
     const int ct = threadIdx.x - 192;  // 0..127
     int stage = 0;
     uint32_t phase = 0;
-    if constexpr (H16) {
+    if constexpr (H16 && CV) {
       // Two groups of two warps take alternate stages (even / odd), so two
       // stages are converted at once. In a group, thread gt converts rows
       // gt and gt + 64 of the CTA's 128 A rows: each fp32 row (128-byte
@@ -1256,6 +1310,17 @@ int prepare_out_maps(const GemmArgs& g, KParams& kp, OutMaps* om) {
   kp.tma_out = 0;
   kp.tma_out_lo = 0;
   kp.tma_qk = 0;
+  kp.tma_out16 = 0;
+  if (g.epi.out16) {
+    const GemmEpilogue& e = g.epi;
+    if (!e.geglu || !e.out16_lo || (reinterpret_cast<uintptr_t>(e.out16) & 15) != 0 ||
+        (reinterpret_cast<uintptr_t>(e.out16_lo) & 15) != 0 || kp.Nout % 8 != 0)
+      return set_error(FG_EINVAL, "gemm: fp16-parts output needs the gated epilogue and aligned buffers");
+    FG_TRY(make_map_f16(&om->m[0], e.out16, g.M, kp.Nout, kp.Nout, 32));
+    FG_TRY(make_map_f16(&om->m[1], e.out16_lo, g.M, kp.Nout, kp.Nout, 32));
+    kp.tma_out16 = 1;
+    return FG_OK;
+  }
   if (g.epi.qkv_attn) {
     const GemmEpilogue& e = g.epi;
     const void* ps[4] = {e.q_hi, e.q_lo, e.k_hi, e.k_lo};
@@ -1312,8 +1377,13 @@ template <bool CV, bool SA = false, bool SB = false, bool H16 = false>
 int launch_pair(const GemmArgs& g, KParams kp, int* dev_err, cudaStream_t stream) {
   using C = PairCfg<CV, SA, SB, H16>;
   CUtensorMap mA, mAlo, mB, mBlo;
-  FG_TRY(make_map(&mA, g.A, g.M, g.K, g.lda, 128, 32));
-  if (SA) FG_TRY(make_map(&mAlo, g.A_lo, g.M, g.K, g.lda, 128, 32)); else mAlo = mA;
+  if (H16 && SA) {
+    FG_TRY(make_map_f16(&mA, g.A16, g.M, g.K, g.lda, 128));
+    FG_TRY(make_map_f16(&mAlo, g.A16_lo, g.M, g.K, g.lda, 128));
+  } else {
+    FG_TRY(make_map(&mA, g.A, g.M, g.K, g.lda, 128, 32));
+    if (SA) FG_TRY(make_map(&mAlo, g.A_lo, g.M, g.K, g.lda, 128, 32)); else mAlo = mA;
+  }
   if (H16) FG_TRY(make_map_f16(&mB, g.B16, g.Nb, g.K, g.ldb, 128));
   else FG_TRY(make_map(&mB, g.B, g.Nb, g.K, g.ldb, 128, 32));
   if (SB && H16) FG_TRY(make_map_f16(&mBlo, g.B16_lo, g.Nb, g.K, g.ldb, 128));
@@ -1376,6 +1446,21 @@ int launch_b_mode(const GemmArgs& g, const KParams& kp, int* dev_err, cudaStream
 
 int dispatch(const GemmArgs& g, KParams& kp, int* dev_err, cudaStream_t stream) {
   kp.nk = (g.K + 31) / 32;
+  // split-fp16 with A's parts made by A's producer (fp16 [M, lda], 16-byte rows)
+  if (g.A16) {
+    if (!g.A16_lo || !g.B16 || !use_pair(g) || !(g.epi.geglu || g.Nb > 128) || g.lda % 8 != 0 || g.ldb % 8 != 0 ||
+        g.a_gain || (g.a_exp_rs && !kp.a_rs))
+      return set_error(FG_EINVAL, "gemm: pre-split fp16 A needs the split-fp16 pair kernel");
+    if (g.epi.geglu) {
+      kp.Nout = g.Nb / 2;
+      kp.ntn = g.Nb / 256;
+    } else {
+      kp.Nout = g.Nb;
+      kp.ntn = (g.Nb + 255) / 256;
+    }
+    if (g.B16_lo) return launch_pair<false, true, true, true>(g, kp, dev_err, stream);
+    return launch_pair<false, true, false, true>(g, kp, dev_err, stream);
+  }
   // split-fp16 where B has an exact fp16 form and A's parts are made here
   const bool h16 = g.B16 && g.a_lo_smem && !g.A_lo && (g.ldb % 8) == 0 && (!g.a_exp_rs || kp.a_rs) &&
                    (!g.a_gain || (g.K % 32 == 0 && (reinterpret_cast<uintptr_t>(g.a_gain) & 15) == 0)) &&
@@ -1422,7 +1507,7 @@ int gemm_tn(const GemmArgs& g, int* dev_err, cudaStream_t stream) {
     if (g.M == 0 || g.Nb == 0) return FG_OK;
     return set_error(FG_EINVAL, "gemm: bad shape M=%d Nb=%d K=%d", g.M, g.Nb, g.K);
   }
-  if (g.epi.out == nullptr && !g.epi.qkv_attn) return set_error(FG_EINVAL, "gemm: no output");
+  if (g.epi.out == nullptr && !g.epi.qkv_attn && !g.epi.out16) return set_error(FG_EINVAL, "gemm: no output");
   if (g.epi.qkv_attn && (g.Nb != (g.epi.Hq + 2 * g.epi.Hkv) * 256 || g.epi.T <= 0))
     return set_error(FG_EINVAL, "gemm: attention-operand epilogue needs 256-wide heads");
   if (g.epi.geglu && (g.Nb % 256) != 0)
@@ -1440,7 +1525,9 @@ int gemm_tn(const GemmArgs& g, int* dev_err, cudaStream_t stream) {
   kp.b_exp = g.b_exp;
   kp.b_exp_dev = g.b_exp_dev;
   // all-zero gains make A zero: any exponent serves, keep the bound positive
-  kp.a_norm_k = sqrtf(float(g.K)) * (g.a_gain && g.a_gain_max > 0.f ? g.a_gain_max : 1.f);
+  // (a_bound_gain: the gain a producer applied to pre-split A parts)
+  kp.a_norm_k = sqrtf(float(g.K)) * (g.a_gain && g.a_gain_max > 0.f ? g.a_gain_max
+                                     : g.a_bound_gain > 0.f ? g.a_bound_gain : 1.f);
   kp.a_rs = g.a_rs ? g.a_rs : g.epi.rowscale;
   kp.a_gain = g.a_gain;
   return dispatch(g, kp, dev_err, stream);

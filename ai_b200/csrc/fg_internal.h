@@ -86,6 +86,12 @@ struct GemmEpilogue {
   int64_t ldr = 0;
   int act = 0;                      // FG_ACT_*
   int geglu = 0;  // B rows interleaved per 128: gate rows then up rows; out = GELU(rs·g)·(rs·u)
+  // gated product only: instead of `out`, the next product's split-fp16 A
+  // operand — out·2^out16_exp cut into fp16 hi (top 11 significant bits)
+  // and lo (the rounded remainder), [M, Nout] each, 16-byte aligned rows
+  uint16_t* out16 = nullptr;
+  uint16_t* out16_lo = nullptr;
+  int out16_exp = 0;
 
   // QKV projection → attention operands (BN = 256 = head_dim, so N-tile tn
   // is head tn of q | k | v). For q and k heads: rs·acc, per-head RMSNorm
@@ -140,6 +146,14 @@ struct GemmArgs {
   // K a multiple of 32), the product of a fold W·diag(g) moved to A's side.
   const float* a_gain = nullptr;
   float a_gain_max = 1.f;
+  // Split-fp16 with A's two fp16 parts already in memory ([M, lda] each),
+  // written by A's producer as the converters would make them: A·2^e_r
+  // (times a column gain, whose maximum a_bound_gain enters the row bound
+  // sqrt(K)·a_bound_gain/rs) cut into its top 11 significant bits and the
+  // rounded remainder (a_exp / a_exp_rs give e_r as above).
+  const uint16_t* A16 = nullptr;
+  const uint16_t* A16_lo = nullptr;
+  float a_bound_gain = 0.f;
   GemmEpilogue epi;
 };
 

@@ -25,13 +25,26 @@ int qk_norm_rope(float* qkv, float* qkv_lo, int64_t rows, int Hq, int Hkv, int D
                  const float* qgain, const float* kgain, const float* vgain, float eps,
                  const float* cos_t, const float* sin_t, int T, cudaStream_t s);
 
+// The next product's split-fp16 A operand written by its producer: row r
+// of A·2^e_r (times the column gain when given), e_r = 13 −
+// ilogb(norm_k / rs_r) clamped to ±60 from the row's RMS scale rs_r,
+// cut into its top 11 significant bits (hi) and the rounded remainder
+// (lo), fp16 [rows, n] each — the parts the GEMM's converters would make.
+struct Split16Out {
+  uint16_t* hi;
+  uint16_t* lo;
+  const float* gain;  // [n] or null
+  float norm_k;       // sqrt(n) · max|gain| (sqrt(n) without a gain)
+};
+
 // x ← x + RMSNorm(o, gain) (embed.go:216-220, 231-235), then the next
-// pre-norm factor rowscale = 1/√(Σx²/n + eps). x_lo (optional) receives the
-// split-TF32 low part of the new x. x_new is (x + RMSNorm(o, gain))·scalar
-// (EmbeddingGemma 2's layer scalar, embed.go:370-371; 1 = plain residual).
-// When final_gain is given, x is replaced by RMSNorm(x_new, final_gain)
-// instead (embed.go:237) and rowscale/x_lo are not written.
-int residual_postnorm(float* x, float* x_lo, const float* o, const float* gain, float eps,
+// pre-norm factor rowscale = 1/√(Σx²/n + eps). parts (optional) receives
+// the new x's split-fp16 operand for the next product. x_new is (x +
+// RMSNorm(o, gain))·scalar (EmbeddingGemma 2's layer scalar,
+// embed.go:370-371; 1 = plain residual). When final_gain is given, x is
+// replaced by RMSNorm(x_new, final_gain) instead (embed.go:237) and
+// rowscale/parts are not written.
+int residual_postnorm(float* x, const Split16Out* parts, const float* o, const float* gain, float eps,
                       float* rowscale, const float* final_gain, int64_t rows, int n,
                       cudaStream_t s, float scalar = 1.0f);
 
@@ -78,6 +91,12 @@ struct AttnArgs {
   const int32_t* qlen;
   int window;
   float scale;
+  // tensor-core kernel only: instead of `out`, the next product's split-fp16
+  // A operand — out·2^out16_exp cut into fp16 hi (top 11 significant bits)
+  // and lo (the rounded remainder), laid out like `out` (row stride ost)
+  uint16_t* out16 = nullptr;
+  uint16_t* out16_lo = nullptr;
+  int out16_exp = 0;
 };
 int attention_simt(const AttnArgs& a, cudaStream_t s);
 

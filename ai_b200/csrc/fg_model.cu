@@ -173,6 +173,10 @@ struct fg_model {
   int cap_batch = 0;
   float *x = nullptr, *rowscale = nullptr, *qkv = nullptr, *att = nullptr, *gu = nullptr,
         *tmp = nullptr;
+  // the split-fp16 parts of x for the gate/up product ([tokens, H] hi, then
+  // lo); those of the attention output and of the gated activations take
+  // the place of att and gu, whose fp32 forms are then not written
+  uint16_t* x16 = nullptr;
   float *pooled = nullptr, *head_a = nullptr, *head_b = nullptr;
   int32_t* eff_len = nullptr;
   int* err = nullptr;
@@ -584,6 +588,7 @@ int ensure_workspace(fg_model* m, int64_t tokens, int batch) {
     FG_TRY(dev_alloc_t(m, &m->att, tokens * attw));
     FG_TRY(dev_alloc_t(m, &m->gu, tokens * F));
     FG_TRY(dev_alloc_t(m, &m->tmp, tokens * std::max(H, attw)));
+    if (c.variant != 2) FG_TRY(dev_alloc_t(m, &m->x16, 2 * tokens * H));
     if (c.variant == 2) {
       const int64_t P = c.ple_dim, L = c.num_layers;
       FG_TRY(dev_alloc_t(m, &m->ple_buf, tokens * L * P));
@@ -1397,6 +1402,24 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
       FG_TRY(grow_attn_ws(m, attn_tc_workspace_bytes(B, T, T, Hq, Hkv), s));
       FG_TRY(attn_tc_carve(m->attn_ws, B, T, T, Hq, Hkv, &ops));
     }
+    // Split-fp16 with producer-made operands: the attention kernel, the
+    // gated epilogue and the residual write the next product's two fp16
+    // parts — the ones its converter warps would cut from the fp32 tile —
+    // so the O, down and gate/up products load them by TMA and convert
+    // nothing (the same parts, so the same result).
+    const bool pre = split && m->h16 && m->use16 && gemm_h16_applies(int(M));
+    const bool att16 = pre && tc && Wo.h16 && L.att_ok;
+    const bool gu16 = pre && Wd.h16 && L.gu_ok;
+    const bool x16 = pre && Wgu.h16;
+    uint16_t* const att16_hi = reinterpret_cast<uint16_t*>(m->att);  // in place of att
+    uint16_t* const att16_lo = att16_hi + M * attw;
+    uint16_t* const gu16_hi = reinterpret_cast<uint16_t*>(m->gu);    // in place of gu
+    uint16_t* const gu16_lo = gu16_hi + M * F;
+    if (att16) {
+      a.out16 = att16_hi;
+      a.out16_lo = att16_lo;
+      a.out16_exp = L.att_exp;
+    }
     // q|k|v = rowscale ⊙ (x · Wqkv'ᵀ)   (embed.go:193-197)
     GemmArgs g = make_gemm(int(M), m->x, x_lo, H, Wqkv, split);
     g.epi.rowscale = m->rowscale;
@@ -1447,6 +1470,10 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
     g.epi.out = m->tmp;
     g.epi.ldo = H;
     use_h16(m, g, Wo, nullptr, L.att_ok, L.att_exp);
+    if (att16) {
+      g.A16 = att16_hi;
+      g.A16_lo = att16_lo;
+    }
     {
       PhaseScope ps(m, FG_PHASE_GEMM_O, s, gemm_flops(g));
       FG_TRY(gemm_tn(g, m->err, s));
@@ -1454,8 +1481,12 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
     // x += RMSNorm(o0)   (embed.go:216-220), and the FFN pre-norm factor
     {
       PhaseScope ps(m, FG_PHASE_RESIDUAL, s, act_bytes * 3 + double(M) * 4);
-      FG_TRY(residual_postnorm(m->x, x_lo, m->tmp, L.post_attn, c.rms_norm_eps, m->rowscale,
-                               nullptr, M, H, s));
+      // + the gate/up product's parts, with its pre-norm gain when unfolded
+      // and the row bound sqrt(H)·max|gain| the product's exponent takes
+      const float bg = Wgu.h16_gain && Wgu.h16_gmax > 0.f ? Wgu.h16_gmax : 0.f;
+      const Split16Out parts{m->x16, m->x16 + M * H, Wgu.h16_gain, sqrtf(float(H)) * (bg > 0.f ? bg : 1.f)};
+      FG_TRY(residual_postnorm(m->x, x16 ? &parts : nullptr, m->tmp, L.post_attn, c.rms_norm_eps,
+                               m->rowscale, nullptr, M, H, s));
     }
     // gu = GELU(rs·x·Wg') ⊙ (rs·x·Wu')   (embed.go:224-227)
     g = make_gemm(int(M), m->x, x_lo, H, Wgu, split);
@@ -1466,6 +1497,19 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
     g.epi.rowscale = m->rowscale;
     g.epi.geglu = 1;
     use_h16(m, g, Wgu, m->rowscale, true, 0);
+    if (x16) {
+      g.A16 = m->x16;
+      g.A16_lo = m->x16 + M * H;
+      g.a_bound_gain = g.a_gain && g.a_gain_max > 0.f ? g.a_gain_max : 0.f;
+      g.a_gain = nullptr;  // applied by the residual
+    }
+    if (gu16) {
+      g.epi.out = nullptr;
+      g.epi.out_lo = nullptr;
+      g.epi.out16 = gu16_hi;
+      g.epi.out16_lo = gu16_lo;
+      g.epi.out16_exp = L.gu_exp;
+    }
     {
       PhaseScope ps(m, FG_PHASE_GEMM_GATE_UP, s, gemm_flops(g));
       FG_TRY(gemm_tn(g, m->err, s));
@@ -1475,6 +1519,10 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
     g.epi.out = m->tmp;
     g.epi.ldo = H;
     use_h16(m, g, Wd, nullptr, L.gu_ok, L.gu_exp);
+    if (gu16) {
+      g.A16 = gu16_hi;
+      g.A16_lo = gu16_lo;
+    }
     {
       PhaseScope ps(m, FG_PHASE_GEMM_DOWN, s, gemm_flops(g));
       FG_TRY(gemm_tn(g, m->err, s));
@@ -1482,7 +1530,7 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
     // x += RMSNorm(mlp0)   (embed.go:231-235); final norm on the last layer (embed.go:237)
     {
       PhaseScope ps(m, FG_PHASE_RESIDUAL, s, act_bytes * 3 + double(M) * 4);
-      FG_TRY(residual_postnorm(m->x, x_lo, m->tmp, L.post_ffn, c.rms_norm_eps, m->rowscale,
+      FG_TRY(residual_postnorm(m->x, nullptr, m->tmp, L.post_ffn, c.rms_norm_eps, m->rowscale,
                                last ? m->final_gain : nullptr, M, H, s));
     }
   }
