@@ -202,22 +202,28 @@ def test_bf16_resident_projections_are_bitwise_identical(norm_std):
         m16.close()
 
 
-@pytest.mark.parametrize("norm_std", [0.0, 0.1])
-def test_split_fp16_matches_split_tf32(norm_std):
+@pytest.mark.parametrize("norm_std,T,lengths", [
+    (0.0, 128, [128, 100, 1, 77, 128, 64]),
+    (0.1, 128, [128, 100, 1, 77, 128, 64]),
+    # query tiles past a sequence's length (the attention's empty-tile path)
+    (0.0, 512, [512, 1, 200, 129, 300, 512]),
+    (0.1, 512, [3, 512, 255, 130, 384, 90]),
+])
+def test_split_fp16_matches_split_tf32(norm_std, T, lengths):
     """The split-fp16 encoder GEMMs (bf16-exact weights as exact fp16, A as
-    two fp16 parts under a power-of-two row scale) agree with split-TF32 to
-    the size of split-TF32's own error, are in use (not bitwise equal) and
-    repeatable. With non-zero norm gains the folded Q/K/V and gate/up
-    weights have no exact fp16 form: those GEMMs take the unfolded weights
-    and apply the gains to A."""
+    two fp16 parts under a power-of-two row scale, made by A's producer for
+    O, gate/up and down) agree with split-TF32 to the size of split-TF32's
+    own error, are in use (not bitwise equal) and repeatable. With non-zero
+    norm gains the folded Q/K/V and gate/up weights have no exact fp16 form:
+    those GEMMs take the unfolded weights and apply the gains to A."""
     from ai_b200 import gemma
     from ai_b200 import synthetic as S
 
     cfg = S.small_config(layers=3, vocab=2048)
     w = S.make_weights(cfg, seed=43, norm_std=norm_std)
-    ids = S.make_ids(6, 128, 14, cfg["vocab_size"])
-    lengths = np.array([128, 100, 1, 77, 128, 64], np.int32)
-    m1 = gemma.from_synthetic(cfg, w, device=0, max_batch_tokens=4096)
+    ids = S.make_ids(len(lengths), T, 14, cfg["vocab_size"])
+    lengths = np.array(lengths, np.int32)
+    m1 = gemma.from_synthetic(cfg, w, device=0, max_batch_tokens=len(lengths) * T)
     try:
         a = m1.embed_padded(ids, lengths)
         b = m1.embed_padded(ids, lengths, precision=gemma.PREC_SPLIT_TF32)
