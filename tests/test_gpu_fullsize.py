@@ -175,7 +175,7 @@ def test_config4_matmul_sweep_full_m(cuda, k, n, transposed):
     want = a.double() @ w.double()
     err = (got.double() - want).abs()
     scale = a.double().norm(dim=1)[:, None] * w.double().norm(dim=0)[None, :]
-    ok = (err <= 1e-4 * (1 + want.abs())) | (err <= 1e-5 * scale)
+    ok = (err <= 1e-4 * (1 + want.abs())) | (err <= 3e-6 * scale)  # split: measured <= 1.95e-6
     print(f"M={m} K={k} N={n} T={transposed}: max|err| {err.max().item():.3e} "
           f"max err/(|a||w|) {(err / scale).max().item():.3e}")
     assert bool(ok.all())

@@ -50,7 +50,7 @@ def test_matmul_split_tf32_vs_float64(cuda, m, k, n, transposed):
     else:
         wt = _t(w, cuda)
     got = T.MatMul(x, wt).cpu().numpy()
-    ok = _gemm_tol(got, want, a, w)
+    ok = _gemm_tol(got, want, a, w, rel=3e-6)  # split: measured <= 1.95e-6
     scale = np.linalg.norm(a.astype(np.float64), axis=1)[:, None] * \
         np.linalg.norm(w.astype(np.float64), axis=0)[None, :]
     print(f"gemm m={m} k={k} n={n} T={transposed}: max|err| {np.abs(got - want).max():.3e} "
@@ -129,7 +129,7 @@ def test_matmul_plain_tf32_equals_truncated_product(cuda, m, k, n):
     want = trunc(a).astype(np.float64) @ trunc(w).astype(np.float64)
     wt = _t(w.T.copy(), cuda).t()  # K-major weights: no copy on the way in
     got = T.MatMul(_t(a, cuda), wt, precision=T.PREC_TF32).cpu().numpy()
-    ok = _gemm_tol(got, want, a, w)
+    ok = _gemm_tol(got, want, a, w, rel=1e-6)  # vs the truncated product: <= 5.9e-7
     assert ok.all(), f"max err {np.abs(got - want).max()} at {np.argwhere(~ok)[:3]}"
 
 
