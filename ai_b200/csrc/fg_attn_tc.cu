@@ -415,20 +415,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld_wait();
       float mt8[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) mt8[u] = -FLT_MAX;
+      for (int u = 0; u < 8; ++u) mt8[u] = -INFINITY;
       if (full_row) {
 #pragma unroll
         for (int q = 0; q < 2; ++q)
 #pragma unroll
           for (int e = 0; e < 32; ++e) mt8[e & 7] = fmaxf(mt8[e & 7], __uint_as_float(sr[q][e]));
       } else {
+        // masked scores become -inf here, whose exponential in pass 2 is
+        // exactly 0, so pass 2 is the same for every row
+        const int c0 = half * 64 - lo_c;  // column e of this warp's half is visible iff unsigned(c0 + e) < span
 #pragma unroll
         for (int q = 0; q < 2; ++q)
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
-            const int col = half * 64 + q * 32 + e;
-            const bool in = unsigned(col - lo_c) < unsigned(span);
-            mt8[e & 7] = fmaxf(mt8[e & 7], in ? __uint_as_float(sr[q][e]) : -FLT_MAX);
+            const bool in = unsigned(c0 + q * 32 + e) < unsigned(span);
+            const float v = in ? __uint_as_float(sr[q][e]) : -INFINITY;
+            sr[q][e] = __float_as_uint(v);
+            mt8[e & 7] = fmaxf(mt8[e & 7], v);
           }
       }
       const float mh = fmaxf(fmaxf(fmaxf(mt8[0], mt8[1]), fmaxf(mt8[2], mt8[3])),
@@ -490,43 +494,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_st_wait();
       }
       l *= factor;
-      const float mc = m * c;
+      // a row with no visible key so far has only -inf scores: 0 keeps their
+      // exponentials 0 (m·c of the initial -FLT_MAX could overflow to -inf)
+      const float mc = have ? m * c : 0.f;
       // pass 2: probabilities of this warp's 64 columns, split into packed
       // bf16 hi / lo. The 32-column chunk q of S is overwritten by its own
       // P: hi (16 columns of bf16 pairs) at columns 32q.., lo at 32q+16..
       float ps8[8];  // eight independent partial sums
 #pragma unroll
       for (int u = 0; u < 8; ++u) ps8[u] = 0.f;
-      const bool all_vis = have && full_row;
-      {
-        const int hh = half;
+      // (masked scores are -inf since pass 1 and mc is finite, so masked
+      // keys and rows with no visible key so far get exact zeros)
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          uint32_t hw[16], lw[16];
+      for (int q = 0; q < 2; ++q) {
+        uint32_t hw[16], lw[16];
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const int col = hh * 64 + q * 32 + 2 * e;
-            float a, bb;
-            if (all_vis) {
-              a = ex2_approx(fmaf(__uint_as_float(sr[q][2 * e]), c, -mc));
-              bb = ex2_approx(fmaf(__uint_as_float(sr[q][2 * e + 1]), c, -mc));
-            } else {
-              // masked scores become -inf, whose exponential is exactly 0
-              const float s0 = unsigned(col - lo_c) < unsigned(span) ? __uint_as_float(sr[q][2 * e]) : -INFINITY;
-              const float s1 = unsigned(col + 1 - lo_c) < unsigned(span) ? __uint_as_float(sr[q][2 * e + 1]) : -INFINITY;
-              a = have ? ex2_approx(fmaf(s0, c, -mc)) : 0.f;
-              bb = have ? ex2_approx(fmaf(s1, c, -mc)) : 0.f;
-            }
-            ps8[e & 7] += a + bb;
-            const uint32_t h2 = pack_bf16x2(a, bb);  // RN bf16 of both, a in the low half
-            const float ah = __uint_as_float(h2 << 16), bh = __uint_as_float(h2 & 0xffff0000u);
-            hw[e] = h2;
-            lw[e] = pack_bf16x2(a - ah, bb - bh);
-          }
-          const uint32_t cq = uint32_t((hh * 2 + q) * 32);
-          tmem_st_32x32b_x16(tS + cq, hw);
-          tmem_st_32x32b_x16(tS + cq + 16, lw);
+        for (int e = 0; e < 16; ++e) {
+          const float a = ex2_approx(fmaf(__uint_as_float(sr[q][2 * e]), c, -mc));
+          const float bb = ex2_approx(fmaf(__uint_as_float(sr[q][2 * e + 1]), c, -mc));
+          ps8[e & 7] += a + bb;
+          const uint32_t h2 = pack_bf16x2(a, bb);  // RN bf16 of both, a in the low half
+          const float ah = __uint_as_float(h2 << 16), bh = __uint_as_float(h2 & 0xffff0000u);
+          hw[e] = h2;
+          lw[e] = pack_bf16x2(a - ah, bb - bh);
         }
+        const uint32_t cq = uint32_t((half * 2 + q) * 32);
+        tmem_st_32x32b_x16(tS + cq, hw);
+        tmem_st_32x32b_x16(tS + cq + 16, lw);
       }
       l += ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
       tmem_st_wait();
