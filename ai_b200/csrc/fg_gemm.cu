@@ -285,12 +285,11 @@ __device__ __forceinline__ void qkv_attn_epilogue(const GemmEpilogue& e, const O
     const bool is_q = tn < Hq;
     const float* const g = is_q ? e.qgain : e.kgain;
     const float eps = e.eps;
-    // position-minor tables: the warp's 32 consecutive rows read one
-    // 128-byte segment per column instead of 32 scattered words
+    // position-minor table with cos and sin side by side: the warp's 32
+    // consecutive rows read one 256-byte segment per column, one load each
     const int t = row % T;
     const int64_t rld = e.rope_ld;
-    const float* const cs = e.rope_cos + t;
-    const float* const sn = e.rope_sin + t;
+    const float2* const csn = e.rope_cs + t;
     __nv_bfloat16* const hi = static_cast<__nv_bfloat16*>(is_q ? e.q_hi : e.k_hi);
     __nv_bfloat16* const lo = static_cast<__nv_bfloat16*>(is_q ? e.q_lo : e.k_lo);
     const int width = (is_q ? Hq : Hkv) * D;
@@ -337,7 +336,8 @@ __device__ __forceinline__ void qkv_attn_epilogue(const GemmEpilogue& e, const O
         const float g1 = __shfl_sync(0xffffffffu, ga, j), g2 = __shfl_sync(0xffffffffu, gb, j);
         const float x1 = __fmul_rn(__fmul_rn(__fmul_rn(__uint_as_float(ra[j]), rs), inv), g1);
         const float x2 = __fmul_rn(__fmul_rn(__fmul_rn(__uint_as_float(rb[j]), rs), inv), g2);
-        const float c = row_ok ? cs[i * rld] : 0.f, s = row_ok ? sn[i * rld] : 0.f;
+        const float2 f = row_ok ? csn[i * rld] : make_float2(0.f, 0.f);
+        const float c = f.x, s = f.y;
         y1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, s));
         y2 = __fadd_rn(__fmul_rn(x1, s), __fmul_rn(x2, c));
       };

@@ -104,9 +104,10 @@ struct GemmEpilogue {
   const float* qgain = nullptr;
   const float* kgain = nullptr;
   float eps = 0.f;
-  const float* rope_cos = nullptr;  // position-minor: [128, rope_ld], entry (i, t) at i·rope_ld + t
-  const float* rope_sin = nullptr;
-  int64_t rope_ld = 0;              // >= T
+  // RoPE factors, position-minor with cos and sin side by side: entry
+  // (frequency i, position t) at i·rope_ld + t holds (cos, sin)
+  const float2* rope_cs = nullptr;
+  int64_t rope_ld = 0;  // >= T
   void* q_hi = nullptr;  // bf16 [M, Hq·256]
   void* q_lo = nullptr;
   void* k_hi = nullptr;  // bf16 [M, Hkv·256]

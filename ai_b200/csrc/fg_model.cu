@@ -164,7 +164,9 @@ struct fg_model {
   float* final_gain = nullptr;
   std::vector<fg::Dense> dense;
   std::vector<float*> rope_cos, rope_sin;    // [max_tokens, D/2]
-  std::vector<float*> rope_cosT, rope_sinT;  // the same, position-minor [D/2, max_tokens]
+  // the same for 256-wide heads, position-minor with cos and sin side by
+  // side: [D/2][max_tokens][2] (null for other head sizes)
+  std::vector<float*> rope_csT;
   std::vector<double> rope_bases;  // distinct bases, index = Layer::rope
   std::vector<void*> allocations;
 
@@ -552,6 +554,19 @@ std::vector<float> fold(const std::vector<float>& w, const std::vector<float>& g
   return out;
 }
 
+// [half][P][2]: (cos, sin) of frequency i at position t at (i·P + t)·2,
+// from the position-major tables [P][half].
+std::vector<float> rope_pairs_position_minor(const std::vector<float>& cs, const std::vector<float>& sn, int64_t P,
+                                             int64_t half) {
+  std::vector<float> out(size_t(2 * P * half));
+  for (int64_t t = 0; t < P; ++t)
+    for (int64_t i = 0; i < half; ++i) {
+      out[size_t(2 * (i * P + t))] = cs[size_t(t * half + i)];
+      out[size_t(2 * (i * P + t) + 1)] = sn[size_t(t * half + i)];
+    }
+  return out;
+}
+
 void rope_table(double base, int T, int D, std::vector<float>& c, std::vector<float>& s) {
   const int half = D / 2;
   std::vector<double> inv(half);
@@ -644,21 +659,10 @@ int finalize_v2(fg_model* m, int64_t max_tokens) {
     FG_TRY(upload(m, sn, &ds));
     m->rope_cos.push_back(dc);
     m->rope_sin.push_back(ds);
-    // position-minor copies for the fused QKV epilogue (256-wide heads)
-    float *dcT = nullptr, *dsT = nullptr;
-    if (D == 256) {
-      const int64_t P = c.max_tokens, half = D / 2;
-      std::vector<float> cst(cs.size()), snt(sn.size());
-      for (int64_t t = 0; t < P; ++t)
-        for (int64_t i = 0; i < half; ++i) {
-          cst[i * P + t] = cs[t * half + i];
-          snt[i * P + t] = sn[t * half + i];
-        }
-      FG_TRY(upload(m, cst, &dcT));
-      FG_TRY(upload(m, snt, &dsT));
-    }
-    m->rope_cosT.push_back(dcT);
-    m->rope_sinT.push_back(dsT);
+    // position-minor copy for the fused QKV epilogue (256-wide heads)
+    float* dT = nullptr;
+    if (D == 256) FG_TRY(upload(m, rope_pairs_position_minor(cs, sn, c.max_tokens, D / 2), &dT));
+    m->rope_csT.push_back(dT);
     m->rope_bases.push_back(base);
     m->rope_dims.push_back(D);
     *out = int(m->rope_bases.size()) - 1;
@@ -797,17 +801,9 @@ int finalize(fg_model* m, int64_t max_tokens) {
       FG_TRY(upload(m, sn, &ds));
       m->rope_cos.push_back(dc);
       m->rope_sin.push_back(ds);
-      const size_t half = size_t(D) / 2, P = size_t(c.max_tokens);
-      std::vector<float> cst(cs.size()), snt(sn.size());
-      for (size_t t = 0; t < P; ++t)
-        for (size_t i = 0; i < half; ++i) {
-          cst[i * P + t] = cs[t * half + i];
-          snt[i * P + t] = sn[t * half + i];
-        }
-      FG_TRY(upload(m, cst, &dc));
-      FG_TRY(upload(m, snt, &ds));
-      m->rope_cosT.push_back(dc);
-      m->rope_sinT.push_back(ds);
+      float* dT = nullptr;
+      FG_TRY(upload(m, rope_pairs_position_minor(cs, sn, c.max_tokens, int(D) / 2), &dT));
+      m->rope_csT.push_back(dT);
     }
   }
 
@@ -1175,7 +1171,7 @@ int forward_v2(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, i
     // 256-wide layers the epilogue also applies the q/k norms, RoPE and the
     // v_norm and writes the tensor-core attention's operands
     const bool tc = attn_tc_supported(a);
-    const bool fused = tc && D == 256 && m->rope_cosT[size_t(Ly.rope)] != nullptr;
+    const bool fused = tc && D == 256 && m->rope_csT[size_t(Ly.rope)] != nullptr;
     AttnOperands ops{};
     if (tc) FG_TRY(grow_attn_ws(m, attn_tc_workspace_bytes(B, T, T, Hq, Hkv, D), s));
     GemmArgs g = make_gemm(int(M), m->x, nullptr, H, Ly.wqkv, split);
@@ -1191,8 +1187,7 @@ int forward_v2(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, i
       g.epi.qgain = Ly.qgain;
       g.epi.kgain = Ly.kgain;
       g.epi.eps = c.rms_norm_eps;
-      g.epi.rope_cos = m->rope_cosT[size_t(Ly.rope)];
-      g.epi.rope_sin = m->rope_sinT[size_t(Ly.rope)];
+      g.epi.rope_cs = reinterpret_cast<const float2*>(m->rope_csT[size_t(Ly.rope)]);
       g.epi.rope_ld = c.max_tokens;
       g.epi.q_hi = ops.q_hi;
       g.epi.q_lo = ops.q_lo;
@@ -1433,8 +1428,7 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
       g.epi.qgain = L.qgain;
       g.epi.kgain = L.kgain;
       g.epi.eps = c.rms_norm_eps;
-      g.epi.rope_cos = m->rope_cosT[L.rope];
-      g.epi.rope_sin = m->rope_sinT[L.rope];
+      g.epi.rope_cs = reinterpret_cast<const float2*>(m->rope_csT[L.rope]);
       g.epi.rope_ld = c.max_tokens;
       g.epi.q_hi = ops.q_hi;
       g.epi.q_lo = ops.q_lo;
