@@ -85,44 +85,27 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// The same with a suspend-time bound: the thread waits at most about
-// hint_ns for the phase before the test returns false (it returns true as
-// soon as the phase completes), so a caller's own time limit is checked at
-// that granularity rather than after the hardware's default window.
-__device__ __forceinline__ bool mbar_try_wait_for(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.b32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity), "r"(hint_ns)
-      : "memory");
-  return ok != 0;
-}
-// Suspend bound for the polling loops below: a quarter of the wait limit,
-// at most 100 µs.
-__device__ __forceinline__ uint32_t wait_hint_ns(uint64_t limit) {
-  return uint32_t(limit / 4 < 100000u ? limit / 4 : 100000u) + 1u;
-}
-
 // Waits for the phase with the given parity to complete. Gives up after
 // the device's wait limit (gerr's status block), or as soon as another role of the CTA has aborted
 // (*abort != 0); on a timeout it raises the abort flag and records `code`.
+// A try_wait on an open phase holds the thread for a while (about 4 µs on
+// B200, whatever suspend-time hint it is given), so the limit is checked
+// between tries: a wait gives up at the first check past the limit, i.e.
+// waits shorter than one try never do. The time is taken before the first
+// try, so a limit below one try binds on every wait that outlasts a try.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
                                           int* gerr, int code) {
-  if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
+  if (mbar_try_wait(bar, parity)) return true;
   const uint64_t limit = wait_limit_ns(gerr);
-  const uint32_t hint = wait_hint_ns(limit);
   while (true) {
-    if (mbar_try_wait_for(bar, parity, hint)) return true;
     if (*abort) return false;
     if (globaltimer_ns() - t0 > limit) {
       *abort = 1;
       atomicCAS(gerr, 0, code);
       return false;
     }
+    if (mbar_try_wait(bar, parity)) return true;
   }
 }
 
@@ -243,32 +226,20 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
       : "memory");
   return ok != 0;
 }
-__device__ __forceinline__ bool mbar_try_wait_cluster_for(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.b32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity), "r"(hint_ns)
-      : "memory");
-  return ok != 0;
-}
 // mbar_wait for a barrier that threads of the other CTA arrive on.
 __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, volatile int* abort,
                                                   int* gerr, int code) {
-  if (mbar_try_wait_cluster(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
+  if (mbar_try_wait_cluster(bar, parity)) return true;
   const uint64_t limit = wait_limit_ns(gerr);
-  const uint32_t hint = wait_hint_ns(limit);
   while (true) {
-    if (mbar_try_wait_cluster_for(bar, parity, hint)) return true;
     if (*abort) return false;
     if (globaltimer_ns() - t0 > limit) {
       *abort = 1;
       atomicCAS(gerr, 0, code);
       return false;
     }
+    if (mbar_try_wait_cluster(bar, parity)) return true;
   }
 }
 // Same warp index in both CTAs; both receive the same TMEM address.

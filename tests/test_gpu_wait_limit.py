@@ -3,9 +3,13 @@
 up their waits, drain their own copies and MMAs, free their tensor memory
 and return; fg_synchronize reports FG_ETIMEOUT once and clears the record;
 and the next call with the default limit gives the same result, bit for
-bit, as before. No fault is injected: the limit (1 µs) is shorter than the
-kernels' own pipeline latencies (a K = 8192 main loop; a 1024-key score
-tile), so their waits run out on their own and the context stays usable.
+bit, as before. No fault is injected: the limit (1 µs) is shorter than
+waits the kernels have anyway, so those run out on their own and the
+context stays usable. A wait checks its limit between tries of the
+barrier, and a try holds the thread about 4 µs on B200, so the cases are
+chosen for waits longer than that: a K = 8192 main loop under the GEMM
+epilogue; for attention, a first wave of 148 CTAs whose Q and K come from
+HBM together (operands larger than L2) before the first score tile.
 """
 import numpy as np
 import pytest
@@ -55,10 +59,12 @@ def test_attention_wait_limit_reports_timeout_and_recovers(cuda):
     from ai_b200 import tensor as T
 
     g = torch.Generator(device=cuda).manual_seed(6)
-    q = torch.randn(2, 3, 1024, 256, generator=g, device=cuda)
-    k = torch.randn(2, 1, 1024, 256, generator=g, device=cuda)
-    v = torch.randn(2, 1, 1024, 256, generator=g, device=cuda)
-    lens = torch.tensor([1024, 700], dtype=torch.int32)
+    B = 128  # 1536 CTAs; split q, k and vᵀ are 168 MB, more than L2 holds
+    q = torch.randn(B, 3, 512, 256, generator=g, device=cuda)
+    k = torch.randn(B, 1, 512, 256, generator=g, device=cuda)
+    v = torch.randn(B, 1, 512, 256, generator=g, device=cuda)
+    lens = torch.full((B,), 512, dtype=torch.int32)
+    lens[1] = 300
     ref = T.AttentionScaled(q, k, v, lens, 0, 1 / 16)
     torch.cuda.synchronize()
     _expect_timeout(lambda: T.AttentionScaled(q, k, v, lens, 0, 1 / 16))
