@@ -10,7 +10,7 @@
 // part: a TF32 hi/lo pair does not fit shared memory beside the K/V ring,
 // the bf16 pair does.)
 //
-// One CTA per (query tile of 128 rows, query head, sequence), 6 warps:
+// One CTA per (query tile of 128 rows, query head, sequence), 10 warps:
 //   warp 0      TMA producer: Q (hi/lo, resident), then per key tile the K
 //               d-chunks and the Vᵀ (d-half × key-half) chunks through a
 //               3-stage ring of 32 KB, in the order the MMA warp uses them.
@@ -18,11 +18,14 @@
 //               S_j = Q·K_jᵀ into one of two 128-column S buffers while the
 //               softmax warps work on S_{j−1}; then O += P_{j−1}·V_{j−1}
 //               with P read from TMEM (A operand), O in columns 256..511.
-//   warps 2..5  softmax, one query row per thread: visibility by index
-//               arithmetic (padding: j < len; sliding layers: |i−j| < window),
-//               running max with lazy rescaling (O is rescaled in TMEM only
-//               when the max grows by more than 2^8), P = exp2 written back
-//               over S as packed bf16 hi/lo; the final 1/Σ and the store.
+//   warps 2..9  softmax, two warps per TMEM lane quadrant (one query row
+//               per thread, 64 of the 128 score columns each): visibility by
+//               index arithmetic (padding: j < len; sliding layers:
+//               |i−j| < window; masked scores become -inf while the row
+//               maximum is taken), running max with lazy rescaling (O is
+//               rescaled in TMEM only when the max grows by more than 2^8),
+//               P = exp2 written back over S as packed bf16 hi/lo; the final
+//               1/Σ and the store.
 // Head_dim 512 (EmbeddingGemma 2's global layers): Q (256 KB as split
 // bf16) does not fit beside the ring, so its d-chunks are streamed through
 // the ring with the K chunks they meet, and each CTA produces one 256-wide
