@@ -23,7 +23,9 @@
 #include <cstring>
 #include <map>
 #include <memory>
+#include <set>
 #include <string>
+#include <tuple>
 #include <vector>
 
 #include <cuda_fp16.h>
@@ -223,6 +225,23 @@ struct fg_model {
   std::vector<cudaEvent_t> event_pool;
   int64_t launches[FG_NUM_PHASES] = {};
   double work[FG_NUM_PHASES] = {};
+
+  // CUDA graphs of the device-API forward, per (B, T, dim, precision, ids,
+  // lengths, out): a key's first call runs eagerly (it makes any
+  // allocation and one-time set-up the shape needs), its second is
+  // captured on cap_stream and then launched, later ones launch the graph
+  // on the caller's stream. A graph also carries the launch counts and
+  // algorithmic work its capture recorded, added on every launch. Graphs
+  // are dropped when a buffer they use is freed.
+  using GraphKey = std::tuple<int, int, int, int, const void*, const void*, const void*>;
+  struct Graph {
+    cudaGraphExec_t exec = nullptr;
+    int64_t launches[FG_NUM_PHASES] = {};
+    double work[FG_NUM_PHASES] = {};
+  };
+  std::map<GraphKey, Graph> graphs;
+  std::set<GraphKey> graph_seen;
+  cudaStream_t cap_stream = nullptr;
 };
 
 namespace fg {
@@ -1094,10 +1113,20 @@ void plan_batches(const int* len, int nseq, int64_t budget, std::vector<int>& or
   if (count > 0) batches.push_back({start, count, std::max(max_len, 1)});
 }
 
+// Destroys the cached forward graphs (before a buffer they use is freed),
+// after every launch of them has finished.
+void drop_graphs(fg_model* m) {
+  if (!m->graphs.empty()) cudaDeviceSynchronize();
+  for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second.exec);
+  m->graphs.clear();
+  m->graph_seen.clear();
+}
+
 // The tensor-core attention's operand workspace, grown (never shrunk) to
 // `need` bytes; growing waits for the work already queued on `s`.
 int grow_attn_ws(fg_model* m, size_t need, cudaStream_t s) {
   if (need <= m->attn_ws_bytes) return FG_OK;
+  drop_graphs(m);
   if (m->attn_ws) {
     FG_CUDA_TRY(cudaStreamSynchronize(s));
     FG_CUDA_TRY(cudaFree(m->attn_ws));
@@ -1551,6 +1580,65 @@ int forward(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int 
   return FG_OK;
 }
 
+// The forward through the model's graph cache (see fg_model::graphs); the
+// eager path while profiling (its event pairs are per launch).
+int forward_graphed(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int T, int dim,
+                    int precision, float* out, cudaStream_t s) {
+  if (m->prof) return forward(m, ids, lengths, B, T, dim, precision, out, s);
+  const fg_model::GraphKey key{B, T, dim, precision, ids, lengths, out};
+  auto it = m->graphs.find(key);
+  if (it != m->graphs.end()) {
+    m->use16 = precision == FG_PREC_SPLIT;
+    FG_CUDA_TRY(cudaGraphLaunch(it->second.exec, s));
+    for (int i = 0; i < FG_NUM_PHASES; ++i) {
+      m->launches[i] += it->second.launches[i];
+      m->work[i] += it->second.work[i];
+    }
+    return FG_OK;
+  }
+  if (!m->graph_seen.count(key)) {
+    if (m->graph_seen.size() >= 64) m->graph_seen.clear();
+    m->graph_seen.insert(key);
+    return forward(m, ids, lengths, B, T, dim, precision, out, s);
+  }
+  if (!m->cap_stream) FG_CUDA_TRY(cudaStreamCreateWithFlags(&m->cap_stream, cudaStreamNonBlocking));
+  int64_t l0[FG_NUM_PHASES];
+  double w0[FG_NUM_PHASES];
+  std::copy(m->launches, m->launches + FG_NUM_PHASES, l0);
+  std::copy(m->work, m->work + FG_NUM_PHASES, w0);
+  FG_CUDA_TRY(cudaStreamBeginCapture(m->cap_stream, cudaStreamCaptureModeThreadLocal));
+  const int rc = forward(m, ids, lengths, B, T, dim, precision, out, m->cap_stream);
+  cudaGraph_t g = nullptr;
+  const cudaError_t ce = cudaStreamEndCapture(m->cap_stream, &g);
+  fg_model::Graph gr;
+  for (int i = 0; i < FG_NUM_PHASES; ++i) {
+    gr.launches[i] = m->launches[i] - l0[i];
+    gr.work[i] = m->work[i] - w0[i];
+  }
+  // the captured launches did not run: their counts come with the graph
+  std::copy(l0, l0 + FG_NUM_PHASES, m->launches);
+  std::copy(w0, w0 + FG_NUM_PHASES, m->work);
+  cudaError_t ie = cudaErrorUnknown;
+  if (rc == FG_OK && ce == cudaSuccess && g) ie = cudaGraphInstantiate(&gr.exec, g, 0);
+  if (g) cudaGraphDestroy(g);
+  if (ie != cudaSuccess) {
+    // not capturable after all: this key stays eager
+    cudaGetLastError();
+    clear_error();
+    m->graph_seen.erase(key);
+    return forward(m, ids, lengths, B, T, dim, precision, out, s);
+  }
+  if (m->graphs.size() >= 16) drop_graphs(m);
+  m->graphs[key] = gr;
+  m->graph_seen.insert(key);
+  FG_CUDA_TRY(cudaGraphLaunch(gr.exec, s));
+  for (int i = 0; i < FG_NUM_PHASES; ++i) {
+    m->launches[i] += gr.launches[i];
+    m->work[i] += gr.work[i];
+  }
+  return FG_OK;
+}
+
 // (*Model).Dim (model.go:336-344): the embedding projection's width for
 // EmbeddingGemma 2, else the last Dense layer's, else hidden.
 int model_dim(const fg_model* m) {
@@ -1698,7 +1786,7 @@ int fg_embed_ids_device(fg_model* m, const int32_t* d_ids, const int32_t* d_leng
   const int full = model_dim(m);
   if (dim < 1 || dim > full) return set_error(FG_EINVAL, "gemma: Dim(%d) outside 1..%d", dim, full);
   FG_CUDA_TRY(cudaSetDevice(m->device));
-  return forward(m, d_ids, d_lengths, B, T, dim, precision, d_out, static_cast<cudaStream_t>(stream));
+  return forward_graphed(m, d_ids, d_lengths, B, T, dim, precision, d_out, static_cast<cudaStream_t>(stream));
 }
 
 int fg_embed_ids(fg_model* m, const int32_t* ids, const int32_t* lengths, int B, int T, int dim,
@@ -1721,6 +1809,11 @@ int fg_embed_ids(fg_model* m, const int32_t* ids, const int32_t* lengths, int B,
   FG_CUDA_TRY(cudaSetDevice(m->device));
   if (!m->stream) FG_CUDA_TRY(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
   const int64_t nid = int64_t(B) * T;
+  if (nid > m->d_ids_cap || B > m->d_len_cap || int64_t(B) * dim > m->d_out_cap) {
+    // graphs may hold the staging buffers about to be replaced
+    FG_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    drop_graphs(m);
+  }
   if (nid > m->d_ids_cap) {
     if (m->d_ids) cudaFree(m->d_ids);
     FG_CUDA_TRY(cudaMalloc(&m->d_ids, size_t(nid) * 4));
@@ -1935,6 +2028,8 @@ void fg_model_destroy(fg_model* m) {
     cudaEventDestroy(mk.b);
   }
   for (auto e : m->event_pool) cudaEventDestroy(e);
+  drop_graphs(m);
+  if (m->cap_stream) cudaStreamDestroy(m->cap_stream);
   if (m->attn_ws) cudaFree(m->attn_ws);
   for (void* p : m->allocations) cudaFree(p);
   if (m->d_ids) cudaFree(m->d_ids);

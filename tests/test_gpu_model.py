@@ -340,3 +340,45 @@ def test_device_api(small):
     model.check()
     want = model.embed_padded(ids, lengths)
     assert np.array_equal(out.cpu().numpy(), want)
+
+
+def test_device_api_graph_replay(small):
+    """Repeated device-API calls with one shape and one set of buffers: the
+    first runs eagerly, the second is captured into a CUDA graph and
+    launched, the third launches the graph. Every result is bitwise the
+    eager forward's, the per-phase launch counts still count every call,
+    and ids written into the same buffer afterwards are the ones embedded."""
+    import torch
+
+    from ai_b200 import synthetic as S
+
+    cfg, w, model, orc = small
+    B, T = 4, 64
+    ids = S.make_ids(B, T, 31, cfg["vocab_size"])
+    lengths = np.array([64, 17, 40, 2], np.int32)
+    d_ids = torch.from_numpy(ids).cuda()
+    d_len = torch.from_numpy(lengths).cuda()
+    out = torch.empty((B, 768), dtype=torch.float32, device="cuda")
+    s = torch.cuda.current_stream()
+
+    def run():
+        model.embed_device(d_ids, d_len, B, T, 768, out, s)
+        s.synchronize()
+        model.check()
+        return out.cpu().numpy().copy()
+
+    def launches():
+        return sum(v["launches"] for v in model.read_profile().values())
+
+    launches()
+    first = run()
+    per_call = launches()
+    second = run()
+    third = run()
+    assert per_call > 0 and launches() == 2 * per_call
+    assert np.array_equal(first, second) and np.array_equal(first, third)
+    ids2 = S.make_ids(B, T, 32, cfg["vocab_size"])
+    d_ids.copy_(torch.from_numpy(ids2))
+    got = run()
+    assert np.array_equal(got, model.embed_padded(ids2, lengths))
+    assert not np.array_equal(got, first)
