@@ -240,7 +240,13 @@ double fg_sequence_cost(int length);
 int fg_plan_batches(const int32_t* lengths, int nseq, int64_t batch_tokens, int32_t* order, int32_t* batch_end);
 
 /* As fg_embed_ids with device buffers on the model's device, asynchronous
- * on `stream` (a cudaStream_t, NULL = default stream). */
+ * on `stream` (a cudaStream_t, NULL = default stream). Repeated calls with
+ * the same B, T, dim, precision and buffers run the forward as a CUDA graph
+ * (the first call runs it eagerly, the second captures it on a stream of
+ * the model's and launches it on `stream`); the result is the same bit
+ * for bit, and the graph reads the buffers' contents when it runs, so new
+ * ids in the same buffer are what it embeds. While profiling is enabled
+ * (fg_model_set_profiling) every call runs eagerly. */
 int fg_embed_ids_device(fg_model* m, const int32_t* d_ids, const int32_t* d_lengths, int B, int T,
                         int dim, int precision, float* d_out, void* stream);
 
