@@ -85,6 +85,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+
 // Waits for the phase with the given parity to complete. Gives up after
 // the device's wait limit (gerr's status block), or as soon as another role of the CTA has aborted
 // (*abort != 0); on a timeout it raises the abort flag and records `code`.
