@@ -580,16 +580,17 @@ __global__ void __launch_bounds__(kThreads, 1)
               rl[j ^ sw] = make_uint4(lw[4 * j], lw[4 * j + 1], lw[4 * j + 2], lw[4 * j + 3]);
             }
           }
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0 && tw < p.T) {
-          for (int ch = 0; ch < 4; ++ch) {
-            const int col = h * Dh + oh * kD + col_base + ch * 32;
-            tma_store_3d(&mO, smem_u32(stg + ch * 4096), col, tw, b);
-            tma_store_3d(&mOlo, smem_u32(stg + ch * 4096 + 2048), col, tw, b);
+          // this pair of chunks goes out while the next is staged
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && tw < p.T) {
+            for (int u = 0; u < 2; ++u) {
+              const int col = h * Dh + oh * kD + col_base + (ch + u) * 32;
+              tma_store_3d(&mO, smem_u32(stg + (ch + u) * 4096), col, tw, b);
+              tma_store_3d(&mOlo, smem_u32(stg + (ch + u) * 4096 + 2048), col, tw, b);
+            }
+            tma_store_commit();
           }
-          tma_store_commit();
         }
         if (lane == 0) tma_store_wait_read<0>();  // the boxes are read; the writes complete on their own
         __syncwarp();
